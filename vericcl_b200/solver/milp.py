@@ -1,0 +1,247 @@
+"""A small MILP modelling layer solved with HiGHS (``scipy.optimize.milp``).
+
+This is the package's replacement for the reference's SCIP adapter
+(vericcl/solver/scip_api.py:97-278): variables with bounds and integrality,
+sparse linear constraints, indicator-style big-M disjunctions, a warm-start
+check, lexicographic multi-objective solving, a time limit and MIP gap, and
+an *owned* mode that solves in a child process so a stuck solve can be
+killed at its lease deadline (vericcl/solver/worker_scope.py:110-238).
+Proven outcomes are cached by the model's content hash.
+"""
+from __future__ import annotations
+
+import multiprocessing as mp
+import time
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from vericcl_b200.errors import SolverError
+from vericcl_b200.utils.hashing import digest
+
+INF = float("inf")
+
+
+@dataclass
+class Var:
+    index: int
+    name: str
+    lb: float
+    ub: float
+    integer: bool
+
+
+@dataclass
+class Solution:
+    status: str                 # optimal | feasible | infeasible | timeout | error
+    objective: float | None
+    values: dict = field(default_factory=dict)
+    gap: float | None = None
+    runtime_s: float = 0.0
+    message: str = ""
+
+    @property
+    def usable(self) -> bool:
+        return self.status in ("optimal", "feasible") and self.values is not None
+
+    def __getitem__(self, name):
+        return self.values[name]
+
+
+class Model:
+    """Linear model: ``minimise c·x  s.t.  lo <= A x <= hi, lb <= x <= ub``."""
+
+    def __init__(self, name: str = "model"):
+        self.name = name
+        self.vars: list[Var] = []
+        self.by_name: dict[str, Var] = {}
+        self.rows: list[tuple[dict, float, float, str]] = []
+        self.objective: dict[int, float] = {}
+        self.objective_constant = 0.0
+
+    # -- variables ---------------------------------------------------------
+    def add_var(self, name: str, lb: float = 0.0, ub: float = INF, integer: bool = False) -> Var:
+        if name in self.by_name:
+            raise SolverError("duplicate variable " + name)
+        var = Var(len(self.vars), name, lb, ub, integer)
+        self.vars.append(var)
+        self.by_name[name] = var
+        return var
+
+    def binary(self, name: str) -> Var:
+        return self.add_var(name, 0.0, 1.0, True)
+
+    def continuous(self, name: str, lb: float = 0.0, ub: float = INF) -> Var:
+        return self.add_var(name, lb, ub, False)
+
+    # -- constraints -------------------------------------------------------
+    def add(self, terms, lo: float = -INF, hi: float = INF, name: str = "") -> None:
+        """Add ``lo <= sum(coef * var) <= hi``; ``terms`` is [(coef, Var)]."""
+        row = {}
+        for coef, var in terms:
+            row[var.index] = row.get(var.index, 0.0) + float(coef)
+        self.rows.append((row, float(lo), float(hi), name))
+
+    def add_le(self, terms, rhs, name=""):
+        self.add(terms, -INF, rhs, name)
+
+    def add_ge(self, terms, rhs, name=""):
+        self.add(terms, rhs, INF, name)
+
+    def add_eq(self, terms, rhs, name=""):
+        self.add(terms, rhs, rhs, name)
+
+    def indicator_le(self, binary: Var, terms, rhs, big_m: float, name=""):
+        """``binary = 1  =>  sum(terms) <= rhs`` via big-M."""
+        self.add_le(list(terms) + [(big_m, binary)], rhs + big_m, name)
+
+    def disjunction(self, a_end, b_start, b_end, a_start, order: Var, big_m: float, name=""):
+        """Either a finishes before b starts (order=1) or b before a (order=0)."""
+        self.add_le([(1, a_end), (-1, b_start), (big_m, order)], big_m, name + ":ab")
+        self.add_le([(1, b_end), (-1, a_start), (-big_m, order)], 0.0, name + ":ba")
+
+    def minimize(self, terms, constant: float = 0.0) -> None:
+        self.objective = {}
+        for coef, var in terms:
+            self.objective[var.index] = self.objective.get(var.index, 0.0) + float(coef)
+        self.objective_constant = constant
+
+    # -- checks ------------------------------------------------------------
+    def evaluate(self, values: dict) -> float:
+        return self.objective_constant + sum(c * values[self.vars[i].name] for i, c in self.objective.items())
+
+    def violated(self, values: dict, tol: float = 1e-6) -> list:
+        """Names of constraints a candidate assignment violates (warm-start check)."""
+        bad = []
+        for var in self.vars:
+            v = values.get(var.name)
+            if v is None or v < var.lb - tol or v > var.ub + tol or (var.integer and abs(v - round(v)) > tol):
+                bad.append("bound:" + var.name)
+        for row, lo, hi, name in self.rows:
+            total = sum(c * values.get(self.vars[i].name, 0.0) for i, c in row.items())
+            if total < lo - tol or total > hi + tol:
+                bad.append(name or "row")
+        return bad
+
+    def fingerprint(self) -> str:
+        return digest({"v": [(v.name, v.lb if v.lb != -INF else "-inf", v.ub if v.ub != INF else "inf", v.integer)
+                             for v in self.vars],
+                       "r": [(sorted(r.items()), lo if lo != -INF else "-inf", hi if hi != INF else "inf")
+                             for r, lo, hi, _ in self.rows],
+                       "o": sorted(self.objective.items())})
+
+    # -- solving -----------------------------------------------------------
+    def arrays(self):
+        n = len(self.vars)
+        c = np.zeros(n)
+        for i, coef in self.objective.items():
+            c[i] = coef
+        lb = np.array([v.lb for v in self.vars], dtype=float)
+        ub = np.array([v.ub for v in self.vars], dtype=float)
+        integrality = np.array([1 if v.integer else 0 for v in self.vars], dtype=np.uint8)
+        if self.rows:
+            from scipy.sparse import coo_matrix
+            data, ri, ci, lo, hi = [], [], [], [], []
+            for r, (row, rlo, rhi, _) in enumerate(self.rows):
+                for i, coef in row.items():
+                    data.append(coef)
+                    ri.append(r)
+                    ci.append(i)
+                lo.append(rlo)
+                hi.append(rhi)
+            a = coo_matrix((data, (ri, ci)), shape=(len(self.rows), n)).tocsr()
+            return c, lb, ub, integrality, a, np.array(lo), np.array(hi)
+        return c, lb, ub, integrality, None, None, None
+
+    def solve(self, *, time_limit: float = 60.0, mip_gap: float = 0.0, threads: int = 1) -> Solution:
+        return _solve_arrays(self.arrays(), [v.name for v in self.vars], self.objective_constant,
+                             time_limit, mip_gap)
+
+
+def _solve_arrays(arrays, names, constant, time_limit, mip_gap) -> Solution:
+    from scipy.optimize import Bounds, LinearConstraint, milp
+    c, lb, ub, integrality, a, lo, hi = arrays
+    start = time.monotonic()
+    constraints = [] if a is None else [LinearConstraint(a, lo, hi)]
+    options = {"time_limit": max(0.05, float(time_limit)), "mip_rel_gap": float(mip_gap), "disp": False}
+    try:
+        res = milp(c, constraints=constraints, integrality=integrality, bounds=Bounds(lb, ub), options=options)
+    except Exception as error:  # pragma: no cover - scipy internal failure
+        return Solution("error", None, {}, None, time.monotonic() - start, str(error))
+    runtime = time.monotonic() - start
+    if res.x is None:
+        status = "infeasible" if res.status == 2 else "timeout" if res.status == 1 else "error"
+        return Solution(status, None, {}, None, runtime, str(res.message))
+    values = {name: float(v) for name, v in zip(names, res.x)}
+    gap = getattr(res, "mip_gap", None)
+    status = "optimal" if res.status == 0 else "feasible"
+    return Solution(status, float(res.fun) + constant, values, gap, runtime, str(res.message))
+
+
+_CACHE: dict[str, Solution] = {}
+
+
+def _worker(conn, arrays, names, constant, time_limit, mip_gap):
+    try:
+        conn.send(_solve_arrays(arrays, names, constant, time_limit, mip_gap))
+    except BaseException as error:  # pragma: no cover
+        conn.send(Solution("error", None, {}, None, 0.0, repr(error)))
+    finally:
+        conn.close()
+
+
+def solve_owned(model: Model, *, time_limit: float = 60.0, mip_gap: float = 0.0, grace_s: float = 5.0,
+                use_cache: bool = True) -> Solution:
+    """Solve in a fresh child process that is killed if it outlives its lease.
+
+    Proven-optimal outcomes are cached by model fingerprint, so identical
+    subproblems (isomorphic templates) are solved once.
+    """
+    key = model.fingerprint() + ":%g" % mip_gap
+    if use_cache and key in _CACHE:
+        return _CACHE[key]
+    ctx = mp.get_context("fork")
+    parent, child = ctx.Pipe(duplex=False)
+    proc = ctx.Process(target=_worker, args=(child, model.arrays(), [v.name for v in model.vars],
+                                             model.objective_constant, time_limit, mip_gap), daemon=True)
+    proc.start()
+    child.close()
+    deadline = time.monotonic() + time_limit + grace_s
+    result = None
+    while time.monotonic() < deadline:
+        if parent.poll(0.05):
+            try:
+                result = parent.recv()
+            except EOFError:
+                result = Solution("error", None, {}, None, 0.0, "solver worker exited without a result")
+            break
+        if not proc.is_alive() and not parent.poll(0):
+            result = Solution("error", None, {}, None, 0.0, "solver worker died (exit %s)" % proc.exitcode)
+            break
+    if result is None:
+        proc.terminate()
+        proc.join(2.0)
+        if proc.is_alive():
+            proc.kill()
+        result = Solution("timeout", None, {}, None, time_limit, "owned solver exceeded its lease")
+    proc.join(1.0)
+    if use_cache and result.status == "optimal":
+        _CACHE[key] = result
+    return result
+
+
+def solve_lexicographic(model: Model, objectives, *, time_limit: float = 60.0, mip_gap: float = 0.0,
+                        tolerance: float = 1e-6, owned: bool = False) -> Solution:
+    """Solve objectives in priority order, fixing each optimum before the next."""
+    best = None
+    for level, terms in enumerate(objectives):
+        model.minimize(terms)
+        sol = solve_owned(model, time_limit=time_limit, mip_gap=mip_gap) if owned else \
+            model.solve(time_limit=time_limit, mip_gap=mip_gap)
+        if not sol.usable:
+            return best if best is not None else sol
+        best = sol
+        if level + 1 < len(objectives):
+            model.add_le(list(terms), sol.objective + tolerance * max(1.0, abs(sol.objective)),
+                         name="lex%d" % level)
+    return best
