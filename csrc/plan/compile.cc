@@ -1,0 +1,733 @@
+// Schedule compiler: XML program -> pull-based device programs.
+//
+// Pipeline:
+//   1. index steps, check peers/channels/dependencies, pair every send with
+//      its receive (per connection (src, dst, channel) in TB order, as in
+//      MSCCL's FIFO connections);
+//   2. topological order of the global step graph (TB order, explicit deps,
+//      send->receive); a cycle is a deadlock under MSCCL semantics;
+//   3. symbolic replay (contributor masks) to place the fused scale on the
+//      step that completes each reduction;
+//   4. thread blocks made only of sends are elided (the receiver pulls; the
+//      sender only needs its dependencies to be complete), every other block
+//      becomes a device block;
+//   5. waits: explicit dependencies, data readiness of pulled sends, and
+//      write-after-read acknowledgements: a step that overwrites a region a
+//      send reads waits for that send's receiver to finish; each rank finally
+//      waits for all of its sends to be consumed before the kernel ends;
+//   6. optional chain fusion (receive-reduce chains into one n-ary reduce);
+//   7. a final deadlock check of the device event graph.
+#include <algorithm>
+#include <deque>
+#include <functional>
+#include <map>
+#include <set>
+#include <sstream>
+#include <tuple>
+
+#include "vb/plan.h"
+
+namespace vb {
+namespace {
+
+bool has_send(XKind k) { return k == X_S || k == X_RCS || k == X_RRS || k == X_RRCS; }
+bool has_recv(XKind k) { return k == X_R || k == X_RRC || k == X_RCS || k == X_RRS || k == X_RRCS; }
+bool writes_dst(XKind k) { return k == X_R || k == X_RRC || k == X_RCS || k == X_RRCS || k == X_CPY || k == X_RE; }
+bool reduces(XKind k) { return k == X_RRC || k == X_RRS || k == X_RRCS || k == X_RE; }
+const char* kname(XKind k) {
+  static const char* names[] = {"s", "r", "rrc", "rcs", "rrs", "rrcs", "cpy", "re", "nop"};
+  return names[k];
+}
+
+struct SRef {
+  int rank = -1, tb = -1, step = -1;
+  bool valid() const { return rank >= 0; }
+  bool operator<(const SRef& o) const { return std::tie(rank, tb, step) < std::tie(o.rank, o.tb, o.step); }
+  bool operator==(const SRef& o) const { return rank == o.rank && tb == o.tb && step == o.step; }
+};
+
+struct Region {
+  int rank, buf, chunk;
+  bool operator<(const Region& o) const { return std::tie(rank, buf, chunk) < std::tie(o.rank, o.buf, o.chunk); }
+};
+
+// (rank, device block) -> max event.  Block -1 is the per-rank start flag.
+using EventSet = std::map<std::pair<int, int>, int>;
+
+void merge(EventSet& into, const EventSet& from) {
+  for (auto& kv : from) {
+    auto it = into.find(kv.first);
+    if (it == into.end() || it->second < kv.second) into[kv.first] = kv.second;
+  }
+}
+
+struct Value {
+  int index = -1;
+  uint32_t mask = 0;
+  bool scaled = false;
+  bool known = false;
+};
+
+class Compiler {
+ public:
+  Compiler(const XAlgo& a, const CompileOptions& o) : a_(a), o_(o), P_(a.ngpus) {}
+
+  CompiledPlan run() {
+    index_steps();
+    pair_connections();
+    topo_order();
+    if (o_.reducing) place_scale();
+    assign_blocks();
+    build_waits_and_hazards();
+    emit();
+    deadlock_check();
+    CompiledPlan plan;
+    plan.algo = a_;
+    plan.options = o_;
+    plan.ranks = std::move(out_);
+    plan.stats = stats_;
+    return plan;
+  }
+
+ private:
+  [[noreturn]] void fail(const std::string& m) { throw CompileError(m); }
+
+  const XStep& step(const SRef& r) const { return a_.gpus[r.rank].tbs[r.tb].steps[r.step]; }
+  const XTB& tb(int rank, int t) const { return a_.gpus[rank].tbs[t]; }
+
+  // In-place aliasing resolved to one canonical (buffer, chunk).
+  Region canon(int rank, int buf, int chunk) const {
+    if (!a_.inplace || buf == BUF_SCR) return Region{rank, buf, chunk};
+    const XGpu& g = a_.gpus[rank];
+    if (a_.coll == "allgather") return buf == BUF_IN ? Region{rank, BUF_OUT, rank * g.i_chunks + chunk} : Region{rank, BUF_OUT, chunk};
+    if (a_.coll == "reduce_scatter") return buf == BUF_OUT ? Region{rank, BUF_IN, rank * g.o_chunks + chunk} : Region{rank, BUF_IN, chunk};
+    return Region{rank, BUF_OUT, chunk};
+  }
+
+  int slots(int rank, int buf) const {
+    const XGpu& g = a_.gpus[rank];
+    return buf == BUF_IN ? g.i_chunks : buf == BUF_OUT ? g.o_chunks : g.s_chunks;
+  }
+
+  void check_region(int rank, int buf, int off, int cnt, const char* what) {
+    if (off < 0) fail(std::string("step ") + what + " offset is missing");
+    Region c = canon(rank, buf, off);
+    int limit = slots(rank, c.buf);
+    if (c.chunk + cnt > limit) {
+      std::ostringstream m;
+      m << "rank " << rank << " " << what << " region " << "ios"[buf] << "[" << off << "+" << cnt
+        << "] exceeds its " << limit << " slots";
+      fail(m.str());
+    }
+  }
+
+  void index_steps() {
+    for (int r = 0; r < P_; ++r) {
+      const XGpu& g = a_.gpus[r];
+      std::map<int, int> ids;
+      for (int t = 0; t < (int)g.tbs.size(); ++t) {
+        if (ids.count(g.tbs[t].id)) fail("rank " + std::to_string(r) + " has duplicate TB id");
+        ids[g.tbs[t].id] = t;
+      }
+      tb_index_.push_back(ids);
+      for (int t = 0; t < (int)g.tbs.size(); ++t) {
+        const XTB& b = g.tbs[t];
+        if (b.send >= P_ || b.recv >= P_ || b.send == r || b.recv == r) fail("TB peer outside the rank range");
+        for (int s = 0; s < (int)b.steps.size(); ++s) {
+          const XStep& st = b.steps[s];
+          ++stats_.xml_steps;
+          if (has_send(st.kind) && b.send < 0) fail(std::string("step '") + kname(st.kind) + "' in a TB without a send peer");
+          if (has_recv(st.kind) && b.recv < 0) fail(std::string("step '") + kname(st.kind) + "' in a TB without a receive peer");
+          if (st.kind == X_RRS) fail("'rrs' (reduce-and-forward without a local store) needs a staging buffer; not supported");
+          if (st.kind == X_S || st.kind == X_CPY || st.kind == X_RRC || st.kind == X_RE) check_region(r, st.srcbuf, st.srcoff, st.cnt, "source");
+          if (writes_dst(st.kind)) check_region(r, st.dstbuf, st.dstoff, st.cnt, "destination");
+          if (st.depid >= 0) {
+            auto it = ids.find(st.depid);
+            if (it == ids.end()) fail("dependency names an unknown TB");
+            if (st.deps < 0 || st.deps >= (int)g.tbs[it->second].steps.size()) fail("dependency names an unknown step");
+            if (it->second == t && st.deps >= s) fail("dependency points at the same or a later step of its TB");
+          } else if (st.deps >= 0) {
+            fail("dependency step without a dependency TB");
+          }
+          all_.push_back(SRef{r, t, s});
+        }
+      }
+    }
+  }
+
+  void pair_connections() {
+    std::map<std::tuple<int, int, int>, std::vector<SRef>> sends, recvs;
+    std::set<std::tuple<int, int, int, int>> owners;
+    for (const SRef& x : all_) {
+      const XTB& b = tb(x.rank, x.tb);
+      const XStep& st = step(x);
+      if (has_send(st.kind)) sends[{x.rank, b.send, b.chan}].push_back(x);
+      if (has_recv(st.kind)) recvs[{b.recv, x.rank, b.chan}].push_back(x);
+    }
+    for (int r = 0; r < P_; ++r)
+      for (auto& b : a_.gpus[r].tbs) {
+        bool s = false, v = false;
+        for (auto& st : b.steps) { s |= has_send(st.kind); v |= has_recv(st.kind); }
+        if (s && !owners.insert({r, b.send, b.chan, 0}).second) fail("two TBs send to one peer on one channel");
+        if (v && !owners.insert({r, b.recv, b.chan, 1}).second) fail("two TBs receive from one peer on one channel");
+      }
+    for (auto& kv : sends) {
+      auto it = recvs.find(kv.first);
+      size_t n = it == recvs.end() ? 0 : it->second.size();
+      if (n != kv.second.size()) {
+        std::ostringstream m;
+        m << "connection " << std::get<0>(kv.first) << "->" << std::get<1>(kv.first) << " channel " << std::get<2>(kv.first)
+          << " has " << kv.second.size() << " sends but " << n << " receives";
+        fail(m.str());
+      }
+      for (size_t i = 0; i < n; ++i) {
+        match_recv_[kv.second[i]] = it->second[i];
+        match_send_[it->second[i]] = kv.second[i];
+        if (step(kv.second[i]).cnt != step(it->second[i]).cnt) fail("matched send and receive disagree on cnt");
+      }
+    }
+    for (auto& kv : recvs)
+      if (!sends.count(kv.first)) fail("a receive has no matching send");
+  }
+
+  std::vector<SRef> preds(const SRef& x) const {
+    std::vector<SRef> p;
+    if (x.step > 0) p.push_back(SRef{x.rank, x.tb, x.step - 1});
+    const XStep& st = step(x);
+    if (st.depid >= 0) p.push_back(SRef{x.rank, tb_index_[x.rank].at(st.depid), st.deps});
+    auto it = match_send_.find(x);
+    if (it != match_send_.end()) p.push_back(it->second);
+    return p;
+  }
+
+  void topo_order() {
+    std::map<SRef, int> indeg;
+    std::map<SRef, std::vector<SRef>> succ;
+    for (const SRef& x : all_) indeg[x] = 0;
+    for (const SRef& x : all_)
+      for (const SRef& p : preds(x)) { indeg[x]++; succ[p].push_back(x); }
+    std::deque<SRef> ready;
+    for (const SRef& x : all_) if (indeg[x] == 0) ready.push_back(x);
+    while (!ready.empty()) {
+      SRef x = ready.front();
+      ready.pop_front();
+      topo_pos_[x] = (int)order_.size();
+      order_.push_back(x);
+      for (const SRef& y : succ[x]) if (--indeg[y] == 0) ready.push_back(y);
+    }
+    if (order_.size() != all_.size()) fail("schedule deadlocks: the step dependency graph has a cycle");
+  }
+
+  void place_scale() {
+    const uint32_t full = P_ >= 32 ? 0xffffffffu : ((1u << P_) - 1u);
+    std::map<Region, Value> state;
+    for (int r = 0; r < P_; ++r)
+      for (int k = 0; k < a_.gpus[r].i_chunks; ++k) {
+        Value v;
+        v.index = k; v.mask = 1u << r; v.known = true;
+        state[canon(r, BUF_IN, k)] = v;
+      }
+    std::map<SRef, std::vector<Value>> carried;   // value captured at each send
+    auto read = [&](int rank, int buf, int off, int cnt) {
+      std::vector<Value> vs;
+      for (int k = 0; k < cnt; ++k) vs.push_back(state[canon(rank, buf, off + k)]);
+      return vs;
+    };
+    auto combine = [&](const Value& a, const Value& b, bool& scale) {
+      Value v;
+      if (!a.known || !b.known) return v;
+      v.known = true;
+      v.index = a.index;
+      v.mask = a.mask | b.mask;
+      v.scaled = a.scaled || b.scaled;
+      if (v.mask == full && !v.scaled && !(a.mask & b.mask)) { v.scaled = true; scale = true; }
+      return v;
+    };
+    for (const SRef& x : order_) {
+      const XStep& st = step(x);
+      bool scale = false;
+      std::vector<Value> result;
+      std::vector<Value> incoming;
+      if (has_recv(st.kind)) incoming = carried[match_send_.at(x)];
+      switch (st.kind) {
+        case X_S: carried[x] = read(x.rank, st.srcbuf, st.srcoff, st.cnt); break;
+        case X_R: case X_RCS: result = incoming; break;
+        case X_CPY: result = read(x.rank, st.srcbuf, st.srcoff, st.cnt); break;
+        case X_RRC: case X_RRCS: {
+          auto local = read(x.rank, st.srcbuf, st.srcoff, st.cnt);
+          for (int k = 0; k < st.cnt; ++k) result.push_back(combine(incoming[k], local[k], scale));
+          break;
+        }
+        case X_RE: {
+          auto src = read(x.rank, st.srcbuf, st.srcoff, st.cnt);
+          auto dst = read(x.rank, st.dstbuf, st.dstoff, st.cnt);
+          for (int k = 0; k < st.cnt; ++k) result.push_back(combine(src[k], dst[k], scale));
+          break;
+        }
+        default: break;
+      }
+      if (st.kind == X_R || st.kind == X_RCS || st.kind == X_CPY) {
+        // A complete value that was never scaled (single-rank programs) is scaled where it is copied.
+        for (auto& v : result)
+          if (v.known && v.mask == full && !v.scaled) { v.scaled = true; scale = true; }
+      }
+      if (writes_dst(st.kind))
+        for (int k = 0; k < st.cnt; ++k) state[canon(x.rank, st.dstbuf, st.dstoff + k)] = result[k];
+      if (st.kind == X_RCS || st.kind == X_RRCS) carried[x] = result;
+      if (scale) { scale_steps_.insert(x); ++stats_.scale_steps; }
+    }
+  }
+
+  void assign_blocks() {
+    dblock_.resize(P_);
+    out_.resize(P_);
+    for (int r = 0; r < P_; ++r) {
+      const XGpu& g = a_.gpus[r];
+      dblock_[r].assign(g.tbs.size(), -1);
+      int next = 0;
+      for (int t = 0; t < (int)g.tbs.size(); ++t) {
+        bool only_sends = true;
+        for (auto& st : g.tbs[t].steps) if (st.kind != X_S && st.kind != X_NOP) only_sends = false;
+        if (o_.elide_sends && only_sends) { ++stats_.elided_blocks; continue; }
+        dblock_[r][t] = next++;
+      }
+      out_[r].i_chunks = g.i_chunks;
+      out_[r].o_chunks = g.o_chunks;
+      out_[r].s_chunks = g.s_chunks;
+      nblocks_.push_back(next == 0 ? 1 : next);   // a rank always runs at least one (possibly empty) block
+      synthetic_.push_back(next == 0);
+    }
+  }
+
+  bool elided(const SRef& x) const { return dblock_[x.rank][x.tb] < 0; }
+
+  // Event set that is complete once step x is complete under pull semantics.
+  EventSet completion(const SRef& x) {
+    auto it = completion_memo_.find(x);
+    if (it != completion_memo_.end()) return it->second;
+    EventSet e;
+    const XStep& st = step(x);
+    if (st.kind == X_S) {
+      SRef rv = match_recv_.at(x);
+      e[{rv.rank, redirect_block(rv)}] = 2 * redirect_step(rv) + 2;
+    } else if (elided(x)) {
+      e = arrival(x);
+    } else {
+      e[{x.rank, redirect_block(x)}] = 2 * redirect_step(x) + 2;
+      if (st.kind == X_RCS || st.kind == X_RRCS) {
+        SRef rv = match_recv_.at(x);
+        merge(e, EventSet{{{rv.rank, redirect_block(rv)}, 2 * redirect_step(rv) + 2}});
+      }
+    }
+    completion_memo_[x] = e;
+    return e;
+  }
+
+  // Events implied once an elided TB reaches step x (all earlier dependencies complete).
+  EventSet arrival(const SRef& x) {
+    auto it = arrival_memo_.find(x);
+    if (it != arrival_memo_.end()) return it->second;
+    EventSet e;
+    if (x.step > 0) e = arrival(SRef{x.rank, x.tb, x.step - 1});
+    const XStep& st = step(x);
+    if (st.depid >= 0) merge(e, completion(SRef{x.rank, tb_index_[x.rank].at(st.depid), st.deps}));
+    arrival_memo_[x] = e;
+    return e;
+  }
+
+  // Events after which the data a receive pulls from send x is ready.
+  EventSet data_ready(const SRef& x) {
+    const XStep& st = step(x);
+    EventSet e;
+    if (elided(x)) {
+      e = arrival(x);
+    } else if (st.kind == X_S) {
+      e[{x.rank, dblock_[x.rank][x.tb]}] = 2 * x.step + 1;
+      need_arrive_.insert(x);
+    } else {
+      e[{x.rank, dblock_[x.rank][x.tb]}] = 2 * x.step + 2;
+    }
+    bool local = false;
+    for (auto& kv : e) if (kv.first.first == x.rank) local = true;
+    if (!local) e[{x.rank, -1}] = 1;   // the sender's kernel must have started
+    return e;
+  }
+
+  // Source region a receive of send x pulls from (sender's memory).
+  Region pull_source(const SRef& x) const {
+    const XStep& st = step(x);
+    if (st.kind == X_S) return canon(x.rank, st.srcbuf, st.srcoff);
+    return canon(x.rank, st.dstbuf, st.dstoff);   // rcs / rrcs forward what they stored
+  }
+
+  // Chain fusion bookkeeping: a fused-away step's events are served by its chain's final step.
+  int redirect_block(const SRef& x) const {
+    auto it = fused_into_.find(x);
+    const SRef& y = it == fused_into_.end() ? x : it->second;
+    return dblock_[y.rank][y.tb];
+  }
+  int redirect_step(const SRef& x) const {
+    auto it = fused_into_.find(x);
+    return it == fused_into_.end() ? x.step : it->second.step;
+  }
+
+  void find_chains() {
+    if (!o_.fuse_chains) return;
+    // readers of each canonical region, in topological order
+    std::map<Region, std::vector<SRef>> readers, writers;
+    for (const SRef& x : order_) {
+      const XStep& st = step(x);
+      auto add_read = [&](int buf, int off) { for (int k = 0; k < st.cnt; ++k) readers[canon(x.rank, buf, off + k)].push_back(x); };
+      if (st.kind == X_S || st.kind == X_CPY || st.kind == X_RRC || st.kind == X_RE) add_read(st.srcbuf, st.srcoff);
+      if (st.kind == X_RE || st.kind == X_RCS || st.kind == X_RRCS) add_read(st.dstbuf, st.dstoff);
+      if (writes_dst(st.kind)) for (int k = 0; k < st.cnt; ++k) writers[canon(x.rank, st.dstbuf, st.dstoff + k)].push_back(x);
+    }
+    // an rrc y whose local source is exactly the destination written by rrc x, where y is the only
+    // reader of that value and nothing else writes the region in between, extends x's chain.
+    std::map<SRef, SRef> next;
+    for (const SRef& x : order_) {
+      const XStep& sx = step(x);
+      if (sx.kind != X_RRC || sx.cnt != 1 || elided(x)) continue;
+      Region d = canon(x.rank, sx.dstbuf, sx.dstoff);
+      auto& rd = readers[d];
+      auto& wr = writers[d];
+      int px = topo_pos_[x];
+      std::vector<SRef> later;
+      for (auto& r : rd) if (topo_pos_[r] > px) later.push_back(r);
+      if (later.empty()) continue;
+      const SRef& y = later.front();
+      const XStep& sy = step(y);
+      if (sy.kind != X_RRC || sy.cnt != 1 || y.rank != x.rank) continue;
+      if (!(canon(y.rank, sy.srcbuf, sy.srcoff).buf == d.buf && canon(y.rank, sy.srcbuf, sy.srcoff).chunk == d.chunk)) continue;
+      // y must be the only reader of x's value before the region is written again
+      int nw = 1 << 30;
+      for (auto& w : wr) if (topo_pos_[w] > px) nw = std::min(nw, topo_pos_[w]);
+      bool exclusive = true;
+      for (auto& r : later)
+        if (topo_pos_[r] <= nw && !(r == y)) exclusive = false;
+      if (topo_pos_[y] > nw) exclusive = false;
+      if (!exclusive) continue;
+      if (scale_steps_.count(x)) continue;
+      next[x] = y;
+    }
+    std::set<SRef> has_prev;
+    for (auto& kv : next) has_prev.insert(kv.second);
+    for (auto& kv : next) {
+      if (has_prev.count(kv.first)) continue;   // not a chain head
+      std::vector<SRef> chain{kv.first};
+      SRef cur = kv.first;
+      while (next.count(cur) && (int)chain.size() < 15) { cur = next[cur]; chain.push_back(cur); }
+      if (chain.size() < 2) continue;
+      SRef last = chain.back();
+      for (size_t i = 0; i + 1 < chain.size(); ++i) fused_into_[chain[i]] = last;
+      chains_[last] = chain;
+      stats_.fused_reduces++;
+    }
+  }
+
+  struct PendingStep {
+    DevStep st;
+    std::vector<DevSrc> srcs;
+    EventSet waits;
+  };
+
+  void build_waits_and_hazards() {
+    find_chains();
+    dsteps_count_.resize(P_);
+    for (int r = 0; r < P_; ++r) {
+      dsteps_count_[r].assign(nblocks_[r], 0);
+      for (int t = 0; t < (int)a_.gpus[r].tbs.size(); ++t)
+        if (dblock_[r][t] >= 0) dsteps_count_[r][dblock_[r][t]] = (int)a_.gpus[r].tbs[t].steps.size();
+    }
+    // write-after-read acknowledgements: sends reading a region since its previous write
+    std::map<Region, std::vector<SRef>> open_sends;
+    std::map<SRef, std::vector<SRef>> acks;   // writer -> sends whose receivers it must wait for
+    for (const SRef& x : order_) {
+      const XStep& st = step(x);
+      if (writes_dst(st.kind)) {
+        for (int k = 0; k < st.cnt; ++k) {
+          Region d = canon(x.rank, st.dstbuf, st.dstoff + k);
+          auto it = open_sends.find(d);
+          if (it != open_sends.end()) {
+            for (auto& s : it->second) if (!(s == x)) acks[x].push_back(s);
+            open_sends.erase(it);
+          }
+        }
+      }
+      if (has_send(st.kind)) {
+        Region src = pull_source(x);
+        for (int k = 0; k < st.cnt; ++k) open_sends[Region{src.rank, src.buf, src.chunk + k}].push_back(x);
+      }
+    }
+    pending_.resize(P_);
+    for (int r = 0; r < P_; ++r) pending_[r].resize(nblocks_[r]);
+    for (const SRef& x : all_) {
+      int db = dblock_[x.rank][x.tb];
+      if (db < 0) continue;
+      const XStep& st = step(x);
+      PendingStep ps{};
+      ps.st.cnt = st.cnt;
+      ps.st.flags = 0;
+      if (st.depid >= 0) merge(ps.waits, completion(SRef{x.rank, tb_index_[x.rank].at(st.depid), st.deps}));
+      for (auto& s : acks[x]) merge(ps.waits, completion(s));
+      auto fused = fused_into_.find(x);
+      if (fused != fused_into_.end()) {
+        ps.st.op = OP_NOP;   // work moves to the chain's final step
+      } else if (chains_.count(x)) {
+        const auto& chain = chains_[x];
+        const XStep& head = step(chain.front());
+        Region base = canon(x.rank, head.srcbuf, head.srcoff);
+        ps.srcs.push_back(DevSrc{(int16_t)x.rank, (uint8_t)base.buf, 0, base.chunk});
+        for (const SRef& c : chain) {
+          const SRef& snd = match_send_.at(c);
+          Region src = pull_source(snd);
+          ps.srcs.push_back(DevSrc{(int16_t)src.rank, (uint8_t)src.buf, 0, src.chunk});
+          merge(ps.waits, data_ready(snd));
+          const XStep& cs = step(c);
+          if (cs.depid >= 0) merge(ps.waits, completion(SRef{c.rank, tb_index_[c.rank].at(cs.depid), cs.deps}));
+          for (auto& s : acks[c]) merge(ps.waits, completion(s));
+        }
+        Region d = canon(x.rank, st.dstbuf, st.dstoff);
+        ps.st.op = OP_REDUCE;
+        ps.st.dst_buf = (uint8_t)d.buf;
+        ps.st.dst_chunk = d.chunk;
+      } else {
+        switch (st.kind) {
+          case X_S: case X_NOP: ps.st.op = OP_NOP; break;
+          case X_R: case X_RCS: {
+            Region src = pull_source(match_send_.at(x));
+            ps.srcs.push_back(DevSrc{(int16_t)src.rank, (uint8_t)src.buf, 0, src.chunk});
+            merge(ps.waits, data_ready(match_send_.at(x)));
+            ps.st.op = OP_COPY;
+            break;
+          }
+          case X_RRC: case X_RRCS: {
+            Region loc = canon(x.rank, st.srcbuf, st.srcoff);
+            Region src = pull_source(match_send_.at(x));
+            ps.srcs.push_back(DevSrc{(int16_t)x.rank, (uint8_t)loc.buf, 0, loc.chunk});
+            ps.srcs.push_back(DevSrc{(int16_t)src.rank, (uint8_t)src.buf, 0, src.chunk});
+            merge(ps.waits, data_ready(match_send_.at(x)));
+            ps.st.op = OP_REDUCE;
+            break;
+          }
+          case X_CPY: {
+            Region loc = canon(x.rank, st.srcbuf, st.srcoff);
+            ps.srcs.push_back(DevSrc{(int16_t)x.rank, (uint8_t)loc.buf, 0, loc.chunk});
+            ps.st.op = OP_COPY;
+            break;
+          }
+          case X_RE: {
+            Region s1 = canon(x.rank, st.srcbuf, st.srcoff);
+            Region s2 = canon(x.rank, st.dstbuf, st.dstoff);
+            ps.srcs.push_back(DevSrc{(int16_t)x.rank, (uint8_t)s1.buf, 0, s1.chunk});
+            ps.srcs.push_back(DevSrc{(int16_t)x.rank, (uint8_t)s2.buf, 0, s2.chunk});
+            ps.st.op = OP_REDUCE;
+            break;
+          }
+          default: fail("unsupported step kind");
+        }
+        if (writes_dst(st.kind)) {
+          Region d = canon(x.rank, st.dstbuf, st.dstoff);
+          ps.st.dst_buf = (uint8_t)d.buf;
+          ps.st.dst_chunk = d.chunk;
+        }
+      }
+      if (scale_steps_.count(x)) ps.st.flags |= F_SCALE;
+      // drop waits implied by this CTA's own sequential order
+      auto own = ps.waits.find({x.rank, db});
+      if (own != ps.waits.end()) {
+        // earlier steps of this CTA are complete by program order; a fused chain member's completion
+        // is redirected to this very step and needs no wait either
+        if (own->second <= 2 * x.step || (chains_.count(x) && own->second == 2 * x.step + 2)) ps.waits.erase(own);
+        else fail("a step waits on its own or a later step of its block");
+      }
+      pending_[x.rank][db].resize(std::max<size_t>(pending_[x.rank][db].size(), x.step + 1));
+      pending_[x.rank][db][x.step] = ps;
+    }
+    // end-of-kernel acknowledgements: every send must be consumed
+    end_waits_.resize(P_);
+    for (const SRef& x : all_) {
+      const XStep& st = step(x);
+      if (!has_send(st.kind)) continue;
+      SRef rv = match_recv_.at(x);
+      merge(end_waits_[x.rank], EventSet{{{rv.rank, redirect_block(rv)}, 2 * redirect_step(rv) + 2}});
+    }
+  }
+
+  void emit() {
+    for (int r = 0; r < P_; ++r) {
+      RankProgram& rp = out_[r];
+      for (int db = 0; db < nblocks_[r]; ++db) {
+        DevBlock blk{};
+        blk.step_begin = (int)rp.steps.size();
+        blk.xml_tb = -1;
+        for (int t = 0; t < (int)dblock_[r].size(); ++t) if (dblock_[r][t] == db) blk.xml_tb = a_.gpus[r].tbs[t].id;
+        auto& steps = pending_[r][db];
+        blk.nsteps = (int)steps.size();
+        for (int s = 0; s < (int)steps.size(); ++s) {
+          PendingStep& ps = steps[s];
+          DevStep st = ps.st;
+          st.src_begin = (int)rp.srcs.size();
+          st.nsrc = (int)ps.srcs.size();
+          for (auto& sr : ps.srcs) rp.srcs.push_back(sr);
+          st.wait_begin = (int)rp.waits.size();
+          st.wait_count = 0;
+          for (auto& kv : ps.waits) {
+            DevWait w{};
+            w.rank = (int16_t)kv.first.first;
+            w.block = (int16_t)kv.first.second;
+            w.stride = w.block < 0 ? 0 : 2 * dsteps_count_[w.rank][w.block];
+            w.event = kv.second;
+            w.iter_delta = 0;
+            rp.waits.push_back(w);
+            st.wait_count++;
+            stats_.waits++;
+            if (w.rank != r) stats_.remote_waits++;
+            if (w.block >= 0) published_.insert({w.rank, w.block, w.event});
+          }
+          rp.steps.push_back(st);
+          ++stats_.device_steps;
+        }
+        blk.end_wait_begin = (int)rp.waits.size();
+        blk.end_wait_count = 0;
+        if (db == 0) {
+          for (auto& kv : end_waits_[r]) {
+            DevWait w{};
+            w.rank = (int16_t)kv.first.first;
+            w.block = (int16_t)kv.first.second;
+            w.stride = 2 * dsteps_count_[w.rank][w.block];
+            w.event = kv.second;
+            w.iter_delta = -1;
+            rp.waits.push_back(w);
+            blk.end_wait_count++;
+            published_.insert({w.rank, w.block, w.event});
+          }
+        }
+        rp.blocks.push_back(blk);
+      }
+    }
+    // publication flags
+    for (auto& e : published_) {
+      int rank, block, event;
+      std::tie(rank, block, event) = e;
+      DevStep& st = out_[rank].steps[out_[rank].blocks[block].step_begin + (event - 1) / 2];
+      st.flags |= (event % 2 == 1) ? F_PUB_ARRIVE : F_PUB_DONE;
+    }
+  }
+
+  // Device-level deadlock check: arrive/done events of every step as graph nodes.
+  void deadlock_check() {
+    std::map<std::tuple<int, int, int>, std::vector<std::tuple<int, int, int>>> succ;
+    std::map<std::tuple<int, int, int>, int> indeg;
+    auto node = [&](int r, int b, int e) { return std::make_tuple(r, b, e); };
+    for (int r = 0; r < P_; ++r)
+      for (int b = 0; b < (int)out_[r].blocks.size(); ++b) {
+        const DevBlock& blk = out_[r].blocks[b];
+        for (int s = 0; s < blk.nsteps; ++s) {
+          indeg[node(r, b, 2 * s + 1)];
+          indeg[node(r, b, 2 * s + 2)];
+          succ[node(r, b, 2 * s + 1)].push_back(node(r, b, 2 * s + 2));
+          indeg[node(r, b, 2 * s + 2)]++;
+          if (s > 0) { succ[node(r, b, 2 * s)].push_back(node(r, b, 2 * s + 1)); indeg[node(r, b, 2 * s + 1)]++; }
+          const DevStep& st = out_[r].steps[blk.step_begin + s];
+          for (int w = 0; w < st.wait_count; ++w) {
+            const DevWait& dw = out_[r].waits[st.wait_begin + w];
+            if (dw.block < 0) continue;
+            if (dw.rank >= P_ || dw.block >= (int)out_[dw.rank].blocks.size() || dw.event < 1 ||
+                dw.event > 2 * out_[dw.rank].blocks[dw.block].nsteps)
+              fail("compiled wait names an unknown event");
+            succ[node(dw.rank, dw.block, dw.event)].push_back(node(r, b, 2 * s + 1));
+            indeg[node(r, b, 2 * s + 1)]++;
+          }
+        }
+      }
+    std::deque<std::tuple<int, int, int>> q;
+    for (auto& kv : indeg) if (kv.second == 0) q.push_back(kv.first);
+    size_t seen = 0;
+    while (!q.empty()) {
+      auto n = q.front();
+      q.pop_front();
+      ++seen;
+      for (auto& m : succ[n]) if (--indeg[m] == 0) q.push_back(m);
+    }
+    if (seen != indeg.size())
+      fail("compiled device program deadlocks under pull semantics (the schedule relies on FIFO buffering)");
+  }
+
+  const XAlgo& a_;
+  CompileOptions o_;
+  int P_;
+  std::vector<std::map<int, int>> tb_index_;
+  std::vector<SRef> all_, order_;
+  std::map<SRef, int> topo_pos_;
+  std::map<SRef, SRef> match_recv_, match_send_;
+  std::set<SRef> scale_steps_, need_arrive_;
+  std::vector<std::vector<int>> dblock_;
+  std::vector<int> nblocks_;
+  std::vector<bool> synthetic_;
+  std::vector<std::vector<int>> dsteps_count_;
+  std::map<SRef, EventSet> completion_memo_, arrival_memo_;
+  std::map<SRef, SRef> fused_into_;
+  std::map<SRef, std::vector<SRef>> chains_;
+  std::vector<std::vector<std::vector<PendingStep>>> pending_;
+  std::vector<EventSet> end_waits_;
+  std::set<std::tuple<int, int, int>> published_;
+  std::vector<RankProgram> out_;
+  CompileStats stats_;
+};
+
+}  // namespace
+
+CompiledPlan compile_plan(const XAlgo& algo, const CompileOptions& options) {
+  if (options.nlanes < 1 || options.nlanes > kMaxFlagLanes) throw CompileError("nlanes must be in [1, 256]");
+  if (options.niters < 1) throw CompileError("niters must be positive");
+  if (options.fuse_chains) {
+    try {
+      Compiler c(algo, options);
+      return c.run();
+    } catch (const CompileError& e) {
+      // Fusion can order a chain's reads later than a dependent overwrite; retry without it.
+      if (std::string(e.what()).find("deadlocks under pull") == std::string::npos) throw;
+      CompileOptions plain = options;
+      plain.fuse_chains = false;
+      Compiler c(algo, plain);
+      return c.run();
+    }
+  }
+  Compiler c(algo, options);
+  return c.run();
+}
+
+std::string describe_rank(const CompiledPlan& plan, int rank) {
+  static const char* ops[] = {"nop", "copy", "reduce", "mc_reduce", "mc_store", "mc_allreduce"};
+  std::ostringstream o;
+  const RankProgram& rp = plan.ranks.at(rank);
+  for (size_t b = 0; b < rp.blocks.size(); ++b) {
+    const DevBlock& blk = rp.blocks[b];
+    o << "block " << b << " (xml tb " << blk.xml_tb << ")\n";
+    for (int s = 0; s < blk.nsteps; ++s) {
+      const DevStep& st = rp.steps[blk.step_begin + s];
+      o << "  " << s << ": " << ops[st.op];
+      if (st.op != OP_NOP) o << " -> " << "ios"[st.dst_buf] << "[" << st.dst_chunk << "]";
+      for (int i = 0; i < st.nsrc; ++i) {
+        const DevSrc& sr = rp.srcs[st.src_begin + i];
+        o << (i ? ", " : " <- ") << "r" << sr.rank << ":" << "ios"[sr.buf] << "[" << sr.chunk << "]";
+      }
+      if (st.flags & F_SCALE) o << " scale";
+      if (st.flags & F_PUB_ARRIVE) o << " pubA";
+      if (st.flags & F_PUB_DONE) o << " pubD";
+      for (int w = 0; w < st.wait_count; ++w) {
+        const DevWait& dw = rp.waits[st.wait_begin + w];
+        o << " wait(r" << dw.rank << ",b" << dw.block << ",e" << dw.event << ")";
+      }
+      o << "\n";
+    }
+    for (int w = 0; w < blk.end_wait_count; ++w) {
+      const DevWait& dw = rp.waits[blk.end_wait_begin + w];
+      o << "  end wait(r" << dw.rank << ",b" << dw.block << ",e" << dw.event << ")\n";
+    }
+  }
+  return o.str();
+}
+
+}  // namespace vb

@@ -81,7 +81,7 @@ def compose_routes(plan, demands, trees, topology, slice_bytes: int, *, channels
             if tree is None:
                 continue
             arrival = {d.root: src_dep}
-            for a, b in tree.edges:
+            for a, b in _from_root(tree.edges, d.root):
                 if a not in arrival:
                     raise SemanticError("broadcast tree edge leaves a rank that has not received the value")
                 op_id = "%s:%d>%d" % (d.demand_id, a, b)
@@ -147,6 +147,24 @@ def compose_routes(plan, demands, trees, topology, slice_bytes: int, *, channels
                 raise SemanticError("reduction tree does not deliver the node's target contributors")
     timed = list_schedule(ops, topology, slice_bytes)
     return NetworkCandidate(p, n, slice_bytes, tuple(timed), origin, channels)
+
+
+def _from_root(edges, root):
+    """Broadcast tree edges ordered so that every edge leaves an already-reached rank."""
+    children = {}
+    for a, b in edges:
+        children.setdefault(a, []).append(b)
+    out, frontier = [], [root]
+    while frontier:
+        nxt = []
+        for a in frontier:
+            for b in children.get(a, ()):
+                out.append((a, b))
+                nxt.append(b)
+        frontier = nxt
+    if len(out) != len(edges):
+        raise SemanticError("broadcast tree is not an arborescence rooted at %d" % root)
+    return out
 
 
 def list_schedule(ops, topology, slice_bytes: int):

@@ -1,0 +1,183 @@
+"""In-tree builds of the native modules.
+
+* ``_vbplan`` — the schedule compiler and CPU interpreter (C++17, pybind11,
+  built with g++; no CUDA needed).
+* ``_vbcuda`` — the sm_100a kernels, the symmetric heap and the launch path
+  (a PyTorch CUDA extension built with nvcc for ``compute_100a/sm_100a``).
+* ``libvericcl_b200.so`` and ``vericcl-native`` — the C API and its driver.
+
+Outputs live next to the package (``vericcl_b200/_native/``) so they travel
+with a source snapshot; a stamp file holding the hash of sources and flags
+decides whether a rebuild is needed.
+"""
+from __future__ import annotations
+
+import hashlib
+import os
+import shutil
+import subprocess
+import sys
+import sysconfig
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[2]
+CSRC = ROOT / "csrc"
+OUT = ROOT / "vericcl_b200" / "_native"
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
+EXT = sysconfig.get_config_var("EXT_SUFFIX") or ".so"
+
+PLAN_SOURCES = ["plan/xml_parse.cc", "plan/compile.cc", "plan/cpu_interp.cc"]
+RUNTIME_SOURCES = ["runtime/contract.cc", "runtime/control_transport.cc"]
+
+
+def _digest(paths, flags) -> str:
+    h = hashlib.sha256()
+    for p in sorted(paths):
+        h.update(str(p).encode())
+        h.update(Path(p).read_bytes())
+    for f in flags:
+        h.update(f.encode())
+    for header in sorted((CSRC / "include").rglob("*.h")):
+        h.update(header.read_bytes())
+    return h.hexdigest()
+
+
+def _fresh(target: Path, stamp: str) -> bool:
+    s = target.with_suffix(target.suffix + ".stamp")
+    return target.exists() and s.exists() and s.read_text() == stamp
+
+
+def _mark(target: Path, stamp: str) -> None:
+    target.with_suffix(target.suffix + ".stamp").write_text(stamp)
+
+
+def _run(cmd, what):
+    proc = subprocess.run(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
+    if proc.returncode != 0:
+        raise RuntimeError("%s failed (%d):\n%s\n%s" % (what, proc.returncode, " ".join(map(str, cmd)),
+                                                        proc.stdout[-8000:]))
+    return proc.stdout
+
+
+def pybind_includes():
+    import pybind11
+    return [pybind11.get_include(), sysconfig.get_paths()["include"]]
+
+
+def build_plan_module(force: bool = False) -> Path:
+    OUT.mkdir(parents=True, exist_ok=True)
+    target = OUT / ("_vbplan" + EXT)
+    sources = [CSRC / s for s in PLAN_SOURCES] + [CSRC / "plan" / "bindings.cc"]
+    flags = ["-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden", "-Wall", "-Wno-unused-function"]
+    stamp = _digest(sources, flags)
+    if not force and _fresh(target, stamp):
+        return target
+    cmd = ["g++", *flags, "-I", str(CSRC / "include")]
+    for inc in pybind_includes():
+        cmd += ["-I", inc]
+    cmd += [str(s) for s in sources] + ["-o", str(target) + ".tmp"]
+    _run(cmd, "g++ build of _vbplan")
+    os.replace(str(target) + ".tmp", target)
+    _mark(target, stamp)
+    return target
+
+
+def torch_flags():
+    import torch.utils.cpp_extension as ext
+    inc = ext.include_paths(device_type="cuda") if "device_type" in ext.include_paths.__code__.co_varnames \
+        else ext.include_paths(cuda=True)
+    libs = ext.library_paths(device_type="cuda") if "device_type" in ext.library_paths.__code__.co_varnames \
+        else ext.library_paths(cuda=True)
+    return inc, libs
+
+
+CUDA_SOURCES = ["cuda/interp.cu", "cuda/helpers.cu", "cuda/direct.cu", "runtime/symheap.cc", "runtime/cuda_ext.cc"]
+
+
+def build_cuda_module(force: bool = False, jobs: int | None = None) -> Path:
+    """nvcc/g++ build of the PyTorch CUDA extension ``_vbcuda`` for sm_100a."""
+    OUT.mkdir(parents=True, exist_ok=True)
+    target = OUT / ("_vbcuda" + EXT)
+    sources = [CSRC / s for s in CUDA_SOURCES + PLAN_SOURCES]
+    inc, libs = torch_flags()
+    import torch
+    abi = "-D_GLIBCXX_USE_CXX11_ABI=%d" % int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    common = ["-O3", "-std=c++17", abi, "-DTORCH_EXTENSION_NAME=_vbcuda", "-DTORCH_API_INCLUDE_EXTENSION_H",
+              "-I", str(CSRC / "include")] + sum((["-I", i] for i in inc + pybind_includes()), [])
+    nvflags = ARCH_FLAGS + ["-lineinfo", "--use_fast_math", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
+                            "-Xptxas", "-v", "-U__CUDA_NO_HALF_OPERATORS__", "-U__CUDA_NO_BFLOAT16_CONVERSIONS__"]
+    ccflags = ["-fPIC", "-Wall", "-Wno-unused-function", "-I", str(CUDA_HOME / "include")]
+    stamp = _digest(sources, common + nvflags + ccflags)
+    if not force and _fresh(target, stamp):
+        return target
+    objdir = ROOT / "build" / "vbcuda"
+    objdir.mkdir(parents=True, exist_ok=True)
+    objects, logs = [], []
+    from concurrent.futures import ThreadPoolExecutor
+
+    def compile_one(src: Path):
+        obj = objdir / (src.name + ".o")
+        if src.suffix == ".cu":
+            cmd = [str(CUDA_HOME / "bin" / "nvcc"), "-c", str(src), "-o", str(obj), *common, *nvflags]
+        else:
+            cmd = ["g++", "-c", str(src), "-o", str(obj), *common, *ccflags]
+        out = _run(cmd, "compile " + src.name)
+        return obj, out
+
+    with ThreadPoolExecutor(max_workers=jobs or min(8, os.cpu_count() or 2)) as pool:
+        for obj, out in pool.map(compile_one, sources):
+            objects.append(obj)
+            logs.append(out)
+    (objdir / "ptxas.log").write_text("\n".join(logs))
+    link = ["g++", "-shared", "-o", str(target) + ".tmp", *map(str, objects)]
+    for lib in libs:
+        link += ["-L", lib, "-Wl,-rpath," + lib]
+    link += ["-L", str(CUDA_HOME / "lib64"), "-Wl,-rpath," + str(CUDA_HOME / "lib64"),
+             "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-ltorch_python", "-lcudart", "-lcuda"]
+    stubs = CUDA_HOME / "lib64" / "stubs"
+    if stubs.exists():
+        link += ["-L", str(stubs)]
+    _run(link, "link _vbcuda")
+    os.replace(str(target) + ".tmp", target)
+    _mark(target, stamp)
+    return target
+
+
+CAPI_SOURCES = ["runtime/capi.cc"]
+
+
+def build_capi(force: bool = False) -> Path:
+    """Standalone C API library ``libvericcl_b200.so`` (C ABI, no Python)."""
+    OUT.mkdir(parents=True, exist_ok=True)
+    target = OUT / "libvericcl_b200.so"
+    sources = [CSRC / s for s in CAPI_SOURCES + RUNTIME_SOURCES + PLAN_SOURCES] + \
+        [CSRC / "cuda" / "interp.cu", CSRC / "cuda" / "helpers.cu", CSRC / "runtime" / "symheap.cc"]
+    existing = [s for s in sources if s.exists()]
+    if len(existing) != len(sources):
+        raise FileNotFoundError("C API sources missing: %s" % [str(s) for s in sources if not s.exists()])
+    flags = ARCH_FLAGS + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-shared", "-DVB_NO_TORCH",
+                          "-I", str(CSRC / "include")]
+    stamp = _digest(sources, flags)
+    if not force and _fresh(target, stamp):
+        return target
+    cmd = [str(CUDA_HOME / "bin" / "nvcc"), *flags, *map(str, sources), "-o", str(target) + ".tmp", "-lcuda",
+           "-lpthread"]
+    _run(cmd, "nvcc build of libvericcl_b200")
+    os.replace(str(target) + ".tmp", target)
+    _mark(target, stamp)
+    return target
+
+
+def build_all(force: bool = False) -> dict:
+    out = {"plan": str(build_plan_module(force))}
+    out["cuda"] = str(build_cuda_module(force))
+    try:
+        out["capi"] = str(build_capi(force))
+    except FileNotFoundError:
+        pass
+    return out
+
+
+if __name__ == "__main__":
+    print(build_all(force="--force" in sys.argv))
