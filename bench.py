@@ -1,0 +1,282 @@
+"""Gradient-bucket AllReduce benchmark (the flagship data-parallel step).
+
+Workload: an 8B-parameter model's bf16 gradients (16 GB per rank) in 25 MiB
+buckets with a fused 1/8 scale, one synthesized AllReduce schedule replayed
+for every bucket by the sm_100a interpreter over NVLink/NVSwitch.  Data is
+synthetic N(0, 0.02).  One step = one full gradient sync.
+
+Launch: ``python bench.py`` (1 GPU) or ``torchrun --nproc-per-node N bench.py
+--gpus N``.  Timing: W untimed warm-up steps, then K steps bracketed by a
+barrier and a device synchronize, measured with CUDA events on the launching
+stream; the reported time is the max over ranks.  The 16 GB buffer is larger
+than the 126 MB L2, so no flush is needed between steps.  ``value`` is the
+whole-job aggregate bus bandwidth: the sum over GPUs of the NCCL-convention
+bus bandwidth (2(P-1)/P × bytes / time; with one GPU the bytes count once).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "AllGather/AllReduce bus GB/s vs size at 2/4/8 B200 vs ref MSCCL/NCCL; % of 900GB/s"
+MODEL = "gradient-bucket AllReduce: 8B-param bf16 gradients (16 GB/rank), 25 MiB buckets, fused scale 1/8"
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("vericcl", "reference", "nccl"), default="vericcl")
+    ap.add_argument("--params", type=int, default=8_000_000_000)
+    ap.add_argument("--bucket-bytes", type=int, default=25 * 1024 * 1024)
+    ap.add_argument("--scale", type=float, default=0.125)
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-nccl", action="store_true")
+    return ap.parse_args()
+
+
+def reference_unavailable(reason: str):
+    print(json.dumps({"impl": "reference", "unavailable": reason}), flush=True)
+
+
+def reference_reason() -> str:
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "vericcl")):
+        return "reference package is not installed in baseline/_ref"
+    missing = []
+    for mod in ("pyscipopt", "gmpy2", "dd", "lxml"):
+        try:
+            __import__(mod)
+        except ImportError:
+            missing.append(mod)
+    mpi = any(os.path.exists(os.path.join(d, "mpirun")) for d in os.environ.get("PATH", "").split(os.pathsep))
+    return ("reference installed in baseline/_ref (--no-deps) but its public API cannot run here: "
+            "its synthesis imports %s (absent offline) and its GPU path executes schedules only through "
+            "its patched MSCCL 0.1 / NCCL 2.12.12 runtime launched with Open MPI (%s); NCCL 2.12 predates "
+            "sm_100" % (", ".join(missing) or "nothing missing", "mpirun present" if mpi else "no mpirun"))
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, devices):
+        self.devices = devices
+        self.proc = None
+        self.path = os.path.join("/tmp", "vb_clocks_%d.csv" % os.getpid())
+
+    def __enter__(self):
+        try:
+            self.out = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.out, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.out.close()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, mx, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) not in self.devices:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for name, value in zip(names, parts[5:9]):
+                    if value.lower() == "active":
+                        reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_unavailable(reference_reason())
+        return 0
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world != args.gpus:
+        raise SystemExit("--gpus %d but WORLD_SIZE=%d (launch N>1 with torchrun)" % (args.gpus, world))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    import torch.distributed as dist
+    from datetime import timedelta
+    if world > 1:
+        dist.init_process_group("cpu:gloo,cuda:nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    rank = dist.get_rank() if world > 1 else 0
+    from vericcl_b200.models import GradBucketAllReduce
+    from vericcl_b200.parallel import Communicator
+    dtype = torch.bfloat16
+    esize = 2
+    total_bytes = args.params * esize
+    heap = total_bytes + 2 * args.bucket_bytes + (256 << 20)
+    comm = Communicator(heap_bytes=heap, timeout_s=20.0)
+    ar = GradBucketAllReduce(comm, args.params, dtype=dtype, bucket_bytes=args.bucket_bytes, scale=args.scale)
+    gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    flat = ar.flat
+    step = 1 << 28
+    for lo in range(0, flat.numel(), step):
+        part = flat[lo:lo + step]
+        part.copy_(torch.randn(part.numel(), generator=gen, device="cuda", dtype=torch.float32).mul_(0.02))
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            comm.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=comm.control_group)
+        return float(t.item())
+
+    # correctness of one bucket against NCCL (or the scaled input on one GPU), untimed
+    b0 = ar.bucket(0)
+    saved = b0.clone()
+    comm.run(ar.plan, b0, b0, scale=args.scale)
+    torch.cuda.synchronize()
+    comm.check_status()
+    if world > 1:
+        ref = saved.float()
+        dist.all_reduce(ref)
+        ref.mul_(args.scale)
+    else:
+        ref = saved.float() * args.scale
+    err = (b0.float() - ref).abs().max().item()
+    tol = 2e-2 * max(1e-6, ref.abs().max().item())
+    check_ok = max_over_ranks(0.0 if err <= tol else 1.0) == 0.0
+    b0.copy_(saved)
+    del saved, ref
+
+    for _ in range(args.warmup):
+        ar.sync(stream)
+    torch.cuda.synchronize()
+    comm.check_status()
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler([local] if world == 1 else list(range(world))) as clocks:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(args.steps):
+            ar.sync(stream)
+        end.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+    comm.check_status()
+    clock_info = clocks.summary() if rank == 0 else None
+    bus = ar.bus_bytes_per_rank()
+    busbw = bus / (ms * 1e-3) / 1e9
+    value = busbw * world
+    launches = args.steps * ar.buckets
+
+    nccl = None
+    if world > 1 and not args.no_nccl:
+        premul = dist._make_nccl_premul_sum(args.scale)
+        bufs = [ar.bucket(i) for i in range(ar.buckets)]
+        for _ in range(max(1, args.warmup)):
+            for b in bufs:
+                dist.all_reduce(b, op=premul)
+        torch.cuda.synchronize()
+        barrier()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record(stream)
+        for _ in range(args.steps):
+            for b in bufs:
+                dist.all_reduce(b, op=premul)
+        e2.record(stream)
+        torch.cuda.synchronize()
+        nms = max_over_ranks(s2.elapsed_time(e2) / args.steps)
+        nccl = {"ms_per_step": round(nms, 4), "busbw_gbs": round(bus / (nms * 1e-3) / 1e9, 2),
+                "aggregate_gbs": round(bus / (nms * 1e-3) / 1e9 * world, 2),
+                "op": "ncclAllReduce PREMUL_SUM (torch %s, NCCL %s)" % (torch.__version__,
+                                                                       ".".join(map(str, torch.cuda.nccl.version())))}
+
+    e2e = None
+    if not args.no_e2e:
+        host = None
+        try:
+            host = torch.empty(flat.numel(), dtype=dtype, pin_memory=True)
+            host.copy_(flat)
+        except RuntimeError:
+            host = None
+        if host is not None:
+            out_host = torch.empty(32768, dtype=dtype, pin_memory=True)
+            for _ in range(1):
+                flat.copy_(host, non_blocking=True)
+                ar.sync(stream)
+                out_host.copy_(ar.grads[:32768], non_blocking=True)
+            torch.cuda.synchronize()
+            barrier()
+            s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s3.record(stream)
+            for _ in range(args.e2e_steps):
+                flat.copy_(host, non_blocking=True)
+                ar.sync(stream)
+                out_host.copy_(ar.grads[:32768], non_blocking=True)
+                stream.synchronize()
+                _ = float(out_host[0])
+            e3.record(stream)
+            torch.cuda.synchronize()
+            ems = max_over_ranks(s3.elapsed_time(e3) / args.e2e_steps)
+            e2e = {"value": round(bus / (ems * 1e-3) / 1e9 * world, 2), "unit": "GB/s",
+                   "ms_per_step": round(ems, 3), "h2d_bytes_per_step": int(total_bytes),
+                   "d2h_bytes_per_step": int(out_host.numel() * esize),
+                   "api": "GradBucketAllReduce.sync after a pinned host->heap copy of all gradients"}
+            del host
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,0.02) gradients, random init",
+                "impl": "vericcl_b200",
+                "config": {"model": MODEL, "global_batch": None, "seq_len": None,
+                           "parallelism": "dp%d" % world, "bucket_bytes": args.bucket_bytes,
+                           "buckets": ar.buckets, "bytes_per_rank": total_bytes, "scale": args.scale,
+                           "schedule": "synthesized AllReduce (hierarchy/direct) replayed per bucket",
+                           "plan": {"lanes": ar.plan.nlanes, "iters": ar.plan.niters},
+                           "l2": "inputs (16 GB) larger than the 126 MB L2; no flush needed"},
+                "busbw_per_gpu_gbs": round(busbw, 2), "pct_of_900": round(100 * busbw / 900.0, 2),
+                "check": {"bucket0_max_err": err, "ok": bool(check_ok)},
+                "clocks": clock_info, "e2e": e2e, "gpu_launches": launches, "nccl": nccl}
+        print(json.dumps(line), flush=True)
+    comm.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

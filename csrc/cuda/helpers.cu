@@ -1,0 +1,110 @@
+// Small helper kernels: deterministic fills, a standalone scale pass (the
+// unfused baseline of the reference's post-collective average), an analytic
+// output checker and a %globaltimer reader.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "vb/launch.h"
+
+namespace vb {
+namespace {
+
+__device__ __forceinline__ float ld_elem(const void* p, long long i, int dt) {
+  if (dt == DT_F32) return static_cast<const float*>(p)[i];
+  if (dt == DT_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+  return __half2float(static_cast<const __half*>(p)[i]);
+}
+
+__device__ __forceinline__ void st_elem(void* p, long long i, int dt, float v) {
+  if (dt == DT_F32) static_cast<float*>(p)[i] = v;
+  else if (dt == DT_BF16) static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  else static_cast<__half*>(p)[i] = __float2half_rn(v);
+}
+
+// Pattern 0: value = 1 + ((3*rank + i) mod 5), the analytic pattern of the
+// reference driver (runtime/execution/gpu_operations.cu); pattern 1: a
+// counter-based hash mapped to [-1, 1).
+__device__ __forceinline__ float pattern_value(int pattern, int rank, long long i, unsigned long long seed) {
+  if (pattern == 0) return 1.0f + (float)((3 * rank + i) % 5);
+  unsigned long long x = seed ^ ((unsigned long long)rank << 40) ^ (unsigned long long)i * 0x9E3779B97F4A7C15ull;
+  x ^= x >> 33; x *= 0xff51afd7ed558ccdull; x ^= x >> 33; x *= 0xc4ceb9fe1a85ec53ull; x ^= x >> 33;
+  return (float)((x >> 40) & 0xffffff) / 8388608.0f - 1.0f;
+}
+
+__global__ void fill_kernel(void* dst, long long n, int dt, int pattern, int rank, unsigned long long seed) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    st_elem(dst, i, dt, pattern_value(pattern, rank, i, seed));
+}
+
+__global__ void scale_kernel(void* dst, const void* src, long long n, int dt, float scale) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    st_elem(dst, i, dt, ld_elem(src, i, dt) * scale);
+}
+
+// Checks outputs of pattern-0 inputs analytically in fp64.
+__global__ void check_kernel(const void* out, long long n, int dt, int coll, int redop, int nranks, int rank,
+                             long long count, double atol, double rtol, unsigned long long* bad) {
+  unsigned long long local = 0;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    double expect;
+    if (coll == 1) {   // allgather: output i comes from rank i / count, element i % count
+      int src = (int)(i / count);
+      expect = 1.0 + (double)((3 * src + i % count) % 5);
+    } else {           // reductions over all ranks at element i
+      double acc = 0;
+      for (int r = 0; r < nranks; ++r) {
+        double v = 1.0 + (double)((3 * r + i) % 5);
+        if (r == 0) acc = v;
+        else if (redop == RED_PROD) acc *= v;
+        else if (redop == RED_MIN) acc = acc < v ? acc : v;
+        else if (redop == RED_MAX) acc = acc > v ? acc : v;
+        else acc += v;
+      }
+      expect = acc;
+    }
+    double got = ld_elem(out, i, dt);
+    double err = got - expect;
+    if (err < 0) err = -err;
+    if (!(err <= atol + rtol * (expect < 0 ? -expect : expect))) ++local;
+  }
+  if (local) atomicAdd(bad, local);
+}
+
+__global__ void timer_kernel(unsigned long long* dst) {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  *dst = t;
+}
+
+int grid_for(long long n) {
+  long long g = (n + 255) / 256;
+  return (int)(g > 4096 ? 4096 : (g < 1 ? 1 : g));
+}
+
+}  // namespace
+
+cudaError_t launch_fill(void* dst, long long n, int dtype, int pattern, int rank, unsigned long long seed,
+                        cudaStream_t stream) {
+  fill_kernel<<<grid_for(n), 256, 0, stream>>>(dst, n, dtype, pattern, rank, seed);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scale(void* dst, const void* src, long long n, int dtype, float scale, cudaStream_t stream) {
+  scale_kernel<<<grid_for(n), 256, 0, stream>>>(dst, src, n, dtype, scale);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_check(const void* out, long long n, int dtype, int collective, int redop, int nranks, int rank,
+                         long long count_per_rank, double atol, double rtol, unsigned long long* bad,
+                         cudaStream_t stream) {
+  check_kernel<<<grid_for(n), 256, 0, stream>>>(out, n, dtype, collective, redop, nranks, rank, count_per_rank, atol,
+                                               rtol, bad);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_read_timer(unsigned long long* dst, cudaStream_t stream) {
+  timer_kernel<<<1, 1, 0, stream>>>(dst);
+  return cudaGetLastError();
+}
+
+}  // namespace vb

@@ -1,0 +1,364 @@
+// Persistent schedule interpreter for sm_100a.
+//
+// One CTA per (device block, lane).  A CTA walks its block's steps for every
+// pipeline iteration; each data step moves the CTA's piece of one or more
+// chunks with 16-byte vector loads from local or peer-mapped memory (NVLink
+// through NVSwitch), combines sources in fp32, applies the fused scale and
+// stores once.  Ordering uses 64-bit monotone flags in the symmetric heap:
+// waits poll with ld.acquire.sys (warp 0, one wait per lane), publications
+// use st.release.sys after a CTA barrier.  Every wait is bounded by a
+// %globaltimer deadline; on expiry the CTA records the failure in the
+// control block, raises the abort word for the other CTAs and returns, so a
+// broken schedule or a missing peer never hangs the GPU.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "vb/launch.h"
+
+namespace vb {
+namespace {
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_volatile_int(const int* p) {
+  int v;
+  asm volatile("ld.volatile.global.s32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ uint4 ld_vec(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void st_vec(void* p, const uint4& v) {
+  asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+template <int DT>
+struct VecT;
+
+template <>
+struct VecT<DT_F32> {
+  static constexpr int N = 4;
+  __device__ static void unpack(const uint4& v, float* f) {
+    f[0] = __uint_as_float(v.x); f[1] = __uint_as_float(v.y);
+    f[2] = __uint_as_float(v.z); f[3] = __uint_as_float(v.w);
+  }
+  __device__ static uint4 pack(const float* f) {
+    return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), __float_as_uint(f[3]));
+  }
+};
+
+template <>
+struct VecT<DT_BF16> {
+  static constexpr int N = 8;
+  __device__ static void unpack(const uint4& v, float* f) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  }
+  __device__ static uint4 pack(const float* f) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+      w[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+  }
+};
+
+template <>
+struct VecT<DT_F16> {
+  static constexpr int N = 8;
+  __device__ static void unpack(const uint4& v, float* f) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+      float2 x = __half22float2(h);
+      f[2 * i] = x.x;
+      f[2 * i + 1] = x.y;
+    }
+  }
+  __device__ static uint4 pack(const float* f) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __half2 h = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+      w[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+  }
+};
+
+template <int RED>
+__device__ __forceinline__ float combine(float a, float b) {
+  if (RED == RED_PROD) return a * b;
+  if (RED == RED_MIN) return fminf(a, b);
+  if (RED == RED_MAX) return fmaxf(a, b);
+  return a + b;
+}
+
+// Move one piece: dst[v] = scale? * op(src0[v], ..., src_{K-1}[v]) for vectors v in [0, nvec).
+// K is a compile-time source count so that all K*U loads of a thread are in flight together.
+template <int DT, int RED, int K, int U>
+__device__ __forceinline__ void move_fixed(char* dst, const char* const* src, long long nvec, bool do_scale,
+                                           float scale) {
+  using V = VecT<DT>;
+  const long long stride = (long long)blockDim.x * U;
+  for (long long v0 = threadIdx.x; v0 < nvec; v0 += stride) {
+    uint4 raw[K][U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      long long v = v0 + (long long)u * blockDim.x;
+      if (v < nvec) {
+#pragma unroll
+        for (int k = 0; k < K; ++k) raw[k][u] = ld_vec(src[k] + v * 16);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      long long v = v0 + (long long)u * blockDim.x;
+      if (v >= nvec) continue;
+      if (K == 1 && !do_scale) {
+        st_vec(dst + v * 16, raw[0][u]);
+        continue;
+      }
+      float acc[V::N], tmp[V::N];
+      V::unpack(raw[0][u], acc);
+#pragma unroll
+      for (int k = 1; k < K; ++k) {
+        V::unpack(raw[k][u], tmp);
+#pragma unroll
+        for (int e = 0; e < V::N; ++e) acc[e] = combine<RED>(acc[e], tmp[e]);
+      }
+      if (do_scale) {
+#pragma unroll
+        for (int e = 0; e < V::N; ++e) acc[e] *= scale;
+      }
+      st_vec(dst + v * 16, V::pack(acc));
+    }
+  }
+}
+
+// Any source count: accumulate source by source (used for K > 8).
+template <int DT, int RED>
+__device__ void move_generic(char* dst, const char* const* src, int nsrc, long long nvec, bool do_scale,
+                             float scale) {
+  using V = VecT<DT>;
+  for (long long v = threadIdx.x; v < nvec; v += blockDim.x) {
+    float acc[V::N], tmp[V::N];
+    V::unpack(ld_vec(src[0] + v * 16), acc);
+    for (int k = 1; k < nsrc; ++k) {
+      V::unpack(ld_vec(src[k] + v * 16), tmp);
+#pragma unroll
+      for (int e = 0; e < V::N; ++e) acc[e] = combine<RED>(acc[e], tmp[e]);
+    }
+    if (do_scale)
+#pragma unroll
+      for (int e = 0; e < V::N; ++e) acc[e] *= scale;
+    st_vec(dst + v * 16, V::pack(acc));
+  }
+}
+
+template <int DT, int RED>
+__device__ void move_piece(char* dst, const char* const* src, int nsrc, long long nvec, bool do_scale, float scale) {
+  switch (nsrc) {
+    case 1: move_fixed<DT, RED, 1, 8>(dst, src, nvec, do_scale, scale); break;
+    case 2: move_fixed<DT, RED, 2, 4>(dst, src, nvec, do_scale, scale); break;
+    case 3: move_fixed<DT, RED, 3, 2>(dst, src, nvec, do_scale, scale); break;
+    case 4: move_fixed<DT, RED, 4, 2>(dst, src, nvec, do_scale, scale); break;
+    case 5: move_fixed<DT, RED, 5, 1>(dst, src, nvec, do_scale, scale); break;
+    case 6: move_fixed<DT, RED, 6, 1>(dst, src, nvec, do_scale, scale); break;
+    case 7: move_fixed<DT, RED, 7, 1>(dst, src, nvec, do_scale, scale); break;
+    case 8: move_fixed<DT, RED, 8, 1>(dst, src, nvec, do_scale, scale); break;
+    default: move_generic<DT, RED>(dst, src, nsrc, nvec, do_scale, scale); break;
+  }
+}
+
+__device__ __forceinline__ unsigned long long* flag_ptr(const InterpArgs& a, int rank, long long index) {
+  return reinterpret_cast<unsigned long long*>(a.base[rank] + a.flag_off) + index;
+}
+
+__device__ void record_failure(const InterpArgs& a, int code, int block, int lane, int wait) {
+  if (atomicCAS(&a.control->status, ST_OK, code) == ST_OK) {
+    a.control->detail[0] = a.rank;
+    a.control->detail[1] = block;
+    a.control->detail[2] = lane;
+    a.control->detail[3] = wait;
+  }
+  __threadfence();
+}
+
+// Warp 0 waits for `n` flag targets; returns false when the CTA must stop.
+__device__ bool wait_events(const InterpArgs& a, const DevWait* w, int n, int it, unsigned long long base, int block,
+                            int lane) {
+  const int l = threadIdx.x & 31;
+  bool ok = true;
+  for (int i = l; i < n && ok; i += 32) {
+    const DevWait dw = w[i];
+    unsigned long long target;
+    const unsigned long long* f;
+    if (dw.block < 0) {
+      target = base + 1;
+      f = flag_ptr(a, dw.rank, a.start_slot);
+    } else {
+      int wit = dw.iter_delta < 0 ? a.niters - 1 : it;
+      target = base + (unsigned long long)wit * (unsigned long long)dw.stride + (unsigned long long)dw.event;
+      f = flag_ptr(a, dw.rank, (long long)dw.block * kMaxFlagLanes + lane);
+    }
+    if (ld_acquire_sys(f) >= target) continue;
+    const unsigned long long t0 = globaltimer();
+    unsigned int spins = 0;
+    while (ld_acquire_sys(f) < target) {
+      if ((++spins & 63u) == 0) {
+        if (ld_volatile_int(&a.control->status) != ST_OK || ld_volatile_int(&a.control->abort_request)) {
+          ok = false;
+          break;
+        }
+        if (globaltimer() - t0 > a.timeout_ns) {
+          record_failure(a, ST_TIMEOUT, block, lane, i);
+          ok = false;
+          break;
+        }
+      }
+    }
+  }
+  return __all_sync(0xffffffffu, ok);
+}
+
+template <int DT, int RED>
+__device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long long base, int* s_stop) {
+  const DevBlock blk = a.blocks[block];
+  const int esize = DT == DT_F32 ? 4 : 2;
+  const unsigned long long stride = 2ull * (unsigned long long)blk.nsteps;
+  unsigned long long* my_flag = flag_ptr(a, a.rank, (long long)block * kMaxFlagLanes + lane);
+  __shared__ const char* s_src[16];
+  for (int it = 0; it < a.niters; ++it) {
+    const PieceRange pr = piece_range(a.chunk_elems, a.piece_elems, it, a.nlanes, lane);
+    for (int s = 0; s < blk.nsteps; ++s) {
+      const DevStep st = a.steps[blk.step_begin + s];
+      if (st.wait_count) {
+        if (threadIdx.x < 32) {
+          bool ok = wait_events(a, a.waits + st.wait_begin, st.wait_count, it, base, block, lane);
+          if (threadIdx.x == 0 && !ok) *s_stop = 1;
+        }
+        __syncthreads();
+        if (*s_stop) return;
+      }
+      const unsigned long long ev = base + (unsigned long long)it * stride + 2ull * s;
+      if ((st.flags & F_PUB_ARRIVE) && threadIdx.x == 0) st_release_sys(my_flag, ev + 1);
+      if ((st.op == OP_COPY || st.op == OP_REDUCE) && pr.hi > pr.lo) {
+        const long long nvec = (pr.hi - pr.lo) * esize / 16;
+        for (int k = 0; k < st.cnt; ++k) {
+          if (threadIdx.x < st.nsrc && threadIdx.x < 16) {
+            const DevSrc sr = a.srcs[st.src_begin + threadIdx.x];
+            s_src[threadIdx.x] = a.base[sr.rank] + a.buf_off[sr.buf] +
+                                 ((long long)(sr.chunk + k) * a.chunk_elems + pr.lo) * esize;
+          }
+          __syncthreads();
+          char* dst = a.base[a.rank] + a.buf_off[st.dst_buf] + ((long long)(st.dst_chunk + k) * a.chunk_elems + pr.lo) * esize;
+          move_piece<DT, RED>(dst, s_src, st.nsrc, nvec, (st.flags & F_SCALE) != 0, a.scale);
+          __syncthreads();
+        }
+      }
+      if (st.flags & F_PUB_DONE) {
+        __syncthreads();
+        if (threadIdx.x == 0) st_release_sys(my_flag, ev + 2);
+      }
+    }
+  }
+  if (blk.end_wait_count) {
+    if (threadIdx.x < 32) {
+      bool ok = wait_events(a, a.waits + blk.end_wait_begin, blk.end_wait_count, a.niters - 1, base, block, lane);
+      if (threadIdx.x == 0 && !ok) *s_stop = 1;
+    }
+    __syncthreads();
+  }
+}
+
+template <int DT, int RED>
+__global__ void __launch_bounds__(512, 1) interp_kernel(const InterpArgs a) {
+  __shared__ unsigned long long s_base;
+  __shared__ int s_stop;
+  const int block = blockIdx.x / a.nlanes;
+  const int lane = blockIdx.x % a.nlanes;
+  if (threadIdx.x == 0) {
+    s_base = (*(volatile unsigned long long*)&a.control->epoch) << 32;
+    s_stop = 0;
+    st_release_sys(flag_ptr(a, a.rank, a.start_slot), s_base + 1);
+  }
+  __syncthreads();
+  if (block < a.nblocks) run_cta<DT, RED>(a, block, lane, s_base, &s_stop);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    unsigned int done = atomicAdd(&a.control->arrive, 1u);
+    if (done == gridDim.x - 1) {
+      a.control->arrive = 0;
+      a.control->epoch = a.control->epoch + 1;
+      __threadfence();
+    }
+  }
+}
+
+template <int DT>
+cudaError_t launch_red(const InterpArgs& a, cudaStream_t stream, int threads) {
+  void* args[] = {const_cast<InterpArgs*>(&a)};
+  dim3 grid(a.nblocks * a.nlanes), block(threads);
+  switch (a.redop) {
+    case RED_PROD: return cudaLaunchCooperativeKernel((void*)interp_kernel<DT, RED_PROD>, grid, block, args, 0, stream);
+    case RED_MIN: return cudaLaunchCooperativeKernel((void*)interp_kernel<DT, RED_MIN>, grid, block, args, 0, stream);
+    case RED_MAX: return cudaLaunchCooperativeKernel((void*)interp_kernel<DT, RED_MAX>, grid, block, args, 0, stream);
+    default: return cudaLaunchCooperativeKernel((void*)interp_kernel<DT, RED_SUM>, grid, block, args, 0, stream);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_interp(const InterpArgs& a, cudaStream_t stream, int threads) {
+  if (a.nblocks < 1 || a.nlanes < 1 || a.niters < 1 || threads < 32 || threads > 512 || threads % 32) return cudaErrorInvalidValue;
+  switch (a.dtype) {
+    case DT_F32: return launch_red<DT_F32>(a, stream, threads);
+    case DT_BF16: return launch_red<DT_BF16>(a, stream, threads);
+    case DT_F16: return launch_red<DT_F16>(a, stream, threads);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+int interp_max_ctas(int threads) {
+  int dev = 0, sms = 0, per_sm = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, interp_kernel<DT_BF16, RED_SUM>, threads, 0);
+  int f32 = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&f32, interp_kernel<DT_F32, RED_SUM>, threads, 0);
+  if (f32 < per_sm) per_sm = f32;
+  return sms * per_sm;
+}
+
+}  // namespace vb

@@ -1,0 +1,61 @@
+// Kernel launch arguments and launch entry points of the schedule interpreter.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "vb/devprog.h"
+
+namespace vb {
+
+// Status words written by the kernels (local device memory).
+enum StatusCode : int {
+  ST_OK = 0,
+  ST_TIMEOUT = 1,        // a flag wait exceeded its time limit
+  ST_ABORTED = 2,        // another CTA or the host requested an abort
+  ST_BAD_GEOMETRY = 3,   // a piece or address was out of range / misaligned
+};
+
+struct Control {
+  unsigned long long epoch;       // launch counter of this communicator (starts at 1)
+  unsigned int arrive;            // CTAs finished in the current launch
+  int status;                     // StatusCode of the first failure
+  int detail[4];                  // rank, block, lane, wait index of the first failure
+  int abort_request;              // host-set abort flag (mapped memory or device write)
+  unsigned long long pad[4];
+};
+
+struct InterpArgs {
+  const DevBlock* blocks;
+  const DevStep* steps;
+  const DevSrc* srcs;
+  const DevWait* waits;
+  int nblocks, nlanes, niters, rank, nranks;
+  int dtype, redop;
+  float scale;
+  long long chunk_elems, piece_elems;
+  long long buf_off[BUF_COUNT];      // byte offsets inside the heap (identical on all ranks)
+  long long flag_off;                // byte offset of the flag table inside the heap
+  long long start_slot;              // flag index of the per-rank start flag
+  char* base[kMaxRanks];             // heap base of every rank in this process's address space
+  char* mc_base;                     // multicast address of the heap (nullptr when unavailable)
+  Control* control;                  // local control block
+  unsigned long long timeout_ns;
+  int trace;                         // record per-step timestamps into trace buffer
+  unsigned long long* trace_buf;     // [nblocks*nlanes][max_steps*niters][2] (start, end) globaltimer
+  int trace_stride;
+};
+
+// Launch the interpreter (cooperative launch: every CTA is co-resident).
+cudaError_t launch_interp(const InterpArgs& args, cudaStream_t stream, int threads);
+int interp_max_ctas(int threads);
+
+// Helper kernels.
+cudaError_t launch_fill(void* dst, long long n, int dtype, int pattern, int rank, unsigned long long seed,
+                        cudaStream_t stream);
+cudaError_t launch_scale(void* dst, const void* src, long long n, int dtype, float scale, cudaStream_t stream);
+cudaError_t launch_check(const void* out, long long n, int dtype, int collective, int redop, int nranks,
+                         int rank, long long count_per_rank, double atol, double rtol, unsigned long long* bad,
+                         cudaStream_t stream);
+cudaError_t launch_read_timer(unsigned long long* dst, cudaStream_t stream);
+
+}  // namespace vb

@@ -46,6 +46,7 @@ struct CompileOptions {
   bool elide_sends = true;   // blocks made only of sends run no CTA
   bool fuse_chains = true;   // fold chains of receive-reduce steps into one n-ary reduce
   bool multicast = false;    // map whole-group reduce/broadcast patterns to NVLS multimem ops
+  bool merge_blocks = true;  // run each rank's steps as one CTA group in a global topological order
   bool reducing = false;     // the collective reduces (enables scale placement)
 };
 

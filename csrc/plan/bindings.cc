@@ -75,7 +75,8 @@ PYBIND11_MODULE(_vbplan, m) {
         return py::make_tuple(as_bytes(rp.blocks), as_bytes(rp.steps), as_bytes(rp.srcs), as_bytes(rp.waits));
       });
   m.def("parse_and_compile",
-        [](const std::string& xml, int nlanes, int niters, bool elide, bool fuse, bool multicast, bool reducing) {
+        [](const std::string& xml, int nlanes, int niters, bool elide, bool fuse, bool multicast, bool reducing,
+           bool merge) {
           CompileOptions o;
           o.nlanes = nlanes;
           o.niters = niters;
@@ -83,10 +84,11 @@ PYBIND11_MODULE(_vbplan, m) {
           o.fuse_chains = fuse;
           o.multicast = multicast;
           o.reducing = reducing;
+          o.merge_blocks = merge;
           return compile_plan(parse_xml(xml), o);
         },
         py::arg("xml"), py::arg("nlanes") = 1, py::arg("niters") = 1, py::arg("elide") = true,
-        py::arg("fuse") = true, py::arg("multicast") = false, py::arg("reducing") = false);
+        py::arg("fuse") = true, py::arg("multicast") = false, py::arg("reducing") = false, py::arg("merge") = true);
   m.def("cpu_interpret",
         [](const CompiledPlan& plan, py::list in, py::list out, py::list scr, int dtype, int redop, float scale,
            long long chunk_elems, long long piece_elems, unsigned seed, int launches) {

@@ -79,6 +79,7 @@ class Compiler {
     if (o_.reducing) place_scale();
     assign_blocks();
     build_waits_and_hazards();
+    if (o_.merge_blocks) merge_blocks();
     emit();
     deadlock_check();
     CompiledPlan plan;
@@ -429,6 +430,8 @@ class Compiler {
     DevStep st;
     std::vector<DevSrc> srcs;
     EventSet waits;
+    int prio = 0;
+    int xml_tb = -1;
   };
 
   void build_waits_and_hazards() {
@@ -466,6 +469,8 @@ class Compiler {
       if (db < 0) continue;
       const XStep& st = step(x);
       PendingStep ps{};
+      ps.prio = topo_pos_[x];
+      ps.xml_tb = a_.gpus[x.rank].tbs[x.tb].id;
       ps.st.cnt = st.cnt;
       ps.st.flags = 0;
       if (st.depid >= 0) merge(ps.waits, completion(SRef{x.rank, tb_index_[x.rank].at(st.depid), st.deps}));
@@ -554,6 +559,79 @@ class Compiler {
     }
   }
 
+
+  // Merge every rank's device blocks into one block whose steps follow one global
+  // topological order of the device event graph.  Every wait then refers to a
+  // step that precedes it in that order, so the merged program cannot deadlock,
+  // and every step is spread over all lanes of the rank.
+  void merge_blocks() {
+    using Node = std::tuple<int, int, int>;   // rank, block, step
+    std::map<Node, std::vector<Node>> succ;
+    std::map<Node, int> indeg;
+    for (int r = 0; r < P_; ++r)
+      for (int b = 0; b < nblocks_[r]; ++b)
+        for (int s = 0; s < (int)pending_[r][b].size(); ++s) {
+          Node n{r, b, s};
+          indeg[n];
+          if (s > 0) { succ[Node{r, b, s - 1}].push_back(n); indeg[n]++; }
+          for (auto& kv : pending_[r][b][s].waits) {
+            if (kv.first.second < 0) continue;
+            Node src{kv.first.first, kv.first.second, (kv.second - 1) / 2};
+            succ[src].push_back(n);
+            indeg[n]++;
+          }
+        }
+    auto prio = [&](const Node& n) {
+      return std::make_tuple(pending_[std::get<0>(n)][std::get<1>(n)][std::get<2>(n)].prio, std::get<0>(n),
+                             std::get<1>(n), std::get<2>(n));
+    };
+    std::set<std::tuple<int, int, int, int>> ready;
+    for (auto& kv : indeg) if (kv.second == 0) ready.insert(prio(kv.first));
+    std::map<Node, int> newidx;
+    std::vector<int> count(P_, 0);
+    std::vector<std::vector<Node>> order(P_);
+    while (!ready.empty()) {
+      auto t = *ready.begin();
+      ready.erase(ready.begin());
+      Node n{std::get<1>(t), std::get<2>(t), std::get<3>(t)};
+      int r = std::get<0>(n);
+      newidx[n] = count[r]++;
+      order[r].push_back(n);
+      for (auto& m : succ[n]) if (--indeg[m] == 0) ready.insert(prio(m));
+    }
+    if (newidx.size() != indeg.size()) fail("device program has a cyclic wait graph");
+    auto remap = [&](const EventSet& in) {
+      EventSet out;
+      for (auto& kv : in) {
+        if (kv.first.second < 0) { merge(out, EventSet{{kv.first, kv.second}}); continue; }
+        int idx = newidx.at(Node{kv.first.first, kv.first.second, (kv.second - 1) / 2});
+        int ev = 2 * idx + ((kv.second % 2) ? 1 : 2);
+        merge(out, EventSet{{{kv.first.first, 0}, ev}});
+      }
+      return out;
+    };
+    std::vector<std::vector<std::vector<PendingStep>>> merged(P_);
+    for (int r = 0; r < P_; ++r) {
+      merged[r].resize(1);
+      for (size_t i = 0; i < order[r].size(); ++i) {
+        const Node& n = order[r][i];
+        PendingStep ps = pending_[r][std::get<1>(n)][std::get<2>(n)];
+        ps.waits = remap(ps.waits);
+        auto own = ps.waits.find({r, 0});
+        if (own != ps.waits.end()) {
+          if (own->second <= 2 * (int)i) ps.waits.erase(own);
+          else fail("merged step waits on a later step of its own rank");
+        }
+        merged[r][0].push_back(ps);
+      }
+      end_waits_[r] = remap(end_waits_[r]);
+      nblocks_[r] = 1;
+      dsteps_count_[r].assign(1, (int)order[r].size());
+    }
+    pending_ = std::move(merged);
+    merged_ = true;
+  }
+
   void emit() {
     for (int r = 0; r < P_; ++r) {
       RankProgram& rp = out_[r];
@@ -561,7 +639,8 @@ class Compiler {
         DevBlock blk{};
         blk.step_begin = (int)rp.steps.size();
         blk.xml_tb = -1;
-        for (int t = 0; t < (int)dblock_[r].size(); ++t) if (dblock_[r][t] == db) blk.xml_tb = a_.gpus[r].tbs[t].id;
+        if (!merged_)
+          for (int t = 0; t < (int)dblock_[r].size(); ++t) if (dblock_[r][t] == db) blk.xml_tb = a_.gpus[r].tbs[t].id;
         auto& steps = pending_[r][db];
         blk.nsteps = (int)steps.size();
         for (int s = 0; s < (int)steps.size(); ++s) {
@@ -674,6 +753,7 @@ class Compiler {
   std::set<std::tuple<int, int, int>> published_;
   std::vector<RankProgram> out_;
   CompileStats stats_;
+  bool merged_ = false;
 };
 
 }  // namespace

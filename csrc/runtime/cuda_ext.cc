@@ -1,0 +1,260 @@
+// PyTorch CUDA extension: symmetric heap, compiled device plans and launches.
+#include <cuda_runtime.h>
+#include <pybind11/pybind11.h>
+#include <pybind11/stl.h>
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+
+#include <memory>
+#include <stdexcept>
+#include <string>
+
+#include "vb/launch.h"
+#include "vb/plan.h"
+#include "vb/symheap.h"
+
+namespace py = pybind11;
+using namespace vb;
+
+namespace {
+
+void cuda_check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+int elem_bytes(int dtype) { return dtype == DT_F32 ? 4 : 2; }
+
+at::ScalarType scalar_type(int dtype) {
+  switch (dtype) {
+    case DT_F32: return at::kFloat;
+    case DT_BF16: return at::kBFloat16;
+    case DT_F16: return at::kHalf;
+    default: throw std::runtime_error("unsupported dtype code");
+  }
+}
+
+int dtype_code(at::ScalarType t) {
+  if (t == at::kFloat) return DT_F32;
+  if (t == at::kBFloat16) return DT_BF16;
+  if (t == at::kHalf) return DT_F16;
+  throw std::runtime_error("unsupported tensor dtype (float32, bfloat16, float16)");
+}
+
+template <typename T>
+T* upload(const std::vector<T>& v) {
+  if (v.empty()) return nullptr;
+  T* p = nullptr;
+  cuda_check(cudaMalloc(&p, v.size() * sizeof(T)), "cudaMalloc plan table");
+  cuda_check(cudaMemcpy(p, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice), "upload plan table");
+  return p;
+}
+
+class Heap {
+ public:
+  Heap(int rank, int nranks, int device, size_t bytes, const std::string& session, bool multicast)
+      : h_(std::make_unique<SymHeap>(rank, nranks, device, bytes, session, multicast)) {}
+  SymHeap& get() { return *h_; }
+  Control* control() { return reinterpret_cast<Control*>(h_->base(h_->rank())); }
+
+  py::dict status() {
+    Control c;
+    cuda_check(cudaMemcpy(&c, control(), sizeof(Control), cudaMemcpyDeviceToHost), "read control block");
+    py::dict d;
+    d["epoch"] = c.epoch;
+    d["status"] = c.status;
+    d["detail"] = py::make_tuple(c.detail[0], c.detail[1], c.detail[2], c.detail[3]);
+    d["arrive"] = c.arrive;
+    return d;
+  }
+
+  void clear_status() {
+    cuda_check(cudaMemset(&control()->status, 0, sizeof(int) * 5), "clear status");
+    cuda_check(cudaMemset(&control()->abort_request, 0, sizeof(int)), "clear abort");
+  }
+
+  torch::Tensor tensor(size_t offset, int64_t numel, int dtype) {
+    if (offset + (size_t)numel * elem_bytes(dtype) > h_->size()) throw std::runtime_error("tensor exceeds the heap");
+    auto opts = torch::TensorOptions().dtype(scalar_type(dtype)).device(torch::kCUDA, h_->device());
+    return torch::from_blob(h_->base(h_->rank()) + offset, {numel}, opts);
+  }
+
+  size_t offset_of(const torch::Tensor& t) {
+    auto p = reinterpret_cast<char*>(t.data_ptr());
+    char* b = h_->base(h_->rank());
+    if (p < b || p >= b + h_->size()) throw std::runtime_error("tensor is not inside the symmetric heap");
+    return (size_t)(p - b);
+  }
+
+ private:
+  std::unique_ptr<SymHeap> h_;
+};
+
+class DevicePlan {
+ public:
+  DevicePlan(const std::string& xml, int rank, int nlanes, int niters, bool elide, bool fuse, bool multicast,
+             bool reducing)
+      : rank_(rank) {
+    CompileOptions o;
+    o.nlanes = nlanes;
+    o.niters = niters;
+    o.elide_sends = elide;
+    o.fuse_chains = fuse;
+    o.multicast = multicast;
+    o.reducing = reducing;
+    plan_ = compile_plan(parse_xml(xml), o);
+    if (rank < 0 || rank >= (int)plan_.ranks.size()) throw std::runtime_error("rank outside the plan");
+    const RankProgram& rp = plan_.ranks[rank];
+    if (plan_.max_blocks() > kMaxFlagBlocks) throw std::runtime_error("plan has more blocks than the flag table holds");
+    blocks_ = upload(rp.blocks);
+    steps_ = upload(rp.steps);
+    srcs_ = upload(rp.srcs);
+    waits_ = upload(rp.waits);
+    nblocks_ = (int)rp.blocks.size();
+  }
+  ~DevicePlan() {
+    cudaFree(blocks_);
+    cudaFree(steps_);
+    cudaFree(srcs_);
+    cudaFree(waits_);
+  }
+
+  py::tuple geometry(int64_t count_per_rank, int dtype) const {
+    long long runtime = count_per_rank * ((plan_.algo.coll == "allgather" || plan_.algo.coll == "gather") ? plan_.ranks.size() : 1);
+    long long nch = plan_.algo.nchunksperloop;
+    if (runtime % nch) throw std::runtime_error("element count does not split into nchunksperloop chunks");
+    long long chunk = runtime / nch;
+    int vec = 16 / elem_bytes(dtype);
+    if (chunk % vec) throw std::runtime_error("chunk is not a whole number of 16-byte vectors");
+    long long pieces = (long long)plan_.options.nlanes * plan_.options.niters;
+    long long piece = (chunk + pieces - 1) / pieces;
+    piece = (piece + vec - 1) / vec * vec;
+    return py::make_tuple(chunk, piece);
+  }
+
+  void run(Heap& heap, size_t in_off, size_t out_off, size_t scr_off, int64_t count_per_rank, int dtype, int redop,
+           float scale, uint64_t stream, double timeout_s, int threads) {
+    SymHeap& h = heap.get();
+    if (h.nranks() != (int)plan_.ranks.size()) throw std::runtime_error("heap and plan rank counts differ");
+    py::tuple g = geometry(count_per_rank, dtype);
+    InterpArgs a = {};
+    a.blocks = blocks_;
+    a.steps = steps_;
+    a.srcs = srcs_;
+    a.waits = waits_;
+    a.nblocks = nblocks_;
+    a.nlanes = plan_.options.nlanes;
+    a.niters = plan_.options.niters;
+    a.rank = rank_;
+    a.nranks = h.nranks();
+    a.dtype = dtype;
+    a.redop = redop;
+    a.scale = scale;
+    a.chunk_elems = g[0].cast<long long>();
+    a.piece_elems = g[1].cast<long long>();
+    a.buf_off[BUF_IN] = (long long)in_off;
+    a.buf_off[BUF_OUT] = (long long)out_off;
+    a.buf_off[BUF_SCR] = (long long)scr_off;
+    const RankProgram& rp = plan_.ranks[rank_];
+    size_t esz = elem_bytes(dtype);
+    auto need = [&](size_t off, int chunks, const char* name) {
+      if (chunks && off + (size_t)chunks * a.chunk_elems * esz > h.size())
+        throw std::runtime_error(std::string(name) + " buffer exceeds the heap");
+      if (off % 16) throw std::runtime_error(std::string(name) + " buffer is not 16-byte aligned");
+    };
+    need(in_off, rp.i_chunks, "input");
+    need(out_off, rp.o_chunks, "output");
+    need(scr_off, rp.s_chunks, "scratch");
+    a.flag_off = (long long)h.flag_offset();
+    a.start_slot = h.start_slot();
+    for (int r = 0; r < h.nranks(); ++r) a.base[r] = h.base(r);
+    a.mc_base = h.mc_base();
+    a.control = heap.control();
+    a.timeout_ns = (unsigned long long)(timeout_s * 1e9);
+    int max_ctas = interp_max_ctas(threads);
+    if (a.nblocks * a.nlanes > max_ctas)
+      throw std::runtime_error("plan needs " + std::to_string(a.nblocks * a.nlanes) + " co-resident CTAs; the device holds " +
+                               std::to_string(max_ctas));
+    cuda_check(launch_interp(a, reinterpret_cast<cudaStream_t>(stream), threads), "launch interpreter");
+  }
+
+  int nblocks() const { return nblocks_; }
+  int nlanes() const { return plan_.options.nlanes; }
+  int niters() const { return plan_.options.niters; }
+  py::tuple slots() const {
+    const RankProgram& rp = plan_.ranks[rank_];
+    return py::make_tuple(rp.i_chunks, rp.o_chunks, rp.s_chunks);
+  }
+  std::string describe() const { return describe_rank(plan_, rank_); }
+  py::dict stats() const {
+    py::dict d;
+    d["device_steps"] = plan_.stats.device_steps;
+    d["elided_blocks"] = plan_.stats.elided_blocks;
+    d["fused_reduces"] = plan_.stats.fused_reduces;
+    d["waits"] = plan_.stats.waits;
+    d["remote_waits"] = plan_.stats.remote_waits;
+    d["fused"] = plan_.options.fuse_chains;
+    return d;
+  }
+
+ private:
+  CompiledPlan plan_;
+  int rank_, nblocks_ = 0;
+  DevBlock* blocks_ = nullptr;
+  DevStep* steps_ = nullptr;
+  DevSrc* srcs_ = nullptr;
+  DevWait* waits_ = nullptr;
+};
+
+}  // namespace
+
+PYBIND11_MODULE(_vbcuda, m) {
+  m.doc() = "vericcl_b200 CUDA runtime: symmetric heap, schedule interpreter, helper kernels";
+  py::class_<Heap>(m, "Heap")
+      .def(py::init<int, int, int, size_t, const std::string&, bool>())
+      .def("exchange", [](Heap& h, double t) { py::gil_scoped_release r; h.get().exchange(t); })
+      .def("bind_multicast", [](Heap& h) { h.get().bind_multicast(); })
+      .def("finish", [](Heap& h) { h.get().finish(); })
+      .def("destroy", [](Heap& h) { h.get().destroy(); })
+      .def("alloc", [](Heap& h, size_t b) { return h.get().alloc(b); })
+      .def("free", [](Heap& h, size_t o) { h.get().free(o); })
+      .def("used", [](Heap& h) { return h.get().used(); })
+      .def("tensor", &Heap::tensor)
+      .def("offset_of", &Heap::offset_of)
+      .def("status", &Heap::status)
+      .def("clear_status", &Heap::clear_status)
+      .def_property_readonly("size", [](Heap& h) { return h.get().size(); })
+      .def_property_readonly("multicast", [](Heap& h) { return h.get().multicast(); })
+      .def("base", [](Heap& h, int r) { return (uint64_t)h.get().base(r); });
+  py::class_<DevicePlan>(m, "DevicePlan")
+      .def(py::init<const std::string&, int, int, int, bool, bool, bool, bool>())
+      .def("run", &DevicePlan::run, py::arg("heap"), py::arg("in_off"), py::arg("out_off"), py::arg("scr_off"),
+           py::arg("count_per_rank"), py::arg("dtype"), py::arg("redop"), py::arg("scale"), py::arg("stream"),
+           py::arg("timeout_s") = 10.0, py::arg("threads") = 512)
+      .def("geometry", &DevicePlan::geometry)
+      .def("slots", &DevicePlan::slots)
+      .def("describe", &DevicePlan::describe)
+      .def("stats", &DevicePlan::stats)
+      .def_property_readonly("nblocks", &DevicePlan::nblocks)
+      .def_property_readonly("nlanes", &DevicePlan::nlanes)
+      .def_property_readonly("niters", &DevicePlan::niters);
+  m.def("max_ctas", [](int threads) { return interp_max_ctas(threads); }, py::arg("threads") = 512);
+  m.def("fill", [](torch::Tensor t, int pattern, int rank, uint64_t seed) {
+    cuda_check(launch_fill(t.data_ptr(), t.numel(), dtype_code(t.scalar_type()), pattern, rank, seed,
+                           at::cuda::getCurrentCUDAStream().stream()), "fill");
+  });
+  m.def("scale", [](torch::Tensor dst, torch::Tensor src, float s) {
+    cuda_check(launch_scale(dst.data_ptr(), src.data_ptr(), dst.numel(), dtype_code(dst.scalar_type()), s,
+                            at::cuda::getCurrentCUDAStream().stream()), "scale");
+  });
+  m.def("check", [](torch::Tensor out, int coll, int redop, int nranks, int rank, int64_t count, double atol, double rtol) {
+    auto bad = torch::zeros({1}, torch::TensorOptions().dtype(torch::kInt64).device(out.device()));
+    cuda_check(launch_check(out.data_ptr(), out.numel(), dtype_code(out.scalar_type()), coll, redop, nranks, rank, count,
+                            atol, rtol, reinterpret_cast<unsigned long long*>(bad.data_ptr()),
+                            at::cuda::getCurrentCUDAStream().stream()), "check");
+    return bad;
+  });
+  m.def("read_timer", [](torch::Tensor dst) {
+    cuda_check(launch_read_timer(reinterpret_cast<unsigned long long*>(dst.data_ptr()),
+                                 at::cuda::getCurrentCUDAStream().stream()), "timer");
+  });
+}

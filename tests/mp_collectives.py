@@ -1,0 +1,122 @@
+"""Multi-GPU correctness worker (launched by torchrun, one process per GPU).
+
+For every case: synthesize the schedule, compile it for this rank, run it
+through the sm_100a interpreter on heap buffers filled with seeded data, and
+compare with an fp64 host reference computed from every rank's (regenerated)
+inputs.  Prints one JSON line per case on rank 0 and exits non-zero on any
+mismatch.  Used by tests/test_gpu_multi.py.
+"""
+import json
+import os
+import sys
+import time
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+from vericcl_b200.parallel import Communicator  # noqa: E402
+from vericcl_b200.synthesis import schedule_xml  # noqa: E402
+
+TOL = {torch.float32: 1e-4, torch.bfloat16: 3e-2, torch.float16: 5e-3}
+
+
+def inputs_for(rank, count, dtype, seed):
+    g = torch.Generator().manual_seed(seed * 1000 + rank)
+    return torch.randn(count, generator=g, dtype=torch.float64).to(dtype)
+
+
+def reference(coll, world, count, dtype, seed, op, rank):
+    xs = [inputs_for(r, count, dtype, seed).double() for r in range(world)]
+    if coll == "allreduce":
+        total = sum(xs) if op in ("sum", "avg") else None
+        if op == "avg":
+            total = total / world
+        return total
+    if coll == "allgather":
+        return torch.cat(xs)
+    if coll == "reduce_scatter":
+        total = sum(xs)
+        part = count // world
+        return total[rank * part:(rank + 1) * part]
+    raise ValueError(coll)
+
+
+def main():
+    dist.init_process_group("cpu:gloo,cuda:nccl", device_id=torch.device("cuda", int(os.environ["LOCAL_RANK"])))
+    rank, world = dist.get_rank(), dist.get_world_size()
+    torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
+    quick = os.environ.get("VB_QUICK") == "1"
+    comm = Communicator(heap_bytes=1 << 30, multicast=os.environ.get("VERICCL_NVLS", "0") == "1", timeout_s=5.0)
+    failures = 0
+    cases = []
+    for coll in ("allreduce", "allgather", "reduce_scatter"):
+        for dtype in (torch.float32, torch.bfloat16):
+            for inplace in (False, True):
+                for slices in ((1, world) if coll != "reduce_scatter" else (world,)):
+                    for lanes, iters in ((1, 1), (4, 2), (16, 1)):
+                        for count in ((world * 4096, world * 1 << 18) if not quick else (world * 4096,)):
+                            cases.append((coll, dtype, inplace, slices, lanes, iters, count))
+    for coll, dtype, inplace, slices, lanes, iters, count in cases:
+        dname = str(dtype).split(".")[-1]
+        xml = schedule_xml(coll, world, slices, inplace=inplace, datatype=dname)
+        plan = comm.compile(xml, nlanes=lanes, niters=iters)
+        seed = hash((coll, dname, inplace, slices, lanes, iters, count)) % 100000
+        x = inputs_for(rank, count, dtype, seed).cuda()
+        out_n = count * world if coll == "allgather" else count // world if coll == "reduce_scatter" else count
+        if inplace:
+            buf = comm.empty(max(count, out_n), dtype)
+            if coll == "allgather":
+                buf[rank * count:(rank + 1) * count].copy_(x)
+                inp, out = buf[rank * count:(rank + 1) * count], buf
+            elif coll == "reduce_scatter":
+                buf[:count].copy_(x)
+                inp, out = buf[:count], buf[rank * out_n:(rank + 1) * out_n]
+            else:
+                buf.copy_(x)
+                inp, out = buf, buf
+        else:
+            inp = comm.empty(count, dtype)
+            out = comm.empty(out_n, dtype)
+            inp.copy_(x)
+            out.fill_(float("nan"))
+        op = "avg" if coll == "allreduce" and lanes == 4 else "sum"
+        torch.cuda.synchronize()
+        dist.barrier()
+        if inplace:
+            # in-place programs address one buffer for both roles
+            comm.run(plan, buf, buf, op=op, count_per_rank=count)
+        else:
+            comm.run(plan, inp, out, op=op, count_per_rank=count)
+        torch.cuda.synchronize()
+        comm.check_status()
+        ref = reference(coll, world, count, dtype, seed, op, rank)
+        if inplace and coll == "reduce_scatter":
+            got = buf[rank * out_n:(rank + 1) * out_n]
+        else:
+            got = out if not inplace or coll != "allreduce" else buf
+        got = got.double().cpu()
+        err = (got - ref).abs().max().item() if got.numel() else 0.0
+        scale = max(1.0, ref.abs().max().item())
+        ok = err <= TOL[dtype] * scale * (world if coll != "allgather" else 1) and torch.isfinite(got).all().item()
+        if not ok:
+            failures += 1
+        if rank == 0 or not ok:
+            print(json.dumps({"rank": rank, "coll": coll, "dtype": dname, "inplace": inplace, "slices": slices,
+                              "lanes": lanes, "iters": iters, "count": count, "op": op, "max_err": err, "ok": ok}),
+                  flush=True)
+        dist.barrier()
+        for t in ([buf] if inplace else [inp, out]):
+            comm.free(t)
+    total = torch.tensor([failures])
+    dist.all_reduce(total, group=comm.control_group)
+    comm.close()
+    dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps({"summary": True, "cases": len(cases), "failures": int(total.item())}), flush=True)
+    sys.exit(1 if total.item() else 0)
+
+
+if __name__ == "__main__":
+    main()

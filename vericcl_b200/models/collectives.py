@@ -1,0 +1,115 @@
+"""User-facing collectives bound to a :class:`Communicator`.
+
+``CollectiveEngine`` synthesizes a verified schedule once per (collective,
+rank count, slice count, layout, dtype), compiles it for this rank, picks a
+launch geometry for the message size (lanes × pipeline iterations over the
+co-resident CTA budget), and runs it with the sm_100a interpreter.  Buffers in
+the communicator's heap run zero-copy; other tensors are staged through heap
+buffers (a local device copy on each side).
+"""
+from __future__ import annotations
+
+import torch
+
+from vericcl_b200.errors import RuntimeFailure
+from vericcl_b200.synthesis import schedule_xml
+
+PIECE_MIN_BYTES = 8 * 1024          # smallest useful piece per CTA per iteration
+PIECE_TARGET_BYTES = 512 * 1024     # pipeline a lane's work in pieces of about this size
+MAX_ITERS = 8
+
+
+class CollectiveEngine:
+    def __init__(self, comm, *, method: str = "hierarchy", slices_per_rank: int | None = None,
+                 max_lanes: int | None = None):
+        self.comm = comm
+        self.method = method
+        self.slices_per_rank = slices_per_rank
+        self._max_ctas = comm._mod.max_ctas(512)
+        self.max_lanes = max_lanes or self._max_ctas
+        self._staging: dict = {}
+
+    # -- geometry ---------------------------------------------------------------
+    def geometry(self, plan_blocks: int, chunk_bytes: int):
+        lanes = max(1, min(self.max_lanes, 256, self._max_ctas // max(1, plan_blocks)))
+        lanes = max(1, min(lanes, chunk_bytes // PIECE_MIN_BYTES))
+        iters = max(1, min(MAX_ITERS, chunk_bytes // (lanes * PIECE_TARGET_BYTES)))
+        return lanes, iters
+
+    def plan(self, collective: str, count: int, dtype, *, inplace: bool):
+        world = self.comm.world
+        slices = self.slices_per_rank or world
+        if collective in ("reduce_scatter", "alltoall") and slices % world:
+            slices = world
+        dname = str(dtype).split(".")[-1]
+        xml = schedule_xml(collective, world, slices, inplace=inplace, datatype=dname, method=self.method)
+        probe = self.comm.compile(xml, nlanes=1, niters=1)
+        esize = torch.tensor([], dtype=dtype).element_size()
+        runtime = count * (world if collective == "allgather" else 1)
+        nchunks = slices * (world if collective == "allgather" else 1)
+        chunk_bytes = runtime * esize // nchunks
+        lanes, iters = self.geometry(probe.device_plan.nblocks, chunk_bytes)
+        return self.comm.compile(xml, nlanes=lanes, niters=iters)
+
+    def _heap_copy(self, tensor: torch.Tensor, tag: str) -> torch.Tensor:
+        key = (tag, tensor.numel(), tensor.dtype)
+        buf = self._staging.get(key)
+        if buf is None:
+            buf = self.comm.empty(tensor.numel(), tensor.dtype)
+            self._staging[key] = buf
+        return buf
+
+    # -- collectives ---------------------------------------------------------
+    def all_reduce(self, tensor: torch.Tensor, *, op: str = "sum", scale: float | None = None) -> torch.Tensor:
+        """In-place AllReduce of ``tensor`` (fused reduction, cast and scale)."""
+        flat = tensor.view(-1)
+        pad = self._padding(flat.numel(), flat.dtype, self.slices_per_rank or self.comm.world)
+        if self.comm.in_heap(flat) and pad == 0:
+            plan = self.plan("allreduce", flat.numel(), flat.dtype, inplace=True)
+            self.comm.run(plan, flat, flat, op=op, scale=scale)
+            return tensor
+        count = flat.numel() + pad
+        buf = self._heap_copy(torch.empty(count, dtype=flat.dtype, device="meta"), "ar")
+        buf[:flat.numel()].copy_(flat)
+        if pad:
+            buf[flat.numel():].zero_()
+        plan = self.plan("allreduce", count, flat.dtype, inplace=True)
+        self.comm.run(plan, buf, buf, op=op, scale=scale)
+        flat.copy_(buf[:flat.numel()])
+        return tensor
+
+    def all_gather(self, inp: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        world = self.comm.world
+        if out.numel() != inp.numel() * world:
+            raise RuntimeFailure("all_gather output must hold world × input elements")
+        if self.comm.in_heap(inp) and self.comm.in_heap(out):
+            plan = self.plan("allgather", inp.numel(), inp.dtype, inplace=False)
+            self.comm.run(plan, inp.view(-1), out.view(-1))
+            return out
+        src = self._heap_copy(inp.view(-1), "ag-in")
+        dst = self._heap_copy(out.view(-1), "ag-out")
+        src.copy_(inp.view(-1))
+        plan = self.plan("allgather", inp.numel(), inp.dtype, inplace=False)
+        self.comm.run(plan, src, dst)
+        out.view(-1).copy_(dst)
+        return out
+
+    def reduce_scatter(self, inp: torch.Tensor, out: torch.Tensor, *, op: str = "sum",
+                       scale: float | None = None) -> torch.Tensor:
+        world = self.comm.world
+        if inp.numel() != out.numel() * world:
+            raise RuntimeFailure("reduce_scatter input must hold world × output elements")
+        src = inp.view(-1) if self.comm.in_heap(inp) else self._heap_copy(inp.view(-1), "rs-in")
+        dst = out.view(-1) if self.comm.in_heap(out) else self._heap_copy(out.view(-1), "rs-out")
+        if src.data_ptr() != inp.data_ptr():
+            src.copy_(inp.view(-1))
+        plan = self.plan("reduce_scatter", inp.numel(), inp.dtype, inplace=False)
+        self.comm.run(plan, src, dst, op=op, scale=scale, count_per_rank=inp.numel())
+        if dst.data_ptr() != out.data_ptr():
+            out.view(-1).copy_(dst)
+        return out
+
+    def _padding(self, count: int, dtype, slices: int) -> int:
+        esize = torch.tensor([], dtype=dtype).element_size()
+        unit = slices * (16 // esize)
+        return (-count) % unit

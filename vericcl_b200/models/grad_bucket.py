@@ -1,0 +1,56 @@
+"""Data-parallel gradient synchronisation with bucketed, scaled AllReduce.
+
+Gradients live in one flat buffer of the communicator's symmetric heap, cut
+into fixed-size buckets (25 MiB by default).  One AllReduce schedule is
+synthesized for the bucket shape and replayed for every bucket; the gradient
+scale (for example 1/world for averaging, or a loss-scale correction) is fused
+into the final store of each reduced slice, so no separate elementwise pass
+runs.  A partial last bucket is padded inside the buffer so every bucket uses
+the same compiled plan geometry (the padding holds zeros).
+"""
+from __future__ import annotations
+
+import torch
+
+from vericcl_b200.models.collectives import CollectiveEngine
+
+DEFAULT_BUCKET_BYTES = 25 * 1024 * 1024
+
+
+class GradBucketAllReduce:
+    def __init__(self, comm, numel: int, *, dtype=torch.bfloat16, bucket_bytes: int = DEFAULT_BUCKET_BYTES,
+                 scale: float | None = None, slices_per_rank: int | None = None):
+        self.comm = comm
+        self.dtype = dtype
+        self.numel = numel
+        esize = torch.tensor([], dtype=dtype).element_size()
+        world = comm.world
+        slices = slices_per_rank or world
+        unit = slices * (16 // esize)
+        self.bucket_elems = max(unit, (bucket_bytes // esize) // unit * unit)
+        self.buckets = -(-numel // self.bucket_elems)
+        self.scale = 1.0 / world if scale is None else scale
+        self.grads = comm.empty(self.buckets * self.bucket_elems, dtype)
+        self.grads[numel:].zero_()
+        self.engine = CollectiveEngine(comm, slices_per_rank=slices)
+        self.plan = self.engine.plan("allreduce", self.bucket_elems, dtype, inplace=True)
+
+    @property
+    def flat(self) -> torch.Tensor:
+        """The gradient buffer (first ``numel`` elements are the real gradients)."""
+        return self.grads[:self.numel]
+
+    def bucket(self, i: int) -> torch.Tensor:
+        return self.grads[i * self.bucket_elems:(i + 1) * self.bucket_elems]
+
+    def sync(self, stream=None) -> None:
+        """AllReduce every bucket in place with the fused scale (asynchronous on ``stream``)."""
+        for i in range(self.buckets):
+            b = self.bucket(i)
+            self.comm.run(self.plan, b, b, op="sum", scale=self.scale, stream=stream)
+
+    def bus_bytes_per_rank(self) -> float:
+        """NCCL-convention bus bytes of one full sync (2(P-1)/P × bytes; P=1 counts the bytes once)."""
+        world = self.comm.world
+        nbytes = self.numel * self.grads.element_size()
+        return nbytes * (2.0 * (world - 1) / world if world > 1 else 1.0)

@@ -34,10 +34,10 @@ RUNTIME_SOURCES = ["runtime/contract.cc", "runtime/control_transport.cc"]
 def _digest(paths, flags) -> str:
     h = hashlib.sha256()
     for p in sorted(paths):
-        h.update(str(p).encode())
+        h.update(str(Path(p).relative_to(ROOT)).encode())
         h.update(Path(p).read_bytes())
     for f in flags:
-        h.update(f.encode())
+        h.update(f.replace(str(ROOT), "<root>").encode())
     for header in sorted((CSRC / "include").rglob("*.h")):
         h.update(header.read_bytes())
     return h.hexdigest()

@@ -1,0 +1,212 @@
+"""Communicator: one process per GPU, a symmetric peer-mapped heap, compiled plans.
+
+Bootstrap uses ``torch.distributed`` for the host-side plumbing only (a gloo
+group carries the session token and the barriers between the collective
+set-up phases); every collective byte then moves through this package's own
+kernels over NVLink.  Heap set-up phases: create + export (each rank), import
+and map every peer, add the device to the NVLS multicast object, bind and map
+the multicast range (reference counterpart: NCCL's bootstrap and P2P
+transport, third_party/msccl/src/bootstrap.cc and src/transport/p2p.cc).
+
+Buffers handed to a plan must live in the heap at the same offset on every
+rank (allocate them in the same order on every rank with :meth:`empty`); the
+offsets of each (input, output, scratch) triple are checked across ranks the
+first time a plan sees them.
+"""
+from __future__ import annotations
+
+import os
+import secrets
+import threading
+from dataclasses import dataclass
+
+import torch
+
+from vericcl_b200.errors import RuntimeFailure
+from vericcl_b200.ops import native
+from vericcl_b200.program.device import DTYPES, REDOPS, REDUCING
+
+DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+TORCH_DTYPES = {"float32": torch.float32, "bfloat16": torch.bfloat16, "float16": torch.float16}
+DEFAULT_HEAP_BYTES = 1 << 30
+
+
+def _env_flag(name: str, default: bool) -> bool:
+    value = os.environ.get(name)
+    if value is None:
+        return default
+    return value not in ("0", "false", "False", "")
+
+
+@dataclass
+class PlanHandle:
+    device_plan: object
+    xml: str
+    collective: str
+    nlanes: int
+    niters: int
+    slots: tuple
+    checked: set
+
+
+class Communicator:
+    """A set of ranks (one GPU each) sharing a symmetric heap."""
+
+    def __init__(self, group=None, *, heap_bytes: int | None = None, multicast: bool | None = None,
+                 device: int | None = None, timeout_s: float = 10.0):
+        import torch.distributed as dist
+        self._dist = dist if dist.is_available() and dist.is_initialized() else None
+        if self._dist is not None:
+            self.rank = dist.get_rank(group)
+            self.world = dist.get_world_size(group)
+            backend = dist.get_backend(group)
+            self.control_group = group if backend == "gloo" else dist.new_group(
+                ranks=dist.get_process_group_ranks(group) if group is not None else None, backend="gloo")
+        else:
+            self.rank, self.world, self.control_group = 0, 1, None
+        if device is None:
+            device = int(os.environ.get("LOCAL_RANK", self.rank)) % max(1, torch.cuda.device_count())
+        torch.cuda.set_device(device)
+        self.device = device
+        self.timeout_s = timeout_s
+        heap_bytes = int(heap_bytes or os.environ.get("VERICCL_HEAP_BYTES", DEFAULT_HEAP_BYTES))
+        multicast = _env_flag("VERICCL_NVLS", False) if multicast is None else multicast
+        token = [secrets.token_hex(6) if self.rank == 0 else None]
+        if self._dist is not None and self.world > 1:
+            self._dist.broadcast_object_list(token, src=self._global(0), group=self.control_group)
+        self.session = "%s.%d" % (token[0], os.getpid() if self.world == 1 else 0)
+        mod = native.cuda()
+        self._mod = mod
+        self.heap = mod.Heap(self.rank, self.world, device, heap_bytes, self.session, bool(multicast))
+        self.barrier()
+        self.heap.exchange(60.0)
+        self.barrier()
+        self.heap.bind_multicast()
+        self.barrier()
+        self.heap.finish()
+        self._allocs: dict[int, int] = {}
+        self._plans: dict = {}
+        self._scratch: dict = {}
+        self._lock = threading.Lock()
+        self._closed = False
+
+    # -- host control plane ------------------------------------------------
+    def _global(self, rank: int) -> int:
+        if self._dist is None or self.control_group is None:
+            return rank
+        return self._dist.get_global_rank(self.control_group, rank)
+
+    def barrier(self) -> None:
+        if self._dist is not None and self.world > 1:
+            self._dist.barrier(group=self.control_group)
+
+    def all_gather_object(self, value):
+        if self._dist is None or self.world == 1:
+            return [value]
+        out = [None] * self.world
+        self._dist.all_gather_object(out, value, group=self.control_group)
+        return out
+
+    @property
+    def multicast(self) -> bool:
+        return bool(self.heap.multicast)
+
+    # -- memory --------------------------------------------------------------
+    def empty(self, numel: int, dtype=torch.float32) -> torch.Tensor:
+        """Allocate a heap tensor (collective: every rank allocates in the same order)."""
+        code = DTYPE_CODES[dtype]
+        nbytes = numel * torch.tensor([], dtype=dtype).element_size()
+        offset = self.heap.alloc(max(nbytes, 16))
+        tensor = self.heap.tensor(offset, numel, code)
+        self._allocs[tensor.data_ptr()] = offset
+        return tensor
+
+    def free(self, tensor: torch.Tensor) -> None:
+        offset = self._allocs.pop(tensor.data_ptr(), None)
+        if offset is not None:
+            self.heap.free(offset)
+
+    def offset_of(self, tensor: torch.Tensor) -> int:
+        return self.heap.offset_of(tensor)
+
+    def in_heap(self, tensor: torch.Tensor) -> bool:
+        try:
+            self.heap.offset_of(tensor)
+            return True
+        except RuntimeError:
+            return False
+
+    # -- plans ----------------------------------------------------------------
+    def compile(self, xml: str, *, nlanes: int = 1, niters: int = 1, elide: bool = True, fuse: bool = True,
+                multicast: bool = False) -> PlanHandle:
+        import re
+        coll = re.search(r'coll="([a-z_]+)"', xml)
+        collective = coll.group(1) if coll else "allreduce"
+        key = (xml, nlanes, niters, elide, fuse, multicast)
+        with self._lock:
+            if key in self._plans:
+                return self._plans[key]
+            plan = self._mod.DevicePlan(xml, self.rank, nlanes, niters, elide, fuse, multicast,
+                                        collective in REDUCING)
+            handle = PlanHandle(plan, xml, collective, nlanes, niters, tuple(plan.slots()), set())
+            self._plans[key] = handle
+            return handle
+
+    def scratch_for(self, plan: PlanHandle, count_per_rank: int, dtype) -> int:
+        code = DTYPE_CODES[dtype]
+        chunk, _ = plan.device_plan.geometry(count_per_rank, code)
+        esize = torch.tensor([], dtype=dtype).element_size()
+        need = max(16, plan.slots[2] * chunk * esize)
+        key = id(plan)
+        with self._lock:
+            have = self._scratch.get(key)
+            if have is None or have[1] < need:
+                if have is not None:
+                    self.heap.free(have[0])
+                self._scratch[key] = (self.heap.alloc(need), need)
+            return self._scratch[key][0]
+
+    def run(self, plan: PlanHandle, inp: torch.Tensor, out: torch.Tensor, *, op: str = "sum",
+            scale: float | None = None, stream=None, count_per_rank: int | None = None) -> None:
+        """Launch ``plan`` on heap tensors ``inp`` → ``out`` on ``stream`` (asynchronous)."""
+        if inp.dtype != out.dtype:
+            raise RuntimeFailure("input and output dtypes differ")
+        count = inp.numel() if count_per_rank is None else count_per_rank
+        in_off, out_off = self.offset_of(inp), self.offset_of(out)
+        scr_off = self.scratch_for(plan, count, inp.dtype)
+        key = (in_off, out_off, scr_off, count)
+        if key not in plan.checked:
+            offsets = self.all_gather_object(key)
+            if any(o != key for o in offsets):
+                raise RuntimeFailure("plan buffers are not symmetric across ranks: %s" % (offsets,))
+            plan.checked.add(key)
+        factor = 1.0 / self.world if op == "avg" else 1.0
+        if scale is not None:
+            factor *= scale
+        stream = torch.cuda.current_stream() if stream is None else stream
+        plan.device_plan.run(self.heap, in_off, out_off, scr_off, count, DTYPE_CODES[inp.dtype], REDOPS[op],
+                             float(factor), stream.cuda_stream, self.timeout_s, 512)
+
+    def status(self) -> dict:
+        return self.heap.status()
+
+    def check_status(self) -> None:
+        st = self.heap.status()
+        if st["status"] != 0:
+            raise RuntimeFailure("device status %d (rank, block, lane, wait) = %s" % (st["status"], st["detail"]))
+
+    def close(self) -> None:
+        if self._closed:
+            return
+        self._closed = True
+        torch.cuda.synchronize()
+        self.barrier()
+        self._plans.clear()
+        self.heap.destroy()
+        self.barrier()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()

@@ -1,0 +1,114 @@
+"""One-call synthesis front end: request → checked candidate bundle.
+
+``synthesize`` runs the initial pipeline the workflow uses for one (S, C)
+choice: plan (direct, hierarchy or manual), demands, route MILP,
+composition, storage plan, native lowering, XML emission, the eight
+admission checks and the exact T_pred (reference call stack:
+vericcl/workflow_v5.py:193 initial_candidates → xml/v5_lower.py:338
+lower_and_check).  ``schedule_xml`` is the shortcut the runtime API uses to
+obtain a verified XML for a collective on an NVSwitch domain.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from functools import lru_cache
+
+from vericcl_b200.composer import compose_routes
+from vericcl_b200.errors import SemanticError
+from vericcl_b200.performance.initial import initial_cost_model, model_context
+from vericcl_b200.planner.direct import build_direct_plan
+from vericcl_b200.program.native import build_executable, lower_program
+from vericcl_b200.program.storage import build_storage_plan
+from vericcl_b200.program.xmlio import emit_xml
+from vericcl_b200.solver.demands import build_demands
+from vericcl_b200.solver.routing import choose_trees
+from vericcl_b200.topology import load_topology
+
+
+@dataclass
+class CandidateBundle:
+    request: object
+    plan: object
+    network: object
+    storage: object
+    program: object
+    xml: str
+    executable: object
+    prediction: object
+    checks: dict = field(default_factory=dict)
+    origin: str = "direct"
+
+    @property
+    def t_pred_us(self):
+        return None if self.prediction is None else self.prediction.t_pred_us
+
+    @property
+    def can_execute(self) -> bool:
+        required = ("semantic", "storage", "endpoint", "deadlock", "xml", "launch", "prediction")
+        return all(self.checks.get(k, {}).get("status") == "valid" for k in required) and \
+            self.checks.get("compatibility", {}).get("status") in ("valid", "not_run")
+
+
+def plan_for(request, topology):
+    method = request.selected_synthesis_method
+    if request.request_config["atom"]["manual"]["enabled"]:
+        from vericcl_b200.planner.manual import plan_manual
+        return plan_manual(request, topology)
+    if method == "hierarchy":
+        from vericcl_b200.planner.hierarchy import plan_hierarchy
+        return plan_hierarchy(request, topology)
+    return build_direct_plan(request, topology, reason="constructive_trees_seed")
+
+
+def lower_candidate(request, topology, network, model=None, *, plan=None, origin="direct") -> CandidateBundle:
+    from vericcl_b200.program.checks import evaluate_program
+    from vericcl_b200.performance.simulation import predict
+    storage = build_storage_plan(network, request)
+    program = lower_program(storage, request)
+    xml = emit_xml(program)
+    model = model or initial_cost_model(request)
+    executable = build_executable(program, storage, request, topology, model_context(request))
+    prediction = predict(executable, model, exact=True)
+    bundle = CandidateBundle(request, plan, network, storage, program, xml, executable, prediction, origin=origin)
+    bundle.checks = evaluate_program(bundle, topology)
+    return bundle
+
+
+def synthesize(request, model=None, *, channels: int = 1) -> CandidateBundle:
+    topology = load_topology(request)
+    if request.hyperparameters.slice_count is None:
+        raise SemanticError("synthesize needs a resolved slice size; use the parameter domain first")
+    slice_bytes = request.hyperparameters.slice_size_bytes
+    if request.selected_synthesis_method == "constructive_trees" and \
+            not request.request_config["atom"]["manual"]["enabled"]:
+        from vericcl_b200.solver.trees.construct import construct_network
+        network = construct_network(request, topology, model or initial_cost_model(request), channels=channels)
+        return lower_candidate(request, topology, network, model, origin="constructive_trees")
+    plan = plan_for(request, topology)
+    demands = build_demands(plan, topology)
+    trees = choose_trees(demands, topology, slice_bytes, time_limit=request.solver.per_model_timeout_s)
+    network = compose_routes(plan, demands, trees, topology, slice_bytes, channels=channels, origin=plan.mode.value)
+    return lower_candidate(request, topology, network, model, plan=plan, origin=plan.mode.value)
+
+
+@lru_cache(maxsize=256)
+def schedule_xml(collective: str, ranks: int, slices_per_rank: int, *, inplace: bool = False,
+                 datatype: str = "float32", method: str = "hierarchy", channels: int = 1) -> str:
+    """Verified XML for ``collective`` over ``ranks`` GPUs of one NVSwitch domain.
+
+    The XML is size independent (its chunks scale with the runtime buffer);
+    the request uses a nominal 64 KiB slice so the partition is exact.
+    """
+    from vericcl_b200.examples import example_documents
+    from vericcl_b200.input.loader import resolve_documents
+    elem = {"float32": 4, "bfloat16": 2, "float16": 2}.get(datatype, 4)
+    slice_bytes = 64 * 1024 // elem * elem
+    docs = example_documents(collective, method, ranks, total_size_bytes=slice_bytes * slices_per_rank,
+                             slice_size_bytes=slice_bytes, datatype=datatype, inplace=inplace,
+                             max_channels=channels, scratch_bytes=slice_bytes * slices_per_rank * ranks)
+    request = resolve_documents(docs)
+    bundle = synthesize(request, channels=channels)
+    if not bundle.can_execute:
+        failed = {k: v for k, v in bundle.checks.items() if v.get("status") not in ("valid", "not_run")}
+        raise SemanticError("synthesized schedule failed admission checks: %s" % failed)
+    return bundle.xml
