@@ -1,0 +1,80 @@
+import numpy as np
+import pytest
+
+from vericcl_b200.errors import SemanticError
+from vericcl_b200.program.device import compile_xml, run_cpu
+from vericcl_b200.synthesis import schedule_xml
+from vericcl_b200.verification.chunksim import reference_result
+
+
+def _run(coll, p, slices, inplace, lanes, iters, fuse, merge, dtype="float32", seed=0):
+    xml = schedule_xml(coll, p, slices, inplace=inplace)
+    c = compile_xml(xml, nlanes=lanes, niters=iters, fuse=fuse, merge=merge)
+    count = p * slices * 8 * 3
+    rng = np.random.default_rng(seed)
+    ins = [rng.uniform(-1, 1, count).astype(np.float32) for _ in range(p)]
+    exp = reference_result(coll, [a.astype(np.float64) for a in ins], rank_count=p)
+    outs = run_cpu(c, ins, seed=seed, dtype=dtype)
+    tol = 1e-5 if dtype == "float32" else 2e-2 * p
+    for r in range(p):
+        if exp[r] is not None:
+            np.testing.assert_allclose(outs[r][:len(exp[r])], exp[r], atol=tol)
+    return c
+
+
+@pytest.mark.parametrize("coll", ["allreduce", "allgather", "reduce_scatter"])
+@pytest.mark.parametrize("inplace", [False, True])
+@pytest.mark.parametrize("lanes,iters,fuse,merge", [(1, 1, False, False), (3, 2, True, True), (2, 3, True, False)])
+def test_interpreter_matches_reference(coll, inplace, lanes, iters, fuse, merge):
+    for seed in range(2):
+        _run(coll, 4, 4, inplace, lanes, iters, fuse, merge, seed=seed)
+
+
+def test_bf16_and_fused_chain():
+    c = _run("allreduce", 8, 8, True, 4, 2, True, True, dtype="bfloat16")
+    assert c.stats["fused_reduces"] == 8
+    assert c.max_blocks == 1
+
+
+def test_scale_applied_once():
+    xml = schedule_xml("allreduce", 4, 4)
+    c = compile_xml(xml, nlanes=2)
+    ins = [np.full(4 * 8 * 2, r + 1.0, np.float32) for r in range(4)]
+    outs = run_cpu(c, ins, scale=0.25)
+    np.testing.assert_allclose(outs[0], 2.5)
+
+
+def test_rejects_unmatched_send():
+    xml = """<algo name="x" nchannels="1" nchunksperloop="1" coll="allgather" inplace="0" ngpus="2">
+      <gpu id="0" i_chunks="1" o_chunks="2" s_chunks="0">
+        <tb id="0" send="1" recv="-1" chan="0"><step s="0" type="s" srcbuf="i" srcoff="0" dstbuf="o" dstoff="0" cnt="1" depid="-1" deps="-1" hasdep="0"/></tb>
+      </gpu>
+      <gpu id="1" i_chunks="1" o_chunks="2" s_chunks="0"></gpu></algo>"""
+    with pytest.raises(SemanticError, match="receives"):
+        compile_xml(xml)
+
+
+def test_rejects_cyclic_schedule():
+    xml = """<algo name="x" nchannels="1" nchunksperloop="2" coll="allgather" inplace="0" ngpus="2">
+      <gpu id="0" i_chunks="1" o_chunks="2" s_chunks="0">
+        <tb id="0" send="-1" recv="1" chan="0"><step s="0" type="r" srcbuf="o" srcoff="1" dstbuf="o" dstoff="1" cnt="1" depid="-1" deps="-1" hasdep="0"/></tb>
+        <tb id="1" send="1" recv="-1" chan="0"><step s="0" type="s" srcbuf="i" srcoff="0" dstbuf="o" dstoff="0" cnt="1" depid="-1" deps="-1" hasdep="0"/></tb>
+      </gpu>
+      <gpu id="1" i_chunks="1" o_chunks="2" s_chunks="0">
+        <tb id="0" send="0" recv="0" chan="0">
+          <step s="0" type="r" srcbuf="o" srcoff="0" dstbuf="o" dstoff="0" cnt="1" depid="-1" deps="-1" hasdep="0"/>
+          <step s="1" type="s" srcbuf="i" srcoff="0" dstbuf="o" dstoff="1" cnt="1" depid="-1" deps="-1" hasdep="0"/>
+        </tb>
+      </gpu></algo>"""
+    # rank 1 receives before it sends; rank 0's receive needs rank 1's send: fine.  Make it cyclic:
+    cyclic = xml.replace('<tb id="1" send="1" recv="-1" chan="0"><step s="0" type="s"',
+                         '<tb id="1" send="1" recv="-1" chan="0"><step s="0" type="s"').replace(
+        'type="s" srcbuf="i" srcoff="0" dstbuf="o" dstoff="0" cnt="1" depid="-1"',
+        'type="s" srcbuf="i" srcoff="0" dstbuf="o" dstoff="0" cnt="1" depid="0" deps="0" hasdep="0" x="', 1)
+    with pytest.raises(SemanticError):
+        compile_xml(cyclic.replace(' x="', ' y="'))
+
+
+def test_xml_reader_rejects_garbage():
+    with pytest.raises(SemanticError):
+        compile_xml("<algo ngpus='2'><gpu></algo>")

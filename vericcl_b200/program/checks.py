@@ -138,7 +138,9 @@ def check_storage(program, request):
         slots = {"i": program.input_slots.get(block.rank, 0), "o": program.output_slots.get(block.rank, 0),
                  "s": program.scratch_slots.get(block.rank, 0)}
         for st in block.steps:
-            for addr in (st.src, st.dst):
+            # a send's dst and a receive's src name the peer's buffer and are informational
+            used = {"s": (st.src,), "r": (st.dst,), "rcs": (st.dst,), "nop": ()}.get(st.kind, (st.src, st.dst))
+            for addr in used:
                 if addr is None:
                     continue
                 if addr.offset > limits["buffer_offset"]:
