@@ -188,10 +188,10 @@ __device__ void move_generic(char* dst, const char* const* src, int nsrc, long l
 template <int DT, int RED>
 __device__ void move_piece(char* dst, const char* const* src, int nsrc, long long nvec, bool do_scale, float scale) {
   switch (nsrc) {
-    case 1: move_fixed<DT, RED, 1, 8>(dst, src, nvec, do_scale, scale); break;
-    case 2: move_fixed<DT, RED, 2, 4>(dst, src, nvec, do_scale, scale); break;
+    case 1: move_fixed<DT, RED, 1, 4>(dst, src, nvec, do_scale, scale); break;
+    case 2: move_fixed<DT, RED, 2, 2>(dst, src, nvec, do_scale, scale); break;
     case 3: move_fixed<DT, RED, 3, 2>(dst, src, nvec, do_scale, scale); break;
-    case 4: move_fixed<DT, RED, 4, 2>(dst, src, nvec, do_scale, scale); break;
+    case 4: move_fixed<DT, RED, 4, 1>(dst, src, nvec, do_scale, scale); break;
     case 5: move_fixed<DT, RED, 5, 1>(dst, src, nvec, do_scale, scale); break;
     case 6: move_fixed<DT, RED, 6, 1>(dst, src, nvec, do_scale, scale); break;
     case 7: move_fixed<DT, RED, 7, 1>(dst, src, nvec, do_scale, scale); break;
@@ -252,7 +252,8 @@ __device__ bool wait_events(const InterpArgs& a, const DevWait* w, int n, int it
 }
 
 template <int DT, int RED>
-__device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long long base, int* s_stop) {
+__device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long long base, int* s_stop,
+                        char* const* s_rank_base, const long long* s_buf_off) {
   const DevBlock blk = a.blocks[block];
   const int esize = DT == DT_F32 ? 4 : 2;
   const unsigned long long stride = 2ull * (unsigned long long)blk.nsteps;
@@ -277,11 +278,11 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
         for (int k = 0; k < st.cnt; ++k) {
           if (threadIdx.x < st.nsrc && threadIdx.x < 16) {
             const DevSrc sr = a.srcs[st.src_begin + threadIdx.x];
-            s_src[threadIdx.x] = a.base[sr.rank] + a.buf_off[sr.buf] +
+            s_src[threadIdx.x] = s_rank_base[sr.rank] + s_buf_off[sr.buf] +
                                  ((long long)(sr.chunk + k) * a.chunk_elems + pr.lo) * esize;
           }
           __syncthreads();
-          char* dst = a.base[a.rank] + a.buf_off[st.dst_buf] + ((long long)(st.dst_chunk + k) * a.chunk_elems + pr.lo) * esize;
+          char* dst = s_rank_base[a.rank] + s_buf_off[st.dst_buf] + ((long long)(st.dst_chunk + k) * a.chunk_elems + pr.lo) * esize;
           move_piece<DT, RED>(dst, s_src, st.nsrc, nvec, (st.flags & F_SCALE) != 0, a.scale);
           __syncthreads();
         }
@@ -305,6 +306,10 @@ template <int DT, int RED>
 __global__ void __launch_bounds__(512, 1) interp_kernel(const InterpArgs a) {
   __shared__ unsigned long long s_base;
   __shared__ int s_stop;
+  __shared__ char* s_rank_base[kMaxRanks];
+  __shared__ long long s_buf_off[BUF_COUNT];
+  if (threadIdx.x < kMaxRanks) s_rank_base[threadIdx.x] = a.base[threadIdx.x];
+  if (threadIdx.x < BUF_COUNT) s_buf_off[threadIdx.x] = a.buf_off[threadIdx.x];
   const int block = blockIdx.x / a.nlanes;
   const int lane = blockIdx.x % a.nlanes;
   if (threadIdx.x == 0) {
@@ -313,7 +318,7 @@ __global__ void __launch_bounds__(512, 1) interp_kernel(const InterpArgs a) {
     st_release_sys(flag_ptr(a, a.rank, a.start_slot), s_base + 1);
   }
   __syncthreads();
-  if (block < a.nblocks) run_cta<DT, RED>(a, block, lane, s_base, &s_stop);
+  if (block < a.nblocks) run_cta<DT, RED>(a, block, lane, s_base, &s_stop, s_rank_base, s_buf_off);
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();

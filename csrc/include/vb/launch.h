@@ -58,4 +58,10 @@ cudaError_t launch_check(const void* out, long long n, int dtype, int collective
                          cudaStream_t stream);
 cudaError_t launch_read_timer(unsigned long long* dst, cudaStream_t stream);
 
+// Calibration probes.
+cudaError_t launch_copy_probe(void* dst, const void* src, long long bytes, int ctas, int threads, int unroll,
+                              cudaStream_t stream);
+cudaError_t launch_reduce_probe(void* dst, const void* const* srcs, int k, long long bytes, int ctas, int threads,
+                                cudaStream_t stream);
+
 }  // namespace vb

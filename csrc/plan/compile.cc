@@ -276,7 +276,21 @@ class Compiler {
         for (int k = 0; k < st.cnt; ++k) state[canon(x.rank, st.dstbuf, st.dstoff + k)] = result[k];
       if (st.kind == X_RCS || st.kind == X_RRCS) carried[x] = result;
       if (scale) { scale_steps_.insert(x); ++stats_.scale_steps; }
+      if (writes_dst(st.kind))
+        for (int k = 0; k < st.cnt; ++k) last_writer_[canon(x.rank, st.dstbuf, st.dstoff + k)] = x;
     }
+    // Outputs that hold a complete value nobody scaled (single-rank programs, or an
+    // in-place output that already aliases its complete input) get an in-place scale step.
+    for (int r = 0; r < P_; ++r)
+      for (int k = 0; k < a_.gpus[r].o_chunks; ++k) {
+        Region reg = canon(r, BUF_OUT, k);
+        auto it = state.find(reg);
+        if (it != state.end() && it->second.known && it->second.mask == full && !it->second.scaled) {
+          it->second.scaled = true;
+          unscaled_outputs_.push_back(reg);
+          ++stats_.scale_steps;
+        }
+      }
   }
 
   void assign_blocks() {
@@ -549,6 +563,37 @@ class Compiler {
       pending_[x.rank][db].resize(std::max<size_t>(pending_[x.rank][db].size(), x.step + 1));
       pending_[x.rank][db][x.step] = ps;
     }
+    // in-place scale steps for complete but unscaled outputs
+    for (const Region& reg : unscaled_outputs_) {
+      int r = reg.rank;
+      int db = synthetic_[r] ? 0 : nblocks_[r];
+      if (!synthetic_[r] && (int)pending_[r].size() <= db) {
+        pending_[r].resize(db + 1);
+        nblocks_[r] = db + 1;
+        dsteps_count_[r].resize(db + 1, 0);
+        synthetic_extra_.insert(r);
+      }
+      PendingStep ps{};
+      ps.prio = (int)order_.size();
+      ps.st.op = OP_COPY;
+      ps.st.cnt = 1;
+      ps.st.flags = F_SCALE;
+      ps.st.dst_buf = (uint8_t)reg.buf;
+      ps.st.dst_chunk = reg.chunk;
+      ps.srcs.push_back(DevSrc{(int16_t)r, (uint8_t)reg.buf, 0, reg.chunk});
+      auto lw = last_writer_.find(reg);
+      if (lw != last_writer_.end()) merge(ps.waits, completion(lw->second));
+      // every pull of this region by a send must finish before it is rescaled
+      for (const SRef& x : all_) {
+        const XStep& st = step(x);
+        if (has_send(st.kind) && x.rank == r) {
+          Region src = pull_source(x);
+          if (src.buf == reg.buf && reg.chunk >= src.chunk && reg.chunk < src.chunk + st.cnt) merge(ps.waits, completion(x));
+        }
+      }
+      pending_[r][db].push_back(ps);
+      dsteps_count_[r][db] = (int)pending_[r][db].size();
+    }
     // end-of-kernel acknowledgements: every send must be consumed
     end_waits_.resize(P_);
     for (const SRef& x : all_) {
@@ -754,6 +799,9 @@ class Compiler {
   std::vector<RankProgram> out_;
   CompileStats stats_;
   bool merged_ = false;
+  std::map<Region, SRef> last_writer_;
+  std::vector<Region> unscaled_outputs_;
+  std::set<int> synthetic_extra_;
 };
 
 }  // namespace

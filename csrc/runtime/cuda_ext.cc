@@ -253,6 +253,25 @@ PYBIND11_MODULE(_vbcuda, m) {
                             at::cuda::getCurrentCUDAStream().stream()), "check");
     return bad;
   });
+  m.def("copy_probe", [](uint64_t dst, uint64_t src, int64_t bytes, int ctas, int threads, int unroll) {
+    cuda_check(launch_copy_probe(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), bytes, ctas, threads,
+                                 unroll, at::cuda::getCurrentCUDAStream().stream()), "copy probe");
+  });
+  m.def("reduce_probe", [](uint64_t dst, std::vector<uint64_t> srcs, int64_t bytes, int ctas, int threads) {
+    std::vector<const void*> p;
+    for (auto s : srcs) p.push_back(reinterpret_cast<const void*>(s));
+    cuda_check(launch_reduce_probe(reinterpret_cast<void*>(dst), p.data(), (int)p.size(), bytes, ctas, threads,
+                                   at::cuda::getCurrentCUDAStream().stream()), "reduce probe");
+  });
+  m.def("enable_peer_access", [](int device, int peer) {
+    int cur = 0;
+    cudaGetDevice(&cur);
+    cudaSetDevice(device);
+    cudaError_t e = cudaDeviceEnablePeerAccess(peer, 0);
+    if (e == cudaErrorPeerAccessAlreadyEnabled) { cudaGetLastError(); e = cudaSuccess; }
+    cudaSetDevice(cur);
+    cuda_check(e, "enable peer access");
+  });
   m.def("read_timer", [](torch::Tensor dst) {
     cuda_check(launch_read_timer(reinterpret_cast<unsigned long long*>(dst.data_ptr()),
                                  at::cuda::getCurrentCUDAStream().stream()), "timer");

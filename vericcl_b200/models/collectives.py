@@ -9,6 +9,8 @@ buffers (a local device copy on each side).
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from vericcl_b200.errors import RuntimeFailure
@@ -34,6 +36,10 @@ class CollectiveEngine:
         lanes = max(1, min(self.max_lanes, 256, self._max_ctas // max(1, plan_blocks)))
         lanes = max(1, min(lanes, chunk_bytes // PIECE_MIN_BYTES))
         iters = max(1, min(MAX_ITERS, chunk_bytes // (lanes * PIECE_TARGET_BYTES)))
+        if os.environ.get("VERICCL_LANES"):
+            lanes = int(os.environ["VERICCL_LANES"])
+        if os.environ.get("VERICCL_ITERS"):
+            iters = int(os.environ["VERICCL_ITERS"])
         return lanes, iters
 
     def plan(self, collective: str, count: int, dtype, *, inplace: bool):
