@@ -1,0 +1,149 @@
+"""Bottleneck analysis of an exact prediction and lazy repair-strategy streams.
+
+The exact prediction gives every operation's start/end and the rate segments
+it ran at.  ``analyze`` walks the critical chain that ends at T_pred and
+classifies each link of it:
+
+* ``resource_overlap`` — the operation ran below its own link rate because a
+  shared resource (NVLink port, NIC) was split with concurrent flows;
+* ``tb_wait`` — the operation started later than its data was ready because
+  its thread block was still busy with earlier work (TB order);
+* ``critical_service`` — the operation's own α + β·S dominates.
+
+Strategies are then generated lazily, round-robin over the eight families
+(path, allocation, order, channel, joint, internal_root, structure,
+partition) from the causes, and a compatible batch (no two strategies touch
+the same operation) is chosen with the BDD selector (reference:
+vericcl/verification/bottlenecks.py:164-453, search_coverage.py:9).
+"""
+from __future__ import annotations
+
+from collections import defaultdict
+from dataclasses import dataclass, field
+
+from vericcl_b200.verification.bdd import select_compatible
+
+FAMILIES = ("path", "allocation", "order", "channel", "joint", "internal_root", "structure", "partition")
+
+
+@dataclass(frozen=True)
+class Cause:
+    kind: str
+    operation_id: str
+    detail: dict = field(default_factory=dict, hash=False, compare=False)
+
+
+@dataclass(frozen=True)
+class StrategyRecord:
+    strategy_id: str
+    family: str
+    operations: tuple
+    parameters: tuple = ()
+
+    def as_json(self):
+        return {"id": self.strategy_id, "family": self.family, "operations": list(self.operations),
+                "parameters": dict(self.parameters)}
+
+
+@dataclass
+class Analysis:
+    t_pred_us: float
+    critical_path: list
+    causes: list
+    utilisation: dict
+    strategies: list
+
+
+def _utilisation(executable, prediction):
+    busy = defaultdict(float)
+    ops = {op.operation_id: op for op in executable.operations}
+    for key, t0, t1, rate, _src in prediction.segments:
+        for res in ops[key].resources:
+            busy[res] += t1 - t0
+    span = max(prediction.t_pred_us or 0.0, 1e-12)
+    return {res: round(t / span, 6) for res, t in sorted(busy.items())}
+
+
+def causes_on_path(executable, prediction, model, path):
+    ops = {op.operation_id: op for op in executable.operations}
+    seg_by_op = defaultdict(list)
+    for key, t0, t1, rate, src in prediction.segments:
+        seg_by_op[key].append((t0, t1, rate, src))
+    out = []
+    for key in path:
+        op = ops[key]
+        if op.kind == "nop":
+            continue
+        ready = max((prediction.end_times.get(d, 0.0) for d in op.dependencies), default=0.0)
+        start = prediction.start_times.get(key, 0.0)
+        cost = model.service_for(op.cost_key, op.payload_bytes)
+        own_rate = 1.0 / cost.beta_us_per_byte if cost else None
+        slowed = [s for s in seg_by_op[key] if own_rate and s[2] < own_rate * (1 - 1e-9)]
+        if slowed:
+            out.append(Cause("resource_overlap", key, {"min_rate": min(s[2] for s in slowed), "own_rate": own_rate,
+                                                        "resources": list(op.resources)}))
+        elif start > ready + 1e-9:
+            out.append(Cause("tb_wait", key, {"waited_us": start - ready}))
+        else:
+            out.append(Cause("critical_service", key, {"alpha_us": cost.alpha_us if cost else None}))
+    return out
+
+
+def strategy_stream(causes, network, *, max_channels: int = 16):
+    """Yield strategies round-robin over families, derived from the causes."""
+    per_family = {f: [] for f in FAMILIES}
+    by_id = {op.operation_id: op for op in (network.operations if network is not None else ())}
+    for index, cause in enumerate(causes):
+        op = by_id.get(cause.operation_id)
+        if op is None:
+            continue
+        if cause.kind == "resource_overlap":
+            per_family["path"].append(StrategyRecord("path-%d" % index, "path", (op.operation_id,),
+                                                     (("avoid", tuple(cause.detail.get("resources", ()))),)))
+            per_family["allocation"].append(StrategyRecord("alloc-%d" % index, "allocation", (op.operation_id,),
+                                                           (("channel", (op.channel + 1) % max_channels),)))
+            per_family["joint"].append(StrategyRecord("joint-%d" % index, "joint", (op.operation_id,),
+                                                      (("channel", (op.channel + 1) % max_channels),
+                                                       ("avoid", tuple(cause.detail.get("resources", ()))))))
+        elif cause.kind == "tb_wait":
+            per_family["order"].append(StrategyRecord("order-%d" % index, "order", (op.operation_id,),
+                                                      (("advance", 1),)))
+            per_family["channel"].append(StrategyRecord("chan-%d" % index, "channel", (op.operation_id,),
+                                                        (("channel", (op.channel + 1) % max_channels),)))
+        else:
+            if op.kind == "rrc":
+                per_family["internal_root"].append(StrategyRecord("root-%d" % index, "internal_root",
+                                                                  (op.operation_id,), (("reshape", "binomial"),)))
+            per_family["order"].append(StrategyRecord("prio-%d" % index, "order", (op.operation_id,),
+                                                      (("advance", 1),)))
+    per_family["structure"].append(StrategyRecord("structure-0", "structure", (), (("method", "alternate"),)))
+    per_family["partition"].append(StrategyRecord("partition-0", "partition", (), (("slices", "double"),)))
+    cursors = {f: 0 for f in FAMILIES}
+    while any(cursors[f] < len(per_family[f]) for f in FAMILIES):
+        for f in FAMILIES:
+            if cursors[f] < len(per_family[f]):
+                yield per_family[f][cursors[f]]
+                cursors[f] += 1
+
+
+def choose_batch(strategies, batch_size: int):
+    """Pick up to ``batch_size`` pairwise-compatible strategies (BDD selection)."""
+    strategies = list(strategies)[: max(batch_size * 4, batch_size)]
+    names = [s.strategy_id for s in strategies]
+    conflicts = []
+    for i, a in enumerate(strategies):
+        for b in strategies[i + 1:]:
+            if set(a.operations) & set(b.operations) or (not a.operations and not b.operations):
+                conflicts.append((a.strategy_id, b.strategy_id))
+    weights = {s.strategy_id: 1.0 / (1 + i) + 1.0 for i, s in enumerate(strategies)}
+    chosen = set(select_compatible(names, conflicts, weights))
+    return [s for s in strategies if s.strategy_id in chosen][:batch_size]
+
+
+def analyze(bundle, model, *, batch_size: int = 16) -> Analysis:
+    pred = bundle.prediction
+    path = pred.critical_path(bundle.executable)
+    causes = causes_on_path(bundle.executable, pred, model, path)
+    stream = list(strategy_stream(causes, bundle.network))
+    return Analysis(pred.t_pred_us, path, causes, _utilisation(bundle.executable, pred),
+                    choose_batch(stream, batch_size))
