@@ -54,6 +54,40 @@ __device__ __forceinline__ void st_vec(void* p, const uint4& v) {
                : "memory");
 }
 
+// NVLS multimem: the switch reduces the 16 bytes at this offset over every
+// GPU bound to the multicast object, or replicates a store to all of them.
+template <int DT>
+__device__ __forceinline__ uint4 mc_ld_reduce(const char* p);
+
+template <>
+__device__ __forceinline__ uint4 mc_ld_reduce<DT_F32>(const char* p) {
+  uint4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p) : "memory");
+  return v;
+}
+
+template <>
+__device__ __forceinline__ uint4 mc_ld_reduce<DT_BF16>(const char* p) {
+  uint4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p) : "memory");
+  return v;
+}
+
+template <>
+__device__ __forceinline__ uint4 mc_ld_reduce<DT_F16>(const char* p) {
+  uint4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.f16x2 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void mc_st(char* p, const uint4& v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w) : "memory");
+}
+
 template <int DT>
 struct VecT;
 
@@ -185,6 +219,37 @@ __device__ void move_generic(char* dst, const char* const* src, int nsrc, long l
   }
 }
 
+// dst(all ranks) = scale? * sum over ranks of src, through the multicast addresses.
+template <int DT>
+__device__ void mc_allreduce_piece(char* mc_dst, const char* mc_src, long long nvec, bool do_scale, float scale) {
+  using V = VecT<DT>;
+  constexpr int U = 4;
+  const long long stride = (long long)blockDim.x * U;
+  for (long long v0 = threadIdx.x; v0 < nvec; v0 += stride) {
+    uint4 r[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      long long v = v0 + (long long)u * blockDim.x;
+      if (v < nvec) r[u] = mc_ld_reduce<DT>(mc_src + v * 16);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      long long v = v0 + (long long)u * blockDim.x;
+      if (v >= nvec) continue;
+      uint4 out = r[u];
+      if (do_scale) {
+        float f[V::N];
+        V::unpack(r[u], f);
+#pragma unroll
+        for (int e = 0; e < V::N; ++e) f[e] *= scale;
+        out = V::pack(f);
+      }
+      mc_st(mc_dst + v * 16, out);
+    }
+  }
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
 template <int DT, int RED>
 __device__ void move_piece(char* dst, const char* const* src, int nsrc, long long nvec, bool do_scale, float scale) {
   switch (nsrc) {
@@ -227,7 +292,7 @@ __device__ bool wait_events(const InterpArgs& a, const DevWait* w, int n, int it
       target = base + 1;
       f = flag_ptr(a, dw.rank, a.start_slot);
     } else {
-      int wit = dw.iter_delta < 0 ? a.niters - 1 : it;
+      int wit = dw.iter_delta < 0 ? a.niters * a.nbatch - 1 : it;
       target = base + (unsigned long long)wit * (unsigned long long)dw.stride + (unsigned long long)dw.event;
       f = flag_ptr(a, dw.rank, (long long)dw.block * kMaxFlagLanes + lane);
     }
@@ -259,8 +324,10 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
   const unsigned long long stride = 2ull * (unsigned long long)blk.nsteps;
   unsigned long long* my_flag = flag_ptr(a, a.rank, (long long)block * kMaxFlagLanes + lane);
   __shared__ const char* s_src[16];
-  for (int it = 0; it < a.niters; ++it) {
-    const PieceRange pr = piece_range(a.chunk_elems, a.piece_elems, it, a.nlanes, lane);
+  const int total_iters = a.niters * a.nbatch;
+  for (int it = 0; it < total_iters; ++it) {
+    const int batch = it / a.niters;
+    const PieceRange pr = piece_range(a.chunk_elems, a.piece_elems, it - batch * a.niters, a.nlanes, lane);
     for (int s = 0; s < blk.nsteps; ++s) {
       const DevStep st = a.steps[blk.step_begin + s];
       if (st.wait_count) {
@@ -273,16 +340,29 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
       }
       const unsigned long long ev = base + (unsigned long long)it * stride + 2ull * s;
       if ((st.flags & F_PUB_ARRIVE) && threadIdx.x == 0) st_release_sys(my_flag, ev + 1);
+      if (st.op == OP_MC_ALLREDUCE && pr.hi > pr.lo) {
+        const long long nvec = (pr.hi - pr.lo) * esize / 16;
+        const DevSrc sr = a.srcs[st.src_begin];
+        for (int k = 0; k < st.cnt; ++k) {
+          const char* src = a.mc_base + s_buf_off[sr.buf] + batch * a.batch_stride[sr.buf] +
+                            ((long long)(sr.chunk + k) * a.chunk_elems + pr.lo) * esize;
+          char* dst = a.mc_base + s_buf_off[st.dst_buf] + batch * a.batch_stride[st.dst_buf] +
+                      ((long long)(st.dst_chunk + k) * a.chunk_elems + pr.lo) * esize;
+          mc_allreduce_piece<DT>(dst, src, nvec, (st.flags & F_SCALE) != 0, a.scale);
+        }
+        __syncthreads();
+      }
       if ((st.op == OP_COPY || st.op == OP_REDUCE) && pr.hi > pr.lo) {
         const long long nvec = (pr.hi - pr.lo) * esize / 16;
         for (int k = 0; k < st.cnt; ++k) {
           if (threadIdx.x < st.nsrc && threadIdx.x < 16) {
             const DevSrc sr = a.srcs[st.src_begin + threadIdx.x];
-            s_src[threadIdx.x] = s_rank_base[sr.rank] + s_buf_off[sr.buf] +
+            s_src[threadIdx.x] = s_rank_base[sr.rank] + s_buf_off[sr.buf] + batch * a.batch_stride[sr.buf] +
                                  ((long long)(sr.chunk + k) * a.chunk_elems + pr.lo) * esize;
           }
           __syncthreads();
-          char* dst = s_rank_base[a.rank] + s_buf_off[st.dst_buf] + ((long long)(st.dst_chunk + k) * a.chunk_elems + pr.lo) * esize;
+          char* dst = s_rank_base[a.rank] + s_buf_off[st.dst_buf] + batch * a.batch_stride[st.dst_buf] +
+                      ((long long)(st.dst_chunk + k) * a.chunk_elems + pr.lo) * esize;
           move_piece<DT, RED>(dst, s_src, st.nsrc, nvec, (st.flags & F_SCALE) != 0, a.scale);
           __syncthreads();
         }
@@ -295,7 +375,7 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
   }
   if (blk.end_wait_count) {
     if (threadIdx.x < 32) {
-      bool ok = wait_events(a, a.waits + blk.end_wait_begin, blk.end_wait_count, a.niters - 1, base, block, lane);
+      bool ok = wait_events(a, a.waits + blk.end_wait_begin, blk.end_wait_count, total_iters - 1, base, block, lane);
       if (threadIdx.x == 0 && !ok) *s_stop = 1;
     }
     __syncthreads();
@@ -346,7 +426,9 @@ cudaError_t launch_red(const InterpArgs& a, cudaStream_t stream, int threads) {
 }  // namespace
 
 cudaError_t launch_interp(const InterpArgs& a, cudaStream_t stream, int threads) {
-  if (a.nblocks < 1 || a.nlanes < 1 || a.niters < 1 || threads < 32 || threads > 512 || threads % 32) return cudaErrorInvalidValue;
+  if (a.nblocks < 1 || a.nlanes < 1 || a.niters < 1 || a.nbatch < 1 || threads < 32 || threads > 512 || threads % 32)
+    return cudaErrorInvalidValue;
+  if ((long long)a.niters * a.nbatch * 2ll * 65536ll >= (1ll << 32)) return cudaErrorInvalidValue;
   switch (a.dtype) {
     case DT_F32: return launch_red<DT_F32>(a, stream, threads);
     case DT_BF16: return launch_red<DT_BF16>(a, stream, threads);

@@ -34,6 +34,8 @@ struct InterpArgs {
   float scale;
   long long chunk_elems, piece_elems;
   long long buf_off[BUF_COUNT];      // byte offsets inside the heap (identical on all ranks)
+  long long batch_stride[BUF_COUNT]; // byte distance between consecutive batched instances of a buffer
+  int nbatch;                        // instances of the program run back to back in this launch
   long long flag_off;                // byte offset of the flag table inside the heap
   long long start_slot;              // flag index of the per-rank start flag
   char* base[kMaxRanks];             // heap base of every rank in this process's address space

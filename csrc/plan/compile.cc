@@ -80,6 +80,7 @@ class Compiler {
     assign_blocks();
     build_waits_and_hazards();
     if (o_.merge_blocks) merge_blocks();
+    if (o_.multicast && merged_ && P_ > 1) map_multicast();
     emit();
     deadlock_check();
     CompiledPlan plan;
@@ -675,6 +676,60 @@ class Compiler {
     }
     pending_ = std::move(merged);
     merged_ = true;
+  }
+
+  // NVLS mapping on merged programs.  A reduce whose sources are the same
+  // (buffer, chunk) on every rank, whose result every other rank only copies,
+  // becomes one multimem.ld_reduce + multimem.st on the owner: the switch sums
+  // the chunk and writes the result to every rank's destination; the other
+  // ranks' copies become waits on the owner's completion.
+  void map_multicast() {
+    for (int r = 0; r < P_; ++r) {
+      auto& steps = pending_[r][0];
+      for (int i = 0; i < (int)steps.size(); ++i) {
+        PendingStep& ps = steps[i];
+        if (ps.st.op != OP_REDUCE || ps.st.cnt != 1 || (int)ps.srcs.size() != P_) continue;
+        std::set<int> ranks;
+        bool same = true;
+        for (auto& sr : ps.srcs) {
+          ranks.insert(sr.rank);
+          if (sr.buf != ps.srcs[0].buf || sr.chunk != ps.srcs[0].chunk) same = false;
+        }
+        if (!same || (int)ranks.size() != P_) continue;
+        const int owner_done = 2 * i + 2;
+        std::vector<std::pair<int, int>> peers;
+        for (int p = 0; p < P_ && peers.size() + 1 < (size_t)P_ + 1; ++p) {
+          if (p == r) continue;
+          auto& ps2 = pending_[p][0];
+          int found = -1;
+          for (int j = 0; j < (int)ps2.size(); ++j) {
+            const PendingStep& c = ps2[j];
+            if (c.st.op != OP_COPY || c.st.cnt != 1 || c.srcs.size() != 1) continue;
+            const DevSrc& sr = c.srcs[0];
+            if (sr.rank != r || sr.buf != ps.st.dst_buf || sr.chunk != ps.st.dst_chunk) continue;
+            if (c.st.dst_buf != ps.st.dst_buf || c.st.dst_chunk != ps.st.dst_chunk || (c.st.flags & F_SCALE)) continue;
+            bool only_owner = true;
+            for (auto& kv : c.waits)
+              if (kv.first.second >= 0 && !(kv.first.first == r && kv.first.second == 0 && kv.second == owner_done))
+                only_owner = false;
+            if (only_owner) { found = j; break; }
+          }
+          if (found < 0) break;
+          peers.emplace_back(p, found);
+        }
+        if ((int)peers.size() != P_ - 1) continue;
+        ps.st.op = OP_MC_ALLREDUCE;
+        DevSrc first = ps.srcs[0];
+        first.rank = (int16_t)r;
+        ps.srcs.assign(1, first);
+        for (auto& pj : peers) {
+          PendingStep& c = pending_[pj.first][0][pj.second];
+          c.st.op = OP_NOP;
+          c.srcs.clear();
+        }
+        stats_.multicast_ops++;
+      }
+    }
   }
 
   void emit() {

@@ -132,7 +132,8 @@ class DevicePlan {
   }
 
   void run(Heap& heap, size_t in_off, size_t out_off, size_t scr_off, int64_t count_per_rank, int dtype, int redop,
-           float scale, uint64_t stream, double timeout_s, int threads) {
+           float scale, uint64_t stream, double timeout_s, int threads, int nbatch,
+           std::vector<long long> batch_stride) {
     SymHeap& h = heap.get();
     if (h.nranks() != (int)plan_.ranks.size()) throw std::runtime_error("heap and plan rank counts differ");
     py::tuple g = geometry(count_per_rank, dtype);
@@ -154,16 +155,20 @@ class DevicePlan {
     a.buf_off[BUF_IN] = (long long)in_off;
     a.buf_off[BUF_OUT] = (long long)out_off;
     a.buf_off[BUF_SCR] = (long long)scr_off;
+    if (nbatch < 1 || batch_stride.size() != 3) throw std::runtime_error("invalid batch description");
+    a.nbatch = nbatch;
+    for (int b = 0; b < 3; ++b) a.batch_stride[b] = batch_stride[b];
     const RankProgram& rp = plan_.ranks[rank_];
     size_t esz = elem_bytes(dtype);
-    auto need = [&](size_t off, int chunks, const char* name) {
-      if (chunks && off + (size_t)chunks * a.chunk_elems * esz > h.size())
+    auto need = [&](size_t off, int chunks, long long stride, const char* name) {
+      size_t last = off + (size_t)(nbatch - 1) * (size_t)stride;
+      if (chunks && last + (size_t)chunks * a.chunk_elems * esz > h.size())
         throw std::runtime_error(std::string(name) + " buffer exceeds the heap");
-      if (off % 16) throw std::runtime_error(std::string(name) + " buffer is not 16-byte aligned");
+      if (off % 16 || stride % 16 || stride < 0) throw std::runtime_error(std::string(name) + " buffer is not 16-byte aligned");
     };
-    need(in_off, rp.i_chunks, "input");
-    need(out_off, rp.o_chunks, "output");
-    need(scr_off, rp.s_chunks, "scratch");
+    need(in_off, rp.i_chunks, a.batch_stride[BUF_IN], "input");
+    need(out_off, rp.o_chunks, a.batch_stride[BUF_OUT], "output");
+    need(scr_off, rp.s_chunks, a.batch_stride[BUF_SCR], "scratch");
     a.flag_off = (long long)h.flag_offset();
     a.start_slot = h.start_slot();
     for (int r = 0; r < h.nranks(); ++r) a.base[r] = h.base(r);
@@ -229,7 +234,8 @@ PYBIND11_MODULE(_vbcuda, m) {
       .def(py::init<const std::string&, int, int, int, bool, bool, bool, bool>())
       .def("run", &DevicePlan::run, py::arg("heap"), py::arg("in_off"), py::arg("out_off"), py::arg("scr_off"),
            py::arg("count_per_rank"), py::arg("dtype"), py::arg("redop"), py::arg("scale"), py::arg("stream"),
-           py::arg("timeout_s") = 10.0, py::arg("threads") = 512)
+           py::arg("timeout_s") = 10.0, py::arg("threads") = 512, py::arg("nbatch") = 1,
+           py::arg("batch_stride") = std::vector<long long>{0, 0, 0})
       .def("geometry", &DevicePlan::geometry)
       .def("slots", &DevicePlan::slots)
       .def("describe", &DevicePlan::describe)

@@ -52,6 +52,8 @@ def main():
     comm = Communicator(heap_bytes=1 << 30, multicast=os.environ.get("VERICCL_NVLS", "0") == "1", timeout_s=5.0)
     failures = 0
     cases = []
+    if rank == 0:
+        print(json.dumps({"multicast": comm.multicast, "world": world}), flush=True)
     for coll in ("allreduce", "allgather", "reduce_scatter"):
         for dtype in (torch.float32, torch.bfloat16):
             for inplace in (False, True):
@@ -62,7 +64,8 @@ def main():
     for coll, dtype, inplace, slices, lanes, iters, count in cases:
         dname = str(dtype).split(".")[-1]
         xml = schedule_xml(coll, world, slices, inplace=inplace, datatype=dname)
-        plan = comm.compile(xml, nlanes=lanes, niters=iters)
+        op = "avg" if coll == "allreduce" and lanes == 4 else "sum"
+        plan = comm.compile(xml, nlanes=lanes, niters=iters, multicast=comm.multicast and coll == "allreduce")
         seed = zlib.crc32(repr((coll, dname, inplace, slices, lanes, iters, count)).encode()) % 100000
         x = inputs_for(rank, count, dtype, seed).cuda()
         out_n = count * world if coll == "allgather" else count // world if coll == "reduce_scatter" else count
@@ -82,7 +85,6 @@ def main():
             out = comm.empty(out_n, dtype)
             inp.copy_(x)
             out.fill_(float("nan"))
-        op = "avg" if coll == "allreduce" and lanes == 4 else "sum"
         torch.cuda.synchronize()
         dist.barrier()
         if inplace:

@@ -43,11 +43,25 @@ class GradBucketAllReduce:
     def bucket(self, i: int) -> torch.Tensor:
         return self.grads[i * self.bucket_elems:(i + 1) * self.bucket_elems]
 
-    def sync(self, stream=None) -> None:
-        """AllReduce every bucket in place with the fused scale (asynchronous on ``stream``)."""
+    def sync(self, stream=None, *, batched: bool = True) -> None:
+        """AllReduce every bucket in place with the fused scale (asynchronous on ``stream``).
+
+        By default all buckets run in one persistent launch (the bucket index is an
+        outer pipeline dimension of the replayed schedule); ``batched=False`` issues one
+        launch per bucket.
+        """
+        if batched:
+            b = self.bucket(0)
+            self.comm.run(self.plan, b, b, op="sum", scale=self.scale, stream=stream, nbatch=self.buckets,
+                          in_stride=self.bucket_elems, out_stride=self.bucket_elems)
+            return
         for i in range(self.buckets):
             b = self.bucket(i)
             self.comm.run(self.plan, b, b, op="sum", scale=self.scale, stream=stream)
+
+    @property
+    def launches_per_sync(self) -> int:
+        return 1
 
     def bus_bytes_per_rank(self) -> float:
         """NCCL-convention bus bytes of one full sync (2(P-1)/P × bytes; P=1 counts the bytes once)."""

@@ -47,6 +47,7 @@ class PlanHandle:
     niters: int
     slots: tuple
     checked: set
+    multicast: bool = False
 
 
 class Communicator:
@@ -77,18 +78,37 @@ class Communicator:
         self.session = "%s.%d" % (token[0], os.getpid() if self.world == 1 else 0)
         mod = native.cuda()
         self._mod = mod
-        self.heap = mod.Heap(self.rank, self.world, device, heap_bytes, self.session, bool(multicast))
-        self.barrier()
-        self.heap.exchange(60.0)
-        self.barrier()
-        self.heap.bind_multicast()
-        self.barrier()
-        self.heap.finish()
+        self.heap = self._build_heap(heap_bytes, bool(multicast))
+        if multicast and not self.heap_multicast_everywhere():
+            # NVLS could not be set up on every rank: rebuild the heap without it on all ranks
+            self.heap.destroy()
+            self.barrier()
+            self.session += ".u"
+            self.heap = self._build_heap(heap_bytes, False)
         self._allocs: dict[int, int] = {}
         self._plans: dict = {}
         self._scratch: dict = {}
         self._lock = threading.Lock()
         self._closed = False
+
+    def _build_heap(self, heap_bytes: int, multicast: bool):
+        heap = self._mod.Heap(self.rank, self.world, self.device, heap_bytes, self.session, multicast)
+        self.barrier()
+        heap.exchange(60.0)
+        self.barrier()
+        error = None
+        try:
+            heap.bind_multicast()
+        except RuntimeError as exc:       # a failed bind leaves the heap usable for peer access
+            error = str(exc)
+        self.setup_error = error
+        self.barrier()
+        heap.finish()
+        return heap
+
+    def heap_multicast_everywhere(self) -> bool:
+        flags = self.all_gather_object(bool(self.heap.multicast))
+        return all(flags)
 
     # -- host control plane ------------------------------------------------
     def _global(self, rank: int) -> int:
@@ -148,15 +168,15 @@ class Communicator:
                 return self._plans[key]
             plan = self._mod.DevicePlan(xml, self.rank, nlanes, niters, elide, fuse, multicast,
                                         collective in REDUCING)
-            handle = PlanHandle(plan, xml, collective, nlanes, niters, tuple(plan.slots()), set())
+            handle = PlanHandle(plan, xml, collective, nlanes, niters, tuple(plan.slots()), set(), multicast)
             self._plans[key] = handle
             return handle
 
-    def scratch_for(self, plan: PlanHandle, count_per_rank: int, dtype) -> int:
+    def scratch_for(self, plan: PlanHandle, count_per_rank: int, dtype, copies: int = 1) -> int:
         code = DTYPE_CODES[dtype]
         chunk, _ = plan.device_plan.geometry(count_per_rank, code)
         esize = torch.tensor([], dtype=dtype).element_size()
-        need = max(16, plan.slots[2] * chunk * esize)
+        need = max(16, plan.slots[2] * chunk * esize * copies)
         key = id(plan)
         with self._lock:
             have = self._scratch.get(key)
@@ -167,25 +187,38 @@ class Communicator:
             return self._scratch[key][0]
 
     def run(self, plan: PlanHandle, inp: torch.Tensor, out: torch.Tensor, *, op: str = "sum",
-            scale: float | None = None, stream=None, count_per_rank: int | None = None) -> None:
-        """Launch ``plan`` on heap tensors ``inp`` → ``out`` on ``stream`` (asynchronous)."""
+            scale: float | None = None, stream=None, count_per_rank: int | None = None, nbatch: int = 1,
+            in_stride: int = 0, out_stride: int = 0) -> None:
+        """Launch ``plan`` on heap tensors ``inp`` → ``out`` on ``stream`` (asynchronous).
+
+        With ``nbatch > 1`` one launch runs the plan ``nbatch`` times back to back on
+        buffers ``in_stride`` / ``out_stride`` elements apart (for example every
+        gradient bucket of a flat buffer); the instances pipeline through the same
+        persistent CTAs and only the last one waits for peers at the end.
+        """
         if inp.dtype != out.dtype:
             raise RuntimeFailure("input and output dtypes differ")
         count = inp.numel() if count_per_rank is None else count_per_rank
         in_off, out_off = self.offset_of(inp), self.offset_of(out)
-        scr_off = self.scratch_for(plan, count, inp.dtype)
-        key = (in_off, out_off, scr_off, count)
+        esize = inp.element_size()
+        scr_off = self.scratch_for(plan, count, inp.dtype, copies=nbatch)
+        chunk, _ = plan.device_plan.geometry(count, DTYPE_CODES[inp.dtype])
+        scr_stride = plan.slots[2] * chunk * esize
+        strides = [in_stride * esize, out_stride * esize, scr_stride]
+        key = (in_off, out_off, scr_off, count, nbatch, tuple(strides))
         if key not in plan.checked:
             offsets = self.all_gather_object(key)
             if any(o != key for o in offsets):
                 raise RuntimeFailure("plan buffers are not symmetric across ranks: %s" % (offsets,))
             plan.checked.add(key)
+        if plan.multicast and op not in ("sum", "avg"):
+            raise RuntimeFailure("a multicast-mapped plan only reduces with sum/avg; compile without multicast")
         factor = 1.0 / self.world if op == "avg" else 1.0
         if scale is not None:
             factor *= scale
         stream = torch.cuda.current_stream() if stream is None else stream
         plan.device_plan.run(self.heap, in_off, out_off, scr_off, count, DTYPE_CODES[inp.dtype], REDOPS[op],
-                             float(factor), stream.cuda_stream, self.timeout_s, 512)
+                             float(factor), stream.cuda_stream, self.timeout_s, 512, nbatch, strides)
 
     def status(self) -> dict:
         return self.heap.status()
