@@ -1,0 +1,136 @@
+"""Command line: ``python -m vericcl_b200 {solve,verify,calibrate,inspect,resume}``.
+
+Arguments mirror the reference CLI (vericcl/cli/main.py:22-80): the four
+input files, ``--project-root``, ``--case``, ``--run-id``, repeated
+``--set FIELD=JSON`` overrides and ``--override-input``; ``verify`` adds
+``--xml --sidecar --model [--tune]``; ``inspect`` and ``resume`` take
+``--run``.  Exit codes: 0 ok, 2 invalid input, 5 semantic failure, 7 budget,
+8 runtime failure, 130 interrupted.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+from pathlib import Path
+
+from vericcl_b200 import __version__
+from vericcl_b200.errors import VericclError
+
+
+def _inputs(p):
+    p.add_argument("--project-root", default=".")
+    p.add_argument("--case", required=True)
+    p.add_argument("--run-id", default=None)
+    for name in ("topology", "sketch", "atom", "runtime"):
+        p.add_argument("--" + name, required=True)
+    p.add_argument("--set", dest="overrides", action="append", default=[], metavar="FIELD=JSON")
+    p.add_argument("--override-input", action="store_true")
+
+
+def build_parser():
+    parser = argparse.ArgumentParser(prog="vericcl_b200", description="B200 collective schedule synthesizer")
+    parser.add_argument("--version", action="version", version="vericcl_b200 " + __version__)
+    sub = parser.add_subparsers(dest="command", required=True)
+    _inputs(sub.add_parser("solve", help="synthesize, verify and tune a schedule"))
+    v = sub.add_parser("verify", help="check an existing schedule (optionally tune it)")
+    _inputs(v)
+    v.add_argument("--xml", required=True)
+    v.add_argument("--sidecar", required=True)
+    v.add_argument("--model", required=True)
+    v.add_argument("--tune", action="store_true")
+    _inputs(sub.add_parser("calibrate", help="measure the cost model on the GPUs"))
+    i = sub.add_parser("inspect", help="print a run's status as JSON")
+    i.add_argument("--run", required=True)
+    r = sub.add_parser("resume", help="continue a run from its checkpoint")
+    r.add_argument("--run", required=True)
+    return parser
+
+
+def _files(args):
+    return {name: getattr(args, name) for name in ("topology", "sketch", "atom", "runtime")}
+
+
+def _probe_executor(request):
+    from vericcl_b200.online.native_probe import native_probe_executor
+    return native_probe_executor(request)
+
+
+def new_run(args) -> int:
+    from vericcl_b200.execution.context import RunContext
+    from vericcl_b200.input.loader import load_request
+    from vericcl_b200.performance.model import CostModel
+    from vericcl_b200.utils.jsonio import strict_load
+    from vericcl_b200.workflow import PrimaryWorkflow
+    purpose = args.command
+    request = load_request(_files(args), args.overrides, override_input=args.override_input, purpose=purpose)
+    extra = {}
+    verify_inputs = None
+    model = None
+    if purpose == "verify":
+        extra = {"schedule_xml": args.xml, "schedule_sidecar": args.sidecar, "model": args.model}
+        verify_inputs = {"xml": Path(args.xml).read_text(), "sidecar": strict_load(args.sidecar)}
+        model = CostModel.from_json(strict_load(args.model))
+    ctx = RunContext.create(args.project_root, args.case, purpose, run_id=args.run_id, input_files=_files(args),
+                            extra_inputs=extra)
+    ctx.update_run_json(effective_request=dict(request.request_config), value_sources=dict(request.value_sources),
+                        size_accounting=dict(request.size_accounting), overrides=list(args.overrides))
+    executor = _probe_executor(request) if (purpose == "calibrate" or
+                                            request.request_config["sketch"]["calibration"]["enabled"]) else None
+    wf = PrimaryWorkflow(request, ctx, purpose=purpose, tune=getattr(args, "tune", False), model=model,
+                         verify_inputs=verify_inputs, probe_executor=executor)
+    result = wf.run()
+    print(json.dumps({"run": str(ctx.directory), "status": result.status, "stop_reason": result.stop_reason,
+                      "t_pred_us": None if result.best is None else result.best["t_pred_us"]}))
+    return 0 if result.status == "ok" else 5
+
+
+def inspect_run(args) -> int:
+    from vericcl_b200.utils.jsonio import strict_load
+    run = Path(args.run)
+    meta = strict_load(run / "run.json")
+    checkpoints = sorted(p.name for p in (run / "process" / "checkpoints").glob("*.json"))
+    print(json.dumps({"run_id": meta.get("run_id"), "status": meta.get("status"), "best": meta.get("best"),
+                      "result": meta.get("result"), "checkpoints": checkpoints}, indent=2, default=str))
+    return 0
+
+
+def resume_run(args) -> int:
+    from vericcl_b200.execution.checkpoint import restore_checkpoint
+    from vericcl_b200.execution.context import RunContext
+    from vericcl_b200.input.loader import resolve_documents
+    from vericcl_b200.performance.model import CostModel
+    from vericcl_b200.utils.jsonio import strict_load
+    from vericcl_b200.workflow import PrimaryWorkflow
+    ctx = RunContext.open(args.run)
+    meta = ctx.read_run_json()
+    if meta.get("status") == "finished":
+        print(json.dumps({"run": str(ctx.directory), "status": "already finished"}))
+        return 0
+    state = restore_checkpoint(ctx)
+    request = resolve_documents(meta["effective_request"], purpose=meta["command"] if meta["command"] in (
+        "solve", "verify", "calibrate") else "solve")
+    model_path = ctx.process / "models" / (state["state"]["model_version"] + ".json")
+    model = CostModel.from_json(strict_load(model_path)) if model_path.exists() else None
+    wf = PrimaryWorkflow(request, ctx, purpose=state["state"].get("purpose", "solve"),
+                         tune=state["state"].get("tune", False), model=model, restored=state)
+    result = wf.run()
+    print(json.dumps({"run": str(ctx.directory), "status": result.status, "stop_reason": result.stop_reason,
+                      "resumed_from": state["phase"]}))
+    return 0 if result.status == "ok" else 5
+
+
+def main(argv=None) -> int:
+    parser = build_parser()
+    args = parser.parse_args(argv)
+    try:
+        if args.command in ("solve", "verify", "calibrate"):
+            return new_run(args)
+        if args.command == "inspect":
+            return inspect_run(args)
+        return resume_run(args)
+    except KeyboardInterrupt:
+        return 130
+    except VericclError as error:
+        print("error: %s" % error, file=sys.stderr)
+        return error.exit_code

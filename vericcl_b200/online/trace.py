@@ -1,0 +1,112 @@
+"""Step traces of the interpreter: binary format, parsing and causality.
+
+With tracing enabled the interpreter's CTAs record, for every (iteration,
+step), the %globaltimer value when the step's waits were satisfied and when
+its data work finished.  A rank's trace file is a 40-byte header (magic,
+version, rank, CTA count, steps per CTA, record count) followed by 64-byte
+records (CTA, block, lane, iteration, step, op, start, end, wait, reserved),
+mirroring the reference's fixed-size layout (vericcl/verification/online/
+trace_format.py:18-19 and runtime/msccl-trace/include/vericcl_trace_format.h).
+``analyze_trace_causality`` maps every record to host time with the clock
+maps, then reports per-rank spans, the slowest steps ("tails"), waits that
+dominate, and the cross-GPU orderings that are uncertain.
+"""
+from __future__ import annotations
+
+import struct
+from dataclasses import dataclass
+
+from vericcl_b200.online.clock_sync import ordered
+
+MAGIC = 0x56425452      # "VBTR"
+HEADER = struct.Struct("<IIiiiiqq")            # magic, version, rank, ctas, steps, pad, records, reserved
+RECORD = struct.Struct("<iiiiiiqqq" + "16x")   # cta, block, lane, iter, step, op, start, end, wait
+assert HEADER.size == 40 and RECORD.size == 64
+
+
+@dataclass(frozen=True)
+class TraceRecord:
+    rank: int
+    cta: int
+    block: int
+    lane: int
+    iteration: int
+    step: int
+    op: int
+    start_ns: int
+    end_ns: int
+    wait_ns: int
+
+
+def write_trace(path, rank: int, ctas: int, steps: int, records) -> None:
+    with open(path, "wb") as handle:
+        handle.write(HEADER.pack(MAGIC, 1, rank, ctas, steps, 0, len(records), 0))
+        for r in records:
+            handle.write(RECORD.pack(r.cta, r.block, r.lane, r.iteration, r.step, r.op, r.start_ns, r.end_ns,
+                                     r.wait_ns))
+
+
+def parse_trace(data: bytes, *, partial_ok: bool = True):
+    if len(data) < HEADER.size:
+        raise ValueError("trace shorter than its header")
+    magic, version, rank, ctas, steps, _pad, count, _res = HEADER.unpack_from(data, 0)
+    if magic != MAGIC or version != 1:
+        raise ValueError("not a vericcl_b200 trace")
+    available = (len(data) - HEADER.size) // RECORD.size
+    if available < count and not partial_ok:
+        raise ValueError("trace truncated: %d of %d records" % (available, count))
+    out = []
+    for i in range(min(count, available)):
+        f = RECORD.unpack_from(data, HEADER.size + i * RECORD.size)
+        out.append(TraceRecord(rank, *f))
+    return {"rank": rank, "ctas": ctas, "steps": steps, "declared": count, "records": out,
+            "complete": available >= count}
+
+
+def records_from_buffer(rank, buffer, *, nblocks, nlanes, steps_per_iter, niters, ops):
+    """Decode the kernel's raw (start, end, wait) triples into records."""
+    out = []
+    per_cta = steps_per_iter * niters
+    for cta in range(nblocks * nlanes):
+        block, lane = cta // nlanes, cta % nlanes
+        for it in range(niters):
+            for s in range(steps_per_iter):
+                base = (cta * per_cta + it * steps_per_iter + s) * 3
+                start, end, wait = buffer[base], buffer[base + 1], buffer[base + 2]
+                if start == 0 and end == 0:
+                    continue
+                out.append(TraceRecord(rank, cta, block, lane, it, s, ops[s] if s < len(ops) else -1, int(start),
+                                       int(end), int(wait)))
+    return out
+
+
+def analyze_trace_causality(traces, clock_maps, *, tails: int = 5):
+    """Span per rank, slowest steps, dominant waits and uncertain cross-rank orders."""
+    spans, steps, waits = {}, [], []
+    for rank, recs in traces.items():
+        cmap = clock_maps[rank]
+        if not recs:
+            continue
+        t0 = min(cmap.to_host(r.start_ns) for r in recs)
+        t1 = max(cmap.to_host(r.end_ns) for r in recs)
+        spans[rank] = (t0, t1)
+        for r in recs:
+            steps.append((cmap.to_host(r.end_ns) - cmap.to_host(r.start_ns), rank, r.step, r.iteration, r.lane))
+            waits.append((r.wait_ns, rank, r.step, r.iteration, r.lane))
+    steps.sort(reverse=True)
+    waits.sort(reverse=True)
+    uncertain = []
+    ranks = sorted(spans)
+    for i, a in enumerate(ranks):
+        for b in ranks[i + 1:]:
+            if ordered(spans[a], spans[b]) == "uncertain":
+                uncertain.append((a, b))
+    first = min((s[0] for s in spans.values()), default=0.0)
+    last = max((s[1] for s in spans.values()), default=0.0)
+    return {"global_span_us": (last - first) / 1e3,
+            "rank_spans_us": {r: ((s[1] - s[0]) / 1e3) for r, s in spans.items()},
+            "tails": [{"duration_us": d / 1e3, "rank": r, "step": s, "iteration": it, "lane": l}
+                      for d, r, s, it, l in steps[:tails]],
+            "dominant_waits": [{"wait_us": w / 1e3, "rank": r, "step": s, "iteration": it, "lane": l}
+                               for w, r, s, it, l in waits[:tails]],
+            "overlapping_ranks": uncertain}

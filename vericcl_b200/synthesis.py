@@ -112,3 +112,15 @@ def schedule_xml(collective: str, ranks: int, slices_per_rank: int, *, inplace: 
         failed = {k: v for k, v in bundle.checks.items() if v.get("status") not in ("valid", "not_run")}
         raise SemanticError("synthesized schedule failed admission checks: %s" % failed)
     return bundle.xml
+
+
+class Lowerer:
+    """Callable that lowers, checks and predicts network candidates under one model."""
+
+    def __init__(self, request, topology, model):
+        self.request = request
+        self.topology = topology
+        self.model = model
+
+    def __call__(self, network) -> CandidateBundle:
+        return lower_candidate(self.request, self.topology, network, self.model, origin=network.origin)

@@ -1,0 +1,329 @@
+"""The main loop: initial synthesis → baseline → calibration → tuning rounds.
+
+Stages (reference: vericcl/workflow_v5.py:61-790):
+
+1. **initial candidates** — for each legal (S, C) choice, synthesize with the
+   selected method (hierarchy / constructive_trees / manual) plus the other
+   method as a second stream; every candidate is lowered, checked (eight
+   dimensions) and predicted exactly, and persisted under
+   ``process/candidates/<id>/``.
+2. **baseline** — executable candidates sorted by exact T_pred under the
+   current model; the best is adopted.
+3. **calibration** (optional) — probes refit the cost model; the incumbent
+   and the stored candidates are re-evaluated under the new model version
+   before any comparison.
+4. **tuning rounds** — a directed-cut certificate can end the search; else a
+   bottleneck analysis yields a batch of strategies, local repair and
+   resynthesis branches produce candidates, each is compared with the
+   incumbent under the same model, and only a strictly better one (and, when
+   measurement is enabled, a measured improvement) is adopted.
+5. **finish** — results are published (schedule.xml/json, model.json,
+   report.md, details.zip) and the run is finalised.
+
+A checkpoint is written at every stage boundary and after every stored
+candidate; ``resume`` restores it.
+"""
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field, replace
+
+from vericcl_b200.errors import BudgetExhausted, SemanticError, SolverError
+from vericcl_b200.execution.budget import BudgetManager
+from vericcl_b200.execution.checkpoint import save_checkpoint
+from vericcl_b200.execution.context import finalize_run
+from vericcl_b200.execution.publication import publish_results
+from vericcl_b200.performance.initial import initial_cost_model, model_context
+from vericcl_b200.performance.model import CostModel
+from vericcl_b200.performance.simulation import predict
+from vericcl_b200.planner.parameters import initial_parameter_domain
+from vericcl_b200.program.sidecar import to_sidecar
+from vericcl_b200.synthesis import Lowerer, synthesize
+from vericcl_b200.topology import load_topology
+from vericcl_b200.utils.jsonio import atomic_write_json, atomic_write_text
+
+
+@dataclass
+class RunResult:
+    status: str
+    stop_reason: str
+    best: dict | None
+    rounds: list = field(default_factory=list)
+    proof: dict | None = None
+    timing: dict = field(default_factory=dict)
+    issues: list = field(default_factory=list)
+
+    def as_json(self):
+        return {"status": self.status, "stop_reason": self.stop_reason, "best": self.best, "rounds": self.rounds,
+                "proof": self.proof, "timing": self.timing, "issues": self.issues}
+
+
+def accept_candidate(incumbent, candidate, *, tolerance: float = 1e-9) -> bool:
+    """Strictly better exact T_pred under the same model version, all required checks valid."""
+    if candidate is None or not candidate.can_execute or candidate.t_pred_us is None:
+        return False
+    if incumbent is None:
+        return True
+    if candidate.prediction.model_version != incumbent.prediction.model_version:
+        return False
+    return candidate.t_pred_us < incumbent.t_pred_us * (1 - tolerance)
+
+
+class PrimaryWorkflow:
+    def __init__(self, request, ctx, *, purpose: str = "solve", tune: bool = False, model: CostModel | None = None,
+                 verify_inputs: dict | None = None, probe_executor=None, measure=None, restored: dict | None = None):
+        self.request = request
+        self.ctx = ctx
+        self.purpose = purpose
+        self.tune = tune
+        self.topology = load_topology(request)
+        self.model = model or initial_cost_model(request)
+        self.verify_inputs = verify_inputs or {}
+        self.probe_executor = probe_executor
+        self.measure = measure
+        budgets = dict(request.request_config["sketch"]["budgets"])
+        self.budgets = BudgetManager(budgets, cpu_budget=request.solver.cpu_budget)
+        self.candidates = []
+        self.incumbent = None
+        self.rounds = []
+        self.proof = None
+        self.stage_times = {}
+        self.restored = restored
+        if restored:
+            snap = restored.get("budgets", {})
+            self.budgets.consumed.update(snap.get("consumed", {}))
+            self.budgets.restore_elapsed(snap.get("elapsed_s", 0.0) + restored.get("downtime_s", 0.0))
+
+    # -- persistence ------------------------------------------------------------
+    def store(self, bundle, tag: str) -> str:
+        cid = "%s-%03d" % (tag, len(self.candidates))
+        d = self.ctx.process / "candidates" / cid
+        d.mkdir(parents=True, exist_ok=True)
+        atomic_write_text(d / "schedule.xml", bundle.xml)
+        atomic_write_json(d / "schedule.json", to_sidecar(bundle))
+        atomic_write_json(d / "candidate.json", {"id": cid, "origin": bundle.origin, "t_pred_us": bundle.t_pred_us,
+                                                 "model_version": bundle.prediction.model_version,
+                                                 "slice_size_bytes": bundle.request.hyperparameters.slice_size_bytes,
+                                                 "method": bundle.request.selected_synthesis_method,
+                                                 "can_execute": bundle.can_execute})
+        atomic_write_json(d / "checks.json", bundle.checks)
+        bundle.candidate_id = cid
+        self.candidates.append(bundle)
+        self.ctx.emit("candidate_stored", id=cid, t_pred_us=bundle.t_pred_us, can_execute=bundle.can_execute)
+        return cid
+
+    def checkpoint(self, phase: str):
+        state = {"incumbent": getattr(self.incumbent, "candidate_id", None),
+                 "candidates": [getattr(b, "candidate_id", None) for b in self.candidates],
+                 "rounds": self.rounds, "model_version": self.model.version, "purpose": self.purpose,
+                 "tune": self.tune}
+        files = []
+        if self.incumbent is not None and getattr(self.incumbent, "candidate_id", None):
+            cid = self.incumbent.candidate_id
+            files = ["process/candidates/%s/schedule.xml" % cid, "process/candidates/%s/schedule.json" % cid]
+        atomic_write_json(self.ctx.process / "models" / (self.model.version + ".json"), self.model.as_json())
+        save_checkpoint(self.ctx, phase=phase, state=state, files=files, budgets=self.budgets.snapshot())
+
+    # -- stages -------------------------------------------------------------------
+    def initial_candidates(self):
+        t0 = time.monotonic()
+        with self.budgets.acquire("initial") as lease:
+            if self.request.hyperparameters.slice_size_bytes is not None:
+                choices = [None]
+            else:
+                choices = initial_parameter_domain(self.request)[:4]
+            methods = [self.request.selected_synthesis_method]
+            if not self.request.request_config["atom"]["manual"]["enabled"]:
+                methods.append("constructive_trees" if methods[0] == "hierarchy" else "hierarchy")
+            for choice in choices:
+                req = self.request if choice is None else self.request.with_slice(choice.slice_size_bytes)
+                channels = 1 if choice is None else choice.channels
+                for method in methods:
+                    lease.check()
+                    try:
+                        bundle = synthesize(replace(req, selected_synthesis_method=method), self.model,
+                                            channels=channels)
+                    except (SemanticError, SolverError) as error:
+                        self.ctx.emit("candidate_failed", method=method, error=str(error))
+                        continue
+                    self.store(bundle, "initial")
+        self.stage_times["initial_s"] = time.monotonic() - t0
+        self.checkpoint("initial_done")
+
+    def reevaluate(self, bundle):
+        """The same schedule predicted under the current model version."""
+        if bundle.prediction.model_version == self.model.version:
+            return bundle
+        from vericcl_b200.program.native import build_executable
+        executable = build_executable(bundle.program, bundle.storage, bundle.request, self.topology,
+                                      model_context(bundle.request))
+        new = replace(bundle, executable=executable, prediction=predict(executable, self.model, exact=True))
+        new.checks = dict(bundle.checks)
+        new.checks["prediction"] = {"status": "valid" if new.prediction.t_pred_us is not None else "invalid",
+                                    "detail": {"t_pred_us": new.prediction.t_pred_us}}
+        if hasattr(bundle, "candidate_id"):
+            new.candidate_id = bundle.candidate_id
+        return new
+
+    def baseline(self):
+        ready = [self.reevaluate(b) for b in self.candidates]
+        ready = [b for b in ready if b.can_execute]
+        if not ready:
+            return None
+        ready.sort(key=lambda b: b.t_pred_us)
+        self.adopt(ready[0], reason="baseline")
+        return ready[0]
+
+    def adopt(self, bundle, reason: str):
+        self.incumbent = bundle
+        if not hasattr(bundle, "candidate_id"):
+            self.store(bundle, "adopted")
+        d = self.ctx.process / "best"
+        atomic_write_json(d / "accepted.json", {"id": bundle.candidate_id, "t_pred_us": bundle.t_pred_us,
+                                                "reason": reason, "model_version": self.model.version})
+        self.ctx.emit("candidate_adopted", id=bundle.candidate_id, t_pred_us=bundle.t_pred_us, reason=reason)
+
+    def calibration(self):
+        from vericcl_b200.online.campaign import run_calibration
+        if self.probe_executor is None:
+            self.ctx.emit("calibration_skipped", reason="no probe executor (GPU runtime) available")
+            return False
+        t0 = time.monotonic()
+        try:
+            with self.budgets.acquire("online") as lease:
+                model, diff, report = run_calibration(self.request, self.topology, self.model, self.probe_executor,
+                                                      lease=lease, record_dir=self.ctx.process / "models")
+        except BudgetExhausted as error:
+            self.ctx.emit("calibration_stopped", reason=str(error))
+            return False
+        self.stage_times["calibration_s"] = time.monotonic() - t0
+        atomic_write_json(self.ctx.process / "reports" / "calibration.json", report)
+        if model.version == self.model.version:
+            return False
+        self.model = model
+        self.ctx.emit("model_published", version=model.version, components=len(diff))
+        if self.incumbent is not None:
+            self.incumbent = self.reevaluate(self.incumbent)
+        return True
+
+    def tuning(self):
+        from vericcl_b200.tuning.resynthesis import branches, resynthesize_branch
+        from vericcl_b200.tuning.strategies import solve_repair
+        from vericcl_b200.verification.bottlenecks import analyze
+        from vericcl_b200.verification.global_bound import certify_global_cut, check_global_cut
+        rounds = self.request.request_config["sketch"]["budgets"].get("max_tuning_rounds") or 0
+        batch = self.request.request_config["sketch"]["repair"]["analysis_batch_size"]
+        for index in range(rounds):
+            if self.incumbent is None:
+                return "no incumbent"
+            self.budgets.new_round()
+            record = {"round": index, "start_t_pred_us": self.incumbent.t_pred_us}
+            bound = certify_global_cut(self.request, self.topology, self.model)
+            if bound is not None:
+                record["cut_lower_bound_us"] = bound.lower_bound_us
+                if check_global_cut(bound, self.incumbent.t_pred_us):
+                    self.proof = {"kind": "directed_cut", "lower_bound_us": bound.lower_bound_us,
+                                  "subset": list(bound.subset), "exact": list(bound.exact)}
+                    record["result"] = "certified optimal"
+                    self.rounds.append(record)
+                    return "no-improvement proof"
+            try:
+                with self.budgets.acquire("repair") as lease:
+                    analysis = analyze(self.incumbent, self.model, batch_size=batch)
+                    record["causes"] = [c.kind for c in analysis.causes][:20]
+                    record["strategies"] = [s.as_json() for s in analysis.strategies]
+                    lower = Lowerer(self.incumbent.request, self.topology, self.model)
+                    outcome = solve_repair(self.incumbent, analysis.strategies, lower=lower, lease=lease)
+                    candidates = [outcome.best] if outcome.improved else []
+                    for branch in branches(self.incumbent.request, self.incumbent):
+                        lease.check()
+                        alt = resynthesize_branch(self.incumbent.request, branch, self.model, lease=lease)
+                        if alt is not None:
+                            self.store(alt, "resynth")
+                            candidates.append(alt)
+            except BudgetExhausted:
+                record["result"] = "repair budget exhausted"
+                self.rounds.append(record)
+                return "repair budget exhausted"
+            best = min((c for c in candidates if accept_candidate(self.incumbent, c)),
+                       key=lambda c: c.t_pred_us, default=None)
+            if best is not None and self.measure is not None:
+                verdict = self.measure(self.incumbent, best)
+                record["measured"] = verdict.__dict__ if hasattr(verdict, "__dict__") else verdict
+                if not getattr(verdict, "accepted", False):
+                    best = None
+            if best is None:
+                record["result"] = "no improvement"
+                self.rounds.append(record)
+                self.checkpoint("round_%d" % index)
+                continue
+            self.adopt(best, reason="round %d" % index)
+            record["result"] = "improved"
+            record["t_pred_us"] = best.t_pred_us
+            self.rounds.append(record)
+            self.checkpoint("round_%d" % index)
+        return "round limit"
+
+    def run(self) -> RunResult:
+        t0 = time.monotonic()
+        self.ctx.emit("workflow_started", purpose=self.purpose, tune=self.tune)
+        stop = "finished"
+        try:
+            if self.purpose == "calibrate":
+                changed = self.calibration()
+                stop = "calibrated" if changed else "calibration produced no qualified component"
+            else:
+                if self.purpose == "verify":
+                    from vericcl_b200.program.sidecar import bundle_from_sidecar
+                    bundle = bundle_from_sidecar(self.request, self.topology, self.verify_inputs["xml"],
+                                                 self.verify_inputs["sidecar"], self.model)
+                    self.store(bundle, "verify")
+                elif self.restored:
+                    self.restore_candidates()
+                else:
+                    self.initial_candidates()
+                self.baseline()
+                cal = self.request.request_config["sketch"]["calibration"]["enabled"]
+                if cal:
+                    self.calibration()
+                self.checkpoint("baseline")
+                if self.purpose == "solve" or self.tune:
+                    stop = self.tuning()
+                else:
+                    stop = "verified"
+        except BudgetExhausted as error:
+            stop = "budget: %s" % error
+        self.stage_times["total_s"] = time.monotonic() - t0
+        best = None
+        if self.incumbent is not None:
+            best = {"id": self.incumbent.candidate_id, "t_pred_us": self.incumbent.t_pred_us,
+                    "model_version": self.model.version, "origin": self.incumbent.origin,
+                    "checks": self.incumbent.checks,
+                    "slice_size_bytes": self.incumbent.request.hyperparameters.slice_size_bytes}
+        status = "ok" if (best is not None or self.purpose == "calibrate") else "no_candidate"
+        result = RunResult(status, stop, best, self.rounds, self.proof, self.stage_times)
+        publish_results(self.ctx, xml=self.incumbent.xml if self.incumbent else None,
+                        sidecar=to_sidecar(self.incumbent) if self.incumbent else None,
+                        model=self.model.as_json(), result=result.as_json(), best=best)
+        self.ctx.update_run_json(best=best, effective_request=dict(self.request.request_config),
+                                 value_sources=dict(self.request.value_sources),
+                                 size_accounting=dict(self.request.size_accounting), timing=self.stage_times)
+        self.checkpoint("finished")
+        finalize_run(self.ctx, result.as_json())
+        return result
+
+    def restore_candidates(self):
+        from vericcl_b200.program.sidecar import bundle_from_sidecar
+        from vericcl_b200.utils.jsonio import strict_load
+        ids = [c for c in self.restored["state"].get("candidates", []) if c]
+        for cid in ids:
+            d = self.ctx.process / "candidates" / cid
+            try:
+                bundle = bundle_from_sidecar(self.request, self.topology, (d / "schedule.xml").read_text(),
+                                             strict_load(d / "schedule.json"), self.model)
+            except (OSError, SemanticError):
+                continue
+            bundle.candidate_id = cid
+            self.candidates.append(bundle)
+        if not self.candidates:
+            self.initial_candidates()
