@@ -1,0 +1,96 @@
+import random
+
+import pytest
+
+from vericcl_b200.examples import example_documents
+from vericcl_b200.input.loader import resolve_documents
+from vericcl_b200.online import campaign
+from vericcl_b200.online.acceptance import compare_measured, one_sided_binomial, pair_order
+from vericcl_b200.online.clock_sync import align_bracketed_globaltimers, ordered
+from vericcl_b200.online.fitting import Sample, fit_curve, qualify
+from vericcl_b200.online.probe_jobs import build_probe_xml, plan_probes
+from vericcl_b200.online.statistical_ledger import StatisticalLedger
+from vericcl_b200.online.trace import TraceRecord, analyze_trace_causality, parse_trace, write_trace
+from vericcl_b200.performance.initial import initial_cost_model
+from vericcl_b200.program.device import compile_xml, run_cpu
+from vericcl_b200.topology import load_topology
+
+
+def request(**kw):
+    d = example_documents("allreduce", "hierarchy", 4, total_size_bytes=1 << 16, slice_size_bytes=1 << 14, **kw)
+    d["sketch"]["calibration"]["enabled"] = True
+    return resolve_documents(d)
+
+
+def test_probe_plan_and_xml_compile():
+    req = request()
+    jobs = plan_probes(req, load_topology(req))
+    assert jobs[0].group == "link_intra"
+    assert any(j.mode == "shared" for j in jobs)
+    assert all(len(j.payload_sizes) >= 3 for j in jobs)
+    for job in jobs[:6] + [j for j in jobs if j.mode == "shared"][:2]:
+        c = compile_xml(build_probe_xml(job, 4))
+        import numpy as np
+        outs = run_cpu(c, [np.ones(len(job.flows) * 8, np.float32)] * 4)
+        assert all(np.isfinite(o).all() for o in outs)
+
+
+def test_fit_curve_recovers_alpha_beta():
+    samples = [Sample("link:0:1", b, 2.0 + b / 1000.0, "native_interpreter", l) for b in (1000, 4000, 16000)
+               for l in range(3)]
+    good, reasons = qualify(samples, max_cv=0.05)
+    seg = fit_curve(good, max_relative_error=0.01)
+    assert seg[0].alpha_us == pytest.approx(2.0, rel=1e-6)
+    assert seg[0].beta_us_per_byte == pytest.approx(1e-3, rel=1e-6)
+
+
+def test_simulated_samples_never_qualify():
+    req = request()
+    model, diff, report = campaign.run_calibration(req, load_topology(req), initial_cost_model(req),
+                                                   campaign.simulated_executor(load_topology(req)))
+    assert model.version.startswith("initial") and not diff
+
+
+def test_campaign_publishes_measured_model(monkeypatch):
+    req = request()
+    topo = load_topology(req)
+    executor = campaign.simulated_executor(topo, source="native_interpreter", noise=0.001)
+    model, diff, report = campaign.run_calibration(req, topo, initial_cost_model(req), executor)
+    assert model.version.startswith("measured-")
+    assert model.service_for("link:0:1", 1 << 14).source == "measured"
+    assert model.profiles, "shared modes must produce measured rate profiles"
+
+
+def test_paired_acceptance_and_ledger(tmp_path):
+    assert one_sided_binomial(10, 10) == pytest.approx(1 / 1024)
+    assert sorted(pair_order(4, 1)).count("AB") == 2
+    rng = random.Random(0)
+    verdict = compare_measured(lambda label: (100.0 if label == "A" else 90.0) * (1 + rng.uniform(-.001, .001)),
+                               pairs=20, seed=3, alpha=0.01, max_cv=0.05, max_rounds=3, min_relative_gain=0.05)
+    assert verdict.accepted and verdict.median_gain == pytest.approx(0.1, abs=0.01)
+    sim = compare_measured(lambda label: 1.0, pairs=4, seed=1, alpha=0.05, max_cv=0.05, max_rounds=1,
+                           min_relative_gain=0.0, source="test_simulation")
+    assert not sim.accepted
+    ledger = StatisticalLedger(tmp_path / "ledger.jsonl", task_alpha=0.05)
+    a1, a2 = ledger.allocate("x"), ledger.allocate("y")
+    assert a1 == pytest.approx(0.025) and a2 == pytest.approx(0.0125)
+    assert ledger.spent() <= 0.05 and ledger.verify()
+    (tmp_path / "ledger.jsonl").write_text((tmp_path / "ledger.jsonl").read_text().replace("0.0125", "0.02"))
+    assert not ledger.verify()
+
+
+def test_clock_alignment_and_trace(tmp_path):
+    maps = align_bracketed_globaltimers({0: [(1000 + i * 100, 500 + i * 100, 1010 + i * 100) for i in range(8)],
+                                         1: [(1000 + i * 100, 9000 + i * 100, 1004 + i * 100) for i in range(8)]})
+    assert maps[0].to_host(500) == pytest.approx(1005, abs=6)
+    assert maps[1].to_host(9000) == pytest.approx(1002, abs=3)
+    assert ordered((0, 1), (2, 3)) == "before" and ordered((0, 5), (2, 3)) == "uncertain"
+    recs = [TraceRecord(0, 0, 0, 0, 0, s, 1, 500 + s * 10, 505 + s * 10, 2) for s in range(4)]
+    write_trace(tmp_path / "t.bin", 0, 1, 4, recs)
+    parsed = parse_trace((tmp_path / "t.bin").read_bytes())
+    assert parsed["complete"] and parsed["records"] == recs
+    partial = parse_trace((tmp_path / "t.bin").read_bytes()[:-10])
+    assert not partial["complete"] and len(partial["records"]) == 3
+    report = analyze_trace_causality({0: recs, 1: [r.__class__(1, *list(r.__dict__.values())[1:]) for r in recs]},
+                                     maps)
+    assert report["global_span_us"] > 0 and report["tails"]

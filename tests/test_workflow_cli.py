@@ -1,0 +1,71 @@
+import json
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+from vericcl_b200.cli.main import main
+from vericcl_b200.examples import example_documents, write_documents
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _args(indir, project, case, run_id):
+    return ["--project-root", str(project), "--case", case, "--run-id", run_id,
+            "--topology", str(indir / "topology.json"), "--sketch", str(indir / "sketch.json"),
+            "--atom", str(indir / "atom.json"), "--runtime", str(indir / "runtime.json")]
+
+
+@pytest.fixture
+def inputs(tmp_path):
+    d = example_documents("allgather", "hierarchy", 4, total_size_bytes=1 << 16, slice_size_bytes=1 << 14,
+                          tuning_rounds=2, alpha_us=2.0, link_gbps=150.0)
+    write_documents(tmp_path / "in", d)
+    return tmp_path / "in"
+
+
+def test_solve_publishes_and_verify_roundtrip(inputs, tmp_path, capsys):
+    assert main(["solve"] + _args(inputs, tmp_path, "c", "s1")) == 0
+    run = tmp_path / "examples" / "c" / "output" / "s1"
+    for name in ("run.json", "report.md", "schedule.xml", "schedule.json", "model.json", "details.zip",
+                 "checkpoint.json", "process/events.jsonl"):
+        assert (run / name).exists(), name
+    meta = json.loads((run / "run.json").read_text())
+    assert meta["status"] == "finished" and meta["best"]["t_pred_us"] > 0
+    assert meta["value_sources"]["sketch.collective.operator"]["kind"] == "input"
+    rc = main(["verify"] + _args(inputs, tmp_path, "c", "v1") + ["--xml", str(run / "schedule.xml"), "--sidecar",
+                                                                 str(run / "schedule.json"), "--model",
+                                                                 str(run / "model.json")])
+    assert rc == 0
+    vmeta = json.loads((tmp_path / "examples" / "c" / "output" / "v1" / "run.json").read_text())
+    assert vmeta["best"]["t_pred_us"] == pytest.approx(meta["best"]["t_pred_us"])
+    assert main(["inspect", "--run", str(run)]) == 0
+
+
+def test_invalid_input_exit_code(inputs, tmp_path):
+    rc = main(["solve"] + _args(inputs, tmp_path, "c", "bad") + ["--set", "sketch.collective.datatype=\"int8\""])
+    assert rc == 2
+
+
+def test_resume_after_interruption(inputs, tmp_path):
+    from vericcl_b200.execution.context import RunContext
+    from vericcl_b200.input.loader import load_request
+    from vericcl_b200.workflow import PrimaryWorkflow
+    files = {k: inputs / (k + ".json") for k in ("topology", "sketch", "atom", "runtime")}
+    req = load_request(files)
+    ctx = RunContext.create(tmp_path, "c", "solve", run_id="r", input_files=files)
+    ctx.update_run_json(effective_request=dict(req.request_config))
+    wf = PrimaryWorkflow(req, ctx)
+    wf.initial_candidates()         # interrupted after the initial stage's checkpoint
+    assert main(["resume", "--run", str(ctx.directory)]) == 0
+    meta = json.loads((ctx.directory / "run.json").read_text())
+    assert meta["status"] == "finished" and meta["best"] is not None
+
+
+def test_module_entry_point(inputs, tmp_path):
+    env = dict(os.environ, PYTHONPATH=str(ROOT))
+    proc = subprocess.run([sys.executable, "-m", "vericcl_b200", "--version"], capture_output=True, text=True,
+                          env=env, timeout=120)
+    assert proc.returncode == 0 and "vericcl_b200" in proc.stdout

@@ -82,11 +82,27 @@ class BDD:
         return rec(u, 0)
 
     def best_assignment(self, u: int, weights=None):
-        """Satisfying assignment maximising the summed weight of true variables."""
+        """Satisfying assignment maximising the summed weight of true variables.
+
+        Variables that a path skips are unconstrained there and are set true
+        exactly when their weight is positive.
+        """
         weights = weights or {name: 1.0 for name in self.vars}
+        nvars = len(self.vars)
         memo = {}
 
+        def free(lo, hi):
+            assign = {}
+            score = 0.0
+            for level in range(lo, hi):
+                name = self.vars[level]
+                take = weights.get(name, 0.0) > 0
+                assign[name] = take
+                score += weights.get(name, 0.0) if take else 0.0
+            return score, assign
+
         def rec(x):
+            # best over variables from this node's level to the end
             if x == self.FALSE:
                 return None
             if x == self.TRUE:
@@ -99,9 +115,11 @@ class BDD:
                 sub = rec(child)
                 if sub is None:
                     continue
-                score = sub[0] + (weights.get(self.vars[v], 0.0) if value else 0.0)
+                gap_score, gap = free(v + 1, self._var_of(child) if child > 1 else nvars)
+                score = sub[0] + gap_score + (weights.get(self.vars[v], 0.0) if value else 0.0)
                 if best is None or score > best[0]:
                     assign = dict(sub[1])
+                    assign.update(gap)
                     assign[self.vars[v]] = value
                     best = (score, assign)
             memo[x] = best
@@ -110,8 +128,11 @@ class BDD:
         res = rec(u)
         if res is None:
             return None
-        return {name: res[1].get(name, weights.get(name, 0) > 0 and False) for name in self.vars} | \
-            {k: v for k, v in res[1].items()}
+        top = self._var_of(u) if u > 1 else nvars
+        lead_score, lead = free(0, top)
+        assign = dict(res[1])
+        assign.update(lead)
+        return assign
 
 
 def select_compatible(strategies, conflicts, weights=None):
