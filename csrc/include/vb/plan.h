@@ -56,6 +56,7 @@ struct RankProgram {
   std::vector<DevSrc> srcs;
   std::vector<DevWait> waits;
   int i_chunks = 0, o_chunks = 0, s_chunks = 0;
+  int s_used = 0;   // scratch chunks the device steps actually touch (fusion can drop them all)
 };
 
 struct CompileStats {
@@ -73,6 +74,12 @@ struct CompiledPlan {
     size_t m = 0;
     for (auto& r : ranks) m = r.blocks.size() > m ? r.blocks.size() : m;
     return (int)m;
+  }
+  // Scratch chunks per rank that every rank must reserve (symmetric layout).
+  int max_scratch_used() const {
+    int m = 0;
+    for (auto& r : ranks) m = r.s_used > m ? r.s_used : m;
+    return m;
   }
 };
 

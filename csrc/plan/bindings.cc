@@ -69,6 +69,7 @@ PYBIND11_MODULE(_vbplan, m) {
         const RankProgram& rp = p.ranks.at(r);
         return py::make_tuple(rp.i_chunks, rp.o_chunks, rp.s_chunks);
       })
+      .def_property_readonly("scratch_used", &CompiledPlan::max_scratch_used)
       .def("describe", [](const CompiledPlan& p, int r) { return describe_rank(p, r); })
       .def("tables", [](const CompiledPlan& p, int r) {
         const RankProgram& rp = p.ranks.at(r);

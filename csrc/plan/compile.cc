@@ -785,6 +785,22 @@ class Compiler {
         rp.blocks.push_back(blk);
       }
     }
+    // scratch actually referenced by device steps
+    for (int r = 0; r < P_; ++r) out_[r].s_used = 0;
+    for (int r = 0; r < P_; ++r) {
+      RankProgram& rp = out_[r];
+      for (auto& st : rp.steps) {
+        if (st.op == OP_NOP) continue;
+        if (st.dst_buf == BUF_SCR) rp.s_used = std::max(rp.s_used, st.dst_chunk + st.cnt);
+        for (int i = 0; i < st.nsrc; ++i) {
+          const DevSrc& sr = rp.srcs[st.src_begin + i];
+          if (sr.buf == BUF_SCR) {
+            // a remote source lives in the source rank's scratch
+            out_[sr.rank].s_used = std::max(out_[sr.rank].s_used, sr.chunk + st.cnt);
+          }
+        }
+      }
+    }
     // publication flags
     for (auto& e : published_) {
       int rank, block, event;

@@ -168,7 +168,7 @@ class DevicePlan {
     };
     need(in_off, rp.i_chunks, a.batch_stride[BUF_IN], "input");
     need(out_off, rp.o_chunks, a.batch_stride[BUF_OUT], "output");
-    need(scr_off, rp.s_chunks, a.batch_stride[BUF_SCR], "scratch");
+    need(scr_off, plan_.max_scratch_used(), a.batch_stride[BUF_SCR], "scratch");
     a.flag_off = (long long)h.flag_offset();
     a.start_slot = h.start_slot();
     for (int r = 0; r < h.nranks(); ++r) a.base[r] = h.base(r);
@@ -187,7 +187,8 @@ class DevicePlan {
   int niters() const { return plan_.options.niters; }
   py::tuple slots() const {
     const RankProgram& rp = plan_.ranks[rank_];
-    return py::make_tuple(rp.i_chunks, rp.o_chunks, rp.s_chunks);
+    // scratch: chunks every rank reserves (symmetric), only those device steps use
+    return py::make_tuple(rp.i_chunks, rp.o_chunks, plan_.max_scratch_used());
   }
   std::string describe() const { return describe_rank(plan_, rank_); }
   py::dict stats() const {
