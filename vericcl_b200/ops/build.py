@@ -162,9 +162,45 @@ def build_capi(force: bool = False) -> Path:
     stamp = _digest(sources, flags)
     if not force and _fresh(target, stamp):
         return target
-    cmd = [str(CUDA_HOME / "bin" / "nvcc"), *flags, *map(str, sources), "-o", str(target) + ".tmp", "-lcuda",
-           "-lpthread"]
+    stubs = CUDA_HOME / "lib64" / "stubs"
+    cmd = [str(CUDA_HOME / "bin" / "nvcc"), *flags, *map(str, sources), "-o", str(target) + ".tmp"]
+    if stubs.exists():
+        cmd += ["-L", str(stubs)]
+    cmd += ["-lcuda", "-lpthread"]
     _run(cmd, "nvcc build of libvericcl_b200")
+    os.replace(str(target) + ".tmp", target)
+    _mark(target, stamp)
+    return target
+
+
+def build_driver(force: bool = False) -> Path:
+    """``vericcl-native``: one rank of a schedule through the C API, with a JSON receipt."""
+    lib = build_capi(force)
+    target = OUT / "vericcl-native"
+    sources = [CSRC / "runtime" / "driver.cc"]
+    flags = ["-O2", "-std=c++17", "-I", str(CSRC / "include"), "-I", str(CUDA_HOME / "include")]
+    stamp = _digest(sources + [lib], flags)
+    if not force and _fresh(target, stamp):
+        return target
+    cmd = ["g++", *flags, str(sources[0]), "-o", str(target) + ".tmp", "-L", str(OUT), "-lvericcl_b200",
+           "-Wl,-rpath,$ORIGIN", "-L", str(CUDA_HOME / "lib64"), "-Wl,-rpath," + str(CUDA_HOME / "lib64"), "-lcudart",
+           "-L", str(CUDA_HOME / "lib64" / "stubs"), "-lcuda"]
+    _run(cmd, "driver build")
+    os.replace(str(target) + ".tmp", target)
+    _mark(target, stamp)
+    return target
+
+
+def build_native_tests(force: bool = False) -> Path:
+    """CPU-only tests of the contract utilities and the control plane (g++, no CUDA)."""
+    OUT.mkdir(parents=True, exist_ok=True)
+    target = OUT / "native_cpu_tests"
+    sources = [CSRC / s for s in RUNTIME_SOURCES] + [ROOT / "tests" / "native" / "test_control_and_contract.cc"]
+    flags = ["-O1", "-std=c++17", "-pthread", "-I", str(CSRC / "include")]
+    stamp = _digest(sources, flags)
+    if not force and _fresh(target, stamp):
+        return target
+    _run(["g++", *flags, *map(str, sources), "-o", str(target) + ".tmp"], "native test build")
     os.replace(str(target) + ".tmp", target)
     _mark(target, stamp)
     return target
@@ -173,10 +209,9 @@ def build_capi(force: bool = False) -> Path:
 def build_all(force: bool = False) -> dict:
     out = {"plan": str(build_plan_module(force))}
     out["cuda"] = str(build_cuda_module(force))
-    try:
-        out["capi"] = str(build_capi(force))
-    except FileNotFoundError:
-        pass
+    out["capi"] = str(build_capi(force))
+    out["driver"] = str(build_driver(force))
+    out["native_tests"] = str(build_native_tests(force))
     return out
 
 
