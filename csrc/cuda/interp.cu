@@ -223,7 +223,7 @@ __device__ void move_generic(char* dst, const char* const* src, int nsrc, long l
 template <int DT>
 __device__ void mc_allreduce_piece(char* mc_dst, const char* mc_src, long long nvec, bool do_scale, float scale) {
   using V = VecT<DT>;
-  constexpr int U = 4;
+  constexpr int U = 8;
   const long long stride = (long long)blockDim.x * U;
   for (long long v0 = threadIdx.x; v0 < nvec; v0 += stride) {
     uint4 r[U];
@@ -289,6 +289,8 @@ __device__ bool wait_events(const InterpArgs& a, const DevWait* w, int n, int it
     unsigned long long target;
     const unsigned long long* f;
     if (dw.block < 0) {
+      // a peer's start flag holds for the whole launch: checking it in the first iteration suffices
+      if (it > 0) continue;
       target = base + 1;
       f = flag_ptr(a, dw.rank, a.start_slot);
     } else {

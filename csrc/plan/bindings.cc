@@ -21,6 +21,7 @@ py::dict stats_dict(const CompileStats& s) {
   d["waits"] = s.waits;
   d["remote_waits"] = s.remote_waits;
   d["scale_steps"] = s.scale_steps;
+  d["deferred_waits"] = s.deferred_waits;
   return d;
 }
 

@@ -447,6 +447,8 @@ class Compiler {
     EventSet waits;
     int prio = 0;
     int xml_tb = -1;
+    bool mc_peer = false;      // a copy replaced by the owner's multicast store
+    int mc_buf = -1, mc_chunk = -1;
   };
 
   void build_waits_and_hazards() {
@@ -726,8 +728,41 @@ class Compiler {
           PendingStep& c = pending_[pj.first][0][pj.second];
           c.st.op = OP_NOP;
           c.srcs.clear();
+          c.mc_peer = true;
+          c.mc_buf = ps.st.dst_buf;
+          c.mc_chunk = ps.st.dst_chunk;
         }
         stats_.multicast_ops++;
+      }
+    }
+    defer_multicast_arrivals();
+  }
+
+  // A rank learns that an owner's multicast store reached its memory by waiting
+  // for the owner's completion.  When nothing later on this rank reads that
+  // destination, the wait is only needed before the kernel returns: it moves to
+  // the end-of-kernel waits (last pipeline iteration), so the ranks no longer
+  // meet at every chunk and stream through all iterations independently.
+  void defer_multicast_arrivals() {
+    for (int r = 0; r < P_; ++r) {
+      auto& steps = pending_[r][0];
+      for (int i = 0; i < (int)steps.size(); ++i) {
+        PendingStep& ps = steps[i];
+        if (!ps.mc_peer || ps.waits.empty()) continue;
+        bool read_later = false;
+        for (int j = i + 1; j < (int)steps.size() && !read_later; ++j)
+          for (auto& sr : steps[j].srcs)
+            if (sr.rank == r && sr.buf == ps.mc_buf && sr.chunk == ps.mc_chunk) read_later = true;
+        for (int q = 0; q < P_ && !read_later; ++q)
+          if (q != r)
+            for (auto& other : pending_[q][0])
+              for (auto& sr : other.srcs)
+                if (sr.rank == r && sr.buf == ps.mc_buf && sr.chunk == ps.mc_chunk) read_later = true;
+        if (read_later) continue;
+        for (auto& kv : ps.waits)
+          if (kv.first.second >= 0) merge(end_waits_[r], EventSet{{kv.first, kv.second}});
+        ps.waits.clear();
+        stats_.deferred_waits++;
       }
     }
   }

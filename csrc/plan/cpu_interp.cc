@@ -129,7 +129,7 @@ InterpResult cpu_interpret(const CompiledPlan& plan, HostBuffers& bufs, int dtyp
           for (int w = 0; w < count; ++w) {
             const DevWait& dw = rp.waits[begin + w];
             if (dw.block < 0) {
-              if (flags[dw.rank][start_slot] < base + 1) return false;
+              if (it == 0 && flags[dw.rank][start_slot] < base + 1) return false;
               continue;
             }
             int wit = dw.iter_delta < 0 ? I - 1 : it;

@@ -199,6 +199,8 @@ class DevicePlan {
     d["waits"] = plan_.stats.waits;
     d["remote_waits"] = plan_.stats.remote_waits;
     d["fused"] = plan_.options.fuse_chains;
+    d["multicast_ops"] = plan_.stats.multicast_ops;
+    d["deferred_waits"] = plan_.stats.deferred_waits;
     return d;
   }
 
