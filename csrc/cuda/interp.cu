@@ -332,6 +332,8 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
     const PieceRange pr = piece_range(a.chunk_elems, a.piece_elems, it - batch * a.niters, a.nlanes, lane);
     for (int s = 0; s < blk.nsteps; ++s) {
       const DevStep st = a.steps[blk.step_begin + s];
+      unsigned long long t_reach = 0, t_ready = 0;
+      if (a.trace_buf && threadIdx.x == 0) t_reach = globaltimer();
       if (st.wait_count) {
         if (threadIdx.x < 32) {
           bool ok = wait_events(a, a.waits + st.wait_begin, st.wait_count, it, base, block, lane);
@@ -340,6 +342,7 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
         __syncthreads();
         if (*s_stop) return;
       }
+      if (a.trace_buf && threadIdx.x == 0) t_ready = globaltimer();
       const unsigned long long ev = base + (unsigned long long)it * stride + 2ull * s;
       if ((st.flags & F_PUB_ARRIVE) && threadIdx.x == 0) st_release_sys(my_flag, ev + 1);
       if (st.op == OP_MC_ALLREDUCE && pr.hi > pr.lo) {
@@ -372,6 +375,14 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
       if (st.flags & F_PUB_DONE) {
         __syncthreads();
         if (threadIdx.x == 0) st_release_sys(my_flag, ev + 2);
+      }
+      if (a.trace_buf && threadIdx.x == 0) {
+        const long long slot = ((long long)blockIdx.x * a.trace_stride + (long long)it * blk.nsteps + s) * 3;
+        if ((long long)it * blk.nsteps + s < a.trace_stride) {
+          a.trace_buf[slot] = t_ready;
+          a.trace_buf[slot + 1] = globaltimer();
+          a.trace_buf[slot + 2] = t_ready - t_reach;
+        }
       }
     }
   }

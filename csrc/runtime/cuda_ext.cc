@@ -133,7 +133,7 @@ class DevicePlan {
 
   void run(Heap& heap, size_t in_off, size_t out_off, size_t scr_off, int64_t count_per_rank, int dtype, int redop,
            float scale, uint64_t stream, double timeout_s, int threads, int nbatch,
-           std::vector<long long> batch_stride) {
+           std::vector<long long> batch_stride, uint64_t trace_ptr, int64_t trace_stride) {
     SymHeap& h = heap.get();
     if (h.nranks() != (int)plan_.ranks.size()) throw std::runtime_error("heap and plan rank counts differ");
     py::tuple g = geometry(count_per_rank, dtype);
@@ -175,6 +175,8 @@ class DevicePlan {
     a.mc_base = h.mc_base();
     a.control = heap.control();
     a.timeout_ns = (unsigned long long)(timeout_s * 1e9);
+    a.trace_buf = reinterpret_cast<unsigned long long*>(trace_ptr);
+    a.trace_stride = (int)trace_stride;
     int max_ctas = interp_max_ctas(threads);
     if (a.nblocks * a.nlanes > max_ctas)
       throw std::runtime_error("plan needs " + std::to_string(a.nblocks * a.nlanes) + " co-resident CTAs; the device holds " +
@@ -191,6 +193,18 @@ class DevicePlan {
     return py::make_tuple(rp.i_chunks, rp.o_chunks, plan_.max_scratch_used());
   }
   std::string describe() const { return describe_rank(plan_, rank_); }
+  int max_steps() const {
+    int m = 0;
+    for (auto& b : plan_.ranks[rank_].blocks) m = b.nsteps > m ? b.nsteps : m;
+    return m;
+  }
+  std::vector<int> step_ops() const {
+    std::vector<int> out;
+    const RankProgram& rp = plan_.ranks[rank_];
+    if (!rp.blocks.empty())
+      for (int s = 0; s < rp.blocks[0].nsteps; ++s) out.push_back(rp.steps[rp.blocks[0].step_begin + s].op);
+    return out;
+  }
   py::dict stats() const {
     py::dict d;
     d["device_steps"] = plan_.stats.device_steps;
@@ -238,11 +252,14 @@ PYBIND11_MODULE(_vbcuda, m) {
       .def("run", &DevicePlan::run, py::arg("heap"), py::arg("in_off"), py::arg("out_off"), py::arg("scr_off"),
            py::arg("count_per_rank"), py::arg("dtype"), py::arg("redop"), py::arg("scale"), py::arg("stream"),
            py::arg("timeout_s") = 10.0, py::arg("threads") = 512, py::arg("nbatch") = 1,
-           py::arg("batch_stride") = std::vector<long long>{0, 0, 0})
+           py::arg("batch_stride") = std::vector<long long>{0, 0, 0}, py::arg("trace_ptr") = 0,
+           py::arg("trace_stride") = 0)
       .def("geometry", &DevicePlan::geometry)
       .def("slots", &DevicePlan::slots)
       .def("describe", &DevicePlan::describe)
       .def("stats", &DevicePlan::stats)
+      .def("max_steps", &DevicePlan::max_steps)
+      .def("step_ops", &DevicePlan::step_ops)
       .def_property_readonly("nblocks", &DevicePlan::nblocks)
       .def_property_readonly("nlanes", &DevicePlan::nlanes)
       .def_property_readonly("niters", &DevicePlan::niters);

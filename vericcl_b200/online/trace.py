@@ -110,3 +110,30 @@ def analyze_trace_causality(traces, clock_maps, *, tails: int = 5):
             "dominant_waits": [{"wait_us": w / 1e3, "rank": r, "step": s, "iteration": it, "lane": l}
                                for w, r, s, it, l in waits[:tails]],
             "overlapping_ranks": uncertain}
+
+
+def capture_once(comm, plan, inp, out, *, warmup: int = 3, op: str = "sum", scale=None, count_per_rank=None):
+    """Warm up, bracket one traced invocation with clock samples, return this rank's records + clock map.
+
+    Every rank calls this collectively.  The returned dict holds the rank's
+    decoded records and its fitted :class:`ClockMap`; gather them (for example
+    with ``comm.all_gather_object``) and pass them to
+    :func:`analyze_trace_causality`.
+    """
+    import torch
+    from vericcl_b200.online.clock_sync import fit_transform
+    for _ in range(warmup):
+        comm.run(plan, inp, out, op=op, scale=scale, count_per_rank=count_per_rank)
+    torch.cuda.synchronize()
+    before = comm.clock_samples()
+    buf = comm.trace_buffer(plan)
+    comm.barrier()
+    comm.run(plan, inp, out, op=op, scale=scale, count_per_rank=count_per_rank, trace=buf)
+    torch.cuda.synchronize()
+    comm.check_status()
+    after = comm.clock_samples()
+    raw = buf.cpu().tolist()
+    records = records_from_buffer(comm.rank, raw, nblocks=plan.device_plan.nblocks, nlanes=plan.nlanes,
+                                  steps_per_iter=plan.device_plan.max_steps(), niters=plan.niters,
+                                  ops=plan.device_plan.step_ops())
+    return {"rank": comm.rank, "records": records, "clock": fit_transform(before + after)}

@@ -188,7 +188,7 @@ class Communicator:
 
     def run(self, plan: PlanHandle, inp: torch.Tensor, out: torch.Tensor, *, op: str = "sum",
             scale: float | None = None, stream=None, count_per_rank: int | None = None, nbatch: int = 1,
-            in_stride: int = 0, out_stride: int = 0) -> None:
+            in_stride: int = 0, out_stride: int = 0, trace: torch.Tensor | None = None) -> None:
         """Launch ``plan`` on heap tensors ``inp`` → ``out`` on ``stream`` (asynchronous).
 
         With ``nbatch > 1`` one launch runs the plan ``nbatch`` times back to back on
@@ -217,8 +217,35 @@ class Communicator:
         if scale is not None:
             factor *= scale
         stream = torch.cuda.current_stream() if stream is None else stream
+        trace_ptr, trace_stride = 0, 0
+        if trace is not None:
+            trace_stride = plan.niters * nbatch * plan.device_plan.max_steps()
+            need = plan.device_plan.nblocks * plan.nlanes * trace_stride * 3
+            if trace.dtype != torch.int64 or trace.numel() < need or not trace.is_cuda:
+                raise RuntimeFailure("trace buffer needs %d int64 elements on the device" % need)
+            trace.zero_()
+            trace_ptr = trace.data_ptr()
         plan.device_plan.run(self.heap, in_off, out_off, scr_off, count, DTYPE_CODES[inp.dtype], REDOPS[op],
-                             float(factor), stream.cuda_stream, self.timeout_s, 512, nbatch, strides)
+                             float(factor), stream.cuda_stream, self.timeout_s, 512, nbatch, strides, trace_ptr,
+                             trace_stride)
+
+    def trace_buffer(self, plan: PlanHandle, nbatch: int = 1) -> torch.Tensor:
+        n = plan.device_plan.nblocks * plan.nlanes * plan.niters * nbatch * plan.device_plan.max_steps() * 3
+        return torch.zeros(n, dtype=torch.int64, device="cuda")
+
+    def clock_samples(self, count: int = 16):
+        """(host_before_ns, gpu_globaltimer_ns, host_after_ns) bracketing samples of this rank's GPU."""
+        import time as _time
+        buf = torch.zeros(1, dtype=torch.int64, device="cuda")
+        out = []
+        for _ in range(count):
+            torch.cuda.synchronize()
+            t0 = _time.time_ns()
+            self._mod.read_timer(buf)
+            torch.cuda.synchronize()
+            t1 = _time.time_ns()
+            out.append((t0, int(buf.item()), t1))
+        return out
 
     def status(self) -> dict:
         return self.heap.status()
