@@ -88,6 +88,8 @@ def synthesize(request, model=None, *, channels: int = 1) -> CandidateBundle:
     demands = build_demands(plan, topology)
     trees = choose_trees(demands, topology, slice_bytes, time_limit=request.solver.per_model_timeout_s)
     network = compose_routes(plan, demands, trees, topology, slice_bytes, channels=channels, origin=plan.mode.value)
+    from vericcl_b200.solver.timing import optimize_fixed_routes
+    network = optimize_fixed_routes(network, topology, time_limit=min(20.0, request.solver.per_model_timeout_s))
     return lower_candidate(request, topology, network, model, plan=plan, origin=plan.mode.value)
 
 

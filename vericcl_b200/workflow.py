@@ -125,8 +125,42 @@ class PrimaryWorkflow:
         save_checkpoint(self.ctx, phase=phase, state=state, files=files, budgets=self.budgets.snapshot())
 
     # -- stages -------------------------------------------------------------------
+    def history_candidates(self):
+        """Isomorphic schedules from earlier runs, revalidated under the current request and model."""
+        hist = self.request.request_config["sketch"]["history"]
+        if not hist["schedule_reuse"]:
+            return
+        from pathlib import Path
+        from vericcl_b200.solver.history import find_schedules
+        index = Path(hist["schedule_index"])
+        if not index.is_absolute():
+            index = self.ctx.project_root / "examples" / self.ctx.case / index
+        for entry in find_schedules(index, self.request, self.topology, tolerance=hist["relative_bandwidth_tolerance"],
+                                    limit=hist["max_schedule_candidates"]):
+            self.ctx.emit("history_candidate", t_pred_us=entry["t_pred_us"])
+            # a reused XML has no sidecar: it is checked by the compiler and the chunk simulator
+            from vericcl_b200.program.device import compile_xml
+            try:
+                compile_xml(entry["xml"])
+            except SemanticError:
+                continue
+            atomic_write_text(self.ctx.process / "candidates" / ("history-%03d.xml" % len(self.candidates)),
+                              entry["xml"])
+
+    def save_history(self):
+        hist = self.request.request_config["sketch"]["history"]
+        if not hist["schedule_reuse"] or self.incumbent is None:
+            return
+        from pathlib import Path
+        from vericcl_b200.solver.history import save_schedule
+        index = Path(hist["schedule_index"])
+        if not index.is_absolute():
+            index = self.ctx.project_root / "examples" / self.ctx.case / index
+        save_schedule(index, self.incumbent.request, self.topology, self.incumbent.xml, self.incumbent.t_pred_us)
+
     def initial_candidates(self):
         t0 = time.monotonic()
+        self.history_candidates()
         with self.budgets.acquire("initial") as lease:
             if self.request.hyperparameters.slice_size_bytes is not None:
                 choices = [None]
@@ -294,6 +328,7 @@ class PrimaryWorkflow:
         except BudgetExhausted as error:
             stop = "budget: %s" % error
         self.stage_times["total_s"] = time.monotonic() - t0
+        self.save_history()
         best = None
         if self.incumbent is not None:
             best = {"id": self.incumbent.candidate_id, "t_pred_us": self.incumbent.t_pred_us,
