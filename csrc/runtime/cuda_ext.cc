@@ -264,6 +264,38 @@ PYBIND11_MODULE(_vbcuda, m) {
       .def_property_readonly("nlanes", &DevicePlan::nlanes)
       .def_property_readonly("niters", &DevicePlan::niters);
   m.def("max_ctas", [](int threads) { return interp_max_ctas(threads); }, py::arg("threads") = 512);
+  // Launches a one-step program whose only wait targets an event this CTA would publish later:
+  // nothing ever sets it, so the bounded wait must expire and report ST_TIMEOUT.  Every address is
+  // local and valid; used by the failure-detection test.
+  m.def("wait_probe", [](Heap& heap, double timeout_s) {
+    SymHeap& h = heap.get();
+    std::vector<DevBlock> blocks(1);
+    blocks[0] = DevBlock{0, 1, -1, 0, 0};
+    std::vector<DevStep> steps(1);
+    steps[0] = DevStep{};
+    steps[0].op = OP_NOP;
+    steps[0].cnt = 1;
+    steps[0].wait_begin = 0;
+    steps[0].wait_count = 1;
+    std::vector<DevWait> waits(1);
+    waits[0] = DevWait{(int16_t)h.rank(), 0, 2, 2, 0};   // this block's own completion event: never ahead of itself
+    DevBlock* b = upload(blocks);
+    DevStep* st = upload(steps);
+    DevWait* w = upload(waits);
+    InterpArgs a = {};
+    a.blocks = b; a.steps = st; a.waits = w; a.srcs = nullptr;
+    a.nblocks = 1; a.nlanes = 1; a.niters = 1; a.nbatch = 1; a.rank = h.rank(); a.nranks = h.nranks();
+    a.dtype = DT_F32; a.redop = RED_SUM; a.scale = 1.f; a.chunk_elems = 4; a.piece_elems = 4;
+    a.flag_off = (long long)h.flag_offset();
+    a.start_slot = h.start_slot();
+    for (int r = 0; r < h.nranks(); ++r) a.base[r] = h.base(r);
+    a.control = heap.control();
+    a.timeout_ns = (unsigned long long)(timeout_s * 1e9);
+    cuda_check(launch_interp(a, at::cuda::getCurrentCUDAStream().stream(), 64), "wait probe");
+    cuda_check(cudaStreamSynchronize(at::cuda::getCurrentCUDAStream().stream()), "wait probe sync");
+    cudaFree(b); cudaFree(st); cudaFree(w);
+    return heap.status();
+  });
   m.def("fill", [](torch::Tensor t, int pattern, int rank, uint64_t seed) {
     cuda_check(launch_fill(t.data_ptr(), t.numel(), dtype_code(t.scalar_type()), pattern, rank, seed,
                            at::cuda::getCurrentCUDAStream().stream()), "fill");
