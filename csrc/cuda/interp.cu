@@ -250,6 +250,26 @@ __device__ void mc_allreduce_piece(char* mc_dst, const char* mc_src, long long n
   asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
 
+// dst(all ranks) = src(local), through the multicast address of the destination.
+__device__ void mc_store_piece(char* mc_dst, const char* src, long long nvec) {
+  constexpr int U = 8;
+  const long long stride = (long long)blockDim.x * U;
+  for (long long v0 = threadIdx.x; v0 < nvec; v0 += stride) {
+    uint4 r[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      long long v = v0 + (long long)u * blockDim.x;
+      if (v < nvec) r[u] = ld_vec(src + v * 16);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      long long v = v0 + (long long)u * blockDim.x;
+      if (v < nvec) mc_st(mc_dst + v * 16, r[u]);
+    }
+  }
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
 template <int DT, int RED>
 __device__ void move_piece(char* dst, const char* const* src, int nsrc, long long nvec, bool do_scale, float scale) {
   switch (nsrc) {
@@ -354,6 +374,18 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
           char* dst = a.mc_base + s_buf_off[st.dst_buf] + batch * a.batch_stride[st.dst_buf] +
                       ((long long)(st.dst_chunk + k) * a.chunk_elems + pr.lo) * esize;
           mc_allreduce_piece<DT>(dst, src, nvec, (st.flags & F_SCALE) != 0, a.scale);
+        }
+        __syncthreads();
+      }
+      if (st.op == OP_MC_STORE && pr.hi > pr.lo) {
+        const long long nvec = (pr.hi - pr.lo) * esize / 16;
+        const DevSrc sr = a.srcs[st.src_begin];
+        for (int k = 0; k < st.cnt; ++k) {
+          const char* src = s_rank_base[a.rank] + s_buf_off[sr.buf] + batch * a.batch_stride[sr.buf] +
+                            ((long long)(sr.chunk + k) * a.chunk_elems + pr.lo) * esize;
+          char* dst = a.mc_base + s_buf_off[st.dst_buf] + batch * a.batch_stride[st.dst_buf] +
+                      ((long long)(st.dst_chunk + k) * a.chunk_elems + pr.lo) * esize;
+          mc_store_piece(dst, src, nvec);
         }
         __syncthreads();
       }

@@ -735,7 +735,61 @@ class Compiler {
         stats_.multicast_ops++;
       }
     }
+    map_multicast_broadcasts();
     defer_multicast_arrivals();
+  }
+
+  // A chunk the owner copies locally into (OUT, c) while every other rank pulls the
+  // same source into its own (OUT, c) is a broadcast: the owner's copy becomes one
+  // multimem.st that writes (OUT, c) on every rank, the pulls become waits.
+  void map_multicast_broadcasts() {
+    for (int r = 0; r < P_; ++r) {
+      auto& steps = pending_[r][0];
+      for (int i = 0; i < (int)steps.size(); ++i) {
+        PendingStep& ps = steps[i];
+        if (ps.st.op != OP_COPY || ps.st.cnt != 1 || ps.srcs.size() != 1 || ps.srcs[0].rank != r ||
+            (ps.st.flags & F_SCALE))
+          continue;
+        const DevSrc src = ps.srcs[0];
+        const int owner_done = 2 * i + 2;
+        std::vector<std::pair<int, int>> peers;
+        for (int p = 0; p < P_; ++p) {
+          if (p == r) continue;
+          auto& ps2 = pending_[p][0];
+          int found = -1;
+          for (int j = 0; j < (int)ps2.size(); ++j) {
+            const PendingStep& c = ps2[j];
+            if (c.st.op != OP_COPY || c.st.cnt != 1 || c.srcs.size() != 1 || (c.st.flags & F_SCALE)) continue;
+            const DevSrc& sr = c.srcs[0];
+            if (sr.rank != r || sr.buf != src.buf || sr.chunk != src.chunk) continue;
+            if (c.st.dst_buf != ps.st.dst_buf || c.st.dst_chunk != ps.st.dst_chunk) continue;
+            // the pull may only wait for the data to be ready (start flags / owner events)
+            bool plain = true;
+            for (auto& kv : c.waits)
+              if (kv.first.second >= 0 && kv.first.first != r) plain = false;
+            if (plain) { found = j; break; }
+          }
+          if (found < 0) break;
+          peers.emplace_back(p, found);
+        }
+        if ((int)peers.size() != P_ - 1) continue;
+        // the owner now writes the peers' destinations: it must wait for their kernels to have started
+        for (int p = 0; p < P_; ++p)
+          if (p != r) merge(ps.waits, EventSet{{{p, -1}, 1}});
+        ps.st.op = OP_MC_STORE;
+        for (auto& pj : peers) {
+          PendingStep& c = pending_[pj.first][0][pj.second];
+          c.st.op = OP_NOP;
+          c.srcs.clear();
+          c.waits.clear();
+          c.waits[{r, 0}] = owner_done;
+          c.mc_peer = true;
+          c.mc_buf = ps.st.dst_buf;
+          c.mc_chunk = ps.st.dst_chunk;
+        }
+        stats_.multicast_ops++;
+      }
+    }
   }
 
   // A rank learns that an owner's multicast store reached its memory by waiting

@@ -1,0 +1,113 @@
+"""AllReduce / AllGather bus-bandwidth sweep, 1 KiB … 1 GiB per rank (powers of 4), vs stock NCCL.
+
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 sweep.py [--colls allreduce,allgather]
+             [--dtype bfloat16] [--min-bytes 1024] [--max-bytes 1073741824] [--iters 20] [--warmup 5]
+
+Each point: the synthesized schedule through the sm_100a interpreter (heap
+buffers, CUDA-event device time, max over ranks) and torch.distributed NCCL
+on the same buffers.  busbw follows nccl-tests: AllReduce algbw·2(P−1)/P
+with size M; AllGather algbw·(P−1)/P with size P·M.  Rank 0 prints one JSON
+line per point and a final summary line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--colls", default="allreduce,allgather")
+    ap.add_argument("--dtype", default="bfloat16")
+    ap.add_argument("--min-bytes", type=int, default=1024)
+    ap.add_argument("--max-bytes", type=int, default=1 << 30)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--no-nccl", action="store_true")
+    args = ap.parse_args()
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        dist.init_process_group("cpu:gloo,cuda:nccl", device_id=torch.device("cuda", local))
+    from vericcl_b200.models import CollectiveEngine
+    from vericcl_b200.parallel import Communicator
+    dtype = {"bfloat16": torch.bfloat16, "float32": torch.float32, "float16": torch.float16}[args.dtype]
+    esize = torch.tensor([], dtype=dtype).element_size()
+    heap = args.max_bytes * (world + 2) + (256 << 20)
+    comm = Communicator(heap_bytes=heap, multicast=world >= 4)
+    eng = CollectiveEngine(comm)
+    rank = comm.rank
+    stream = torch.cuda.current_stream()
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        comm.barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        for _ in range(args.iters):
+            fn()
+        e.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([s.elapsed_time(e) / args.iters * 1e3], dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=comm.control_group)
+        return float(t.item())
+
+    results = []
+    size = args.min_bytes
+    while size <= args.max_bytes:
+        count = size // esize
+        for coll in args.colls.split(","):
+            if coll == "allreduce":
+                buf = comm.empty(count, dtype)
+                buf.normal_()
+                plan = eng.plan("allreduce", count, dtype, inplace=True)
+                ours = timed(lambda: comm.run(plan, buf, buf))
+                comm.check_status()
+                nccl = None if (args.no_nccl or world == 1) else timed(lambda: dist.all_reduce(buf))
+                factor = 2.0 * (world - 1) / world if world > 1 else 1.0
+                nbytes = size
+                comm.free(buf)
+            else:
+                inp = comm.empty(count, dtype)
+                out = comm.empty(count * world, dtype)
+                inp.normal_()
+                plan = eng.plan("allgather", count, dtype, inplace=False)
+                ours = timed(lambda: comm.run(plan, inp, out))
+                comm.check_status()
+                nccl = None if (args.no_nccl or world == 1) else timed(
+                    lambda: dist.all_gather_into_tensor(out, inp))
+                factor = (world - 1) / world if world > 1 else 1.0
+                nbytes = size * world
+                comm.free(inp)
+                comm.free(out)
+            point = {"coll": coll, "n_gpus": world, "bytes_per_rank": size, "dtype": args.dtype,
+                     "time_us": round(ours, 3), "busbw_gbs": round(nbytes / ours / 1e3 * factor, 2),
+                     "lanes": plan.nlanes, "iters": plan.niters, "nvls": plan.multicast}
+            if nccl is not None:
+                point.update({"nccl_time_us": round(nccl, 3),
+                              "nccl_busbw_gbs": round(nbytes / nccl / 1e3 * factor, 2),
+                              "speedup_vs_nccl": round(nccl / ours, 3)})
+            results.append(point)
+            if rank == 0:
+                print(json.dumps(point), flush=True)
+        size *= 4
+    if rank == 0:
+        print(json.dumps({"summary": True, "points": len(results)}), flush=True)
+    comm.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

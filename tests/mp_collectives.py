@@ -65,7 +65,7 @@ def main():
         dname = str(dtype).split(".")[-1]
         xml = schedule_xml(coll, world, slices, inplace=inplace, datatype=dname)
         op = "avg" if coll == "allreduce" and lanes == 4 else "sum"
-        plan = comm.compile(xml, nlanes=lanes, niters=iters, multicast=comm.multicast and coll == "allreduce")
+        plan = comm.compile(xml, nlanes=lanes, niters=iters, multicast=comm.multicast and coll in ("allreduce", "allgather"))
         seed = zlib.crc32(repr((coll, dname, inplace, slices, lanes, iters, count)).encode()) % 100000
         x = inputs_for(rank, count, dtype, seed).cuda()
         out_n = count * world if coll == "allgather" else count // world if coll == "reduce_scatter" else count

@@ -44,7 +44,11 @@ class CollectiveEngine:
 
     def use_multicast(self, collective: str, op: str) -> bool:
         """NVLS pays off from 4 ranks up (it cuts AllReduce NVLink traffic from 2(P-1)/P·M to about (1+1/P)·M)."""
-        return bool(self.comm.multicast and self.comm.world >= 4 and collective == "allreduce" and op in ("sum", "avg"))
+        if not self.comm.multicast or self.comm.world < 4:
+            return False
+        if collective == "allreduce":
+            return op in ("sum", "avg")
+        return collective == "allgather"
 
     def plan(self, collective: str, count: int, dtype, *, inplace: bool, op: str = "sum"):
         world = self.comm.world
