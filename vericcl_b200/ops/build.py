@@ -153,7 +153,8 @@ def build_capi(force: bool = False) -> Path:
     OUT.mkdir(parents=True, exist_ok=True)
     target = OUT / "libvericcl_b200.so"
     sources = [CSRC / s for s in CAPI_SOURCES + RUNTIME_SOURCES + PLAN_SOURCES] + \
-        [CSRC / "cuda" / "interp.cu", CSRC / "cuda" / "helpers.cu", CSRC / "runtime" / "symheap.cc"]
+        [CSRC / "cuda" / "interp.cu", CSRC / "cuda" / "helpers.cu", CSRC / "cuda" / "noalloc.cu",
+         CSRC / "runtime" / "symheap.cc"]
     existing = [s for s in sources if s.exists()]
     if len(existing) != len(sources):
         raise FileNotFoundError("C API sources missing: %s" % [str(s) for s in sources if not s.exists()])
