@@ -45,6 +45,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-nccl", action="store_true")
     ap.add_argument("--per-bucket", action="store_true", help="one launch per bucket instead of one batched launch")
+    ap.add_argument("--slices", type=int, default=None, help="slices per rank of the synthesized schedule")
     return ap.parse_args()
 
 
@@ -144,7 +145,8 @@ def main():
     nvls = os.environ.get("VERICCL_NVLS")
     multicast = (world >= 4) if nvls is None else nvls not in ("0", "")
     comm = Communicator(heap_bytes=heap, timeout_s=20.0, multicast=multicast)
-    ar = GradBucketAllReduce(comm, args.params, dtype=dtype, bucket_bytes=args.bucket_bytes, scale=args.scale)
+    ar = GradBucketAllReduce(comm, args.params, dtype=dtype, bucket_bytes=args.bucket_bytes, scale=args.scale,
+                             slices_per_rank=args.slices)
     gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
     flat = ar.flat
     step = 1 << 28

@@ -47,6 +47,7 @@ struct CompileOptions {
   bool fuse_chains = true;   // fold chains of receive-reduce steps into one n-ary reduce
   bool multicast = false;    // map whole-group reduce/broadcast patterns to NVLS multimem ops
   bool merge_blocks = true;  // run each rank's steps as one CTA group in a global topological order
+  int mc_keep = 1, mc_period = 1;  // map a reduce chunk to NVLS when chunk % mc_period < mc_keep (rest stays P2P)
   bool reducing = false;     // the collective reduces (enables scale placement)
 };
 

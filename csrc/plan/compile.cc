@@ -691,6 +691,7 @@ class Compiler {
       for (int i = 0; i < (int)steps.size(); ++i) {
         PendingStep& ps = steps[i];
         if (ps.st.op != OP_REDUCE || ps.st.cnt != 1 || (int)ps.srcs.size() != P_) continue;
+        if (o_.mc_period > 1 && (ps.st.dst_chunk % o_.mc_period) >= o_.mc_keep) continue;
         std::set<int> ranks;
         bool same = true;
         for (auto& sr : ps.srcs) {

@@ -92,7 +92,7 @@ class Heap {
 class DevicePlan {
  public:
   DevicePlan(const std::string& xml, int rank, int nlanes, int niters, bool elide, bool fuse, bool multicast,
-             bool reducing)
+             bool reducing, int mc_keep, int mc_period)
       : rank_(rank) {
     CompileOptions o;
     o.nlanes = nlanes;
@@ -101,6 +101,8 @@ class DevicePlan {
     o.fuse_chains = fuse;
     o.multicast = multicast;
     o.reducing = reducing;
+    o.mc_keep = mc_keep;
+    o.mc_period = mc_period;
     plan_ = compile_plan(parse_xml(xml), o);
     if (rank < 0 || rank >= (int)plan_.ranks.size()) throw std::runtime_error("rank outside the plan");
     const RankProgram& rp = plan_.ranks[rank];
@@ -248,7 +250,9 @@ PYBIND11_MODULE(_vbcuda, m) {
       .def_property_readonly("multicast", [](Heap& h) { return h.get().multicast(); })
       .def("base", [](Heap& h, int r) { return (uint64_t)h.get().base(r); });
   py::class_<DevicePlan>(m, "DevicePlan")
-      .def(py::init<const std::string&, int, int, int, bool, bool, bool, bool>())
+      .def(py::init<const std::string&, int, int, int, bool, bool, bool, bool, int, int>(), py::arg("xml"),
+           py::arg("rank"), py::arg("nlanes"), py::arg("niters"), py::arg("elide"), py::arg("fuse"),
+           py::arg("multicast"), py::arg("reducing"), py::arg("mc_keep") = 1, py::arg("mc_period") = 1)
       .def("run", &DevicePlan::run, py::arg("heap"), py::arg("in_off"), py::arg("out_off"), py::arg("scr_off"),
            py::arg("count_per_rank"), py::arg("dtype"), py::arg("redop"), py::arg("scale"), py::arg("stream"),
            py::arg("timeout_s") = 10.0, py::arg("threads") = 512, py::arg("nbatch") = 1,

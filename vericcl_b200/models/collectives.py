@@ -63,7 +63,9 @@ class CollectiveEngine:
         nchunks = slices * (world if collective == "allgather" else 1)
         chunk_bytes = runtime * esize // nchunks
         lanes, iters = self.geometry(probe.device_plan.nblocks, chunk_bytes)
-        return self.comm.compile(xml, nlanes=lanes, niters=iters, multicast=self.use_multicast(collective, op))
+        share = tuple(int(v) for v in os.environ.get("VERICCL_MC_SHARE", "1/1").split("/"))
+        return self.comm.compile(xml, nlanes=lanes, niters=iters, multicast=self.use_multicast(collective, op),
+                                 mc_share=share)
 
     def _heap_copy(self, tensor: torch.Tensor, tag: str) -> torch.Tensor:
         key = (tag, tensor.numel(), tensor.dtype)
