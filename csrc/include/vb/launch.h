@@ -60,6 +60,12 @@ cudaError_t launch_check(const void* out, long long n, int dtype, int collective
                          cudaStream_t stream);
 cudaError_t launch_read_timer(unsigned long long* dst, cudaStream_t stream);
 
+// Block-scaled FP8 (e4m3) payloads.
+cudaError_t launch_quantize_fp8(const void* in, unsigned char* q, float* scales, long long n, int block, int dtype,
+                                cudaStream_t stream);
+cudaError_t launch_dequantize_fp8(const unsigned char* q, const float* scales, void* out, long long n, int block,
+                                  int dtype, cudaStream_t stream);
+
 // Calibration probes.
 cudaError_t launch_copy_probe(void* dst, const void* src, long long bytes, int ctas, int threads, int unroll,
                               cudaStream_t stream);

@@ -325,6 +325,18 @@ PYBIND11_MODULE(_vbcuda, m) {
     cuda_check(launch_reduce_probe(reinterpret_cast<void*>(dst), p.data(), (int)p.size(), bytes, ctas, threads,
                                    at::cuda::getCurrentCUDAStream().stream()), "reduce probe");
   });
+  m.def("quantize_fp8", [](torch::Tensor in, torch::Tensor q, torch::Tensor scales, int block) {
+    cuda_check(launch_quantize_fp8(in.data_ptr(), reinterpret_cast<unsigned char*>(q.data_ptr()),
+                                   reinterpret_cast<float*>(scales.data_ptr()), in.numel(), block,
+                                   dtype_code(in.scalar_type()), at::cuda::getCurrentCUDAStream().stream()),
+               "quantize fp8");
+  });
+  m.def("dequantize_fp8", [](torch::Tensor q, torch::Tensor scales, torch::Tensor out, int block) {
+    cuda_check(launch_dequantize_fp8(reinterpret_cast<const unsigned char*>(q.data_ptr()),
+                                     reinterpret_cast<const float*>(scales.data_ptr()), out.data_ptr(), out.numel(),
+                                     block, dtype_code(out.scalar_type()), at::cuda::getCurrentCUDAStream().stream()),
+               "dequantize fp8");
+  });
   m.def("enable_peer_access", [](int device, int peer) {
     int cur = 0;
     cudaGetDevice(&cur);

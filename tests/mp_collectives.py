@@ -112,6 +112,21 @@ def main():
         dist.barrier()
         for t in ([buf] if inplace else [inp, out]):
             comm.free(t)
+    # block-scaled FP8 AllGather through the engine
+    from vericcl_b200.models import CollectiveEngine
+    eng = CollectiveEngine(comm)
+    n = 1 << 14
+    x = inputs_for(rank, n, torch.float32, 4242).cuda()
+    out = torch.empty(n * world, device="cuda")
+    eng.all_gather_fp8(x, out)
+    torch.cuda.synchronize()
+    ref = torch.cat([inputs_for(r, n, torch.float32, 4242) for r in range(world)]).cuda()
+    amax = ref.view(-1, 128).abs().amax(dim=1).repeat_interleave(128)
+    rel = ((out - ref).abs() / amax.clamp_min(1e-6)).max().item()
+    ok = rel < 0.07
+    failures += 0 if ok else 1
+    if rank == 0 or not ok:
+        print(json.dumps({"rank": rank, "coll": "allgather_fp8", "max_rel_err": rel, "ok": ok}), flush=True)
     total = torch.tensor([failures])
     dist.all_reduce(total, group=comm.control_group)
     comm.close()

@@ -109,3 +109,34 @@ def test_device_timeout_is_reported_not_hung(comm):
     x.fill_(2.0)
     torch.cuda.synchronize()
     assert float(x.sum()) == 8192.0
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_fp8_block_quantization_matches_torch(comm, dtype):
+    mod = comm._mod
+    n, block = 4096 + 77, 128
+    x = (torch.randn(n, device="cuda") * 3).to(dtype)
+    nb = -(-n // block)
+    q = torch.empty(n, dtype=torch.uint8, device="cuda")
+    s = torch.empty(nb, dtype=torch.float32, device="cuda")
+    mod.quantize_fp8(x, q, s, block)
+    xf = torch.nn.functional.pad(x.float(), (0, nb * block - n)).view(nb, block)
+    ref_s = xf.abs().amax(dim=1) / 448.0
+    ref_s[ref_s == 0] = 1.0
+    assert torch.allclose(s, ref_s, rtol=1e-6)
+    ref_q = (xf / ref_s[:, None]).to(torch.float8_e4m3fn).view(-1)[:n].view(torch.uint8)
+    assert (q != ref_q).sum().item() <= n // 1000 + 1
+    out = torch.empty(n, dtype=dtype, device="cuda")
+    mod.dequantize_fp8(q, s, out, block)
+    rel = ((out.float() - x.float()).abs() / xf.abs().amax(dim=1).repeat_interleave(block)[:n].clamp_min(1e-6))
+    assert rel.max().item() < 0.07          # e4m3 keeps 3 mantissa bits
+
+
+def test_engine_all_gather_fp8_single_rank(comm):
+    from vericcl_b200.models import CollectiveEngine
+    eng = CollectiveEngine(comm)
+    x = torch.randn(10240, device="cuda")
+    out = torch.empty_like(x)
+    eng.all_gather_fp8(x, out)
+    torch.cuda.synchronize()
+    assert torch.allclose(out, x, atol=0.07 * x.abs().max().item())

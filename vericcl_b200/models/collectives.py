@@ -110,6 +110,41 @@ class CollectiveEngine:
         out.view(-1).copy_(dst)
         return out
 
+    def all_gather_fp8(self, inp: torch.Tensor, out: torch.Tensor, *, block: int = 128) -> torch.Tensor:
+        """AllGather with block-scaled FP8 (e4m3) payloads.
+
+        Each rank quantizes its input (one fp32 scale per ``block`` elements),
+        gathers the packed [fp8 bytes | scales] payloads with the synthesized
+        AllGather schedule, and dequantizes every rank's part into ``out``.
+        Moves about a quarter (fp32) or half (bf16) of the bytes of a plain
+        AllGather; values carry e4m3 precision.
+        """
+        world = self.comm.world
+        n = inp.numel()
+        if out.numel() != n * world:
+            raise RuntimeFailure("all_gather_fp8 output must hold world × input elements")
+        nblocks = -(-n // block)
+        packed = -(-(n + 4 * nblocks) // 16) * 16        # bytes per rank, 16-byte aligned
+        key = ("fp8", n, block)
+        bufs = self._staging.get(key)
+        if bufs is None:
+            src = self.comm.empty(packed // 2, torch.bfloat16)
+            dst = self.comm.empty(packed // 2 * world, torch.bfloat16)
+            bufs = (src, dst)
+            self._staging[key] = bufs
+        src, dst = bufs
+        raw = src.view(torch.uint8)
+        self.comm._mod.quantize_fp8(inp.contiguous().view(-1), raw[:n], raw[n:n + 4 * nblocks].view(torch.float32),
+                                    block)
+        plan = self.plan("allgather", packed // 2, torch.bfloat16, inplace=False)
+        self.comm.run(plan, src, dst)
+        gathered = dst.view(torch.uint8).view(world, packed)
+        flat_out = out.view(world, n)
+        for r in range(world):
+            part = gathered[r]
+            self.comm._mod.dequantize_fp8(part[:n], part[n:n + 4 * nblocks].view(torch.float32), flat_out[r], block)
+        return out
+
     def reduce_scatter(self, inp: torch.Tensor, out: torch.Tensor, *, op: str = "sum",
                        scale: float | None = None) -> torch.Tensor:
         world = self.comm.world
