@@ -247,7 +247,6 @@ __device__ void mc_allreduce_piece(char* mc_dst, const char* mc_src, long long n
       mc_st(mc_dst + v * 16, out);
     }
   }
-  asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
 
 // dst(all ranks) = src(local), through the multicast address of the destination.
@@ -267,7 +266,6 @@ __device__ void mc_store_piece(char* mc_dst, const char* src, long long nvec) {
       if (v < nvec) mc_st(mc_dst + v * 16, r[u]);
     }
   }
-  asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
 
 template <int DT, int RED>
@@ -346,13 +344,15 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
   const unsigned long long stride = 2ull * (unsigned long long)blk.nsteps;
   unsigned long long* my_flag = flag_ptr(a, a.rank, (long long)block * kMaxFlagLanes + lane);
   __shared__ const char* s_src[16];
+  bool mc_pending = false;   // multimem stores of this thread not yet fenced
   const int total_iters = a.niters * a.nbatch;
   for (int it = 0; it < total_iters; ++it) {
     const int batch = it / a.niters;
     const PieceRange pr = piece_range(a.chunk_elems, a.piece_elems, it - batch * a.niters, a.nlanes, lane);
     for (int s = 0; s < blk.nsteps; ++s) {
       const DevStep st = a.steps[blk.step_begin + s];
-      unsigned long long t_reach = 0, t_ready = 0;
+      unsigned long long t_reach = 0, t_ready = 0, t_step0 = 0;
+      if (a.pace_group > 0 && threadIdx.x == 0) t_step0 = globaltimer();
       if (a.trace_buf && threadIdx.x == 0) t_reach = globaltimer();
       if (st.wait_count) {
         if (threadIdx.x < 32) {
@@ -364,7 +364,14 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
       }
       if (a.trace_buf && threadIdx.x == 0) t_ready = globaltimer();
       const unsigned long long ev = base + (unsigned long long)it * stride + 2ull * s;
-      if ((st.flags & F_PUB_ARRIVE) && threadIdx.x == 0) st_release_sys(my_flag, ev + 1);
+      if (st.flags & F_PUB_ARRIVE) {
+        if (mc_pending) {
+          asm volatile("fence.acq_rel.sys;" ::: "memory");
+          mc_pending = false;
+          __syncthreads();
+        }
+        if (threadIdx.x == 0) st_release_sys(my_flag, ev + 1);
+      }
       if (st.op == OP_MC_ALLREDUCE && pr.hi > pr.lo) {
         const long long nvec = (pr.hi - pr.lo) * esize / 16;
         const DevSrc sr = a.srcs[st.src_begin];
@@ -375,7 +382,13 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
                       ((long long)(st.dst_chunk + k) * a.chunk_elems + pr.lo) * esize;
           mc_allreduce_piece<DT>(dst, src, nvec, (st.flags & F_SCALE) != 0, a.scale);
         }
-        __syncthreads();
+        mc_pending = true;
+        if (s + 1 < blk.nsteps && a.steps[blk.step_begin + s + 1].op != OP_NOP) {
+          // the next step may read what these multicast stores wrote: fence and join the CTA first
+          asm volatile("fence.acq_rel.sys;" ::: "memory");
+          mc_pending = false;
+          __syncthreads();
+        }
       }
       if (st.op == OP_MC_STORE && pr.hi > pr.lo) {
         const long long nvec = (pr.hi - pr.lo) * esize / 16;
@@ -387,7 +400,13 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
                       ((long long)(st.dst_chunk + k) * a.chunk_elems + pr.lo) * esize;
           mc_store_piece(dst, src, nvec);
         }
-        __syncthreads();
+        mc_pending = true;
+        if (s + 1 < blk.nsteps && a.steps[blk.step_begin + s + 1].op != OP_NOP) {
+          // the next step may read what these multicast stores wrote: fence and join the CTA first
+          asm volatile("fence.acq_rel.sys;" ::: "memory");
+          mc_pending = false;
+          __syncthreads();
+        }
       }
       if ((st.op == OP_COPY || st.op == OP_REDUCE) && pr.hi > pr.lo) {
         const long long nvec = (pr.hi - pr.lo) * esize / 16;
@@ -404,7 +423,23 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
           __syncthreads();
         }
       }
+      if (a.pace_group > 0 && (st.op == OP_COPY || st.op == OP_REDUCE) && threadIdx.x == 0 && pr.hi > pr.lo) {
+        // link emulation: a step that pulled from another rank group lasts at least bytes / emulated rate
+        bool crosses = false;
+        for (int i = 0; i < st.nsrc; ++i)
+          crosses |= (a.srcs[st.src_begin + i].rank / a.pace_group) != (a.rank / a.pace_group);
+        if (crosses) {
+          const unsigned long long need =
+              (unsigned long long)((double)(pr.hi - pr.lo) * esize * st.cnt * a.pace_ns_per_byte);
+          while (globaltimer() - t_step0 < need) {
+          }
+        }
+      }
       if (st.flags & F_PUB_DONE) {
+        if (mc_pending) {
+          asm volatile("fence.acq_rel.sys;" ::: "memory");
+          mc_pending = false;
+        }
         __syncthreads();
         if (threadIdx.x == 0) st_release_sys(my_flag, ev + 2);
       }
@@ -418,6 +453,11 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
       }
     }
   }
+  // final event of this block: implies every event of every iteration
+  if (mc_pending) asm volatile("fence.acq_rel.sys;" ::: "memory");
+  __syncthreads();
+  if (threadIdx.x == 0)
+    st_release_sys(my_flag, base + (unsigned long long)(total_iters - 1) * stride + 2ull * blk.nsteps);
   if (blk.end_wait_count) {
     if (threadIdx.x < 32) {
       bool ok = wait_events(a, a.waits + blk.end_wait_begin, blk.end_wait_count, total_iters - 1, base, block, lane);
@@ -483,13 +523,20 @@ cudaError_t launch_interp(const InterpArgs& a, cudaStream_t stream, int threads)
 }
 
 int interp_max_ctas(int threads) {
+  static int cached_threads[64] = {};
+  static int cached_value[64] = {};
   int dev = 0, sms = 0, per_sm = 0;
   cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && cached_threads[dev] == threads && cached_value[dev] > 0) return cached_value[dev];
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, interp_kernel<DT_BF16, RED_SUM>, threads, 0);
   int f32 = 0;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&f32, interp_kernel<DT_F32, RED_SUM>, threads, 0);
   if (f32 < per_sm) per_sm = f32;
+  if (dev >= 0 && dev < 64) {
+    cached_threads[dev] = threads;
+    cached_value[dev] = sms * per_sm;
+  }
   return sms * per_sm;
 }
 

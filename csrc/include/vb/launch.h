@@ -42,6 +42,8 @@ struct InterpArgs {
   char* mc_base;                     // multicast address of the heap (nullptr when unavailable)
   Control* control;                  // local control block
   unsigned long long timeout_ns;
+  int pace_group;                    // >0: emulate slow links between rank groups of this size
+  float pace_ns_per_byte;            // per-CTA pacing of a data step that reads another group's memory
   int trace;                         // record per-step timestamps into trace buffer
   unsigned long long* trace_buf;     // [nblocks*nlanes][max_steps*niters][2] (start, end) globaltimer
   int trace_stride;

@@ -81,6 +81,7 @@ class Compiler {
     build_waits_and_hazards();
     if (o_.merge_blocks) merge_blocks();
     if (o_.multicast && merged_ && P_ > 1) map_multicast();
+    dedupe_start_waits();
     emit();
     deadlock_check();
     CompiledPlan plan;
@@ -822,6 +823,23 @@ class Compiler {
     }
   }
 
+  // A peer's start flag holds for the whole launch: once a block waited for it,
+  // later steps of the block need not poll it again.
+  void dedupe_start_waits() {
+    for (int r = 0; r < P_; ++r)
+      for (auto& blk : pending_[r]) {
+        std::set<int> seen;
+        for (auto& ps : blk) {
+          for (auto it = ps.waits.begin(); it != ps.waits.end();) {
+            if (it->first.second < 0 && seen.count(it->first.first)) it = ps.waits.erase(it);
+            else ++it;
+          }
+          for (auto& kv : ps.waits)
+            if (kv.first.second < 0) seen.insert(kv.first.first);
+        }
+      }
+  }
+
   void emit() {
     for (int r = 0; r < P_; ++r) {
       RankProgram& rp = out_[r];
@@ -860,16 +878,17 @@ class Compiler {
         blk.end_wait_begin = (int)rp.waits.size();
         blk.end_wait_count = 0;
         if (db == 0) {
+          // End-of-kernel waits target the peer block's final event (every CTA publishes it once,
+          // after its last step), which implies every earlier event of that block.
           for (auto& kv : end_waits_[r]) {
             DevWait w{};
             w.rank = (int16_t)kv.first.first;
             w.block = (int16_t)kv.first.second;
             w.stride = 2 * dsteps_count_[w.rank][w.block];
-            w.event = kv.second;
+            w.event = 2 * dsteps_count_[w.rank][w.block];
             w.iter_delta = -1;
             rp.waits.push_back(w);
             blk.end_wait_count++;
-            published_.insert({w.rank, w.block, w.event});
           }
         }
         rp.blocks.push_back(blk);

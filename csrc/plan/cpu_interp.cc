@@ -152,7 +152,12 @@ InterpResult cpu_interpret(const CompiledPlan& plan, HostBuffers& bufs, int dtyp
           continue;
         }
         if (!c.in_end) {
-          if (c.it >= I || blk.nsteps == 0) { c.in_end = true; progressed = true; continue; }
+          if (c.it >= I || blk.nsteps == 0) {
+            c.in_end = true;
+            publish(2 * blk.nsteps, I - 1);   // final event of the block
+            progressed = true;
+            continue;
+          }
           const DevStep& st = rp.steps[blk.step_begin + c.s];
           if (!wait_ok(st.wait_begin, st.wait_count, c.it)) continue;
           if (st.flags & F_PUB_ARRIVE) publish(2 * c.s + 1, c.it);

@@ -5,6 +5,8 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 
+#include <cstdio>
+#include <cstdlib>
 #include <memory>
 #include <stdexcept>
 #include <string>
@@ -89,6 +91,30 @@ class Heap {
   std::unique_ptr<SymHeap> h_;
 };
 
+// VERICCL_EMULATE="group=4,gbps=25": pace data steps that read another group of 4 ranks to an
+// emulated 25 GB/s inter-group link (split across the CTAs of the launch).  Off when unset.
+void emulation_from_env(InterpArgs* a) {
+  const char* env = std::getenv("VERICCL_EMULATE");
+  a->pace_group = 0;
+  a->pace_ns_per_byte = 0.f;
+  if (!env || !*env) return;
+  int group = 0;
+  double gbps = 0;
+  if (sscanf(env, "group=%d,gbps=%lf", &group, &gbps) == 2 && group > 0 && gbps > 0) {
+    a->pace_group = group;
+    // bytes/ns of one CTA = gbps / ctas
+    a->pace_ns_per_byte = (float)((double)(a->nblocks * a->nlanes) / gbps);
+  }
+}
+
+struct BoundLaunch {
+  InterpArgs args;
+  int threads;
+  void launch(uint64_t stream) {
+    cuda_check(launch_interp(args, reinterpret_cast<cudaStream_t>(stream), threads), "launch interpreter");
+  }
+};
+
 class DevicePlan {
  public:
   DevicePlan(const std::string& xml, int rank, int nlanes, int niters, bool elide, bool fuse, bool multicast,
@@ -136,6 +162,15 @@ class DevicePlan {
   void run(Heap& heap, size_t in_off, size_t out_off, size_t scr_off, int64_t count_per_rank, int dtype, int redop,
            float scale, uint64_t stream, double timeout_s, int threads, int nbatch,
            std::vector<long long> batch_stride, uint64_t trace_ptr, int64_t trace_stride) {
+    InterpArgs a = bind(heap, in_off, out_off, scr_off, count_per_rank, dtype, redop, scale, timeout_s, threads, nbatch,
+                        batch_stride, trace_ptr, trace_stride);
+    cuda_check(launch_interp(a, reinterpret_cast<cudaStream_t>(stream), threads), "launch interpreter");
+  }
+
+  // Validated launch arguments for repeated launches of the same buffers (no per-launch checks).
+  InterpArgs bind(Heap& heap, size_t in_off, size_t out_off, size_t scr_off, int64_t count_per_rank, int dtype,
+                  int redop, float scale, double timeout_s, int threads, int nbatch,
+                  std::vector<long long> batch_stride, uint64_t trace_ptr, int64_t trace_stride) {
     SymHeap& h = heap.get();
     if (h.nranks() != (int)plan_.ranks.size()) throw std::runtime_error("heap and plan rank counts differ");
     py::tuple g = geometry(count_per_rank, dtype);
@@ -178,12 +213,13 @@ class DevicePlan {
     a.control = heap.control();
     a.timeout_ns = (unsigned long long)(timeout_s * 1e9);
     a.trace_buf = reinterpret_cast<unsigned long long*>(trace_ptr);
+    emulation_from_env(&a);
     a.trace_stride = (int)trace_stride;
     int max_ctas = interp_max_ctas(threads);
     if (a.nblocks * a.nlanes > max_ctas)
       throw std::runtime_error("plan needs " + std::to_string(a.nblocks * a.nlanes) + " co-resident CTAs; the device holds " +
                                std::to_string(max_ctas));
-    cuda_check(launch_interp(a, reinterpret_cast<cudaStream_t>(stream), threads), "launch interpreter");
+    return a;
   }
 
   int nblocks() const { return nblocks_; }
@@ -249,6 +285,7 @@ PYBIND11_MODULE(_vbcuda, m) {
       .def_property_readonly("size", [](Heap& h) { return h.get().size(); })
       .def_property_readonly("multicast", [](Heap& h) { return h.get().multicast(); })
       .def("base", [](Heap& h, int r) { return (uint64_t)h.get().base(r); });
+  py::class_<BoundLaunch>(m, "BoundLaunch").def("launch", &BoundLaunch::launch);
   py::class_<DevicePlan>(m, "DevicePlan")
       .def(py::init<const std::string&, int, int, int, bool, bool, bool, bool, int, int>(), py::arg("xml"),
            py::arg("rank"), py::arg("nlanes"), py::arg("niters"), py::arg("elide"), py::arg("fuse"),
@@ -258,6 +295,12 @@ PYBIND11_MODULE(_vbcuda, m) {
            py::arg("timeout_s") = 10.0, py::arg("threads") = 512, py::arg("nbatch") = 1,
            py::arg("batch_stride") = std::vector<long long>{0, 0, 0}, py::arg("trace_ptr") = 0,
            py::arg("trace_stride") = 0)
+      .def("bind", [](DevicePlan& p, Heap& heap, size_t in_off, size_t out_off, size_t scr_off, int64_t count, int dtype,
+                      int redop, float scale, double timeout_s, int threads, int nbatch,
+                      std::vector<long long> strides) {
+        return BoundLaunch{p.bind(heap, in_off, out_off, scr_off, count, dtype, redop, scale, timeout_s, threads, nbatch,
+                                  strides, 0, 0), threads};
+      })
       .def("geometry", &DevicePlan::geometry)
       .def("slots", &DevicePlan::slots)
       .def("describe", &DevicePlan::describe)

@@ -31,6 +31,7 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--no-nccl", action="store_true")
+    ap.add_argument("--graph", action="store_true", help="capture the timed launches in CUDA graphs (both impls)")
     args = ap.parse_args()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -51,11 +52,22 @@ def main():
         for _ in range(args.warmup):
             fn()
         torch.cuda.synchronize()
+        graph = None
+        if args.graph:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for _ in range(args.iters):
+                    fn()
+            graph.replay()
+            torch.cuda.synchronize()
         comm.barrier()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record(stream)
-        for _ in range(args.iters):
-            fn()
+        if graph is not None:
+            graph.replay()
+        else:
+            for _ in range(args.iters):
+                fn()
         e.record(stream)
         torch.cuda.synchronize()
         t = torch.tensor([s.elapsed_time(e) / args.iters * 1e3], dtype=torch.float64)
@@ -91,7 +103,7 @@ def main():
                 nbytes = size * world
                 comm.free(inp)
                 comm.free(out)
-            point = {"coll": coll, "n_gpus": world, "bytes_per_rank": size, "dtype": args.dtype,
+            point = {"coll": coll, "n_gpus": world, "bytes_per_rank": size, "dtype": args.dtype, "graph": args.graph,
                      "time_us": round(ours, 3), "busbw_gbs": round(nbytes / ours / 1e3 * factor, 2),
                      "lanes": plan.nlanes, "iters": plan.niters, "nvls": plan.multicast}
             if nccl is not None:

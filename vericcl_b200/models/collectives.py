@@ -52,7 +52,8 @@ class CollectiveEngine:
 
     def plan(self, collective: str, count: int, dtype, *, inplace: bool, op: str = "sum"):
         world = self.comm.world
-        slices = self.slices_per_rank or world
+        default = 1 if collective in ("allgather", "broadcast") else world
+        slices = self.slices_per_rank or default
         if collective in ("reduce_scatter", "alltoall") and slices % world:
             slices = world
         dname = str(dtype).split(".")[-1]
