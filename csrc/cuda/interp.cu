@@ -14,6 +14,9 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <cstdio>
+#include <cstdlib>
+
 #include "vb/launch.h"
 
 namespace vb {
@@ -519,6 +522,21 @@ cudaError_t launch_interp(const InterpArgs& a, cudaStream_t stream, int threads)
     case DT_BF16: return launch_red<DT_BF16>(a, stream, threads);
     case DT_F16: return launch_red<DT_F16>(a, stream, threads);
     default: return cudaErrorInvalidValue;
+  }
+}
+
+void apply_emulation_env(InterpArgs* a) {
+  // VERICCL_EMULATE="group=4,gbps=25": pace data steps that read another group of 4 ranks so the
+  // inter-group traffic of the launch runs at an emulated 25 GB/s (split across its CTAs).
+  const char* env = getenv("VERICCL_EMULATE");
+  a->pace_group = 0;
+  a->pace_ns_per_byte = 0.f;
+  if (!env || !*env) return;
+  int group = 0;
+  double gbps = 0;
+  if (sscanf(env, "group=%d,gbps=%lf", &group, &gbps) == 2 && group > 0 && gbps > 0) {
+    a->pace_group = group;
+    a->pace_ns_per_byte = (float)((double)(a->nblocks * a->nlanes) / gbps);
   }
 }
 

@@ -52,6 +52,8 @@ struct InterpArgs {
 // Launch the interpreter (cooperative launch: every CTA is co-resident).
 cudaError_t launch_interp(const InterpArgs& args, cudaStream_t stream, int threads);
 int interp_max_ctas(int threads);
+// Inter-group link emulation from VERICCL_EMULATE (off when unset).
+void apply_emulation_env(InterpArgs* a);
 
 // Helper kernels.
 cudaError_t launch_fill(void* dst, long long n, int dtype, int pattern, int rank, unsigned long long seed,

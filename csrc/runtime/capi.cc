@@ -201,6 +201,7 @@ extern "C" vb_result vb_execute(vb_context* c, const void* in, void* out, size_t
     a.mc_base = c->heap->mc_base();
     a.control = reinterpret_cast<Control*>(c->heap->base(c->rank));
     a.timeout_ns = (unsigned long long)(timeout_s * 1e9);
+    apply_emulation_env(&a);
     if (a.nblocks * a.nlanes > interp_max_ctas(512)) return fail(c, VB_INVALID, "too many CTAs for the device");
     cudaError_t e = launch_interp(a, stream, 512);
     if (e != cudaSuccess) return fail(c, VB_FAILED, cudaGetErrorString(e));

@@ -91,22 +91,6 @@ class Heap {
   std::unique_ptr<SymHeap> h_;
 };
 
-// VERICCL_EMULATE="group=4,gbps=25": pace data steps that read another group of 4 ranks to an
-// emulated 25 GB/s inter-group link (split across the CTAs of the launch).  Off when unset.
-void emulation_from_env(InterpArgs* a) {
-  const char* env = std::getenv("VERICCL_EMULATE");
-  a->pace_group = 0;
-  a->pace_ns_per_byte = 0.f;
-  if (!env || !*env) return;
-  int group = 0;
-  double gbps = 0;
-  if (sscanf(env, "group=%d,gbps=%lf", &group, &gbps) == 2 && group > 0 && gbps > 0) {
-    a->pace_group = group;
-    // bytes/ns of one CTA = gbps / ctas
-    a->pace_ns_per_byte = (float)((double)(a->nblocks * a->nlanes) / gbps);
-  }
-}
-
 struct BoundLaunch {
   InterpArgs args;
   int threads;
@@ -213,7 +197,7 @@ class DevicePlan {
     a.control = heap.control();
     a.timeout_ns = (unsigned long long)(timeout_s * 1e9);
     a.trace_buf = reinterpret_cast<unsigned long long*>(trace_ptr);
-    emulation_from_env(&a);
+    apply_emulation_env(&a);
     a.trace_stride = (int)trace_stride;
     int max_ctas = interp_max_ctas(threads);
     if (a.nblocks * a.nlanes > max_ctas)

@@ -77,8 +77,12 @@ def new_run(args) -> int:
                         size_accounting=dict(request.size_accounting), overrides=list(args.overrides))
     executor = _probe_executor(request) if (purpose == "calibrate" or
                                             request.request_config["sketch"]["calibration"]["enabled"]) else None
+    measure = None
+    if request.request_config["sketch"]["trace_and_measure"]["enabled"] and executor is not None:
+        from vericcl_b200.online.measure import measured_acceptance
+        measure = measured_acceptance(request, ctx.process / "statistics" / "ledger.jsonl")
     wf = PrimaryWorkflow(request, ctx, purpose=purpose, tune=getattr(args, "tune", False), model=model,
-                         verify_inputs=verify_inputs, probe_executor=executor)
+                         verify_inputs=verify_inputs, probe_executor=executor, measure=measure)
     result = wf.run()
     print(json.dumps({"run": str(ctx.directory), "status": result.status, "stop_reason": result.stop_reason,
                       "t_pred_us": None if result.best is None else result.best["t_pred_us"]}))
