@@ -75,22 +75,47 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, devices):
+    def __init__(self, devices, enabled=True):
+        self.enabled = enabled
+        # nvidia-smi numbers GPUs physically; map CUDA ordinals through CUDA_VISIBLE_DEVICES when it lists indices
+        visible = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+        if visible and all(v.isdigit() for v in visible):
+            devices = [int(visible[d]) for d in devices if d < len(visible)]
         self.devices = devices
         self.proc = None
         self.path = os.path.join("/tmp", "vb_clocks_%d.csv" % os.getpid())
 
     def __enter__(self):
+        if not self.enabled:
+            return self
         try:
             self.out = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=self.out, stderr=subprocess.DEVNULL)
+                                          "-i", ",".join(str(d) for d in self.devices), "-lms", "100"], stdout=self.out, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return self
+        # start timing only once the sampler is producing lines, so the samples cover the timed region
+        deadline = time.monotonic() + 10.0
+        while time.monotonic() < deadline and self.proc.poll() is None:
+            self.out.flush()
+            if os.path.getsize(self.path) > 0:
+                break
+            time.sleep(0.05)
+        self.started = time.monotonic()
         return self
+
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
 
     def __exit__(self, *exc):
         if self.proc is not None:
+            # keep sampling until at least 0.3 s have passed so short timed regions still get samples
+            while time.monotonic() - getattr(self, "started", 0.0) < 0.3:
+                time.sleep(0.05)
             self.proc.terminate()
             try:
                 self.proc.wait(5)
@@ -190,7 +215,7 @@ def main():
     comm.check_status()
     barrier()
     torch.cuda.synchronize()
-    with ClockSampler([local] if world == 1 else list(range(world))) as clocks:
+    with ClockSampler([local] if world == 1 else list(range(world)), enabled=rank == 0) as clocks:
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
         torch.cuda.synchronize()

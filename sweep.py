@@ -2,10 +2,15 @@
 
     torchrun --nproc-per-node N --master-addr 127.0.0.1 sweep.py [--colls allreduce,allgather]
              [--dtype bfloat16] [--min-bytes 1024] [--max-bytes 1073741824] [--iters 20] [--warmup 5]
+             [--method hierarchy|constructive_trees] [--slices S] [--nvls auto|on|off] [--graph]
+             [--check-max-bytes B]
 
 Each point: the synthesized schedule through the sm_100a interpreter (heap
 buffers, CUDA-event device time, max over ranks) and torch.distributed NCCL
-on the same buffers.  busbw follows nccl-tests: AllReduce algbw·2(P−1)/P
+on the same buffers.  ``--slices`` sets the slices per rank (S = M/slices);
+``--nvls`` forces the NVLink-SHARP mapping on or off.  Up to
+``--check-max-bytes`` per rank, each point first runs once on seeded inputs
+and compares against an fp64 host reference.  busbw follows nccl-tests: AllReduce algbw·2(P−1)/P
 with size M; AllGather algbw·(P−1)/P with size P·M.  Rank 0 prints one JSON
 line per point and a final summary line.
 """
@@ -15,6 +20,7 @@ import argparse
 import json
 import os
 import sys
+import time
 
 import torch
 import torch.distributed as dist
@@ -32,6 +38,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--no-nccl", action="store_true")
     ap.add_argument("--graph", action="store_true", help="capture the timed launches in CUDA graphs (both impls)")
+    ap.add_argument("--method", default="hierarchy", choices=("hierarchy", "constructive_trees"))
+    ap.add_argument("--slices", type=int, default=None, help="slices per rank (default: P for AR, 1 for AG)")
+    ap.add_argument("--nvls", default="auto", choices=("auto", "on", "off"))
+    ap.add_argument("--check-max-bytes", type=int, default=1 << 24)
     args = ap.parse_args()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -43,10 +53,13 @@ def main():
     dtype = {"bfloat16": torch.bfloat16, "float32": torch.float32, "float16": torch.float16}[args.dtype]
     esize = torch.tensor([], dtype=dtype).element_size()
     heap = args.max_bytes * (world + 2) + (256 << 20)
-    comm = Communicator(heap_bytes=heap, multicast=world >= 4)
-    eng = CollectiveEngine(comm)
+    multicast = {"auto": world >= 4, "on": True, "off": False}[args.nvls]
+    comm = Communicator(heap_bytes=heap, multicast=multicast)
+    eng = CollectiveEngine(comm, method=args.method, slices_per_rank=args.slices)
     rank = comm.rank
     stream = torch.cuda.current_stream()
+
+    host_us = [0.0]
 
     def timed(fn):
         for _ in range(args.warmup):
@@ -63,17 +76,39 @@ def main():
         comm.barrier()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record(stream)
+        h0 = time.perf_counter()
         if graph is not None:
             graph.replay()
         else:
             for _ in range(args.iters):
                 fn()
+        host_us[0] = (time.perf_counter() - h0) / args.iters * 1e6
         e.record(stream)
         torch.cuda.synchronize()
         t = torch.tensor([s.elapsed_time(e) / args.iters * 1e3], dtype=torch.float64)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX, group=comm.control_group)
         return float(t.item())
+
+    def seeded(r, count):
+        g = torch.Generator().manual_seed(1234 + r)
+        return torch.randn(count, generator=g, dtype=torch.float64)
+
+    def check(coll, plan, count, inp, out):
+        """One run on seeded N(0,1) inputs against an fp64 host reference; returns the max relative error."""
+        mine = seeded(rank, count)
+        inp.copy_(mine.to(dtype))
+        torch.cuda.synchronize()
+        comm.barrier()
+        comm.run(plan, inp, out)
+        torch.cuda.synchronize()
+        comm.check_status()
+        if coll == "allreduce":
+            want = sum(seeded(r, count).to(dtype).double() for r in range(world))
+        else:
+            want = torch.cat([seeded(r, count).to(dtype).double() for r in range(world)])
+        got = out.double().cpu()
+        return float((got - want).abs().max() / max(1e-12, float(want.abs().max())))
 
     results = []
     size = args.min_bytes
@@ -82,9 +117,11 @@ def main():
         for coll in args.colls.split(","):
             if coll == "allreduce":
                 buf = comm.empty(count, dtype)
-                buf.normal_()
                 plan = eng.plan("allreduce", count, dtype, inplace=True)
+                err = check(coll, plan, count, buf, buf) if size <= args.check_max_bytes else None
+                buf.normal_()
                 ours = timed(lambda: comm.run(plan, buf, buf))
+                ours_host = host_us[0]
                 comm.check_status()
                 nccl = None if (args.no_nccl or world == 1) else timed(lambda: dist.all_reduce(buf))
                 factor = 2.0 * (world - 1) / world if world > 1 else 1.0
@@ -93,9 +130,11 @@ def main():
             else:
                 inp = comm.empty(count, dtype)
                 out = comm.empty(count * world, dtype)
-                inp.normal_()
                 plan = eng.plan("allgather", count, dtype, inplace=False)
+                err = check(coll, plan, count, inp, out) if size <= args.check_max_bytes else None
+                inp.normal_()
                 ours = timed(lambda: comm.run(plan, inp, out))
+                ours_host = host_us[0]
                 comm.check_status()
                 nccl = None if (args.no_nccl or world == 1) else timed(
                     lambda: dist.all_gather_into_tensor(out, inp))
@@ -104,8 +143,11 @@ def main():
                 comm.free(inp)
                 comm.free(out)
             point = {"coll": coll, "n_gpus": world, "bytes_per_rank": size, "dtype": args.dtype, "graph": args.graph,
-                     "time_us": round(ours, 3), "busbw_gbs": round(nbytes / ours / 1e3 * factor, 2),
-                     "lanes": plan.nlanes, "iters": plan.niters, "nvls": plan.multicast}
+                     "time_us": round(ours, 3), "host_enqueue_us": round(ours_host, 2), "busbw_gbs": round(nbytes / ours / 1e3 * factor, 2),
+                     "lanes": plan.nlanes, "iters": plan.niters, "nvls": plan.multicast, "method": args.method,
+                     "slices": eng.slices_per_rank or (1 if coll == "allgather" else world)}
+            if err is not None:
+                point["max_rel_err_vs_fp64"] = err
             if nccl is not None:
                 point.update({"nccl_time_us": round(nccl, 3),
                               "nccl_busbw_gbs": round(nbytes / nccl / 1e3 * factor, 2),

@@ -94,3 +94,17 @@ def test_clock_alignment_and_trace(tmp_path):
     report = analyze_trace_causality({0: recs, 1: [r.__class__(1, *list(r.__dict__.values())[1:]) for r in recs]},
                                      maps)
     assert report["global_span_us"] > 0 and report["tails"]
+
+
+def test_online_loop_two_groups_without_gpu(tmp_path):
+    """The emulated 2×4 online loop runs end to end; without GPUs calibration and measurement are skipped."""
+    from vericcl_b200.online.loop import loop_documents, run_loop
+    docs = loop_documents(groups=2, per_group=4, inter_gbps=25.0, size_bytes=1 << 23, rounds=1,
+                          datatype="float32", pairs=4)
+    assert docs["topology"]["ranks"] == 8
+    assert any(r["kind"] == "nic" for r in docs["topology"]["shared_resources"])
+    summary = run_loop(tmp_path, size_bytes=1 << 23, rounds=1, pairs=4, measure_final=False)
+    assert summary["exit_code"] == 0
+    assert summary["best"]["checks"]["semantic"]["status"] == "valid"
+    assert len(summary["rounds"]) == 1
+    assert summary["rounds"][0]["cut_lower_bound_us"] <= summary["rounds"][0]["start_t_pred_us"]
