@@ -227,6 +227,17 @@ class DevicePlan {
       for (int s = 0; s < rp.blocks[0].nsteps; ++s) out.push_back(rp.steps[rp.blocks[0].step_begin + s].op);
     return out;
   }
+  // Opcode of every step, per block (the trace buffer indexes a CTA's records by its block's step count).
+  std::vector<std::vector<int>> block_ops() const {
+    std::vector<std::vector<int>> out;
+    const RankProgram& rp = plan_.ranks[rank_];
+    for (const auto& b : rp.blocks) {
+      std::vector<int> ops;
+      for (int s = 0; s < b.nsteps; ++s) ops.push_back(rp.steps[b.step_begin + s].op);
+      out.push_back(std::move(ops));
+    }
+    return out;
+  }
   py::dict stats() const {
     py::dict d;
     d["device_steps"] = plan_.stats.device_steps;
@@ -291,6 +302,7 @@ PYBIND11_MODULE(_vbcuda, m) {
       .def("stats", &DevicePlan::stats)
       .def("max_steps", &DevicePlan::max_steps)
       .def("step_ops", &DevicePlan::step_ops)
+      .def("block_ops", &DevicePlan::block_ops)
       .def_property_readonly("nblocks", &DevicePlan::nblocks)
       .def_property_readonly("nlanes", &DevicePlan::nlanes)
       .def_property_readonly("niters", &DevicePlan::niters);

@@ -108,3 +108,36 @@ def test_online_loop_two_groups_without_gpu(tmp_path):
     assert summary["best"]["checks"]["semantic"]["status"] == "valid"
     assert len(summary["rounds"]) == 1
     assert summary["rounds"][0]["cut_lower_bound_us"] <= summary["rounds"][0]["start_t_pred_us"]
+
+
+def test_trace_buffer_decoding_with_uneven_blocks():
+    """Records are decoded per block: block 0 has 3 steps, block 1 has 1 step, two iterations, two lanes."""
+    from vericcl_b200.online.trace import records_from_buffer
+    nblocks, nlanes, max_steps, niters = 2, 2, 3, 2
+    buf = [0] * (nblocks * nlanes * max_steps * niters * 3)
+    block_ops = [[1, 2, 0], [4]]
+    for cta in range(nblocks * nlanes):
+        nsteps = len(block_ops[cta // nlanes])
+        for it in range(niters):
+            for s in range(nsteps):
+                base = (cta * max_steps * niters + it * nsteps + s) * 3
+                buf[base:base + 3] = [1000 * cta + 100 * it + 10 * s + 1, 1000 * cta + 100 * it + 10 * s + 5, 2]
+    recs = records_from_buffer(0, buf, nblocks=nblocks, nlanes=nlanes, steps_per_iter=max_steps, niters=niters,
+                               block_ops=block_ops)
+    assert len(recs) == 2 * 2 * 3 + 2 * 2 * 1
+    for r in recs:
+        assert r.start_ns == 1000 * r.cta + 100 * r.iteration + 10 * r.step + 1
+        assert r.op == block_ops[r.block][r.step]
+
+
+def test_trace_timeline_offsets():
+    from vericcl_b200.online.clock_sync import ClockMap
+    from vericcl_b200.online.trace import TraceRecord
+    from vericcl_b200.online.trace_worker import timeline
+    traces = {0: [TraceRecord(0, 0, 0, 0, 0, 0, 1, 1000, 3000, 500), TraceRecord(0, 0, 0, 0, 0, 1, 2, 5000, 6000, 0)],
+              1: [TraceRecord(1, 0, 0, 0, 0, 0, 1, 10_000, 11_000, 100)]}
+    clocks = {0: ClockMap(0.0, 0.0, 10.0), 1: ClockMap(-8000.0, 0.0, 10.0)}
+    rows = {(r["rank"], r["step"]): r for r in timeline(traces, clocks)}
+    assert rows[(0, 0)]["start_us"] == 0.0 and rows[(0, 1)]["local_start_us"] == 4.0
+    assert rows[(1, 0)]["start_us"] == 1.0 and rows[(1, 0)]["local_start_us"] == 0.0
+    assert rows[(0, 0)]["duration_us"] == 2.0 and rows[(0, 0)]["wait_us"] == 0.5

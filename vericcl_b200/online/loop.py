@@ -38,7 +38,8 @@ def loop_documents(*, groups: int, per_group: int, inter_gbps: float, size_bytes
                              tuning_rounds=rounds, calibration=True, scratch_bytes=4 * size_bytes)
     docs["sketch"]["trace_and_measure"].update({"enabled": True, "pairs": pairs, "max_rounds": 2,
                                                 "max_cv": 0.05, "warmup_iterations": 2, "timed_iterations": 5})
-    docs["sketch"]["calibration"].update({"warmup_iterations": 2, "timed_iterations": 5, "launches": 2})
+    docs["sketch"]["calibration"].update({"warmup_iterations": 2, "timed_iterations": 5, "launches": 2,
+                                          "payload_sizes": [2 << 20, 8 << 20, 32 << 20]})
     return docs
 
 
@@ -90,6 +91,7 @@ def _run_loop(root: Path, emulate: str, *, groups, per_group, inter_gbps, size_b
         import torch
         if torch.cuda.device_count() >= groups * per_group:
             summary["device_us"] = _measure_first_and_final(run_dir, files)
+            summary["trace"] = _capture_trace(run_dir, groups * per_group, size_bytes, datatype)
         else:
             summary["device_us"] = "skipped: fewer GPUs than ranks"
     return summary
@@ -107,6 +109,24 @@ def _measure_first_and_final(run_dir: Path, files: dict) -> dict:
     if final.exists():
         out["final"] = native_measure(final.read_text(), request, iters=10, warmup=3)
     return out
+
+
+def _capture_trace(run_dir: Path, ranks: int, size_bytes: int, datatype: str) -> dict:
+    """One traced invocation of the final schedule (per-step timeline under ``process/traces``)."""
+    import subprocess
+    out = run_dir / "process" / "traces"
+    root = Path(__file__).resolve().parents[2]
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=%d" % ranks,
+           "--master-addr", "127.0.0.1", "--master-port", "29633", "-m", "vericcl_b200.online.trace_worker",
+           "--out", str(out), "--xml", str(run_dir / "schedule.xml"), "--bytes-per-rank", str(size_bytes),
+           "--dtype", datatype, "--nvls", "off", "--lanes", "32"]
+    env = dict(os.environ, PYTHONPATH=str(root) + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    res = subprocess.run(cmd, env=env, cwd=str(root), capture_output=True, text=True, timeout=600)
+    if res.returncode != 0 or not (out / "trace.json").exists():
+        return {"error": "trace capture failed (%d): %s" % (res.returncode, res.stderr[-500:])}
+    report = json.loads((out / "trace.json").read_text())
+    return {"path": str(out / "trace.json"), "global_span_us": report["global_span_us"],
+            "tails": report["tails"][:3]}
 
 
 def main(argv=None) -> int:

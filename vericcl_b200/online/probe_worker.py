@@ -21,7 +21,7 @@ def main(spec_path: str) -> int:
         spec["datatype"], torch.float32)
     esize = torch.tensor([], dtype=dtype).element_size()
     max_bytes = max(max(j["payload_sizes"]) for j in spec["jobs"]) * 8
-    comm = Comm = Communicator(heap_bytes=4 * max_bytes + (64 << 20))
+    comm = Communicator(heap_bytes=4 * max_bytes + (64 << 20))
     results = {}
     for jd in spec["jobs"]:
         job = ProbeJob(jd["job_id"], "", tuple(ProbeFlow(f["kind"], f["src"], f["dst"], f["channels"])
@@ -34,19 +34,21 @@ def main(spec_path: str) -> int:
             out = comm.empty(count, dtype)
             inp.fill_(1.0)
             for launch in range(spec["launches"]):
+                # one barrier per launch round, then back-to-back invocations: after the warm-up the ranks run
+                # in lockstep, so an invocation's device time is not inflated by the barrier's exit skew
+                comm.barrier()
                 for _ in range(spec["warmup"]):
                     comm.run(plan, inp, out)
-                times = []
-                for _ in range(spec["timed"]):
-                    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                    comm.barrier()
+                events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                          for _ in range(spec["timed"])]
+                for s, e in events:
                     s.record()
                     comm.run(plan, inp, out)
                     e.record()
-                    torch.cuda.synchronize()
-                    t = torch.tensor([s.elapsed_time(e) * 1e3], dtype=torch.float64)
-                    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=comm.control_group)
-                    times.append(float(t.item()))
+                torch.cuda.synchronize()
+                t = torch.tensor([s.elapsed_time(e) * 1e3 for s, e in events], dtype=torch.float64)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX, group=comm.control_group)
+                times = [float(v) for v in t.tolist()]
                 comm.check_status()
                 for f in job.flows:
                     comp = f.flow_id if job.mode == "shared" else (

@@ -63,19 +63,28 @@ def parse_trace(data: bytes, *, partial_ok: bool = True):
             "complete": available >= count}
 
 
-def records_from_buffer(rank, buffer, *, nblocks, nlanes, steps_per_iter, niters, ops):
-    """Decode the kernel's raw (start, end, wait) triples into records."""
+def records_from_buffer(rank, buffer, *, nblocks, nlanes, steps_per_iter, niters, ops=None, block_ops=None):
+    """Decode the kernel's raw (start, end, wait) triples into records.
+
+    CTA ``c`` (block ``c // nlanes``) owns ``steps_per_iter * niters`` slots
+    from ``c * steps_per_iter * niters``; its record for (iteration ``i``,
+    step ``s``) sits at slot ``i * nsteps(block) + s``.  ``block_ops`` gives
+    every block's step opcodes (and so its step count); ``ops`` is the
+    single-layout form where every block has ``steps_per_iter`` steps.
+    """
     out = []
     per_cta = steps_per_iter * niters
     for cta in range(nblocks * nlanes):
         block, lane = cta // nlanes, cta % nlanes
+        bops = block_ops[block] if block_ops is not None else (ops or [])
+        nsteps = len(bops) if block_ops is not None else steps_per_iter
         for it in range(niters):
-            for s in range(steps_per_iter):
-                base = (cta * per_cta + it * steps_per_iter + s) * 3
+            for s in range(nsteps):
+                base = (cta * per_cta + it * nsteps + s) * 3
                 start, end, wait = buffer[base], buffer[base + 1], buffer[base + 2]
                 if start == 0 and end == 0:
                     continue
-                out.append(TraceRecord(rank, cta, block, lane, it, s, ops[s] if s < len(ops) else -1, int(start),
+                out.append(TraceRecord(rank, cta, block, lane, it, s, bops[s] if s < len(bops) else -1, int(start),
                                        int(end), int(wait)))
     return out
 
@@ -135,5 +144,5 @@ def capture_once(comm, plan, inp, out, *, warmup: int = 3, op: str = "sum", scal
     raw = buf.cpu().tolist()
     records = records_from_buffer(comm.rank, raw, nblocks=plan.device_plan.nblocks, nlanes=plan.nlanes,
                                   steps_per_iter=plan.device_plan.max_steps(), niters=plan.niters,
-                                  ops=plan.device_plan.step_ops())
+                                  block_ops=plan.device_plan.block_ops())
     return {"rank": comm.rank, "records": records, "clock": fit_transform(before + after)}
