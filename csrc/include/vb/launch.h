@@ -21,7 +21,9 @@ struct Control {
   int status;                     // StatusCode of the first failure
   int detail[4];                  // rank, block, lane, wait index of the first failure
   int abort_request;              // host-set abort flag (mapped memory or device write)
-  unsigned long long pad[4];
+  unsigned int ll_arrive;         // CTAs finished in the current one-shot launch
+  unsigned long long ll_seq;      // one-shot launch counter (tags the flag-in-data lines)
+  unsigned long long pad[3];
 };
 
 struct InterpArgs {
@@ -69,6 +71,28 @@ cudaError_t launch_quantize_fp8(const void* in, unsigned char* q, float* scales,
                                 cudaStream_t stream);
 cudaError_t launch_dequantize_fp8(const unsigned char* q, const float* scales, void* out, long long n, int block,
                                   int dtype, cudaStream_t stream);
+
+// One-shot low-latency AllReduce / AllGather (flag-in-data lines pushed into every peer's LL region).
+enum OneShotColl : int { OS_ALLREDUCE = 0, OS_ALLGATHER = 1 };
+
+struct OneShotArgs {
+  char* base[kMaxRanks];     // heap base of every rank in this process's address space
+  long long in_off, out_off; // byte offsets of this call's buffers (identical on all ranks)
+  long long ll_off;          // byte offset of the LL region: [2 parities][nranks sources][bytes/8 lines of 16 B]
+  long long ll_src_bytes;    // bytes of one source's lines (>= 2 * bytes)
+  long long bytes;           // payload bytes per rank (multiple of 8)
+  int rank, nranks, dtype, redop, coll;
+  float scale;
+  int do_scale;
+  Control* control;
+  unsigned long long timeout_ns;
+  char* mc_base;             // multicast address of the heap: one NVLS store reaches every rank (nullptr: unicast)
+};
+
+// Bytes of LL region needed for payloads up to max_bytes per rank.
+long long oneshot_region_bytes(int nranks, long long max_bytes);
+cudaError_t launch_oneshot(const OneShotArgs& args, cudaStream_t stream);
+int oneshot_max_ctas();
 
 // Calibration probes.
 cudaError_t launch_copy_probe(void* dst, const void* src, long long bytes, int ctas, int threads, int unroll,

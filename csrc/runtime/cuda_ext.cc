@@ -66,6 +66,7 @@ class Heap {
     d["status"] = c.status;
     d["detail"] = py::make_tuple(c.detail[0], c.detail[1], c.detail[2], c.detail[3]);
     d["arrive"] = c.arrive;
+    d["ll_seq"] = c.ll_seq;
     return d;
   }
 
@@ -98,6 +99,53 @@ struct BoundLaunch {
     cuda_check(launch_interp(args, reinterpret_cast<cudaStream_t>(stream), threads), "launch interpreter");
   }
 };
+
+struct BoundOneShot {
+  OneShotArgs args;
+  void launch(uint64_t stream) {
+    cuda_check(launch_oneshot(args, reinterpret_cast<cudaStream_t>(stream)), "launch one-shot collective");
+  }
+};
+
+// Validated arguments of a one-shot launch: offsets inside the heap, 8-byte payload units, 16-byte lines.
+BoundOneShot bind_oneshot(Heap& heap, size_t in_off, size_t out_off, size_t ll_off, int64_t ll_src_bytes,
+                          int64_t bytes, int dtype, int redop, int coll, float scale, bool do_scale,
+                          double timeout_s, bool multicast) {
+  SymHeap& h = heap.get();
+  if (coll != OS_ALLREDUCE && coll != OS_ALLGATHER) throw std::runtime_error("one-shot: unknown collective");
+  if (dtype != DT_F32 && dtype != DT_BF16 && dtype != DT_F16) throw std::runtime_error("one-shot: unsupported dtype");
+  if (bytes <= 0 || bytes % 8) throw std::runtime_error("one-shot: payload must be a positive multiple of 8 bytes");
+  if (in_off % 8 || out_off % 8) throw std::runtime_error("one-shot: buffers must be 8-byte aligned");
+  if (ll_off % 16 || ll_src_bytes % 16 || ll_src_bytes < 2 * bytes)
+    throw std::runtime_error("one-shot: LL region too small or misaligned for this payload");
+  const size_t out_bytes = (size_t)bytes * (coll == OS_ALLGATHER ? h.nranks() : 1);
+  if (in_off + (size_t)bytes > h.size() || out_off + out_bytes > h.size() ||
+      ll_off + 2 * (size_t)h.nranks() * (size_t)ll_src_bytes > h.size())
+    throw std::runtime_error("one-shot: buffer exceeds the heap");
+  if (in_off < kReservedBytes || out_off < kReservedBytes || ll_off < kReservedBytes)
+    throw std::runtime_error("one-shot: buffer overlaps the control block or flag table");
+  BoundOneShot b;
+  OneShotArgs& a = b.args;
+  a = OneShotArgs{};
+  for (int r = 0; r < h.nranks(); ++r) a.base[r] = h.base(r);
+  a.in_off = (long long)in_off;
+  a.out_off = (long long)out_off;
+  a.ll_off = (long long)ll_off;
+  a.ll_src_bytes = ll_src_bytes;
+  a.bytes = bytes;
+  a.rank = h.rank();
+  a.nranks = h.nranks();
+  a.dtype = dtype;
+  a.redop = redop;
+  a.coll = coll;
+  a.scale = scale;
+  a.do_scale = do_scale ? 1 : 0;
+  a.control = heap.control();
+  a.timeout_ns = (unsigned long long)(timeout_s * 1e9);
+  if (multicast && h.mc_base() == nullptr) throw std::runtime_error("one-shot: the heap has no multicast mapping");
+  a.mc_base = multicast ? h.mc_base() : nullptr;
+  return b;
+}
 
 class DevicePlan {
  public:
@@ -281,6 +329,11 @@ PYBIND11_MODULE(_vbcuda, m) {
       .def_property_readonly("multicast", [](Heap& h) { return h.get().multicast(); })
       .def("base", [](Heap& h, int r) { return (uint64_t)h.get().base(r); });
   py::class_<BoundLaunch>(m, "BoundLaunch").def("launch", &BoundLaunch::launch);
+  py::class_<BoundOneShot>(m, "BoundOneShot").def("launch", &BoundOneShot::launch);
+  m.def("bind_oneshot", &bind_oneshot, py::arg("heap"), py::arg("in_off"), py::arg("out_off"), py::arg("ll_off"),
+        py::arg("ll_src_bytes"), py::arg("bytes"), py::arg("dtype"), py::arg("redop"), py::arg("coll"),
+        py::arg("scale"), py::arg("do_scale"), py::arg("timeout_s"), py::arg("multicast") = false);
+  m.def("oneshot_region_bytes", [](int nranks, int64_t max_bytes) { return oneshot_region_bytes(nranks, max_bytes); });
   py::class_<DevicePlan>(m, "DevicePlan")
       .def(py::init<const std::string&, int, int, int, bool, bool, bool, bool, int, int>(), py::arg("xml"),
            py::arg("rank"), py::arg("nlanes"), py::arg("niters"), py::arg("elide"), py::arg("fuse"),

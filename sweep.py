@@ -3,7 +3,7 @@
     torchrun --nproc-per-node N --master-addr 127.0.0.1 sweep.py [--colls allreduce,allgather]
              [--dtype bfloat16] [--min-bytes 1024] [--max-bytes 1073741824] [--iters 20] [--warmup 5]
              [--method hierarchy|constructive_trees] [--slices S] [--nvls auto|on|off] [--graph]
-             [--check-max-bytes B]
+             [--check-max-bytes B] [--oneshot-max B]
 
 Each point: the synthesized schedule through the sm_100a interpreter (heap
 buffers, CUDA-event device time, max over ranks) and torch.distributed NCCL
@@ -42,6 +42,8 @@ def main():
     ap.add_argument("--slices", type=int, default=None, help="slices per rank (default: P for AR, 1 for AG)")
     ap.add_argument("--nvls", default="auto", choices=("auto", "on", "off"))
     ap.add_argument("--check-max-bytes", type=int, default=1 << 24)
+    ap.add_argument("--oneshot-max", type=int, default=None,
+                    help="largest per-rank payload of the one-shot path (0: always the interpreter)")
     args = ap.parse_args()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -55,7 +57,7 @@ def main():
     heap = args.max_bytes * (world + 2) + (256 << 20)
     multicast = {"auto": world >= 4, "on": True, "off": False}[args.nvls]
     comm = Communicator(heap_bytes=heap, multicast=multicast)
-    eng = CollectiveEngine(comm, method=args.method, slices_per_rank=args.slices)
+    eng = CollectiveEngine(comm, method=args.method, slices_per_rank=args.slices, oneshot_max_bytes=args.oneshot_max)
     rank = comm.rank
     stream = torch.cuda.current_stream()
 
@@ -144,7 +146,8 @@ def main():
                 comm.free(out)
             point = {"coll": coll, "n_gpus": world, "bytes_per_rank": size, "dtype": args.dtype, "graph": args.graph,
                      "time_us": round(ours, 3), "host_enqueue_us": round(ours_host, 2), "busbw_gbs": round(nbytes / ours / 1e3 * factor, 2),
-                     "lanes": plan.nlanes, "iters": plan.niters, "nvls": plan.multicast, "method": args.method,
+                     "path": plan.kind, "lanes": plan.nlanes, "iters": plan.niters, "nvls": plan.multicast,
+                     "method": args.method,
                      "slices": eng.slices_per_rank or (1 if coll == "allgather" else world)}
             if err is not None:
                 point["max_rel_err_vs_fp64"] = err

@@ -31,7 +31,11 @@ def inputs_for(rank, count, dtype, seed):
 def reference(coll, world, count, dtype, seed, op, rank):
     xs = [inputs_for(r, count, dtype, seed).double() for r in range(world)]
     if coll == "allreduce":
-        total = sum(xs) if op in ("sum", "avg") else None
+        if op == "max":
+            return torch.stack(xs).max(dim=0).values
+        if op == "min":
+            return torch.stack(xs).min(dim=0).values
+        total = sum(xs)
         if op == "avg":
             total = total / world
         return total
@@ -112,9 +116,53 @@ def main():
         dist.barrier()
         for t in ([buf] if inplace else [inp, out]):
             comm.free(t)
-    # block-scaled FP8 AllGather through the engine
+    # one-shot flag-in-data path: every case three times in a row (both LL region halves are reused), AllReduce and
+    # AllGather interleaved so they share the launch counter
     from vericcl_b200.models import CollectiveEngine
     eng = CollectiveEngine(comm)
+    oneshot = []
+    for dtype in (torch.float32, torch.bfloat16, torch.float16):
+        esize = torch.tensor([], dtype=dtype).element_size()
+        for nbytes in (8, 1024, 65536, eng.oneshot_max_bytes):
+            count = nbytes // esize
+            for op in ("sum", "avg", "max"):
+                oneshot.append(("allreduce", dtype, op, count, op == "avg"))
+            oneshot.append(("allgather", dtype, "sum", count, False))
+    for coll, dtype, op, count, inplace in oneshot:
+        dname = str(dtype).split(".")[-1]
+        plan = eng.plan(coll, count, dtype, inplace=inplace, op=op)
+        assert plan.kind == "oneshot", plan
+        seed = zlib.crc32(repr(("oneshot", coll, dname, op, count)).encode()) % 100000
+        x = inputs_for(rank, count, dtype, seed).cuda()
+        out_n = count * world if coll == "allgather" else count
+        inp = comm.empty(count, dtype)
+        out = inp if inplace else comm.empty(out_n, dtype)
+        ref = reference(coll, world, count, dtype, seed, op, rank)
+        worst, ok = 0.0, True
+        for rep in range(3):
+            inp.copy_(x)
+            if not inplace:
+                out.fill_(float("nan"))
+            torch.cuda.synchronize()
+            comm.run(plan, inp, out, op=op)
+            torch.cuda.synchronize()
+            comm.check_status()
+            got = out.double().cpu()
+            err = (got - ref).abs().max().item()
+            worst = max(worst, err)
+            scale = max(1.0, ref.abs().max().item())
+            ok = ok and err <= TOL[dtype] * scale * (world if coll != "allgather" else 1) and \
+                torch.isfinite(got).all().item()
+        if not ok:
+            failures += 1
+        if rank == 0 or not ok:
+            print(json.dumps({"rank": rank, "coll": coll, "path": "oneshot", "dtype": dname, "op": op,
+                              "count": count, "inplace": inplace, "max_err": worst, "ok": ok}), flush=True)
+        comm.free(inp)
+        if not inplace:
+            comm.free(out)
+    cases += oneshot
+    # block-scaled FP8 AllGather through the engine
     n = 1 << 14
     x = inputs_for(rank, n, torch.float32, 4242).cuda()
     out = torch.empty(n * world, device="cuda")

@@ -1,0 +1,35 @@
+"""Engine routing on the host: which collectives and sizes take the one-shot path."""
+from types import SimpleNamespace
+
+import torch
+
+from vericcl_b200.models.collectives import ONESHOT_MAX_BYTES, CollectiveEngine
+
+
+class _Comm:
+    def __init__(self, world):
+        self.world = world
+        self.multicast = world >= 4
+        self._mod = SimpleNamespace(max_ctas=lambda threads=512: 148)
+        self.requests = []
+
+    def oneshot_plan(self, collective, max_bytes, multicast=False):
+        self.requests.append((collective, max_bytes))
+        return SimpleNamespace(kind="oneshot", collective=collective, max_bytes=max_bytes)
+
+
+def test_small_allreduce_and_allgather_take_the_oneshot_path():
+    comm = _Comm(8)
+    eng = CollectiveEngine(comm, oneshot_max_bytes=ONESHOT_MAX_BYTES)
+    assert eng.use_oneshot("allreduce", 512, torch.bfloat16)
+    assert eng.use_oneshot("allgather", ONESHOT_MAX_BYTES // 4, torch.float32)
+    assert not eng.use_oneshot("allgather", ONESHOT_MAX_BYTES // 4 + 2, torch.float32)
+    assert not eng.use_oneshot("reduce_scatter", 512, torch.bfloat16)
+    assert not eng.use_oneshot("allreduce", 3, torch.bfloat16)          # 6 bytes: not whole 8-byte units
+    plan = eng.plan("allreduce", 512, torch.bfloat16, inplace=True)
+    assert plan.kind == "oneshot" and comm.requests == [("allreduce", ONESHOT_MAX_BYTES)]
+
+
+def test_single_rank_and_disabled_threshold_use_the_interpreter():
+    assert not CollectiveEngine(_Comm(1)).use_oneshot("allreduce", 512, torch.bfloat16)
+    assert not CollectiveEngine(_Comm(8), oneshot_max_bytes=0).use_oneshot("allreduce", 512, torch.bfloat16)

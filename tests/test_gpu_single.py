@@ -140,3 +140,27 @@ def test_engine_all_gather_fp8_single_rank(comm):
     eng.all_gather_fp8(x, out)
     torch.cuda.synchronize()
     assert torch.allclose(out, x, atol=0.07 * x.abs().max().item())
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_oneshot_kernel_single_rank(comm, dtype):
+    """The one-shot kernel on one rank: AllReduce is the scaled copy, AllGather the copy; the tag counter advances."""
+    n = 4096
+    plan_ar = comm.oneshot_plan("allreduce", 64 << 10)
+    plan_ag = comm.oneshot_plan("allgather", 64 << 10)
+    x = comm.empty(n, dtype)
+    y = comm.empty(n, dtype)
+    src = torch.randn(n, device="cuda").to(dtype)
+    seq0 = comm.status()["ll_seq"]
+    for rep in range(3):
+        x.copy_(src)
+        comm.run(plan_ar, x, y, scale=0.25)
+        comm.run(plan_ag, x, x)
+        torch.cuda.synchronize()
+        comm.check_status()
+        tol = 1e-6 if dtype == torch.float32 else 1e-2
+        assert torch.allclose(y.float(), src.float() * 0.25, atol=tol, rtol=tol)
+        assert torch.equal(x, src)
+    assert comm.status()["ll_seq"] == seq0 + 6
+    comm.free(x)
+    comm.free(y)

@@ -3,7 +3,9 @@
 ``CollectiveEngine`` synthesizes a verified schedule once per (collective,
 rank count, slice count, layout, dtype), compiles it for this rank, picks a
 launch geometry for the message size (lanes × pipeline iterations over the
-co-resident CTA budget), and runs it with the sm_100a interpreter.  Buffers in
+co-resident CTA budget), and runs it with the sm_100a interpreter.  Payloads
+of at most ``oneshot_max_bytes`` per rank (AllReduce, AllGather) run the
+one-shot flag-in-data kernel instead, whose latency is one NVLink trip.  Buffers in
 the communicator's heap run zero-copy; other tensors are staged through heap
 buffers (a local device copy on each side).
 """
@@ -16,6 +18,7 @@ import torch
 from vericcl_b200.errors import RuntimeFailure
 from vericcl_b200.synthesis import schedule_xml
 
+ONESHOT_MAX_BYTES = 256 * 1024      # per-rank payloads up to this size take the one-shot flag-in-data path
 PIECE_MIN_BYTES = 8 * 1024          # smallest useful piece per CTA per iteration
 PIECE_TARGET_BYTES = 512 * 1024     # pipeline a lane's work in pieces of about this size
 MAX_ITERS = 8
@@ -23,10 +26,13 @@ MAX_ITERS = 8
 
 class CollectiveEngine:
     def __init__(self, comm, *, method: str = "hierarchy", slices_per_rank: int | None = None,
-                 max_lanes: int | None = None):
+                 max_lanes: int | None = None, oneshot_max_bytes: int | None = None):
         self.comm = comm
         self.method = method
         self.slices_per_rank = slices_per_rank
+        if oneshot_max_bytes is None:
+            oneshot_max_bytes = int(os.environ.get("VERICCL_ONESHOT_MAX", ONESHOT_MAX_BYTES))
+        self.oneshot_max_bytes = oneshot_max_bytes
         self._max_ctas = comm._mod.max_ctas(512)
         self.max_lanes = max_lanes or self._max_ctas
         self._staging: dict = {}
@@ -50,8 +56,17 @@ class CollectiveEngine:
             return op in ("sum", "avg")
         return collective == "allgather"
 
+    def use_oneshot(self, collective: str, count: int, dtype) -> bool:
+        """Small AllReduce / AllGather payloads go through the one-shot kernel (one NVLink trip, no barrier)."""
+        nbytes = count * torch.tensor([], dtype=dtype).element_size()
+        return (collective in ("allreduce", "allgather") and self.comm.world > 1 and 0 < nbytes
+                <= self.oneshot_max_bytes and nbytes % 8 == 0)
+
     def plan(self, collective: str, count: int, dtype, *, inplace: bool, op: str = "sum"):
         world = self.comm.world
+        if self.use_oneshot(collective, count, dtype):
+            return self.comm.oneshot_plan(collective, self.oneshot_max_bytes,
+                                          multicast=self.comm.multicast and world > 2)
         default = 1 if collective in ("allgather", "broadcast") else world
         slices = self.slices_per_rank or default
         if collective in ("reduce_scatter", "alltoall") and slices % world:

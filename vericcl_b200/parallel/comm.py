@@ -48,6 +48,24 @@ class PlanHandle:
     slots: tuple
     checked: set
     multicast: bool = False
+    kind: str = "interp"
+
+
+@dataclass
+class OneShotPlan:
+    """Small-message AllReduce / AllGather with the one-shot flag-in-data kernel (no device program)."""
+    collective: str
+    max_bytes: int
+    checked: set
+    kind: str = "oneshot"
+    nlanes: int = 0
+    niters: int = 1
+    multicast: bool = False
+    xml: str | None = None
+    device_plan: object = None
+
+
+ONESHOT_COLLS = {"allreduce": 0, "allgather": 1}
 
 
 class Communicator:
@@ -89,6 +107,7 @@ class Communicator:
         self._bound: dict = {}
         self._plans: dict = {}
         self._scratch: dict = {}
+        self._ll = None              # (offset, bytes per source) of the one-shot LL region
         self._lock = threading.Lock()
         self._closed = False
 
@@ -144,7 +163,7 @@ class Communicator:
 
     def free(self, tensor: torch.Tensor) -> None:
         ptr = tensor.data_ptr()
-        self._bound = {k: v for k, v in self._bound.items() if ptr not in (k[1], k[2])}
+        self._bound = {k: v for k, v in self._bound.items() if ptr not in k[1:4]}
         offset = self._allocs.pop(ptr, None)
         if offset is not None:
             self.heap.free(offset)
@@ -189,6 +208,70 @@ class Communicator:
                 self._scratch[key] = (self.heap.alloc(need), need)
             return self._scratch[key][0]
 
+    # -- one-shot small-message path ---------------------------------------------
+    def oneshot_plan(self, collective: str, max_bytes: int, *, multicast: bool = False) -> OneShotPlan:
+        """Plan handle for the one-shot kernel; reserves the LL region on first use (collective call).
+
+        With ``multicast`` (and an NVLS-bound heap) each line is pushed once
+        through the multicast address instead of once per peer.
+        """
+        if collective not in ONESHOT_COLLS:
+            raise RuntimeFailure("the one-shot path covers allreduce and allgather, not %s" % collective)
+        self._ensure_ll(max_bytes)
+        multicast = bool(multicast and self.multicast)
+        key = ("oneshot", collective, multicast)
+        plan = self._plans.get(key)
+        if plan is None or plan.max_bytes < max_bytes:
+            plan = OneShotPlan(collective, max_bytes, set(), multicast=multicast)
+            self._plans[key] = plan
+        return plan
+
+    def _ensure_ll(self, max_bytes: int) -> None:
+        need = -(-max_bytes // 8) * 16
+        if self._ll is not None and self._ll[1] >= need:
+            return
+        if self._ll is not None:
+            # a larger region replaces the old one; nothing may still be using it
+            torch.cuda.synchronize()
+            self.barrier()
+            self.heap.free(self._ll[0])
+        total = int(self._mod.oneshot_region_bytes(self.world, max_bytes))
+        offset = self.heap.alloc(total)
+        self.heap.tensor(offset, total // 4, 0).zero_()
+        torch.cuda.synchronize()
+        self.barrier()
+        self._ll = (offset, need)
+        self._bound = {k: v for k, v in self._bound.items() if k[0] != "oneshot"}
+
+    def _run_oneshot(self, plan: OneShotPlan, inp, out, op, scale, stream, count_per_rank) -> None:
+        key = ("oneshot", id(plan), inp.data_ptr(), out.data_ptr(), count_per_rank, inp.dtype, op, scale,
+               inp.numel())
+        bound = self._bound.get(key)
+        if bound is None:
+            if inp.dtype != out.dtype:
+                raise RuntimeFailure("input and output dtypes differ")
+            count = inp.numel() if count_per_rank is None else count_per_rank
+            nbytes = count * inp.element_size()
+            if nbytes > plan.max_bytes:
+                raise RuntimeFailure("one-shot plan holds %d bytes per rank, call has %d" % (plan.max_bytes, nbytes))
+            in_off, out_off = self.offset_of(inp), self.offset_of(out)
+            offsets = (in_off, out_off, nbytes)
+            if offsets not in plan.checked:
+                got = self.all_gather_object(offsets)
+                if any(o != offsets for o in got):
+                    raise RuntimeFailure("one-shot buffers are not symmetric across ranks: %s" % (got,))
+                plan.checked.add(offsets)
+            factor = 1.0 / self.world if op == "avg" else 1.0
+            if scale is not None:
+                factor *= scale
+            redop = REDOPS["sum" if op == "avg" else op]
+            bound = self._mod.bind_oneshot(self.heap, in_off, out_off, self._ll[0], self._ll[1], nbytes,
+                                           DTYPE_CODES[inp.dtype], redop, ONESHOT_COLLS[plan.collective],
+                                           float(factor), factor != 1.0, self.timeout_s,
+                                           plan.multicast and self.multicast)
+            self._bound[key] = bound
+        bound.launch((torch.cuda.current_stream() if stream is None else stream).cuda_stream)
+
     def run(self, plan: PlanHandle, inp: torch.Tensor, out: torch.Tensor, *, op: str = "sum",
             scale: float | None = None, stream=None, count_per_rank: int | None = None, nbatch: int = 1,
             in_stride: int = 0, out_stride: int = 0, trace: torch.Tensor | None = None) -> None:
@@ -199,6 +282,11 @@ class Communicator:
         gradient bucket of a flat buffer); the instances pipeline through the same
         persistent CTAs and only the last one waits for peers at the end.
         """
+        if plan.kind == "oneshot":
+            if nbatch != 1 or trace is not None:
+                raise RuntimeFailure("the one-shot path runs one instance without tracing")
+            self._run_oneshot(plan, inp, out, op, scale, stream, count_per_rank)
+            return
         if trace is None:
             fast = self._bound.get((id(plan), inp.data_ptr(), out.data_ptr(), count_per_rank, inp.dtype, op, scale,
                                     nbatch, in_stride, out_stride))
