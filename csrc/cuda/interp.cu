@@ -526,8 +526,9 @@ cudaError_t launch_interp(const InterpArgs& a, cudaStream_t stream, int threads)
 }
 
 void apply_emulation_env(InterpArgs* a) {
-  // VERICCL_EMULATE="group=4,gbps=25": pace data steps that read another group of 4 ranks so the
-  // inter-group traffic of the launch runs at an emulated 25 GB/s (split across its CTAs).
+  // VERICCL_EMULATE="group=4,gbps=25": pace data steps that read another group of 4 ranks as if each
+  // group's inter-group traffic shared one 25 GB/s link: every rank of the group gets an even share
+  // (25/4 GB/s), split across the launch's CTAs.
   const char* env = getenv("VERICCL_EMULATE");
   a->pace_group = 0;
   a->pace_ns_per_byte = 0.f;
@@ -536,7 +537,7 @@ void apply_emulation_env(InterpArgs* a) {
   double gbps = 0;
   if (sscanf(env, "group=%d,gbps=%lf", &group, &gbps) == 2 && group > 0 && gbps > 0) {
     a->pace_group = group;
-    a->pace_ns_per_byte = (float)((double)(a->nblocks * a->nlanes) / gbps);
+    a->pace_ns_per_byte = (float)((double)(a->nblocks * a->nlanes) * group / gbps);
   }
 }
 

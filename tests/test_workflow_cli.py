@@ -69,3 +69,30 @@ def test_module_entry_point(inputs, tmp_path):
     proc = subprocess.run([sys.executable, "-m", "vericcl_b200", "--version"], capture_output=True, text=True,
                           env=env, timeout=120)
     assert proc.returncode == 0 and "vericcl_b200" in proc.stdout
+
+
+def test_measured_rejection_is_not_repeated(tmp_path):
+    """A repair candidate the paired measurement rejected is not measured again in later rounds."""
+    from types import SimpleNamespace
+
+    from vericcl_b200.execution.context import RunContext
+    from vericcl_b200.input.loader import load_request
+    from vericcl_b200.online.loop import loop_documents
+    from vericcl_b200.workflow import PrimaryWorkflow
+    docs = loop_documents(groups=2, per_group=4, inter_gbps=25.0, size_bytes=128 << 20, rounds=3,
+                          datatype="float32", pairs=4)
+    docs["sketch"]["calibration"]["enabled"] = False
+    files = write_documents(tmp_path / "in", docs)
+    req = load_request(files)
+    ctx = RunContext.create(tmp_path, "c", "solve", run_id="r", input_files=files)
+    ctx.update_run_json(effective_request=dict(req.request_config))
+    calls = []
+
+    def measure(incumbent, candidate):
+        calls.append(candidate.xml)
+        return SimpleNamespace(accepted=False, reason="slower")
+    wf = PrimaryWorkflow(req, ctx, measure=measure)
+    result = wf.run()
+    assert result.status == "ok"
+    assert calls and len(calls) == len(set(calls))
+    assert len(result.rounds) == 3

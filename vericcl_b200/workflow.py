@@ -81,6 +81,7 @@ class PrimaryWorkflow:
         self.verify_inputs = verify_inputs or {}
         self.probe_executor = probe_executor
         self.measure = measure
+        self.measured_rejects: set = set()
         budgets = dict(request.request_config["sketch"]["budgets"])
         self.budgets = BudgetManager(budgets, cpu_budget=request.solver.cpu_budget)
         self.candidates = []
@@ -279,12 +280,17 @@ class PrimaryWorkflow:
                 record["result"] = "repair budget exhausted"
                 self.rounds.append(record)
                 return "repair budget exhausted"
-            best = min((c for c in candidates if accept_candidate(self.incumbent, c)),
-                       key=lambda c: c.t_pred_us, default=None)
+            # a candidate the paired measurement already turned down is not measured again
+            fresh = [c for c in candidates if accept_candidate(self.incumbent, c)
+                     and self._xml_digest(c) not in self.measured_rejects]
+            if len(fresh) < len([c for c in candidates if accept_candidate(self.incumbent, c)]):
+                record["skipped_rejected"] = True
+            best = min(fresh, key=lambda c: c.t_pred_us, default=None)
             if best is not None and self.measure is not None:
                 verdict = self.measure(self.incumbent, best)
                 record["measured"] = verdict.__dict__ if hasattr(verdict, "__dict__") else verdict
                 if not getattr(verdict, "accepted", False):
+                    self.measured_rejects.add(self._xml_digest(best))
                     best = None
             if best is None:
                 record["result"] = "no improvement"
@@ -297,6 +303,11 @@ class PrimaryWorkflow:
             self.rounds.append(record)
             self.checkpoint("round_%d" % index)
         return "round limit"
+
+    @staticmethod
+    def _xml_digest(bundle) -> str:
+        import hashlib
+        return hashlib.sha256(bundle.xml.encode()).hexdigest()
 
     def run(self) -> RunResult:
         t0 = time.monotonic()
