@@ -84,9 +84,25 @@ def new_run(args) -> int:
     wf = PrimaryWorkflow(request, ctx, purpose=purpose, tune=getattr(args, "tune", False), model=model,
                          verify_inputs=verify_inputs, probe_executor=executor, measure=measure)
     result = wf.run()
+    if measure is not None and result.status == "ok" and (ctx.directory / "schedule.xml").exists():
+        _trace_best(request, ctx)
     print(json.dumps({"run": str(ctx.directory), "status": result.status, "stop_reason": result.stop_reason,
                       "t_pred_us": None if result.best is None else result.best["t_pred_us"]}))
     return 0 if result.status == "ok" else 5
+
+
+def _trace_best(request, ctx) -> None:
+    """With trace_and_measure on GPUs: one traced invocation of the published schedule → ``trace.json``."""
+    import shutil
+    from vericcl_b200.online.trace_worker import capture_schedule_trace
+    summary = capture_schedule_trace(ctx.directory / "schedule.xml", request.rank_count,
+                                     request.hyperparameters.total_size_bytes, request.collective.datatype,
+                                     ctx.process / "traces")
+    if "error" in summary:
+        ctx.emit("trace_failed", reason=summary["error"])
+        return
+    shutil.copyfile(summary["path"], ctx.directory / "trace.json")
+    ctx.emit("trace_captured", global_span_us=summary["global_span_us"])
 
 
 def inspect_run(args) -> int:

@@ -18,7 +18,7 @@ import torch
 from vericcl_b200.errors import RuntimeFailure
 from vericcl_b200.synthesis import schedule_xml
 
-ONESHOT_MAX_BYTES = 256 * 1024      # per-rank payloads up to this size take the one-shot flag-in-data path
+ONESHOT_MAX_BYTES = 1 << 20          # per-rank payloads up to this size take the one-shot flag-in-data path
 PIECE_MIN_BYTES = 8 * 1024          # smallest useful piece per CTA per iteration
 PIECE_TARGET_BYTES = 512 * 1024     # pipeline a lane's work in pieces of about this size
 MAX_ITERS = 8

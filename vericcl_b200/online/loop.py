@@ -112,21 +112,14 @@ def _measure_first_and_final(run_dir: Path, files: dict) -> dict:
 
 
 def _capture_trace(run_dir: Path, ranks: int, size_bytes: int, datatype: str) -> dict:
-    """One traced invocation of the final schedule (per-step timeline under ``process/traces``)."""
-    import subprocess
-    out = run_dir / "process" / "traces"
-    root = Path(__file__).resolve().parents[2]
-    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=%d" % ranks,
-           "--master-addr", "127.0.0.1", "--master-port", "29633", "-m", "vericcl_b200.online.trace_worker",
-           "--out", str(out), "--xml", str(run_dir / "schedule.xml"), "--bytes-per-rank", str(size_bytes),
-           "--dtype", datatype, "--nvls", "off", "--lanes", "32"]
-    env = dict(os.environ, PYTHONPATH=str(root) + os.pathsep + os.environ.get("PYTHONPATH", ""))
-    res = subprocess.run(cmd, env=env, cwd=str(root), capture_output=True, text=True, timeout=600)
-    if res.returncode != 0 or not (out / "trace.json").exists():
-        return {"error": "trace capture failed (%d): %s" % (res.returncode, res.stderr[-500:])}
-    report = json.loads((out / "trace.json").read_text())
-    return {"path": str(out / "trace.json"), "global_span_us": report["global_span_us"],
-            "tails": report["tails"][:3]}
+    """The run's trace of the final schedule (the CLI captures it when measurement is on), else capture one."""
+    from vericcl_b200.online.trace_worker import capture_schedule_trace
+    path = run_dir / "trace.json"
+    if path.exists():
+        report = json.loads(path.read_text())
+        return {"path": str(path), "global_span_us": report["global_span_us"], "tails": report["tails"][:3]}
+    return capture_schedule_trace(run_dir / "schedule.xml", ranks, size_bytes, datatype,
+                                  run_dir / "process" / "traces")
 
 
 def main(argv=None) -> int:

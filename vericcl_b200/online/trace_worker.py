@@ -67,6 +67,25 @@ def timeline(traces, clock_maps):
     return rows
 
 
+def capture_schedule_trace(xml_path, ranks: int, bytes_per_rank: int, datatype: str, out_dir, *, lanes: int = 32,
+                           port: int = 29633, timeout_s: float = 600.0) -> dict:
+    """Run this worker under torchrun on ``ranks`` local GPUs for one schedule; summary of ``trace.json``."""
+    import subprocess
+    out_dir = Path(out_dir)
+    root = Path(__file__).resolve().parents[2]
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=%d" % ranks,
+           "--master-addr", "127.0.0.1", "--master-port", str(port), "-m", "vericcl_b200.online.trace_worker",
+           "--out", str(out_dir), "--xml", str(xml_path), "--bytes-per-rank", str(bytes_per_rank),
+           "--dtype", datatype, "--nvls", "off", "--lanes", str(lanes)]
+    env = dict(os.environ, PYTHONPATH=str(root) + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    res = subprocess.run(cmd, env=env, cwd=str(root), capture_output=True, text=True, timeout=timeout_s)
+    if res.returncode != 0 or not (out_dir / "trace.json").exists():
+        return {"error": "trace capture failed (%d): %s" % (res.returncode, res.stderr[-500:])}
+    report = json.loads((out_dir / "trace.json").read_text())
+    return {"path": str(out_dir / "trace.json"), "global_span_us": report["global_span_us"],
+            "tails": report["tails"][:3]}
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(prog="vericcl_b200.online.trace_worker")
     ap.add_argument("--out", required=True)
