@@ -231,7 +231,7 @@ def main():
     bus = ar.bus_bytes_per_rank()
     busbw = bus / (ms * 1e-3) / 1e9
     value = busbw * world
-    launches = args.steps * (ar.buckets if args.per_bucket else 1)
+    launches = args.steps * (ar.buckets if args.per_bucket else ar.launches_per_sync)
 
     nccl = None
     if world > 1 and not args.no_nccl:

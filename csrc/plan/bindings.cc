@@ -22,6 +22,7 @@ py::dict stats_dict(const CompileStats& s) {
   d["remote_waits"] = s.remote_waits;
   d["scale_steps"] = s.scale_steps;
   d["deferred_waits"] = s.deferred_waits;
+  d["dropped_nops"] = s.dropped_nops;
   return d;
 }
 

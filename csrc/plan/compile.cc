@@ -82,6 +82,7 @@ class Compiler {
     if (o_.merge_blocks) merge_blocks();
     if (o_.multicast && merged_ && P_ > 1) map_multicast();
     dedupe_start_waits();
+    if (merged_) drop_idle_nops();
     emit();
     deadlock_check();
     CompiledPlan plan;
@@ -838,6 +839,59 @@ class Compiler {
             if (kv.first.second < 0) seen.insert(kv.first.first);
         }
       }
+  }
+
+  // A merged NOP step that waits for nothing and whose events no step waits
+  // for does no work: it marks an elided send or a copy that a multicast
+  // store replaced.  Such steps are removed (every rank keeps at least one
+  // step) and the events of later steps are renumbered in every wait.  End
+  // waits are unaffected: they target the block's final event, which emit
+  // derives from the final step count.
+  void drop_idle_nops() {
+    std::vector<std::set<int>> named(P_);
+    for (int r = 0; r < P_; ++r)
+      for (auto& ps : pending_[r][0])
+        for (auto& kv : ps.waits)
+          if (kv.first.second >= 0) named[kv.first.first].insert((kv.second - 1) / 2);
+    std::vector<std::vector<int>> newidx(P_);
+    for (int r = 0; r < P_; ++r) {
+      auto& steps = pending_[r][0];
+      std::vector<bool> keep(steps.size(), true);
+      int kept = 0;
+      for (int i = 0; i < (int)steps.size(); ++i) {
+        const PendingStep& ps = steps[i];
+        if (ps.st.op == OP_NOP && ps.waits.empty() && !named[r].count(i)) keep[i] = false;
+        kept += keep[i] ? 1 : 0;
+      }
+      if (kept == 0 && !steps.empty()) keep.back() = true;
+      newidx[r].assign(steps.size(), -1);
+      int n = 0;
+      for (int i = 0; i < (int)steps.size(); ++i)
+        if (keep[i]) newidx[r][i] = n++;
+      stats_.dropped_nops += (int)steps.size() - n;
+    }
+    for (int r = 0; r < P_; ++r) {
+      std::vector<PendingStep> out;
+      auto& steps = pending_[r][0];
+      for (int i = 0; i < (int)steps.size(); ++i) {
+        if (newidx[r][i] < 0) continue;
+        PendingStep ps = steps[i];
+        EventSet waits;
+        for (auto& kv : ps.waits) {
+          if (kv.first.second < 0) {
+            merge(waits, EventSet{{kv.first, kv.second}});
+            continue;
+          }
+          int target = newidx[kv.first.first][(kv.second - 1) / 2];
+          if (target < 0) fail("a wait names a removed step");
+          merge(waits, EventSet{{kv.first, 2 * target + ((kv.second % 2) ? 1 : 2)}});
+        }
+        ps.waits = std::move(waits);
+        out.push_back(std::move(ps));
+      }
+      steps = std::move(out);
+      dsteps_count_[r].assign(1, (int)steps.size());
+    }
   }
 
   void emit() {

@@ -186,8 +186,32 @@ InterpResult cpu_interpret(const CompiledPlan& plan, HostBuffers& bufs, int dtyp
                 store(dst, dtype, dst_off + e, acc);
               }
             }
+          } else if (st.op == OP_MC_ALLREDUCE || st.op == OP_MC_STORE) {
+            // NVLS emulation: the switch reads the source chunk of every rank (ld_reduce, sum) or this
+            // rank's source (st) and writes the result to the destination chunk of every rank
+            PieceRange pr = piece_range(chunk_elems, piece_elems, c.it, L, c.lane);
+            const DevSrc& sr = rp.srcs[st.src_begin];
+            for (int k = 0; k < st.cnt; ++k) {
+              long long src_off = (long long)(sr.chunk + k) * chunk_elems;
+              long long dst_off = (long long)(st.dst_chunk + k) * chunk_elems;
+              for (int q = 0; q < P; ++q)
+                if (dst_off + pr.hi > buf_elems(q, st.dst_buf) || src_off + pr.hi > buf_elems(q, sr.buf)) {
+                  res.error = "multicast range out of bounds";
+                  return res;
+                }
+              for (long long e = pr.lo; e < pr.hi; ++e) {
+                float acc = 0.f;
+                if (st.op == OP_MC_ALLREDUCE) {
+                  for (int q = 0; q < P; ++q) acc += load(base_ptr(q, sr.buf), dtype, src_off + e);
+                } else {
+                  acc = load(base_ptr(c.rank, sr.buf), dtype, src_off + e);
+                }
+                if (st.flags & F_SCALE) acc *= scale;
+                for (int q = 0; q < P; ++q) store(base_ptr(q, st.dst_buf), dtype, dst_off + e, acc);
+              }
+            }
           } else if (st.op != OP_NOP) {
-            res.error = "multicast ops need the GPU";
+            res.error = "this op needs the GPU";
             return res;
           }
           if (st.flags & F_PUB_DONE) publish(2 * c.s + 2, c.it);

@@ -296,6 +296,7 @@ class DevicePlan {
     d["fused"] = plan_.options.fuse_chains;
     d["multicast_ops"] = plan_.stats.multicast_ops;
     d["deferred_waits"] = plan_.stats.deferred_waits;
+    d["dropped_nops"] = plan_.stats.dropped_nops;
     return d;
   }
 

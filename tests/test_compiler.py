@@ -78,3 +78,32 @@ def test_rejects_cyclic_schedule():
 def test_xml_reader_rejects_garbage():
     with pytest.raises(SemanticError):
         compile_xml("<algo ngpus='2'><gpu></algo>")
+
+
+@pytest.mark.parametrize("coll,inplace", [("allreduce", True), ("allreduce", False), ("allgather", False),
+                                          ("allgather", True)])
+@pytest.mark.parametrize("p", [4, 8])
+@pytest.mark.parametrize("lanes,iters", [(1, 1), (3, 2)])
+def test_multicast_programs_match_reference(coll, inplace, p, lanes, iters):
+    """NVLS-mapped programs (with idle steps removed) through the CPU oracle's multicast emulation."""
+    slices = p if coll == "allreduce" else 1
+    xml = schedule_xml(coll, p, slices, inplace=inplace)
+    c = compile_xml(xml, nlanes=lanes, niters=iters, multicast=True)
+    if not (coll == "allgather" and inplace):       # in-place AllGather has no owner copy to broadcast
+        assert c.stats["multicast_ops"] > 0 and c.stats["dropped_nops"] > 0
+    count = p * slices * 8 * 3
+    for seed in range(2):
+        rng = np.random.default_rng(seed)
+        ins = [rng.uniform(-1, 1, count).astype(np.float32) for _ in range(p)]
+        exp = reference_result(coll, [a.astype(np.float64) for a in ins], rank_count=p)
+        outs = run_cpu(c, ins, seed=seed, launches=2 if not inplace else 1)
+        for r in range(p):
+            np.testing.assert_allclose(outs[r][:len(exp[r])], exp[r], atol=1e-5)
+
+
+def test_idle_nops_removed_and_waits_renumbered():
+    xml = schedule_xml("allreduce", 8, 8, inplace=True)
+    plain = compile_xml(xml, nlanes=1)
+    assert plain.stats["dropped_nops"] == 48
+    text = plain.describe(0)
+    assert "nop" not in text and "wait(r1,b0,e2)" in text

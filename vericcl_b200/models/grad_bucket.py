@@ -48,9 +48,10 @@ class GradBucketAllReduce:
 
         By default all buckets run in one persistent launch (the bucket index is an
         outer pipeline dimension of the replayed schedule); ``batched=False`` issues one
-        launch per bucket.
+        launch per bucket.  Buckets small enough for the one-shot path are launched one by
+        one (that kernel has no batched form; each launch is a few microseconds).
         """
-        if batched:
+        if batched and self.plan.kind != "oneshot":
             b = self.bucket(0)
             self.comm.run(self.plan, b, b, op="sum", scale=self.scale, stream=stream, nbatch=self.buckets,
                           in_stride=self.bucket_elems, out_stride=self.bucket_elems)
@@ -61,7 +62,7 @@ class GradBucketAllReduce:
 
     @property
     def launches_per_sync(self) -> int:
-        return 1
+        return self.buckets if self.plan.kind == "oneshot" else 1
 
     def bus_bytes_per_rank(self) -> float:
         """NCCL-convention bus bytes of one full sync (2(P-1)/P × bytes; P=1 counts the bytes once)."""
