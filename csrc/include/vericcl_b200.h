@@ -16,7 +16,7 @@
 extern "C" {
 #endif
 
-#define VERICCL_B200_ABI_VERSION 1
+#define VERICCL_B200_ABI_VERSION 2
 
 typedef enum vb_result {
   VB_OK = 0,
@@ -52,6 +52,10 @@ vb_result vb_execute(vb_context* ctx, const void* in, void* out, size_t count, i
                      void* cuda_stream, double timeout_s);
 /* Device status word (0 ok, 1 timeout, 2 aborted, 3 bad geometry) and launch epoch; never blocks. */
 vb_result vb_status(vb_context* ctx, int* device_status, unsigned long long* epoch);
+/* Record per-step timestamps in the next vb_execute (after vb_prepare; not collective). */
+vb_result vb_trace_arm(vb_context* ctx);
+/* Write the traced execution of this rank as a trace file (40-byte header, 64-byte records). */
+vb_result vb_trace_write(vb_context* ctx, const char* path);
 vb_result vb_release(vb_context* ctx);
 vb_result vb_close(vb_context* ctx, double timeout_s);
 vb_result vb_destroy(vb_context* ctx);

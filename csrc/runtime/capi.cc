@@ -4,6 +4,7 @@
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <memory>
 #include <mutex>
@@ -15,6 +16,7 @@
 #include "vb/launch.h"
 #include "vb/plan.h"
 #include "vb/symheap.h"
+#include "vb/trace_io.h"
 
 using namespace vb;
 
@@ -33,6 +35,8 @@ struct vb_context {
   bool unresolved = false;
   std::string error;
   cudaStream_t abort_stream = nullptr;
+  unsigned long long* trace_dev = nullptr;   // per-step trace of the next (armed) or last traced execution
+  bool trace_armed = false, trace_ready = false;
 };
 
 namespace {
@@ -61,7 +65,25 @@ T* upload(const std::vector<T>& v) {
 void free_plan(vb_context* c) {
   cudaFree(c->blocks); cudaFree(c->steps); cudaFree(c->srcs); cudaFree(c->waits);
   c->blocks = nullptr; c->steps = nullptr; c->srcs = nullptr; c->waits = nullptr;
+  cudaFree(c->trace_dev);
+  c->trace_dev = nullptr;
+  c->trace_armed = c->trace_ready = false;
   c->prepared = false;
+}
+
+TraceLayout trace_layout(const vb_context* c) {
+  TraceLayout l;
+  const RankProgram& rp = c->plan.ranks[c->rank];
+  l.rank = c->rank;
+  l.nlanes = c->plan.options.nlanes;
+  l.niters = c->plan.options.niters;
+  for (const DevBlock& b : rp.blocks) {
+    std::vector<int> ops;
+    for (int s = 0; s < b.nsteps; ++s) ops.push_back(rp.steps[b.step_begin + s].op);
+    l.max_steps = std::max(l.max_steps, b.nsteps);
+    l.block_ops.push_back(std::move(ops));
+  }
+  return l;
 }
 
 size_t esize(int dtype) { return dtype == VB_FLOAT32 ? 4 : 2; }
@@ -202,8 +224,18 @@ extern "C" vb_result vb_execute(vb_context* c, const void* in, void* out, size_t
     a.control = reinterpret_cast<Control*>(c->heap->base(c->rank));
     a.timeout_ns = (unsigned long long)(timeout_s * 1e9);
     apply_emulation_env(&a);
+    if (c->trace_armed) {
+      TraceLayout l = trace_layout(c);
+      cudaMemsetAsync(c->trace_dev, 0, trace_words(l) * sizeof(unsigned long long), stream);
+      a.trace_buf = c->trace_dev;
+      a.trace_stride = l.niters * l.max_steps;
+    }
     if (a.nblocks * a.nlanes > interp_max_ctas(512)) return fail(c, VB_INVALID, "too many CTAs for the device");
     cudaError_t e = launch_interp(a, stream, 512);
+    if (c->trace_armed) {
+      c->trace_armed = false;
+      c->trace_ready = (e == cudaSuccess);
+    }
     if (e != cudaSuccess) return fail(c, VB_FAILED, cudaGetErrorString(e));
     cudaMemcpyAsync(out, c->heap->base(c->rank) + c->stage_out, user_out, cudaMemcpyDeviceToDevice, stream);
     cudaEvent_t done;
@@ -223,6 +255,42 @@ extern "C" vb_result vb_execute(vb_context* c, const void* in, void* out, size_t
     Control ctl;
     cudaMemcpy(&ctl, a.control, sizeof ctl, cudaMemcpyDeviceToHost);
     if (ctl.status != ST_OK) return fail(c, VB_FAILED, "device status " + std::to_string(ctl.status));
+  } catch (const std::exception& e) {
+    return fail(c, VB_FAILED, e.what());
+  }
+  return VB_OK;
+}
+
+extern "C" vb_result vb_trace_arm(vb_context* c) {
+  if (!c) return VB_INVALID;
+  if (c->closed) return VB_CLOSED;
+  Guard g(c);
+  if (!g.ok) return VB_BUSY;
+  if (!c->prepared) return fail(c, VB_INVALID, "no prepared schedule");
+  TraceLayout l = trace_layout(c);
+  size_t words = std::max<size_t>(trace_words(l), 3);
+  cudaFree(c->trace_dev);
+  c->trace_dev = nullptr;
+  if (cudaMalloc(&c->trace_dev, words * sizeof(unsigned long long)) != cudaSuccess)
+    return fail(c, VB_FAILED, "cannot allocate the trace buffer");
+  c->trace_armed = true;
+  c->trace_ready = false;
+  return VB_OK;
+}
+
+extern "C" vb_result vb_trace_write(vb_context* c, const char* path) {
+  if (!c || !path) return VB_INVALID;
+  if (c->closed) return VB_CLOSED;
+  Guard g(c);
+  if (!g.ok) return VB_BUSY;
+  if (!c->trace_ready) return fail(c, VB_INVALID, "no traced execution to write");
+  try {
+    TraceLayout l = trace_layout(c);
+    std::vector<uint64_t> raw(trace_words(l));
+    if (!raw.empty() &&
+        cudaMemcpy(raw.data(), c->trace_dev, raw.size() * sizeof(uint64_t), cudaMemcpyDeviceToHost) != cudaSuccess)
+      return fail(c, VB_FAILED, "cannot read the trace buffer");
+    write_trace_file(path, l, raw);
   } catch (const std::exception& e) {
     return fail(c, VB_FAILED, e.what());
   }
@@ -275,6 +343,7 @@ extern "C" vb_result vb_destroy(vb_context* c) {
   if (!c) return VB_INVALID;
   if (c->unresolved) return VB_UNRESOLVED;
   if (c->abort_stream) cudaStreamDestroy(c->abort_stream);
+  cudaFree(c->trace_dev);
   delete c;
   return VB_OK;
 }

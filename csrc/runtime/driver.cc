@@ -4,7 +4,7 @@
 // config: {"xml": path, "rank": r, "nranks": p, "device": d, "control_address": "127.0.0.1",
 //          "control_port": port, "session": id, "count": elements per rank, "dtype": 0|1|2,
 //          "redop": 0..3, "scale": f, "nlanes": L, "niters": I, "warmup": W, "iters": K,
-//          "timeout_s": t, "receipt": path}
+//          "timeout_s": t, "receipt": path[, "trace": path of a per-step trace of the last invocation]}
 // Inputs follow the analytic pattern value = 1 + ((3*rank + i) mod 5); outputs
 // are checked on the device in fp64 against the analytic collective result.
 #include <cuda_runtime.h>
@@ -71,7 +71,12 @@ int main(int argc, char** argv) {
   cudaEvent_t e0, e1;
   cudaEventCreate(&e0);
   cudaEventCreate(&e1);
+  const Json* trace_path = cfg.get("trace");
   for (int i = 0; i < warmup + iters; ++i) {
+    if (trace_path && i == warmup + iters - 1 && vb_trace_arm(ctx) != VB_OK) {
+      fprintf(stderr, "vb_trace_arm failed: %s\n", vb_last_error(ctx));
+      return 8;
+    }
     cudaEventRecord(e0, s);
     r = vb_execute(ctx, in, out, count, dtype, redop, scale, s, timeout);
     cudaEventRecord(e1, s);
@@ -80,6 +85,10 @@ int main(int argc, char** argv) {
     float ms = 0;
     cudaEventElapsedTime(&ms, e0, e1);
     if (i >= warmup) times.push_back(ms * 1e3);
+  }
+  if (trace_path && vb_trace_write(ctx, trace_path->as_string().c_str()) != VB_OK) {
+    fprintf(stderr, "vb_trace_write failed: %s\n", vb_last_error(ctx));
+    return 8;
   }
   cudaMemsetAsync(bad, 0, sizeof(unsigned long long), s);
   launch_check(out, (long long)out_count, dtype, coll == "allgather" ? 1 : 0, redop, nranks, rank, (long long)count,

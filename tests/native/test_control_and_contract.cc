@@ -7,6 +7,7 @@
 
 #include "vb/contract.h"
 #include "vb/control.h"
+#include "vb/trace_io.h"
 
 using namespace vb;
 
@@ -18,7 +19,7 @@ bool throws(F f) {
   return false;
 }
 
-int main() {
+int main(int argc, char** argv) {
   // FIPS 180-2 example vectors
   CHECK(sha256_hex("abc") == "ba7816bf8f01cfea414140de5dae2223b00361a396177a9cb410ff61f20015ad");
   CHECK(sha256_hex("") == "e3b0c44298fc1c149afbf4c8996fb92427ae41e4649b934ca495991b7852b855");
@@ -63,6 +64,29 @@ int main() {
   int p4 = w0.coordinator()->port();
   bool rejected = throws([&] { ControlTransport t(1, 2, "127.0.0.1", p4, "other"); t.gather("INIT", "", Deadline::after(2)); });
   CHECK(rejected);
+  // trace file: block 0 has 3 steps, block 1 has 1 step; 2 lanes, 2 iterations
+  if (argc > 1) {
+    TraceLayout l;
+    l.rank = 3;
+    l.nlanes = 2;
+    l.niters = 2;
+    l.max_steps = 3;
+    l.block_ops = {{1, 2, 0}, {4}};
+    std::vector<uint64_t> raw(trace_words(l), 0);
+    CHECK(raw.size() == (size_t)2 * 2 * 2 * 3 * 3);
+    for (int cta = 0; cta < 4; ++cta) {
+      int nsteps = (int)l.block_ops[cta / 2].size();
+      for (int it = 0; it < 2; ++it)
+        for (int s = 0; s < nsteps; ++s) {
+          size_t slot = (size_t)cta * 6 + (size_t)it * nsteps + s;
+          raw[slot * 3] = 1000 * cta + 100 * it + 10 * s + 1;
+          raw[slot * 3 + 1] = 1000 * cta + 100 * it + 10 * s + 5;
+          raw[slot * 3 + 2] = 2;
+        }
+    }
+    CHECK(write_trace_file(argv[1], l, raw) == 2 * 2 * 3 + 2 * 2 * 1);
+    CHECK(throws([&] { write_trace_file(argv[1], l, std::vector<uint64_t>(3)); }));
+  }
   printf("native cpu tests passed\n");
   return 0;
 }

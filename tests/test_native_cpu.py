@@ -5,11 +5,23 @@ from vericcl_b200.execution.native import combine_schedule_results
 from vericcl_b200.ops.build import build_native_tests
 
 
-def test_native_contract_and_control_plane():
+def test_native_contract_and_control_plane(tmp_path):
     binary = build_native_tests()
-    proc = subprocess.run([str(binary)], capture_output=True, text=True, timeout=120)
+    trace = tmp_path / "trace-rank3.bin"
+    proc = subprocess.run([str(binary), str(trace)], capture_output=True, text=True, timeout=120)
     assert proc.returncode == 0, proc.stdout + proc.stderr
     assert "native cpu tests passed" in proc.stdout
+    # the C++ trace writer and the Python reader agree on the file layout
+    from vericcl_b200.online.trace import parse_trace
+    doc = parse_trace(trace.read_bytes(), partial_ok=False)
+    assert doc["rank"] == 3 and doc["ctas"] == 4 and doc["steps"] == 3 and doc["complete"]
+    recs = doc["records"]
+    assert len(recs) == 16
+    ops = {0: [1, 2, 0], 1: [4]}
+    for r in recs:
+        assert r.start_ns == 1000 * r.cta + 100 * r.iteration + 10 * r.step + 1
+        assert r.end_ns == r.start_ns + 4 and r.wait_ns == 2
+        assert r.block == r.cta // 2 and r.lane == r.cta % 2 and r.op == ops[r.block][r.step]
 
 
 def test_combine_takes_slowest_rank_per_invocation():

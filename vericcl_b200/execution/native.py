@@ -42,7 +42,9 @@ class NativeScheduleDriver:
         self.port = port or (20000 + secrets.randbelow(20000))
 
     def measure(self, *, count: int, dtype: int = 0, redop: int = 0, scale: float = 1.0, nlanes: int = 32,
-                niters: int = 1, warmup: int = 3, iters: int = 10, timeout_s: float = 60.0):
+                niters: int = 1, warmup: int = 3, iters: int = 10, timeout_s: float = 60.0, trace_dir=None):
+        """Device-timed invocations; with ``trace_dir`` every rank also writes
+        ``trace-rank<r>.bin`` (per-step trace of its last invocation)."""
         with tempfile.TemporaryDirectory() as tmp:
             tmp = Path(tmp)
             (tmp / "schedule.xml").write_text(self.xml)
@@ -54,6 +56,9 @@ class NativeScheduleDriver:
                        "session": session, "count": count, "dtype": dtype, "redop": redop, "scale": scale,
                        "nlanes": nlanes, "niters": niters, "warmup": warmup, "iters": iters,
                        "timeout_s": timeout_s, "receipt": str(tmp / ("receipt-%d.json" % rank))}
+                if trace_dir is not None:
+                    Path(trace_dir).mkdir(parents=True, exist_ok=True)
+                    cfg["trace"] = str(Path(trace_dir) / ("trace-rank%d.bin" % rank))
                 path = tmp / ("config-%d.json" % rank)
                 path.write_text(json.dumps(cfg))
                 p = subprocess.Popen([str(self.binary), str(path)], stdout=subprocess.PIPE, stderr=subprocess.PIPE,

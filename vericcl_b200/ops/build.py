@@ -28,7 +28,7 @@ CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 EXT = sysconfig.get_config_var("EXT_SUFFIX") or ".so"
 
 PLAN_SOURCES = ["plan/xml_parse.cc", "plan/compile.cc", "plan/cpu_interp.cc"]
-RUNTIME_SOURCES = ["runtime/contract.cc", "runtime/control_transport.cc"]
+RUNTIME_SOURCES = ["runtime/contract.cc", "runtime/control_transport.cc", "runtime/trace_io.cc"]
 
 
 def _digest(paths, flags) -> str:
