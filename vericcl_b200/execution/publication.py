@@ -52,6 +52,9 @@ def publish_results(ctx, *, xml: str | None, sidecar: dict | None, model: dict |
                 z.write(path, path.relative_to(ctx.directory))
     Path(str(archive) + ".tmp").replace(archive)
     artifacts.append("details.zip")
+    from vericcl_b200.execution.transport import export_manifest
+    export_manifest(ctx.directory)
+    artifacts.append("manifest.json")
     ctx.update_run_json(artifacts=artifacts)
     ctx.emit("results_published", artifacts=artifacts)
     return {"artifacts": artifacts}
