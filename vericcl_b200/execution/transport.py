@@ -15,7 +15,6 @@ and vericcl/execution/manifest.py:13).
 from __future__ import annotations
 
 import hashlib
-import os
 import shlex
 import shutil
 import socket
