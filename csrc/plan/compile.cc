@@ -220,6 +220,11 @@ class Compiler {
       for (const SRef& y : succ[x]) if (--indeg[y] == 0) ready.push_back(y);
     }
     if (order_.size() != all_.size()) fail("schedule deadlocks: the step dependency graph has a cycle");
+    for (const SRef& x : order_) {
+      int lv = 0;
+      for (const SRef& p : preds(x)) lv = std::max(lv, level_[p] + 1);
+      level_[x] = lv;
+    }
   }
 
   void place_scale() {
@@ -448,6 +453,7 @@ class Compiler {
     std::vector<DevSrc> srcs;
     EventSet waits;
     int prio = 0;
+    int level = 0;             // dependency depth of the XML step
     int xml_tb = -1;
     bool mc_peer = false;      // a copy replaced by the owner's multicast store
     int mc_buf = -1, mc_chunk = -1;
@@ -489,6 +495,7 @@ class Compiler {
       const XStep& st = step(x);
       PendingStep ps{};
       ps.prio = topo_pos_[x];
+      ps.level = level_[x];
       ps.xml_tb = a_.gpus[x.rank].tbs[x.tb].id;
       ps.st.cnt = st.cnt;
       ps.st.flags = 0;
@@ -631,11 +638,21 @@ class Compiler {
             indeg[n]++;
           }
         }
-    auto prio = [&](const Node& n) {
-      return std::make_tuple(pending_[std::get<0>(n)][std::get<1>(n)][std::get<2>(n)].prio, std::get<0>(n),
-                             std::get<1>(n), std::get<2>(n));
+    // Order: dependency depth, then, among steps of one depth, the cyclic distance from the rank to the
+    // peer it pulls from, so that at each depth rank r reads from r+1, r+2, ... instead of every rank
+    // reading the same peer first; then the XML topological position.
+    auto rotation = [&](const Node& n) {
+      const PendingStep& ps = pending_[std::get<0>(n)][std::get<1>(n)][std::get<2>(n)];
+      const int r = std::get<0>(n);
+      for (auto& sr : ps.srcs)
+        if (sr.rank != r) return (sr.rank - r + P_) % P_;
+      return 0;
     };
-    std::set<std::tuple<int, int, int, int>> ready;
+    auto prio = [&](const Node& n) {
+      const PendingStep& ps = pending_[std::get<0>(n)][std::get<1>(n)][std::get<2>(n)];
+      return std::make_tuple(ps.level, rotation(n), ps.prio, std::get<0>(n), std::get<1>(n), std::get<2>(n));
+    };
+    std::set<std::tuple<int, int, int, int, int, int>> ready;
     for (auto& kv : indeg) if (kv.second == 0) ready.insert(prio(kv.first));
     std::map<Node, int> newidx;
     std::vector<int> count(P_, 0);
@@ -643,7 +660,7 @@ class Compiler {
     while (!ready.empty()) {
       auto t = *ready.begin();
       ready.erase(ready.begin());
-      Node n{std::get<1>(t), std::get<2>(t), std::get<3>(t)};
+      Node n{std::get<3>(t), std::get<4>(t), std::get<5>(t)};
       int r = std::get<0>(n);
       newidx[n] = count[r]++;
       order[r].push_back(n);
@@ -1017,7 +1034,7 @@ class Compiler {
   int P_;
   std::vector<std::map<int, int>> tb_index_;
   std::vector<SRef> all_, order_;
-  std::map<SRef, int> topo_pos_;
+  std::map<SRef, int> topo_pos_, level_;
   std::map<SRef, SRef> match_recv_, match_send_;
   std::set<SRef> scale_steps_, need_arrive_;
   std::vector<std::vector<int>> dblock_;
