@@ -108,3 +108,9 @@ def test_json_schema_export():
         schema = json_schema(node, name)
         assert schema["type"] == "object"
         json.dumps(schema)
+
+
+def test_committed_schema_files_and_docs_are_current():
+    """schemas/*.schema.json and docs/input-schema.md match what the schema DSL generates."""
+    from vericcl_b200.input.docs import stale
+    assert stale() == []
