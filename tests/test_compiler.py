@@ -107,3 +107,20 @@ def test_idle_nops_removed_and_waits_renumbered():
     assert plain.stats["dropped_nops"] == 48
     text = plain.describe(0)
     assert "nop" not in text and "wait(r1,b0,e2)" in text
+
+
+@pytest.mark.parametrize("coll", ["broadcast", "reduce", "alltoall"])
+@pytest.mark.parametrize("lanes,iters,merge", [(1, 1, False), (3, 2, True)])
+def test_rooted_and_alltoall_programs_on_the_oracle(coll, lanes, iters, merge):
+    p = 4
+    slices = p
+    xml = schedule_xml(coll, p, slices, inplace=False)
+    c = compile_xml(xml, nlanes=lanes, niters=iters, merge=merge)
+    count = p * slices * 8 * 3
+    rng = np.random.default_rng(7)
+    ins = [rng.uniform(-1, 1, count).astype(np.float32) for _ in range(p)]
+    exp = reference_result(coll, [a.astype(np.float64) for a in ins], rank_count=p)
+    outs = run_cpu(c, ins, seed=3)
+    for r in range(p):
+        if exp[r] is not None:
+            np.testing.assert_allclose(outs[r][:len(exp[r])], exp[r], atol=1e-5)
