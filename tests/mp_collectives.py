@@ -162,6 +162,39 @@ def main():
         if not inplace:
             comm.free(out)
     cases += oneshot
+    # broadcast / reduce (non-zero roots) and all-to-all through the engine, on non-heap tensors
+    extra = [("broadcast", world - 1), ("reduce", world - 1), ("reduce", 0), ("alltoall", 0)]
+    for coll, root in extra:
+        n = world * 8192
+        seed = zlib.crc32(repr(("engine", coll, root)).encode()) % 100000
+        x = inputs_for(rank, n, torch.float32, seed).cuda()
+        out = torch.full((n,), float("nan"), device="cuda")
+        if coll == "broadcast":
+            eng.broadcast(x, out, root=root)
+        elif coll == "reduce":
+            eng.reduce(x, out, root=root)
+        else:
+            eng.all_to_all(x, out)
+        torch.cuda.synchronize()
+        comm.check_status()
+        xs = [inputs_for(r, n, torch.float32, seed).double() for r in range(world)]
+        if coll == "broadcast":
+            ref = xs[root]
+        elif coll == "reduce":
+            ref = sum(xs) if rank == root else None
+        else:
+            part = n // world
+            ref = torch.cat([xs[s][rank * part:(rank + 1) * part] for s in range(world)])
+        if ref is None:
+            ok, err = True, 0.0                              # non-root output is unspecified
+        else:
+            err = (out.double().cpu() - ref).abs().max().item()
+            ok = err <= 1e-4 * world * max(1.0, ref.abs().max().item())
+        failures += 0 if ok else 1
+        if rank == 0 or not ok:
+            print(json.dumps({"rank": rank, "coll": coll, "root": root, "path": "engine", "max_err": err, "ok": ok}),
+                  flush=True)
+    cases += extra
     # block-scaled FP8 AllGather through the engine
     n = 1 << 14
     x = inputs_for(rank, n, torch.float32, 4242).cuda()

@@ -109,17 +109,18 @@ def test_idle_nops_removed_and_waits_renumbered():
     assert "nop" not in text and "wait(r1,b0,e2)" in text
 
 
-@pytest.mark.parametrize("coll", ["broadcast", "reduce", "alltoall"])
+@pytest.mark.parametrize("coll,root", [("broadcast", 0), ("broadcast", 2), ("reduce", 0), ("reduce", 3),
+                                       ("alltoall", 0)])
 @pytest.mark.parametrize("lanes,iters,merge", [(1, 1, False), (3, 2, True)])
-def test_rooted_and_alltoall_programs_on_the_oracle(coll, lanes, iters, merge):
+def test_rooted_and_alltoall_programs_on_the_oracle(coll, root, lanes, iters, merge):
     p = 4
     slices = p
-    xml = schedule_xml(coll, p, slices, inplace=False)
+    xml = schedule_xml(coll, p, slices, inplace=False, root=root)
     c = compile_xml(xml, nlanes=lanes, niters=iters, merge=merge)
     count = p * slices * 8 * 3
     rng = np.random.default_rng(7)
     ins = [rng.uniform(-1, 1, count).astype(np.float32) for _ in range(p)]
-    exp = reference_result(coll, [a.astype(np.float64) for a in ins], rank_count=p)
+    exp = reference_result(coll, [a.astype(np.float64) for a in ins], rank_count=p, root=root)
     outs = run_cpu(c, ins, seed=3)
     for r in range(p):
         if exp[r] is not None:

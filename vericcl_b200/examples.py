@@ -20,7 +20,7 @@ def example_documents(operator: str = "allreduce", method: str = "hierarchy", ra
                       alpha_us: float | None = None, link_gbps: float | None = None, max_channels: int = 1,
                       tuning_rounds: int = 0, scratch_bytes: int = 1 << 30, calibration: bool = False,
                       per_model_timeout_s: float = 60.0, reduction_op: str | None = None,
-                      scale: float | None = None) -> dict:
+                      scale: float | None = None, root: int = 0) -> dict:
     kw = {}
     if alpha_us is not None:
         kw["alpha_us"] = alpha_us
@@ -33,7 +33,7 @@ def example_documents(operator: str = "allreduce", method: str = "hierarchy", ra
         if scale is not None:
             collective["scale"] = scale
     if operator in ("broadcast", "reduce"):
-        collective["root"] = 0
+        collective["root"] = root
     sketch = {
         "collective": collective,
         "hyperparameters": {"total_size_bytes": total_size_bytes, "slice_size_bytes": slice_size_bytes},

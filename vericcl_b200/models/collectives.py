@@ -62,7 +62,7 @@ class CollectiveEngine:
         return (collective in ("allreduce", "allgather") and self.comm.world > 1 and 0 < nbytes
                 <= self.oneshot_max_bytes and nbytes % 8 == 0)
 
-    def plan(self, collective: str, count: int, dtype, *, inplace: bool, op: str = "sum"):
+    def plan(self, collective: str, count: int, dtype, *, inplace: bool, op: str = "sum", root: int = 0):
         world = self.comm.world
         if self.use_oneshot(collective, count, dtype):
             return self.comm.oneshot_plan(collective, self.oneshot_max_bytes,
@@ -72,7 +72,8 @@ class CollectiveEngine:
         if collective in ("reduce_scatter", "alltoall") and slices % world:
             slices = world
         dname = str(dtype).split(".")[-1]
-        xml = schedule_xml(collective, world, slices, inplace=inplace, datatype=dname, method=self.method)
+        xml = schedule_xml(collective, world, slices, inplace=inplace, datatype=dname, method=self.method,
+                           root=root if collective in ("broadcast", "reduce") else 0)
         probe = self.comm.compile(xml, nlanes=1, niters=1)
         esize = torch.tensor([], dtype=dtype).element_size()
         runtime = count * (world if collective == "allgather" else 1)
@@ -172,6 +173,55 @@ class CollectiveEngine:
             src.copy_(inp.view(-1))
         plan = self.plan("reduce_scatter", inp.numel(), inp.dtype, inplace=False)
         self.comm.run(plan, src, dst, op=op, scale=scale, count_per_rank=inp.numel())
+        if dst.data_ptr() != out.data_ptr():
+            out.view(-1).copy_(dst)
+        return out
+
+    def _staged(self, tensor: torch.Tensor, tag: str, copy_in: bool) -> torch.Tensor:
+        """The heap tensor to run on: ``tensor`` itself when it lives in the heap, else a staging buffer."""
+        flat = tensor.view(-1)
+        if self.comm.in_heap(flat):
+            return flat
+        buf = self._heap_copy(flat, tag)
+        if copy_in:
+            buf.copy_(flat)
+        return buf
+
+    def broadcast(self, inp: torch.Tensor, out: torch.Tensor, *, root: int = 0) -> torch.Tensor:
+        """``out`` on every rank = ``inp`` of rank ``root`` (other ranks' ``inp`` is not read)."""
+        if inp.numel() != out.numel():
+            raise RuntimeFailure("broadcast input and output must have the same size")
+        src, dst = self._staged(inp, "bc-in", True), self._staged(out, "bc-out", False)
+        plan = self.plan("broadcast", inp.numel(), inp.dtype, inplace=False, root=root)
+        self.comm.run(plan, src, dst)
+        if dst.data_ptr() != out.data_ptr():
+            out.view(-1).copy_(dst)
+        return out
+
+    def reduce(self, inp: torch.Tensor, out: torch.Tensor, *, root: int = 0, op: str = "sum",
+               scale: float | None = None) -> torch.Tensor:
+        """``out`` on rank ``root`` = op over every rank's ``inp`` (fused scale).
+
+        The schedule may use other ranks' ``out`` as intermediate storage, so
+        its contents there are unspecified afterwards.
+        """
+        if inp.numel() != out.numel():
+            raise RuntimeFailure("reduce input and output must have the same size")
+        src, dst = self._staged(inp, "rd-in", True), self._staged(out, "rd-out", False)
+        plan = self.plan("reduce", inp.numel(), inp.dtype, inplace=False, op=op, root=root)
+        self.comm.run(plan, src, dst, op=op, scale=scale)
+        if dst.data_ptr() != out.data_ptr():
+            out.view(-1).copy_(dst)
+        return out
+
+    def all_to_all(self, inp: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """Part ``d`` of rank ``s``'s ``inp`` (world equal parts) becomes part ``s`` of rank ``d``'s ``out``."""
+        world = self.comm.world
+        if inp.numel() != out.numel() or inp.numel() % world:
+            raise RuntimeFailure("all_to_all needs equal input/output sizes divisible by the world size")
+        src, dst = self._staged(inp, "a2a-in", True), self._staged(out, "a2a-out", False)
+        plan = self.plan("alltoall", inp.numel(), inp.dtype, inplace=False)
+        self.comm.run(plan, src, dst)
         if dst.data_ptr() != out.data_ptr():
             out.view(-1).copy_(dst)
         return out

@@ -95,7 +95,7 @@ def synthesize(request, model=None, *, channels: int = 1) -> CandidateBundle:
 
 @lru_cache(maxsize=256)
 def schedule_xml(collective: str, ranks: int, slices_per_rank: int, *, inplace: bool = False,
-                 datatype: str = "float32", method: str = "hierarchy", channels: int = 1) -> str:
+                 datatype: str = "float32", method: str = "hierarchy", channels: int = 1, root: int = 0) -> str:
     """Verified XML for ``collective`` over ``ranks`` GPUs of one NVSwitch domain.
 
     The XML is size independent (its chunks scale with the runtime buffer);
@@ -107,7 +107,8 @@ def schedule_xml(collective: str, ranks: int, slices_per_rank: int, *, inplace: 
     slice_bytes = 64 * 1024 // elem * elem
     docs = example_documents(collective, method, ranks, total_size_bytes=slice_bytes * slices_per_rank,
                              slice_size_bytes=slice_bytes, datatype=datatype, inplace=inplace,
-                             max_channels=channels, scratch_bytes=slice_bytes * slices_per_rank * ranks)
+                             max_channels=channels, scratch_bytes=slice_bytes * slices_per_rank * ranks,
+                             root=root)
     request = resolve_documents(docs)
     bundle = synthesize(request, channels=channels)
     if not bundle.can_execute:
