@@ -299,7 +299,8 @@ def main():
                            "launch": "per-bucket" if args.per_bucket else "all buckets in one persistent launch",
                            "plan": {"lanes": ar.plan.nlanes, "iters": ar.plan.niters,
                                     "nvls": bool(ar.plan.multicast), "heap_multicast": comm.multicast,
-                                    "stats": ar.plan.device_plan.stats()},
+                                    "stats": ar.plan.device_plan.stats() if ar.plan.device_plan is not None
+                                    else {"path": ar.plan.kind}},
                            "l2": "inputs (16 GB) larger than the 126 MB L2; no flush needed"},
                 "busbw_per_gpu_gbs": round(busbw, 2), "pct_of_900": round(100 * busbw / 900.0, 2),
                 "check": {"first_last_bucket_max_err": err, "ok": bool(check_ok), "reference": "NCCL all_reduce x scale"},
