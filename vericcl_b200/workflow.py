@@ -294,6 +294,7 @@ class PrimaryWorkflow:
                     best = None
             if best is None:
                 record["result"] = "no improvement"
+                record["scope_proof"] = self.scope_proof(index, analysis.strategies)
                 self.rounds.append(record)
                 self.checkpoint("round_%d" % index)
                 continue
@@ -303,6 +304,22 @@ class PrimaryWorkflow:
             self.rounds.append(record)
             self.checkpoint("round_%d" % index)
         return "round limit"
+
+    def scope_proof(self, index: int, strategies) -> dict:
+        """Certify (and independently check) that no variant of this round's strategies beats the incumbent."""
+        from vericcl_b200.verification.proof_check import certify_scope, check_no_improvement
+        if not strategies or self.incumbent.network is None or self.incumbent.prediction is None:
+            return {"status": "not_applicable"}
+        lower = Lowerer(self.incumbent.request, self.topology, self.model)
+        try:
+            cert = certify_scope(self.incumbent, strategies, self.model, lower=lower)
+            checked = check_no_improvement(cert, self.incumbent, strategies, self.model, lower=lower)
+        except SemanticError as error:
+            return {"status": "not_certified", "reason": str(error)}
+        path = atomic_write_json(self.ctx.process / "proofs" / ("round_%d.json" % index), cert)
+        self.ctx.emit("scope_proof", round=index, status=checked.status, form="bound" if cert["bound"] else "leaves")
+        return {"status": checked.status, "form": "bound" if cert["bound"] else "leaves",
+                "checked_leaves": checked.checked_leaves, "certificate": str(path.relative_to(self.ctx.directory))}
 
     @staticmethod
     def _xml_digest(bundle) -> str:
