@@ -50,7 +50,9 @@ def parse():
 
 
 def reference_unavailable(reason: str):
-    print(json.dumps({"impl": "reference", "unavailable": reason}), flush=True)
+    # under torchrun every rank runs this; only rank 0 prints the line
+    if os.environ.get("RANK", "0") == "0":
+        print(json.dumps({"impl": "reference", "unavailable": reason}), flush=True)
 
 
 def reference_reason() -> str:
