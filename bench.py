@@ -107,12 +107,6 @@ class ClockSampler:
         self.started = time.monotonic()
         return self
 
-    def mark_start(self):
-        self.t0 = time.time()
-
-    def mark_end(self):
-        self.t1 = time.time()
-
     def __exit__(self, *exc):
         if self.proc is not None:
             # keep sampling until at least 0.3 s have passed so short timed regions still get samples
