@@ -37,7 +37,7 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=("vericcl", "reference", "nccl"), default="vericcl")
+    ap.add_argument("--impl", choices=("vericcl", "reference"), default="vericcl")
     ap.add_argument("--params", type=int, default=8_000_000_000)
     ap.add_argument("--bucket-bytes", type=int, default=25 * 1024 * 1024)
     ap.add_argument("--scale", type=float, default=0.125)
