@@ -96,3 +96,19 @@ def test_measured_rejection_is_not_repeated(tmp_path):
     assert result.status == "ok"
     assert calls and len(calls) == len(set(calls))
     assert len(result.rounds) == 3
+
+
+def test_experiment_report_tables(tmp_path):
+    from vericcl_b200.experiments import load_points, markdown, matrix_commands, report_rows
+    log = tmp_path / "sweep.log"
+    log.write_text("noise line\n"
+                   '{"coll": "allreduce", "n_gpus": 4, "bytes_per_rank": 1024, "time_us": 6.1, "busbw_gbs": 0.25, '
+                   '"path": "oneshot", "nvls": true, "graph": true, "nccl_time_us": 18.7, "speedup_vs_nccl": 3.08, '
+                   '"max_rel_err_vs_fp64": 0.002}\n'
+                   '{"summary": true, "points": 1}\n')
+    rows = report_rows(load_points([log]))
+    assert len(rows) == 1 and rows[0]["path"] == "one-shot NVLS" and rows[0]["size"] == "1 KiB"
+    table = markdown(rows)
+    assert "| allreduce | 4 | graph | 1 KiB | one-shot NVLS | 6.1 |" in table
+    cmds = matrix_commands([2, 8], graph=True)
+    assert cmds[1][4] == "--nproc-per-node=8" and cmds[1][-1] == "--graph"
