@@ -26,7 +26,7 @@ def test_synthesize_checks_and_numerics(op, inplace, ranks):
     assert ok, err
 
 
-def test_acceptance_config_1_allgather_p8():
+def test_allgather_p8_1mib_hierarchy_on_the_chunk_simulator():
     """P=8 AllGather, hierarchy, fp32, M=1 MiB, S=256 KiB, alpha=2us, beta=1/150 GB/s."""
     d = example_documents("allgather", "hierarchy", 8, total_size_bytes=1 << 20, slice_size_bytes=1 << 18,
                           alpha_us=2.0, link_gbps=150.0, per_model_timeout_s=60)

@@ -7,7 +7,7 @@ from it in order, so a send never waits for its receiver.  The step kinds are
 the MSCCL interpreter's: ``s r rrc rcs rrs rrcs cpy re nop``.  The simulator
 runs on real NumPy buffers (float64 by default), so a schedule is checked on
 numbers, not only on contributor sets: each output must equal the collective
-of seeded inputs (BASELINE acceptance configuration 1 uses uniform(-1, 1)).
+of seeded inputs (the P=8 AllGather 1 MiB acceptance case uses uniform(-1, 1)).
 It is also the CPU oracle for the GPU interpreter.
 """
 from __future__ import annotations
