@@ -223,10 +223,9 @@ __device__ void move_generic(char* dst, const char* const* src, int nsrc, long l
 }
 
 // dst(all ranks) = scale? * sum over ranks of src, through the multicast addresses.
-template <int DT>
+template <int DT, int U>
 __device__ void mc_allreduce_piece(char* mc_dst, const char* mc_src, long long nvec, bool do_scale, float scale) {
   using V = VecT<DT>;
-  constexpr int U = 8;
   const long long stride = (long long)blockDim.x * U;
   for (long long v0 = threadIdx.x; v0 < nvec; v0 += stride) {
     uint4 r[U];
@@ -253,8 +252,8 @@ __device__ void mc_allreduce_piece(char* mc_dst, const char* mc_src, long long n
 }
 
 // dst(all ranks) = src(local), through the multicast address of the destination.
+template <int U>
 __device__ void mc_store_piece(char* mc_dst, const char* src, long long nvec) {
-  constexpr int U = 8;
   const long long stride = (long long)blockDim.x * U;
   for (long long v0 = threadIdx.x; v0 < nvec; v0 += stride) {
     uint4 r[U];
@@ -271,12 +270,13 @@ __device__ void mc_store_piece(char* mc_dst, const char* src, long long nvec) {
   }
 }
 
-template <int DT, int RED>
+// LEAN selects the register-lean unrolls (2 and 3 sources one vector deep) that build without spills.
+template <int DT, int RED, bool LEAN>
 __device__ void move_piece(char* dst, const char* const* src, int nsrc, long long nvec, bool do_scale, float scale) {
   switch (nsrc) {
     case 1: move_fixed<DT, RED, 1, 4>(dst, src, nvec, do_scale, scale); break;
-    case 2: move_fixed<DT, RED, 2, 2>(dst, src, nvec, do_scale, scale); break;
-    case 3: move_fixed<DT, RED, 3, 2>(dst, src, nvec, do_scale, scale); break;
+    case 2: move_fixed<DT, RED, 2, LEAN ? 1 : 2>(dst, src, nvec, do_scale, scale); break;
+    case 3: move_fixed<DT, RED, 3, LEAN ? 1 : 2>(dst, src, nvec, do_scale, scale); break;
     case 4: move_fixed<DT, RED, 4, 1>(dst, src, nvec, do_scale, scale); break;
     case 5: move_fixed<DT, RED, 5, 1>(dst, src, nvec, do_scale, scale); break;
     case 6: move_fixed<DT, RED, 6, 1>(dst, src, nvec, do_scale, scale); break;
@@ -339,7 +339,7 @@ __device__ bool wait_events(const InterpArgs& a, const DevWait* w, int n, int it
   return __all_sync(0xffffffffu, ok);
 }
 
-template <int DT, int RED>
+template <int DT, int RED, bool LEAN>
 __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long long base, int* s_stop,
                         char* const* s_rank_base, const long long* s_buf_off) {
   const DevBlock blk = a.blocks[block];
@@ -383,7 +383,7 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
                             ((long long)(sr.chunk + k) * a.chunk_elems + pr.lo) * esize;
           char* dst = a.mc_base + s_buf_off[st.dst_buf] + batch * a.batch_stride[st.dst_buf] +
                       ((long long)(st.dst_chunk + k) * a.chunk_elems + pr.lo) * esize;
-          mc_allreduce_piece<DT>(dst, src, nvec, (st.flags & F_SCALE) != 0, a.scale);
+          mc_allreduce_piece<DT, LEAN ? 4 : 8>(dst, src, nvec, (st.flags & F_SCALE) != 0, a.scale);
         }
         mc_pending = true;
         if (s + 1 < blk.nsteps && a.steps[blk.step_begin + s + 1].op != OP_NOP) {
@@ -401,7 +401,7 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
                             ((long long)(sr.chunk + k) * a.chunk_elems + pr.lo) * esize;
           char* dst = a.mc_base + s_buf_off[st.dst_buf] + batch * a.batch_stride[st.dst_buf] +
                       ((long long)(st.dst_chunk + k) * a.chunk_elems + pr.lo) * esize;
-          mc_store_piece(dst, src, nvec);
+          mc_store_piece<LEAN ? 4 : 8>(dst, src, nvec);
         }
         mc_pending = true;
         if (s + 1 < blk.nsteps && a.steps[blk.step_begin + s + 1].op != OP_NOP) {
@@ -422,7 +422,7 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
           __syncthreads();
           char* dst = s_rank_base[a.rank] + s_buf_off[st.dst_buf] + batch * a.batch_stride[st.dst_buf] +
                       ((long long)(st.dst_chunk + k) * a.chunk_elems + pr.lo) * esize;
-          move_piece<DT, RED>(dst, s_src, st.nsrc, nvec, (st.flags & F_SCALE) != 0, a.scale);
+          move_piece<DT, RED, LEAN>(dst, s_src, st.nsrc, nvec, (st.flags & F_SCALE) != 0, a.scale);
           __syncthreads();
         }
       }
@@ -470,7 +470,8 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
   }
 }
 
-template <int DT, int RED>
+// TL: record the launch timeline; LEAN: register-lean unrolls (see move_piece).
+template <int DT, int RED, bool TL = false, bool LEAN = false>
 __global__ void __launch_bounds__(512, 1) interp_kernel(const InterpArgs a) {
   __shared__ unsigned long long s_base;
   __shared__ int s_stop;
@@ -483,15 +484,17 @@ __global__ void __launch_bounds__(512, 1) interp_kernel(const InterpArgs a) {
   if (threadIdx.x == 0) {
     s_base = (*(volatile unsigned long long*)&a.control->epoch) << 32;
     s_stop = 0;
+    if (TL && blockIdx.x == 0) a.timeline[((s_base >> 32) % kTimelineSlots) * 2] = globaltimer();
     st_release_sys(flag_ptr(a, a.rank, a.start_slot), s_base + 1);
   }
   __syncthreads();
-  if (block < a.nblocks) run_cta<DT, RED>(a, block, lane, s_base, &s_stop, s_rank_base, s_buf_off);
+  if (block < a.nblocks) run_cta<DT, RED, LEAN>(a, block, lane, s_base, &s_stop, s_rank_base, s_buf_off);
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
     unsigned int done = atomicAdd(&a.control->arrive, 1u);
     if (done == gridDim.x - 1) {
+      if (TL) a.timeline[((s_base >> 32) % kTimelineSlots) * 2 + 1] = globaltimer();
       a.control->arrive = 0;
       a.control->epoch = a.control->epoch + 1;
       __threadfence();
@@ -503,6 +506,15 @@ template <int DT>
 cudaError_t launch_red(const InterpArgs& a, cudaStream_t stream, int threads) {
   void* args[] = {const_cast<InterpArgs*>(&a)};
   dim3 grid(a.nblocks * a.nlanes), block(threads);
+  if (a.timeline || a.lean) {
+    // the instrumented and the lean instances exist for sum (and average) reductions and copies only
+    if (a.redop != RED_SUM) return cudaErrorInvalidValue;
+    if (a.timeline && a.lean)
+      return cudaLaunchCooperativeKernel((void*)interp_kernel<DT, RED_SUM, true, true>, grid, block, args, 0, stream);
+    if (a.timeline)
+      return cudaLaunchCooperativeKernel((void*)interp_kernel<DT, RED_SUM, true, false>, grid, block, args, 0, stream);
+    return cudaLaunchCooperativeKernel((void*)interp_kernel<DT, RED_SUM, false, true>, grid, block, args, 0, stream);
+  }
   switch (a.redop) {
     case RED_PROD: return cudaLaunchCooperativeKernel((void*)interp_kernel<DT, RED_PROD>, grid, block, args, 0, stream);
     case RED_MIN: return cudaLaunchCooperativeKernel((void*)interp_kernel<DT, RED_MIN>, grid, block, args, 0, stream);

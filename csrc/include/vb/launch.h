@@ -49,7 +49,13 @@ struct InterpArgs {
   int trace;                         // record per-step timestamps into trace buffer
   unsigned long long* trace_buf;     // [nblocks*nlanes][max_steps*niters][2] (start, end) globaltimer
   int trace_stride;
+  // Optional launch timeline: [kTimelineSlots][2] %globaltimer of kernel entry (CTA 0) and exit (last CTA to
+  // finish), indexed by launch epoch modulo kTimelineSlots; nullptr disables it (separate kernel instance).
+  unsigned long long* timeline;
+  int lean;                          // 1: run the register-lean kernel instance (sum reductions and copies)
 };
+
+constexpr int kTimelineSlots = 256;
 
 // Launch the interpreter (cooperative launch: every CTA is co-resident).
 cudaError_t launch_interp(const InterpArgs& args, cudaStream_t stream, int threads);

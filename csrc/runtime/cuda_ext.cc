@@ -346,10 +346,17 @@ PYBIND11_MODULE(_vbcuda, m) {
            py::arg("trace_stride") = 0)
       .def("bind", [](DevicePlan& p, Heap& heap, size_t in_off, size_t out_off, size_t scr_off, int64_t count, int dtype,
                       int redop, float scale, double timeout_s, int threads, int nbatch,
-                      std::vector<long long> strides) {
-        return BoundLaunch{p.bind(heap, in_off, out_off, scr_off, count, dtype, redop, scale, timeout_s, threads, nbatch,
-                                  strides, 0, 0), threads};
-      })
+                      std::vector<long long> strides, uint64_t timeline_ptr, bool lean) {
+        InterpArgs a = p.bind(heap, in_off, out_off, scr_off, count, dtype, redop, scale, timeout_s, threads, nbatch,
+                              strides, 0, 0);
+        if ((timeline_ptr || lean) && redop != RED_SUM)
+          throw std::runtime_error("the launch timeline and the lean kernel cover sum/avg reductions and copies");
+        a.timeline = reinterpret_cast<unsigned long long*>(timeline_ptr);
+        a.lean = lean ? 1 : 0;
+        return BoundLaunch{a, threads};
+      }, py::arg("heap"), py::arg("in_off"), py::arg("out_off"), py::arg("scr_off"), py::arg("count"),
+         py::arg("dtype"), py::arg("redop"), py::arg("scale"), py::arg("timeout_s"), py::arg("threads"),
+         py::arg("nbatch"), py::arg("strides"), py::arg("timeline_ptr") = 0, py::arg("lean") = false)
       .def("geometry", &DevicePlan::geometry)
       .def("slots", &DevicePlan::slots)
       .def("describe", &DevicePlan::describe)

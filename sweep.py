@@ -3,7 +3,7 @@
     torchrun --nproc-per-node N --master-addr 127.0.0.1 sweep.py [--colls allreduce,allgather]
              [--dtype bfloat16] [--min-bytes 1024] [--max-bytes 1073741824] [--iters 20] [--warmup 5]
              [--method hierarchy|constructive_trees] [--slices S] [--nvls auto|on|off] [--graph]
-             [--check-max-bytes B] [--oneshot-max B]
+             [--check-max-bytes B] [--oneshot-max B] [--timeline]
 
 Each point: the synthesized schedule through the sm_100a interpreter (heap
 buffers, CUDA-event device time, max over ranks) and torch.distributed NCCL
@@ -42,6 +42,8 @@ def main():
     ap.add_argument("--slices", type=int, default=None, help="slices per rank (default: P for AR, 1 for AG)")
     ap.add_argument("--nvls", default="auto", choices=("auto", "on", "off"))
     ap.add_argument("--check-max-bytes", type=int, default=1 << 24)
+    ap.add_argument("--timeline", action="store_true",
+                    help="record kernel entry/exit per interpreter launch and report durations and gaps")
     ap.add_argument("--oneshot-max", type=int, default=None,
                     help="largest per-rank payload of the one-shot path (0: always the interpreter)")
     args = ap.parse_args()
@@ -122,8 +124,10 @@ def main():
                 plan = eng.plan("allreduce", count, dtype, inplace=True)
                 err = check(coll, plan, count, buf, buf) if size <= args.check_max_bytes else None
                 buf.normal_()
-                ours = timed(lambda: comm.run(plan, buf, buf))
+                tl = comm.timeline_buffer() if args.timeline and plan.kind == "interp" else None
+                ours = timed(lambda: comm.run(plan, buf, buf, timeline=tl))
                 ours_host = host_us[0]
+                gaps = comm.launch_gaps(tl, args.iters) if tl is not None else None
                 comm.check_status()
                 nccl = None if (args.no_nccl or world == 1) else timed(lambda: dist.all_reduce(buf))
                 factor = 2.0 * (world - 1) / world if world > 1 else 1.0
@@ -135,8 +139,10 @@ def main():
                 plan = eng.plan("allgather", count, dtype, inplace=False)
                 err = check(coll, plan, count, inp, out) if size <= args.check_max_bytes else None
                 inp.normal_()
-                ours = timed(lambda: comm.run(plan, inp, out))
+                tl = comm.timeline_buffer() if args.timeline and plan.kind == "interp" else None
+                ours = timed(lambda: comm.run(plan, inp, out, timeline=tl))
                 ours_host = host_us[0]
+                gaps = comm.launch_gaps(tl, args.iters) if tl is not None else None
                 comm.check_status()
                 nccl = None if (args.no_nccl or world == 1) else timed(
                     lambda: dist.all_gather_into_tensor(out, inp))
@@ -151,6 +157,9 @@ def main():
                      "slices": eng.slices_per_rank or (1 if coll == "allgather" else world)}
             if err is not None:
                 point["max_rel_err_vs_fp64"] = err
+            if gaps is not None:
+                point["kernel_us_median"] = gaps["kernel_us_median"]
+                point["launch_gap_us_median"] = gaps["gap_us_median"]
             if nccl is not None:
                 point.update({"nccl_time_us": round(nccl, 3),
                               "nccl_busbw_gbs": round(nbytes / nccl / 1e3 * factor, 2),

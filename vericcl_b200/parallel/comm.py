@@ -29,6 +29,7 @@ from vericcl_b200.program.device import DTYPES, REDOPS, REDUCING
 DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 TORCH_DTYPES = {"float32": torch.float32, "bfloat16": torch.bfloat16, "float16": torch.float16}
 DEFAULT_HEAP_BYTES = 1 << 30
+TIMELINE_SLOTS = 256      # launch timeline slots (matches the device-side constant)
 
 
 def _env_flag(name: str, default: bool) -> bool:
@@ -108,6 +109,8 @@ class Communicator:
         self._plans: dict = {}
         self._scratch: dict = {}
         self._ll = None              # (offset, bytes per source) of the one-shot LL region
+        # VERICCL_LEAN=1: sum/avg launches use the interpreter instance with register-lean unrolls
+        self.lean = _env_flag("VERICCL_LEAN", False)
         self._lock = threading.Lock()
         self._closed = False
 
@@ -274,22 +277,26 @@ class Communicator:
 
     def run(self, plan: PlanHandle, inp: torch.Tensor, out: torch.Tensor, *, op: str = "sum",
             scale: float | None = None, stream=None, count_per_rank: int | None = None, nbatch: int = 1,
-            in_stride: int = 0, out_stride: int = 0, trace: torch.Tensor | None = None) -> None:
+            in_stride: int = 0, out_stride: int = 0, trace: torch.Tensor | None = None,
+            timeline: torch.Tensor | None = None) -> None:
         """Launch ``plan`` on heap tensors ``inp`` → ``out`` on ``stream`` (asynchronous).
 
         With ``nbatch > 1`` one launch runs the plan ``nbatch`` times back to back on
         buffers ``in_stride`` / ``out_stride`` elements apart (for example every
         gradient bucket of a flat buffer); the instances pipeline through the same
         persistent CTAs and only the last one waits for peers at the end.
+        ``timeline`` (from :meth:`timeline_buffer`) records kernel entry and
+        exit times per launch on this GPU (:meth:`launch_gaps` reads them).
         """
         if plan.kind == "oneshot":
             if nbatch != 1 or trace is not None:
                 raise RuntimeFailure("the one-shot path runs one instance without tracing")
             self._run_oneshot(plan, inp, out, op, scale, stream, count_per_rank)
             return
+        tl_ptr = 0 if timeline is None else timeline.data_ptr()
         if trace is None:
             fast = self._bound.get((id(plan), inp.data_ptr(), out.data_ptr(), count_per_rank, inp.dtype, op, scale,
-                                    nbatch, in_stride, out_stride))
+                                    nbatch, in_stride, out_stride, tl_ptr))
             if fast is not None:
                 fast.launch((torch.cuda.current_stream() if stream is None else stream).cuda_stream)
                 return
@@ -323,15 +330,38 @@ class Communicator:
             trace.zero_()
             trace_ptr = trace.data_ptr()
         if trace is None:
+            if timeline is not None and (timeline.dtype != torch.int64 or timeline.numel() < 2 * TIMELINE_SLOTS
+                                         or not timeline.is_cuda):
+                raise RuntimeFailure("timeline buffer needs %d int64 elements on the device" % (2 * TIMELINE_SLOTS))
+            lean = self.lean and REDOPS[op] == 0
             bound = plan.device_plan.bind(self.heap, in_off, out_off, scr_off, count, DTYPE_CODES[inp.dtype],
-                                          REDOPS[op], float(factor), self.timeout_s, 512, nbatch, strides)
+                                          REDOPS[op], float(factor), self.timeout_s, 512, nbatch, strides, tl_ptr,
+                                          lean)
             self._bound[(id(plan), inp.data_ptr(), out.data_ptr(), count_per_rank, inp.dtype, op, scale, nbatch,
-                         in_stride, out_stride)] = bound
+                         in_stride, out_stride, tl_ptr)] = bound
             bound.launch(stream.cuda_stream)
             return
         plan.device_plan.run(self.heap, in_off, out_off, scr_off, count, DTYPE_CODES[inp.dtype], REDOPS[op],
                              float(factor), stream.cuda_stream, self.timeout_s, 512, nbatch, strides, trace_ptr,
                              trace_stride)
+
+    def timeline_buffer(self) -> torch.Tensor:
+        return torch.zeros(2 * TIMELINE_SLOTS, dtype=torch.int64, device="cuda")
+
+    def launch_gaps(self, timeline: torch.Tensor, launches: int) -> dict:
+        """Kernel durations and the idle gaps between consecutive launches (µs) of the last ``launches``."""
+        epoch = int(self.status()["epoch"])
+        tl = timeline.view(TIMELINE_SLOTS, 2).cpu().tolist()
+        spans = []
+        for e in range(max(1, epoch - launches), epoch):
+            entry, exit_ = tl[e % TIMELINE_SLOTS]
+            if entry and exit_:
+                spans.append((entry, exit_))
+        durations = [(b - a) / 1e3 for a, b in spans]
+        gaps = [(spans[i + 1][0] - spans[i][1]) / 1e3 for i in range(len(spans) - 1)]
+        med = (lambda v: sorted(v)[len(v) // 2] if v else None)
+        return {"launches": len(spans), "kernel_us_median": med(durations), "gap_us_median": med(gaps),
+                "kernel_us": durations, "gap_us": gaps}
 
     def trace_buffer(self, plan: PlanHandle, nbatch: int = 1) -> torch.Tensor:
         n = plan.device_plan.nblocks * plan.nlanes * plan.niters * nbatch * plan.device_plan.max_steps() * 3
