@@ -270,11 +270,12 @@ __device__ void mc_store_piece(char* mc_dst, const char* src, long long nvec) {
   }
 }
 
-// LEAN selects the register-lean unrolls (2 and 3 sources one vector deep) that build without spills.
+// LEAN selects the register-lean unrolls (2 and 3 sources one vector deep, copies eight deep) that build
+// without spills.
 template <int DT, int RED, bool LEAN>
 __device__ void move_piece(char* dst, const char* const* src, int nsrc, long long nvec, bool do_scale, float scale) {
   switch (nsrc) {
-    case 1: move_fixed<DT, RED, 1, 4>(dst, src, nvec, do_scale, scale); break;
+    case 1: move_fixed<DT, RED, 1, LEAN ? 8 : 4>(dst, src, nvec, do_scale, scale); break;
     case 2: move_fixed<DT, RED, 2, LEAN ? 1 : 2>(dst, src, nvec, do_scale, scale); break;
     case 3: move_fixed<DT, RED, 3, LEAN ? 1 : 2>(dst, src, nvec, do_scale, scale); break;
     case 4: move_fixed<DT, RED, 4, 1>(dst, src, nvec, do_scale, scale); break;
