@@ -33,3 +33,12 @@ def test_small_allreduce_and_allgather_take_the_oneshot_path():
 def test_single_rank_and_disabled_threshold_use_the_interpreter():
     assert not CollectiveEngine(_Comm(1)).use_oneshot("allreduce", 512, torch.bfloat16)
     assert not CollectiveEngine(_Comm(8), oneshot_max_bytes=0).use_oneshot("allreduce", 512, torch.bfloat16)
+
+
+def test_large_allgathers_pull_from_peers():
+    from vericcl_b200.models.collectives import AG_NVLS_MAX_BYTES
+    eng = CollectiveEngine(_Comm(8))
+    assert eng.use_multicast("allreduce", "sum", 1 << 30)
+    assert eng.use_multicast("allgather", "sum", AG_NVLS_MAX_BYTES - 16)
+    assert not eng.use_multicast("allgather", "sum", AG_NVLS_MAX_BYTES)
+    assert not CollectiveEngine(_Comm(2)).use_multicast("allreduce", "sum", 1 << 20)

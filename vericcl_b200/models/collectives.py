@@ -19,6 +19,7 @@ from vericcl_b200.errors import RuntimeFailure
 from vericcl_b200.synthesis import schedule_xml
 
 ONESHOT_MAX_BYTES = 1 << 20          # per-rank payloads up to this size take the one-shot flag-in-data path
+AG_NVLS_MAX_BYTES = 8 << 20          # larger AllGathers pull from peers (measured faster than multicast stores)
 PIECE_MIN_BYTES = 8 * 1024          # smallest useful piece per CTA per iteration
 PIECE_TARGET_BYTES = 512 * 1024     # pipeline a lane's work in pieces of about this size
 MAX_ITERS = 8
@@ -48,13 +49,19 @@ class CollectiveEngine:
             iters = int(os.environ["VERICCL_ITERS"])
         return lanes, iters
 
-    def use_multicast(self, collective: str, op: str) -> bool:
-        """NVLS pays off from 4 ranks up (it cuts AllReduce NVLink traffic from 2(P-1)/P·M to about (1+1/P)·M)."""
+    def use_multicast(self, collective: str, op: str, nbytes: int = 0) -> bool:
+        """NVLS pays off from 4 ranks up (it cuts AllReduce NVLink traffic from 2(P-1)/P·M to about (1+1/P)·M).
+
+        AllGather moves (P-1)·M into every GPU either way; from ``AG_NVLS_MAX_BYTES``
+        per rank, peer pulls in rotated order (rank r reads r+1, r+2, … first) were
+        faster than owner multicast stores on 4 B200s (16 MiB: 117 vs 132 µs;
+        64 MiB: 364 vs 423 µs), so large AllGathers use them.
+        """
         if not self.comm.multicast or self.comm.world < 4:
             return False
         if collective == "allreduce":
             return op in ("sum", "avg")
-        return collective == "allgather"
+        return collective == "allgather" and nbytes < AG_NVLS_MAX_BYTES
 
     def use_oneshot(self, collective: str, count: int, dtype) -> bool:
         """Small AllReduce / AllGather payloads go through the one-shot kernel (one NVLink trip, no barrier)."""
@@ -81,8 +88,8 @@ class CollectiveEngine:
         chunk_bytes = runtime * esize // nchunks
         lanes, iters = self.geometry(probe.device_plan.nblocks, chunk_bytes)
         share = tuple(int(v) for v in os.environ.get("VERICCL_MC_SHARE", "1/1").split("/"))
-        return self.comm.compile(xml, nlanes=lanes, niters=iters, multicast=self.use_multicast(collective, op),
-                                 mc_share=share)
+        return self.comm.compile(xml, nlanes=lanes, niters=iters,
+                                 multicast=self.use_multicast(collective, op, count * esize), mc_share=share)
 
     def _heap_copy(self, tensor: torch.Tensor, tag: str) -> torch.Tensor:
         key = (tag, tensor.numel(), tensor.dtype)
