@@ -38,6 +38,7 @@ from vericcl_b200.performance.model import CostModel
 from vericcl_b200.performance.simulation import predict
 from vericcl_b200.planner.parameters import initial_parameter_domain
 from vericcl_b200.program.sidecar import to_sidecar
+from vericcl_b200.solver.bounds import dependency_lower_bound
 from vericcl_b200.synthesis import Lowerer, synthesize
 from vericcl_b200.topology import load_topology
 from vericcl_b200.utils.jsonio import atomic_write_json, atomic_write_text
@@ -170,9 +171,19 @@ class PrimaryWorkflow:
             methods = [self.request.selected_synthesis_method]
             if not self.request.request_config["atom"]["manual"]["enabled"]:
                 methods.append("constructive_trees" if methods[0] == "hierarchy" else "hierarchy")
+            # cheapest lower bound first; a choice whose bound already reaches the best candidate is skipped
+            bounded = []
             for choice in choices:
                 req = self.request if choice is None else self.request.with_slice(choice.slice_size_bytes)
+                bounded.append((float(dependency_lower_bound(req, self.topology, self.model)), choice, req))
+            bounded.sort(key=lambda item: item[0])
+            for bound, choice, req in bounded:
                 channels = 1 if choice is None else choice.channels
+                best = min((b.t_pred_us for b in self.candidates if b.t_pred_us is not None), default=None)
+                if best is not None and bound >= best:
+                    self.ctx.emit("choice_pruned", slice_size_bytes=req.hyperparameters.slice_size_bytes,
+                                  lower_bound_us=bound, best_t_pred_us=best)
+                    continue
                 for method in methods:
                     lease.check()
                     try:
