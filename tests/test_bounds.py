@@ -31,3 +31,26 @@ def test_two_group_bound_counts_the_slow_link():
     # a 1 MiB slice must cross the 25 GB/s inter-group link at least once
     assert lb >= (1 << 20) / 25e3
     assert lb <= synthesize(req, model).t_pred_us + 1e-9
+
+
+def test_cut_bound_follows_a_faster_calibrated_model():
+    from dataclasses import replace as dc_replace
+    from vericcl_b200.program.native import build_executable
+    from vericcl_b200.performance.initial import model_context
+    from vericcl_b200.performance.simulation import predict
+    from vericcl_b200.verification.global_bound import certify_global_cut
+    req = resolve_documents(example_documents("allgather", "hierarchy", 4, total_size_bytes=4 * 65536,
+                                              slice_size_bytes=65536, alpha_us=2.0, link_gbps=150.0))
+    topo = load_topology(req)
+    model = initial_cost_model(req)
+    faster, _ = model.with_updates("faster", services={
+        k: tuple(dc_replace(c, beta_us_per_byte=c.beta_us_per_byte / 4) for c in v)
+        for k, v in model.services.items() if k.startswith(("link:", "rrc:"))},
+        resources={k: v * 4 for k, v in model.resources.items()})
+    bundle = synthesize(req, model)
+    exe = build_executable(bundle.program, bundle.storage, req, topo, model_context(req))
+    t_fast = predict(exe, faster, exact=True).t_pred_us
+    nominal = certify_global_cut(req, topo)
+    calibrated = certify_global_cut(req, topo, faster)
+    assert calibrated.lower_bound_us <= t_fast + 1e-9
+    assert calibrated.lower_bound_us < nominal.lower_bound_us

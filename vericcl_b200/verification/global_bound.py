@@ -30,25 +30,44 @@ class CutBound:
     exact: tuple
 
 
-def _rate(topology, inside):
+def _link_cap(topology, model, key) -> Fraction:
+    """Fastest rate (bytes/µs) any operation can reach on link ``key`` under the model."""
+    rates = []
+    if model is not None:
+        for name in ("link:%d:%d" % (key.src, key.dst), "rrc:%d:%d" % (key.src, key.dst)):
+            rates += [1 / Fraction(str(c.beta_us_per_byte)) for c in model.services.get(name, ())]
+        for profile in model.profiles:
+            rates += [Fraction(str(r)) for r in profile.rates.values()]
+    if not rates:
+        rates = [Fraction(1) / Fraction(str(topology.links[key].beta_us_per_byte))]
+    return max(rates)
+
+
+def _rate(topology, inside, model=None):
     """Upper bound on the service rate (bytes/µs) across the cut inside → outside.
 
     Any family of capacity constraints that covers every crossing link bounds
     the cut rate by the sum of its capacities; the smallest of the families
     tried (all links, any single covering resource, the senders' ports, the
-    receivers' ports, a greedy cheapest cover) is returned.
+    receivers' ports, a greedy cheapest cover) is returned.  With a cost
+    model, link rates are the model's fastest for the link and resource
+    capacities the model's; a model with measured concurrency profiles (whose
+    rates may exceed a resource's nominal share) bounds links only.
     """
     outside = set(range(topology.rank_count)) - set(inside)
     crossing = {k for k in topology.links if k.src in inside and k.dst in outside}
     if not crossing:
         return Fraction(0)
-    caps = {k: Fraction(1) / Fraction(str(topology.links[k].beta_us_per_byte)) for k in crossing}
+    caps = {k: _link_cap(topology, model, k) for k in crossing}
     bound = sum(caps.values())
     families = {}
+    if model is not None and model.profiles:
+        return bound
     for rid, res in topology.resources.items():
         members = frozenset(l for l in res.links if l in crossing)
-        if members:
-            families[rid] = (members, Fraction(str(res.capacity_bytes_per_us)))
+        capacity = res.capacity_bytes_per_us if model is None else model.resources.get(rid)
+        if members and capacity is not None:
+            families[rid] = (members, Fraction(str(capacity)))
     for rid, (members, cap) in families.items():
         if members == crossing:
             bound = min(bound, cap)
@@ -104,11 +123,14 @@ def certify_global_cut(request, topology, model=None):
     p = request.rank_count
     if p > MAX_EXACT_RANKS:
         return None
-    alpha = min((l.alpha_us for l in topology.links.values()), default=0.0)
+    alphas = [l.alpha_us for l in topology.links.values()]
+    if model is not None:
+        alphas += [c.alpha_us for segs in model.services.values() for c in segs]
+    alpha = min(alphas, default=0.0)
     best = None
     for size in range(1, p):
         for inside in combinations(range(p), size):
-            rate = _rate(topology, set(inside))
+            rate = _rate(topology, set(inside), model)
             need = _required_bytes(request, set(inside))
             if need == 0 or rate == 0:
                 continue
