@@ -250,9 +250,99 @@ __global__ void __launch_bounds__(kThreads) oneshot_kernel(OneShotArgs a) {
   }
 }
 
+// Two-shot AllReduce for mid-size payloads: a reduce-scatter by LL lines (every rank pushes its part of
+// slice j to rank j, which owns slice j = bytes/P), then an all-gather of the reduced slices by LL lines.
+// Per GPU it moves about 4·bytes·(P−1)/P of lines instead of the one-shot's 2·bytes·(P−1), at the price of
+// a second NVLink trip.  Both areas live in the launch's region half: the reduce-scatter area holds
+// [P sources][2·slice] and the all-gather area after it [P owners][2·slice]; the half-reuse argument of the
+// one-shot kernel applies to each area (a rank writes a half again only two launches later, after every
+// peer has consumed it: its reduce-scatter lines after the owner's reduction of the previous launch that
+// used the half, its all-gather lines after every rank's reduce-scatter push of the launch in between).
+template <int DT, int RED>
+__global__ void __launch_bounds__(kThreads) twoshot_kernel(OneShotArgs a) {
+  using U = Unit<DT>;
+  const unsigned long long seq = ld_volatile_u64(&a.control->ll_seq);
+  const unsigned int tag = (unsigned int)(seq % 0xfffffffeull) + 1u;
+  const long long half = (long long)a.nranks * a.ll_src_bytes;
+  const long long region = a.ll_off + (long long)(seq & 1ull) * half;
+  const long long su = (a.bytes / a.nranks) >> 3;          // 8-byte units of one owner slice
+  const long long lines = su * 16;                          // line bytes of one source (or owner) per area
+  const long long rs = region, ag = region + (long long)a.nranks * lines;
+  const long long first = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const char* in = a.base[a.rank] + a.in_off;
+  char* out = a.base[a.rank] + a.out_off;
+  const char* local = a.base[a.rank];
+
+  // 1. reduce-scatter push: this rank's part of every other owner's slice
+  for (long long u = first; u < su; u += stride)
+    for (int k = 1; k < a.nranks; ++k) {
+      const int j = (a.rank + k) % a.nranks;
+      const uint2 d = ld_payload(in + ((long long)j * su + u) * 8);
+      st_line(a.base[j] + rs + (long long)a.rank * lines + u * 16, d, tag);
+    }
+
+  // 2. reduce the owned slice in rank order, 3. push the result to every rank
+  bool ok = true;
+  for (long long u = first; u < su && ok; u += stride) {
+    float acc[U::N], x[U::N];
+    for (int src = 0; src < a.nranks && ok; ++src) {
+      uint2 d;
+      if (src == a.rank) {
+        d = ld_payload(in + ((long long)a.rank * su + u) * 8);
+      } else {
+        ok = wait_line(a, local + rs + (long long)src * lines + u * 16, tag, d, src, u);
+        if (!ok) break;
+      }
+      if (src == 0) {
+        U::unpack(d, acc);
+      } else {
+        U::unpack(d, x);
+#pragma unroll
+        for (int e = 0; e < U::N; ++e) acc[e] = combine<RED>(acc[e], x[e]);
+      }
+    }
+    if (!ok) break;
+    if (a.do_scale) {
+#pragma unroll
+      for (int e = 0; e < U::N; ++e) acc[e] *= a.scale;
+    }
+    const uint2 r = U::pack(acc);
+    st_payload(out + ((long long)a.rank * su + u) * 8, r);
+    const long long slot = ag + (long long)a.rank * lines + u * 16;
+    if (a.mc_base != nullptr) {
+      mc_st_line(a.mc_base + slot, r, tag);
+    } else {
+      for (int k = 1; k < a.nranks; ++k) st_line(a.base[(a.rank + k) % a.nranks] + slot, r, tag);
+    }
+  }
+
+  // 4. the other owners' reduced slices
+  for (long long u = first; u < su && ok; u += stride)
+    for (int k = 1; k < a.nranks && ok; ++k) {
+      const int j = (a.rank + k) % a.nranks;
+      uint2 d;
+      ok = wait_line(a, local + ag + (long long)j * lines + u * 16, tag, d, j, u);
+      if (ok) st_payload(out + ((long long)j * su + u) * 8, d);
+    }
+
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned int prev = atomicAdd(&a.control->ll_arrive, 1u);
+    if (prev == gridDim.x - 1) {
+      a.control->ll_arrive = 0;
+      a.control->ll_seq = seq + 1;
+      __threadfence();
+    }
+  }
+}
+
 template <int DT, int RED>
 cudaError_t launch_coll(const OneShotArgs& a, dim3 grid, cudaStream_t stream) {
   void* args[] = {const_cast<OneShotArgs*>(&a)};
+  if (a.coll == OS_ALLREDUCE_TWOSHOT)
+    return cudaLaunchCooperativeKernel((void*)twoshot_kernel<DT, RED>, grid, dim3(kThreads), args, 0, stream);
   if (a.coll == OS_ALLGATHER)
     return cudaLaunchCooperativeKernel((void*)oneshot_kernel<DT, RED, OS_ALLGATHER>, grid, dim3(kThreads), args, 0,
                                        stream);
@@ -288,6 +378,10 @@ int oneshot_max_ctas() {
   int b = 0;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, oneshot_kernel<DT_BF16, RED_SUM, OS_ALLREDUCE>, kThreads, 0);
   if (b < per_sm) per_sm = b;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, twoshot_kernel<DT_BF16, RED_SUM>, kThreads, 0);
+  if (b < per_sm) per_sm = b;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, twoshot_kernel<DT_F32, RED_SUM>, kThreads, 0);
+  if (b < per_sm) per_sm = b;
   const int v = sms * (per_sm < 1 ? 1 : per_sm);
   if (dev >= 0 && dev < 64) cached[dev] = v;
   return v;
@@ -295,9 +389,15 @@ int oneshot_max_ctas() {
 
 cudaError_t launch_oneshot(const OneShotArgs& a, cudaStream_t stream) {
   if (a.nranks < 1 || a.nranks > kMaxRanks || a.rank < 0 || a.rank >= a.nranks) return cudaErrorInvalidValue;
-  if (a.bytes <= 0 || a.bytes % 8 || a.ll_src_bytes < 2 * a.bytes) return cudaErrorInvalidValue;
   if (a.in_off % 8 || a.out_off % 8 || a.ll_off % 16 || a.ll_src_bytes % 16) return cudaErrorInvalidValue;
-  const long long units = a.bytes / 8;
+  if (a.coll == OS_ALLREDUCE_TWOSHOT) {
+    // both areas (4·bytes of lines) must fit the region half
+    if (a.bytes <= 0 || a.bytes % (8ll * a.nranks) || 4 * a.bytes > (long long)a.nranks * a.ll_src_bytes)
+      return cudaErrorInvalidValue;
+  } else if (a.bytes <= 0 || a.bytes % 8 || a.ll_src_bytes < 2 * a.bytes) {
+    return cudaErrorInvalidValue;
+  }
+  const long long units = a.coll == OS_ALLREDUCE_TWOSHOT ? a.bytes / 8 / a.nranks : a.bytes / 8;
   long long ctas = (units + kThreads - 1) / kThreads;
   const int cap = oneshot_max_ctas();
   if (ctas > cap) ctas = cap;

@@ -79,7 +79,7 @@ cudaError_t launch_dequantize_fp8(const unsigned char* q, const float* scales, v
                                   int dtype, cudaStream_t stream);
 
 // One-shot low-latency AllReduce / AllGather (flag-in-data lines pushed into every peer's LL region).
-enum OneShotColl : int { OS_ALLREDUCE = 0, OS_ALLGATHER = 1 };
+enum OneShotColl : int { OS_ALLREDUCE = 0, OS_ALLGATHER = 1, OS_ALLREDUCE_TWOSHOT = 2 };
 
 struct OneShotArgs {
   char* base[kMaxRanks];     // heap base of every rank in this process's address space

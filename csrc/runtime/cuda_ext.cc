@@ -112,12 +112,18 @@ BoundOneShot bind_oneshot(Heap& heap, size_t in_off, size_t out_off, size_t ll_o
                           int64_t bytes, int dtype, int redop, int coll, float scale, bool do_scale,
                           double timeout_s, bool multicast) {
   SymHeap& h = heap.get();
-  if (coll != OS_ALLREDUCE && coll != OS_ALLGATHER) throw std::runtime_error("one-shot: unknown collective");
+  if (coll != OS_ALLREDUCE && coll != OS_ALLGATHER && coll != OS_ALLREDUCE_TWOSHOT)
+    throw std::runtime_error("one-shot: unknown collective");
   if (dtype != DT_F32 && dtype != DT_BF16 && dtype != DT_F16) throw std::runtime_error("one-shot: unsupported dtype");
   if (bytes <= 0 || bytes % 8) throw std::runtime_error("one-shot: payload must be a positive multiple of 8 bytes");
   if (in_off % 8 || out_off % 8) throw std::runtime_error("one-shot: buffers must be 8-byte aligned");
-  if (ll_off % 16 || ll_src_bytes % 16 || ll_src_bytes < 2 * bytes)
-    throw std::runtime_error("one-shot: LL region too small or misaligned for this payload");
+  if (ll_off % 16 || ll_src_bytes % 16) throw std::runtime_error("one-shot: LL region misaligned");
+  if (coll == OS_ALLREDUCE_TWOSHOT) {
+    if (bytes % (8ll * h.nranks())) throw std::runtime_error("two-shot: payload must split into 8-byte units per rank");
+    if (4 * bytes > (int64_t)h.nranks() * ll_src_bytes) throw std::runtime_error("two-shot: LL region too small");
+  } else if (ll_src_bytes < 2 * bytes) {
+    throw std::runtime_error("one-shot: LL region too small for this payload");
+  }
   const size_t out_bytes = (size_t)bytes * (coll == OS_ALLGATHER ? h.nranks() : 1);
   if (in_off + (size_t)bytes > h.size() || out_off + out_bytes > h.size() ||
       ll_off + 2 * (size_t)h.nranks() * (size_t)ll_src_bytes > h.size())

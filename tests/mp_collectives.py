@@ -162,6 +162,39 @@ def main():
         if not inplace:
             comm.free(out)
     cases += oneshot
+    # two-shot AllReduce (opt-in path): run only when asked
+    if os.environ.get("VB_TWOSHOT") == "1":
+        two = CollectiveEngine(comm, twoshot_max_bytes=4 << 20)
+        twoshot = []
+        for dtype in (torch.float32, torch.bfloat16):
+            esize = torch.tensor([], dtype=dtype).element_size()
+            for nbytes in (2 << 20, 4 << 20):
+                for op in ("sum", "avg"):
+                    twoshot.append((dtype, nbytes // esize, op))
+        for dtype, count, op in twoshot:
+            dname = str(dtype).split(".")[-1]
+            plan = two.plan("allreduce", count, dtype, inplace=True, op=op)
+            assert plan.collective == "allreduce_twoshot", plan
+            seed = zlib.crc32(repr(("twoshot", dname, op, count)).encode()) % 100000
+            x = inputs_for(rank, count, dtype, seed).cuda()
+            buf = comm.empty(count, dtype)
+            ref = reference("allreduce", world, count, dtype, seed, op, rank)
+            worst, ok = 0.0, True
+            for rep in range(3):
+                buf.copy_(x)
+                torch.cuda.synchronize()
+                comm.run(plan, buf, buf, op=op)
+                torch.cuda.synchronize()
+                comm.check_status()
+                err = (buf.double().cpu() - ref).abs().max().item()
+                worst = max(worst, err)
+                ok = ok and err <= TOL[dtype] * max(1.0, ref.abs().max().item()) * world
+            failures += 0 if ok else 1
+            if rank == 0 or not ok:
+                print(json.dumps({"rank": rank, "coll": "allreduce", "path": "twoshot", "dtype": dname, "op": op,
+                                  "count": count, "max_err": worst, "ok": ok}), flush=True)
+            comm.free(buf)
+        cases += twoshot
     # broadcast / reduce (non-zero roots) and all-to-all through the engine, on non-heap tensors
     extra = [("broadcast", world - 1), ("reduce", world - 1), ("reduce", 0), ("alltoall", 0)]
     for coll, root in extra:

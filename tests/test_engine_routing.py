@@ -42,3 +42,15 @@ def test_large_allgathers_pull_from_peers():
     assert eng.use_multicast("allgather", "sum", AG_NVLS_MAX_BYTES - 16)
     assert not eng.use_multicast("allgather", "sum", AG_NVLS_MAX_BYTES)
     assert not CollectiveEngine(_Comm(2)).use_multicast("allreduce", "sum", 1 << 20)
+
+
+def test_twoshot_window_is_opt_in():
+    comm = _Comm(8)
+    off = CollectiveEngine(comm)
+    assert off.twoshot_max_bytes == 0 and not off.use_twoshot("allreduce", 1 << 21, torch.bfloat16)
+    on = CollectiveEngine(comm, twoshot_max_bytes=8 << 20)
+    assert on.use_twoshot("allreduce", 1 << 21, torch.bfloat16)            # 4 MiB
+    assert not on.use_twoshot("allreduce", 1 << 19, torch.bfloat16)        # 1 MiB: one-shot range
+    assert not on.use_twoshot("allgather", 1 << 21, torch.bfloat16)
+    plan = on.plan("allreduce", 1 << 21, torch.bfloat16, inplace=True)
+    assert plan.collective == "allreduce_twoshot" and comm.requests[-1] == ("allreduce_twoshot", 8 << 20)

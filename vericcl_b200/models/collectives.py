@@ -27,13 +27,17 @@ MAX_ITERS = 8
 
 class CollectiveEngine:
     def __init__(self, comm, *, method: str = "hierarchy", slices_per_rank: int | None = None,
-                 max_lanes: int | None = None, oneshot_max_bytes: int | None = None):
+                 max_lanes: int | None = None, oneshot_max_bytes: int | None = None,
+                 twoshot_max_bytes: int | None = None):
         self.comm = comm
         self.method = method
         self.slices_per_rank = slices_per_rank
         if oneshot_max_bytes is None:
             oneshot_max_bytes = int(os.environ.get("VERICCL_ONESHOT_MAX", ONESHOT_MAX_BYTES))
         self.oneshot_max_bytes = oneshot_max_bytes
+        if twoshot_max_bytes is None:
+            twoshot_max_bytes = int(os.environ.get("VERICCL_TWOSHOT_MAX", 0))
+        self.twoshot_max_bytes = twoshot_max_bytes
         self._max_ctas = comm._mod.max_ctas(512)
         self.max_lanes = max_lanes or self._max_ctas
         self._staging: dict = {}
@@ -69,10 +73,20 @@ class CollectiveEngine:
         return (collective in ("allreduce", "allgather") and self.comm.world > 1 and 0 < nbytes
                 <= self.oneshot_max_bytes and nbytes % 8 == 0)
 
+    def use_twoshot(self, collective: str, count: int, dtype) -> bool:
+        """Mid-size AllReduce (above the one-shot range, up to ``twoshot_max_bytes``; off unless set)."""
+        nbytes = count * torch.tensor([], dtype=dtype).element_size()
+        world = self.comm.world
+        return (collective == "allreduce" and world > 1 and self.oneshot_max_bytes < nbytes <= self.twoshot_max_bytes
+                and nbytes % (8 * world) == 0)
+
     def plan(self, collective: str, count: int, dtype, *, inplace: bool, op: str = "sum", root: int = 0):
         world = self.comm.world
         if self.use_oneshot(collective, count, dtype):
             return self.comm.oneshot_plan(collective, self.oneshot_max_bytes,
+                                          multicast=self.comm.multicast and world > 2)
+        if self.use_twoshot(collective, count, dtype):
+            return self.comm.oneshot_plan("allreduce_twoshot", self.twoshot_max_bytes,
                                           multicast=self.comm.multicast and world > 2)
         default = 1 if collective in ("allgather", "broadcast") else world
         slices = self.slices_per_rank or default

@@ -66,7 +66,7 @@ class OneShotPlan:
     device_plan: object = None
 
 
-ONESHOT_COLLS = {"allreduce": 0, "allgather": 1}
+ONESHOT_COLLS = {"allreduce": 0, "allgather": 1, "allreduce_twoshot": 2}
 
 
 class Communicator:
@@ -220,7 +220,11 @@ class Communicator:
         """
         if collective not in ONESHOT_COLLS:
             raise RuntimeFailure("the one-shot path covers allreduce and allgather, not %s" % collective)
-        self._ensure_ll(max_bytes)
+        if collective == "allreduce_twoshot":
+            # both areas of the two-shot AllReduce (4 · bytes of lines) must fit one region half
+            self._ensure_ll(-(-4 * max_bytes // (16 * self.world)) * 16)
+        else:
+            self._ensure_ll(-(-max_bytes // 8) * 16)
         multicast = bool(multicast and self.multicast)
         key = ("oneshot", collective, multicast)
         plan = self._plans.get(key)
@@ -229,8 +233,8 @@ class Communicator:
             self._plans[key] = plan
         return plan
 
-    def _ensure_ll(self, max_bytes: int) -> None:
-        need = -(-max_bytes // 8) * 16
+    def _ensure_ll(self, need: int) -> None:
+        """LL region of two halves with ``need`` bytes of lines per source (grows, never shrinks)."""
         if self._ll is not None and self._ll[1] >= need:
             return
         if self._ll is not None:
@@ -238,7 +242,7 @@ class Communicator:
             torch.cuda.synchronize()
             self.barrier()
             self.heap.free(self._ll[0])
-        total = int(self._mod.oneshot_region_bytes(self.world, max_bytes))
+        total = 2 * self.world * need
         offset = self.heap.alloc(total)
         self.heap.tensor(offset, total // 4, 0).zero_()
         torch.cuda.synchronize()
@@ -257,6 +261,8 @@ class Communicator:
             nbytes = count * inp.element_size()
             if nbytes > plan.max_bytes:
                 raise RuntimeFailure("one-shot plan holds %d bytes per rank, call has %d" % (plan.max_bytes, nbytes))
+            if plan.collective == "allreduce_twoshot" and nbytes % (8 * self.world):
+                raise RuntimeFailure("two-shot AllReduce needs a payload of whole 8-byte units per rank")
             in_off, out_off = self.offset_of(inp), self.offset_of(out)
             offsets = (in_off, out_off, nbytes)
             if offsets not in plan.checked:
