@@ -8,8 +8,8 @@
 // waits poll with ld.acquire.sys (warp 0, one wait per lane), publications
 // use st.release.sys after a CTA barrier.  Every wait is bounded by a
 // %globaltimer deadline; on expiry the CTA records the failure in the
-// control block, raises the abort word for the other CTAs and returns, so a
-// broken schedule or a missing peer never hangs the GPU.
+// control block's status word, which the other CTAs' waits poll and stop on,
+// and returns, so a broken schedule or a missing peer never hangs the GPU.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
