@@ -121,23 +121,35 @@ def analyze_trace_causality(traces, clock_maps, *, tails: int = 5):
             "overlapping_ranks": uncertain}
 
 
-def capture_once(comm, plan, inp, out, *, warmup: int = 3, op: str = "sum", scale=None, count_per_rank=None):
+def capture_once(comm, plan, inp, out, *, warmup: int = 3, op: str = "sum", scale=None, count_per_rank=None,
+                 steady: bool = False):
     """Warm up, bracket one traced invocation with clock samples, return this rank's records + clock map.
 
     Every rank calls this collectively.  The returned dict holds the rank's
     decoded records and its fitted :class:`ClockMap`; gather them (for example
     with ``comm.all_gather_object``) and pass them to
-    :func:`analyze_trace_causality`.
+    :func:`analyze_trace_causality`.  By default the traced launch follows a
+    barrier (ranks start it at their own host pace); with ``steady`` it is
+    enqueued right behind the warm-up launches, so the ranks enter it the way
+    they enter back-to-back launches.
     """
     import torch
     from vericcl_b200.online.clock_sync import fit_transform
-    for _ in range(warmup):
-        comm.run(plan, inp, out, op=op, scale=scale, count_per_rank=count_per_rank)
-    torch.cuda.synchronize()
-    before = comm.clock_samples()
     buf = comm.trace_buffer(plan)
-    comm.barrier()
-    comm.run(plan, inp, out, op=op, scale=scale, count_per_rank=count_per_rank, trace=buf)
+    if steady:
+        torch.cuda.synchronize()
+        before = comm.clock_samples()
+        comm.barrier()
+        for _ in range(max(1, warmup)):
+            comm.run(plan, inp, out, op=op, scale=scale, count_per_rank=count_per_rank)
+        comm.run(plan, inp, out, op=op, scale=scale, count_per_rank=count_per_rank, trace=buf)
+    else:
+        for _ in range(warmup):
+            comm.run(plan, inp, out, op=op, scale=scale, count_per_rank=count_per_rank)
+        torch.cuda.synchronize()
+        before = comm.clock_samples()
+        comm.barrier()
+        comm.run(plan, inp, out, op=op, scale=scale, count_per_rank=count_per_rank, trace=buf)
     torch.cuda.synchronize()
     comm.check_status()
     after = comm.clock_samples()

@@ -99,6 +99,8 @@ def main(argv=None) -> int:
     ap.add_argument("--lanes", type=int, default=None)
     ap.add_argument("--iters", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--steady", action="store_true",
+                    help="trace a launch enqueued right behind the warm-up launches (no barrier before it)")
     args = ap.parse_args(argv)
 
     import torch.distributed as dist
@@ -136,7 +138,7 @@ def main(argv=None) -> int:
     inp = comm.empty(count, dtype)
     inp.normal_()
     out = inp if inplace else comm.empty(out_count, dtype)
-    got = capture_once(comm, plan, inp, out, warmup=args.warmup)
+    got = capture_once(comm, plan, inp, out, warmup=args.warmup, steady=args.steady)
     outdir = Path(args.out)
     outdir.mkdir(parents=True, exist_ok=True)
     write_trace(outdir / ("trace-rank%d.bin" % comm.rank), comm.rank, plan.device_plan.nblocks * plan.nlanes,
@@ -147,6 +149,7 @@ def main(argv=None) -> int:
         clocks = {g["rank"]: g["clock"] for g in gathered}
         report = analyze_trace_causality(traces, clocks)
         report.update({"collective": coll, "ranks": world, "bytes_per_rank": args.bytes_per_rank,
+                       "steady": args.steady,
                        "dtype": args.dtype, "lanes": plan.nlanes, "iters": plan.niters, "nvls": plan.multicast,
                        "clock_uncertainty_us": {r: round(c.uncertainty_ns / 1e3, 3) for r, c in clocks.items()},
                        "timeline": timeline(traces, clocks)})
