@@ -124,7 +124,8 @@ def main(argv=None) -> int:
         coll = found.group(1) if found else coll
     out_count = count * world if coll == "allgather" else count
     comm = Communicator(heap_bytes=(count + out_count) * esize * 4 + (64 << 20), multicast=multicast)
-    eng = CollectiveEngine(comm, method=args.method, slices_per_rank=args.slices, oneshot_max_bytes=0)  # traces run the interpreter
+    # traces record the interpreter's steps, so the one-shot path is off here
+    eng = CollectiveEngine(comm, method=args.method, slices_per_rank=args.slices, oneshot_max_bytes=0)
     inplace = coll == "allreduce"
     if args.xml:
         lanes, iters = args.lanes or 1, args.iters or 1
