@@ -93,7 +93,8 @@ class ClockSampler:
         try:
             self.out = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
-                                          "-i", ",".join(str(d) for d in self.devices), "-lms", "100"], stdout=self.out, stderr=subprocess.DEVNULL)
+                                          "-i", ",".join(str(d) for d in self.devices), "-lms", "100"],
+                                         stdout=self.out, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
             return self

@@ -151,7 +151,8 @@ def main():
                 comm.free(inp)
                 comm.free(out)
             point = {"coll": coll, "n_gpus": world, "bytes_per_rank": size, "dtype": args.dtype, "graph": args.graph,
-                     "time_us": round(ours, 3), "host_enqueue_us": round(ours_host, 2), "busbw_gbs": round(nbytes / ours / 1e3 * factor, 2),
+                     "time_us": round(ours, 3), "host_enqueue_us": round(ours_host, 2),
+                     "busbw_gbs": round(nbytes / ours / 1e3 * factor, 2),
                      "path": plan.kind, "lanes": plan.nlanes, "iters": plan.niters, "nvls": plan.multicast,
                      "method": args.method,
                      "slices": eng.slices_per_rank or (1 if coll == "allgather" else world)}
