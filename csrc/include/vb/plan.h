@@ -3,6 +3,7 @@
 #include <map>
 #include <stdexcept>
 #include <string>
+#include <array>
 #include <vector>
 
 #include "vb/devprog.h"
@@ -58,6 +59,9 @@ struct RankProgram {
   std::vector<DevWait> waits;
   int i_chunks = 0, o_chunks = 0, s_chunks = 0;
   int s_used = 0;   // scratch chunks the device steps actually touch (fusion can drop them all)
+  // XML origin of every device step (same order as `steps`): thread-block id and step index, or
+  // {-1, -1} for steps the compiler added (in-place scaling)
+  std::vector<std::array<int, 2>> step_origins;
 };
 
 struct CompileStats {

@@ -73,6 +73,20 @@ PYBIND11_MODULE(_vbplan, m) {
       })
       .def_property_readonly("scratch_used", &CompiledPlan::max_scratch_used)
       .def("describe", [](const CompiledPlan& p, int r) { return describe_rank(p, r); })
+      .def("origins", [](const CompiledPlan& p, int r) {
+        // per device block: the (XML thread block id, XML step index) each device step came from
+        const RankProgram& rp = p.ranks.at(r);
+        py::list out;
+        for (const DevBlock& b : rp.blocks) {
+          py::list blk;
+          for (int s = 0; s < b.nsteps; ++s) {
+            const auto& o = rp.step_origins.at(b.step_begin + s);
+            blk.append(py::make_tuple(o[0], o[1]));
+          }
+          out.append(blk);
+        }
+        return out;
+      })
       .def("tables", [](const CompiledPlan& p, int r) {
         const RankProgram& rp = p.ranks.at(r);
         return py::make_tuple(as_bytes(rp.blocks), as_bytes(rp.steps), as_bytes(rp.srcs), as_bytes(rp.waits));

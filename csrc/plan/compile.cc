@@ -455,6 +455,7 @@ class Compiler {
     int prio = 0;
     int level = 0;             // dependency depth of the XML step
     int xml_tb = -1;
+    int xml_step = -1;         // index of the originating step in its XML thread block (-1: compiler-made)
     bool mc_peer = false;      // a copy replaced by the owner's multicast store
     int mc_buf = -1, mc_chunk = -1;
   };
@@ -497,6 +498,7 @@ class Compiler {
       ps.prio = topo_pos_[x];
       ps.level = level_[x];
       ps.xml_tb = a_.gpus[x.rank].tbs[x.tb].id;
+      ps.xml_step = x.step;
       ps.st.cnt = st.cnt;
       ps.st.flags = 0;
       if (st.depid >= 0) merge(ps.waits, completion(SRef{x.rank, tb_index_[x.rank].at(st.depid), st.deps}));
@@ -944,6 +946,7 @@ class Compiler {
             if (w.block >= 0) published_.insert({w.rank, w.block, w.event});
           }
           rp.steps.push_back(st);
+          rp.step_origins.push_back({ps.xml_step >= 0 ? ps.xml_tb : -1, ps.xml_step});
           ++stats_.device_steps;
         }
         blk.end_wait_begin = (int)rp.waits.size();

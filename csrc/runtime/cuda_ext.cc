@@ -281,6 +281,14 @@ class DevicePlan {
       for (int s = 0; s < rp.blocks[0].nsteps; ++s) out.push_back(rp.steps[rp.blocks[0].step_begin + s].op);
     return out;
   }
+  // (XML thread block id, XML step index) of every device step, per block ({-1, -1}: compiler-made step).
+  std::vector<std::vector<std::array<int, 2>>> step_origins() const {
+    std::vector<std::vector<std::array<int, 2>>> out;
+    const RankProgram& rp = plan_.ranks[rank_];
+    for (const auto& b : rp.blocks)
+      out.emplace_back(rp.step_origins.begin() + b.step_begin, rp.step_origins.begin() + b.step_begin + b.nsteps);
+    return out;
+  }
   // Opcode of every step, per block (the trace buffer indexes a CTA's records by its block's step count).
   std::vector<std::vector<int>> block_ops() const {
     std::vector<std::vector<int>> out;
@@ -370,6 +378,7 @@ PYBIND11_MODULE(_vbcuda, m) {
       .def("max_steps", &DevicePlan::max_steps)
       .def("step_ops", &DevicePlan::step_ops)
       .def("block_ops", &DevicePlan::block_ops)
+      .def("step_origins", &DevicePlan::step_origins)
       .def_property_readonly("nblocks", &DevicePlan::nblocks)
       .def_property_readonly("nlanes", &DevicePlan::nlanes)
       .def_property_readonly("niters", &DevicePlan::niters);

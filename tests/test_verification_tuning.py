@@ -54,3 +54,33 @@ def test_variants_keep_semantics():
     assert lower(variant_path(bundle.network, topo, send.operation_id)).can_execute
     rrc = [op for op in bundle.network.operations if op.kind == "rrc"][-1]
     assert lower(variant_reshape(bundle.network, topo, rrc.operation_id)).can_execute
+
+
+def test_measured_trace_tails_become_causes():
+    """A trace report's slowest device steps map back to operations and lead the strategy list."""
+    from vericcl_b200.program.device import compile_xml
+    from vericcl_b200.verification.bottlenecks import trace_causes
+    req = resolve_documents(example_documents("allgather", "hierarchy", 4, total_size_bytes=1 << 18,
+                                              slice_size_bytes=1 << 16, alpha_us=2.0, link_gbps=150.0))
+    model = initial_cost_model(req)
+    bundle = synthesize(req, model)
+    compiled = compile_xml(bundle.xml, nlanes=1)
+    ops_of = {(b.rank, b.tb_id): [x.operation_id for x in b.steps] for b in bundle.program.blocks}
+    network = {op.operation_id for op in bundle.network.operations}
+    # the slow step: rank 2's first device step that carries a network transfer
+    slow = next((2, b, s) for b, blk in enumerate(compiled.origins(2)) for s, (tb, step) in enumerate(blk)
+                if tb >= 0 and ops_of[(2, tb)][step] in network)
+    rows = []
+    for r in range(4):
+        for b, blk in enumerate(compiled.origins(r)):
+            for s, (tb, step) in enumerate(blk):
+                rows.append({"rank": r, "block": b, "step": s, "xml_tb": tb, "xml_step": step,
+                             "duration_us": 1.0 + (50.0 if (r, b, s) == slow else 0.0), "wait_us": 0.0})
+    report = {"timeline": rows, "global_span_us": 60.0}
+    causes = trace_causes(report, bundle, tails=3)
+    assert causes and causes[0].kind == "trace_tail" and causes[0].detail["rank"] == 2
+    ops = {op.operation_id for op in bundle.network.operations}
+    assert all(c.operation_id in ops for c in causes)
+    analysis = analyze(bundle, model, trace=report)
+    assert analysis.causes[0].kind == "trace_tail"
+    assert any(causes[0].operation_id in s.operations for s in analysis.strategies)

@@ -77,12 +77,17 @@ def new_run(args) -> int:
                         size_accounting=dict(request.size_accounting), overrides=list(args.overrides))
     executor = _probe_executor(request) if (purpose == "calibrate" or
                                             request.request_config["sketch"]["calibration"]["enabled"]) else None
-    measure = None
+    measure = trace_provider = None
     if request.request_config["sketch"]["trace_and_measure"]["enabled"] and executor is not None:
         from vericcl_b200.online.measure import measured_acceptance
+        from vericcl_b200.online.trace_worker import trace_report_for_xml
         measure = measured_acceptance(request, ctx.process / "statistics" / "ledger.jsonl")
+        counter = iter(range(1 << 30))
+        trace_provider = (lambda bundle: trace_report_for_xml(
+            bundle.xml, request, ctx.process / "traces" / ("round-%d" % next(counter))))
     wf = PrimaryWorkflow(request, ctx, purpose=purpose, tune=getattr(args, "tune", False), model=model,
-                         verify_inputs=verify_inputs, probe_executor=executor, measure=measure)
+                         verify_inputs=verify_inputs, probe_executor=executor, measure=measure,
+                         trace_provider=trace_provider)
     result = wf.run()
     if measure is not None and result.status == "ok" and (ctx.directory / "schedule.xml").exists():
         _trace_best(request, ctx)

@@ -30,7 +30,7 @@ import torch
 OP_NAMES = {0: "nop", 1: "copy", 2: "reduce", 3: "mc_reduce", 4: "mc_store", 5: "mc_allreduce"}
 
 
-def timeline(traces, clock_maps):
+def timeline(traces, clock_maps, origins=None):
     """Mean step times per (rank, step) in µs.
 
     A step "starts" when its waits are satisfied.  ``start_us`` is on the
@@ -51,7 +51,7 @@ def timeline(traces, clock_maps):
     for rank, recs in traces.items():
         cmap = clock_maps[rank]
         for r in recs:
-            a = acc[(rank, r.step)]
+            a = acc[(rank, r.block, r.step)]
             start = cmap.to_host(r.start_ns)
             a[0] += start - first
             a[1] += r.start_ns - local_first[rank]
@@ -60,10 +60,14 @@ def timeline(traces, clock_maps):
             a[4] += 1
             a[5] = r.op
     rows = []
-    for (rank, step), (s, ls, w, d, n, op) in sorted(acc.items()):
-        rows.append({"rank": rank, "step": step, "op": OP_NAMES.get(op, str(op)), "records": n,
-                     "start_us": round(s / n / 1e3, 3), "local_start_us": round(ls / n / 1e3, 3),
-                     "wait_us": round(w / n / 1e3, 3), "duration_us": round(d / n / 1e3, 3)})
+    for (rank, block, step), (s, ls, w, d, n, op) in sorted(acc.items()):
+        row = {"rank": rank, "block": block, "step": step, "op": OP_NAMES.get(op, str(op)), "records": n,
+               "start_us": round(s / n / 1e3, 3), "local_start_us": round(ls / n / 1e3, 3),
+               "wait_us": round(w / n / 1e3, 3), "duration_us": round(d / n / 1e3, 3)}
+        if origins is not None:
+            tb, xml_step = origins[rank][block][step]
+            row["xml_tb"], row["xml_step"] = tb, xml_step
+        rows.append(row)
     return rows
 
 
@@ -84,6 +88,19 @@ def capture_schedule_trace(xml_path, ranks: int, bytes_per_rank: int, datatype: 
     report = json.loads((out_dir / "trace.json").read_text())
     return {"path": str(out_dir / "trace.json"), "global_span_us": report["global_span_us"],
             "tails": report["tails"][:3]}
+
+
+def trace_report_for_xml(xml: str, request, out_dir, *, port: int = 29641) -> dict | None:
+    """Trace one invocation of ``xml`` on the request's local GPUs; the ``trace.json`` report (None on failure)."""
+    out_dir = Path(out_dir)
+    out_dir.mkdir(parents=True, exist_ok=True)
+    path = out_dir / "schedule.xml"
+    path.write_text(xml)
+    summary = capture_schedule_trace(path, request.rank_count, request.hyperparameters.total_size_bytes,
+                                     request.collective.datatype, out_dir, port=port)
+    if "error" in summary:
+        return None
+    return json.loads((out_dir / "trace.json").read_text())
 
 
 def main(argv=None) -> int:
@@ -144,16 +161,19 @@ def main(argv=None) -> int:
     outdir.mkdir(parents=True, exist_ok=True)
     write_trace(outdir / ("trace-rank%d.bin" % comm.rank), comm.rank, plan.device_plan.nblocks * plan.nlanes,
                 plan.device_plan.max_steps(), got["records"])
-    gathered = comm.all_gather_object({"rank": comm.rank, "records": got["records"], "clock": got["clock"]})
+    origins = [[tuple(o) for o in blk] for blk in plan.device_plan.step_origins()]
+    gathered = comm.all_gather_object({"rank": comm.rank, "records": got["records"], "clock": got["clock"],
+                                       "origins": origins})
     if comm.rank == 0:
         traces = {g["rank"]: g["records"] for g in gathered}
         clocks = {g["rank"]: g["clock"] for g in gathered}
+        step_origins = {g["rank"]: g["origins"] for g in gathered}
         report = analyze_trace_causality(traces, clocks)
         report.update({"collective": coll, "ranks": world, "bytes_per_rank": args.bytes_per_rank,
                        "steady": args.steady,
                        "dtype": args.dtype, "lanes": plan.nlanes, "iters": plan.niters, "nvls": plan.multicast,
                        "clock_uncertainty_us": {r: round(c.uncertainty_ns / 1e3, 3) for r, c in clocks.items()},
-                       "timeline": timeline(traces, clocks)})
+                       "timeline": timeline(traces, clocks, step_origins)})
         (outdir / "trace.json").write_text(json.dumps(report, indent=1, default=str))
         print(json.dumps({"trace": str(outdir / "trace.json"), "global_span_us": report["global_span_us"],
                           "records": sum(len(v) for v in traces.values())}))

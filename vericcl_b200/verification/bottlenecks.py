@@ -140,10 +140,41 @@ def choose_batch(strategies, batch_size: int):
     return [s for s in strategies if s.strategy_id in chosen][:batch_size]
 
 
-def analyze(bundle, model, *, batch_size: int = 16) -> Analysis:
+def trace_causes(report, bundle, *, tails: int = 5):
+    """``trace_tail`` causes: the slowest measured device steps, mapped back to their operations.
+
+    ``report`` is a trace report whose timeline rows carry the XML origin
+    (``xml_tb``, ``xml_step``) of each device step; the schedule's blocks map
+    an XML (rank, thread block, step) to its operation.
+    """
+    if not report or bundle.program is None:
+        return []
+    ops_of = {(b.rank, b.tb_id): [x.operation_id for x in b.steps] for b in bundle.program.blocks}
+    # only network transfers can be repaired; local copies of the lowering are skipped
+    network = {op.operation_id for op in bundle.network.operations} if bundle.network is not None else None
+    rows = sorted((r for r in report.get("timeline", ()) if r.get("xml_tb", -1) is not None
+                   and r.get("xml_tb", -1) >= 0), key=lambda r: (-r["duration_us"], r["rank"], r["step"]))
+    out, seen = [], set()
+    for row in rows:
+        ops = ops_of.get((row["rank"], row["xml_tb"]))
+        if not ops or not 0 <= row["xml_step"] < len(ops):
+            continue
+        op = ops[row["xml_step"]]
+        if op in seen or (network is not None and op not in network):
+            continue
+        seen.add(op)
+        out.append(Cause("trace_tail", op, {"duration_us": row["duration_us"], "wait_us": row.get("wait_us"),
+                                            "rank": row["rank"]}))
+        if len(out) >= tails:
+            break
+    return out
+
+
+def analyze(bundle, model, *, batch_size: int = 16, trace=None) -> Analysis:
+    """Causes on the predicted critical path (and, with a measured ``trace`` report, its slowest steps)."""
     pred = bundle.prediction
     path = pred.critical_path(bundle.executable)
-    causes = causes_on_path(bundle.executable, pred, model, path)
+    causes = trace_causes(trace, bundle) + causes_on_path(bundle.executable, pred, model, path)
     stream = list(strategy_stream(causes, bundle.network))
     return Analysis(pred.t_pred_us, path, causes, _utilisation(bundle.executable, pred),
                     choose_batch(stream, batch_size))

@@ -72,7 +72,8 @@ def accept_candidate(incumbent, candidate, *, tolerance: float = 1e-9) -> bool:
 
 class PrimaryWorkflow:
     def __init__(self, request, ctx, *, purpose: str = "solve", tune: bool = False, model: CostModel | None = None,
-                 verify_inputs: dict | None = None, probe_executor=None, measure=None, restored: dict | None = None):
+                 verify_inputs: dict | None = None, probe_executor=None, measure=None, restored: dict | None = None,
+                 trace_provider=None):
         self.request = request
         self.ctx = ctx
         self.purpose = purpose
@@ -82,6 +83,7 @@ class PrimaryWorkflow:
         self.verify_inputs = verify_inputs or {}
         self.probe_executor = probe_executor
         self.measure = measure
+        self.trace_provider = trace_provider   # bundle -> measured trace report (timeline with XML origins) or None
         self.measured_rejects: set = set()
         budgets = dict(request.request_config["sketch"]["budgets"])
         self.budgets = BudgetManager(budgets, cpu_budget=request.solver.cpu_budget)
@@ -274,8 +276,16 @@ class PrimaryWorkflow:
                     self.rounds.append(record)
                     return "no-improvement proof"
             try:
+                trace = None
+                if self.trace_provider is not None:
+                    try:
+                        trace = self.trace_provider(self.incumbent)
+                    except Exception as error:   # a failed capture leaves the round to the model alone
+                        self.ctx.emit("trace_failed", round=index, reason=str(error))
+                    if trace is not None:
+                        record["trace_span_us"] = trace.get("global_span_us")
                 with self.budgets.acquire("repair") as lease:
-                    analysis = analyze(self.incumbent, self.model, batch_size=batch)
+                    analysis = analyze(self.incumbent, self.model, batch_size=batch, trace=trace)
                     record["causes"] = [c.kind for c in analysis.causes][:20]
                     record["strategies"] = [s.as_json() for s in analysis.strategies]
                     lower = Lowerer(self.incumbent.request, self.topology, self.model)
