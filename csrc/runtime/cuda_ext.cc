@@ -248,6 +248,8 @@ class DevicePlan {
     a.start_slot = h.start_slot();
     for (int r = 0; r < h.nranks(); ++r) a.base[r] = h.base(r);
     a.mc_base = h.mc_base();
+    if (plan_.stats.multicast_ops > 0 && a.mc_base == nullptr)
+      throw std::runtime_error("the plan uses NVLS multicast but the heap has no multicast mapping");
     a.control = heap.control();
     a.timeout_ns = (unsigned long long)(timeout_s * 1e9);
     a.trace_buf = reinterpret_cast<unsigned long long*>(trace_ptr);

@@ -146,8 +146,8 @@ def main(argv=None) -> int:
     inplace = coll == "allreduce"
     if args.xml:
         lanes, iters = args.lanes or 1, args.iters or 1
-        plan = comm.compile(xml, nlanes=lanes, niters=iters, multicast=multicast and coll in ("allreduce",
-                                                                                              "allgather"))
+        plan = comm.compile(xml, nlanes=lanes, niters=iters,
+                            multicast=comm.multicast and coll in ("allreduce", "allgather"))
     else:
         plan = eng.plan(coll, count, dtype, inplace=inplace)
         if args.lanes or args.iters:

@@ -185,6 +185,8 @@ class Communicator:
     def compile(self, xml: str, *, nlanes: int = 1, niters: int = 1, elide: bool = True, fuse: bool = True,
                 multicast: bool = False, mc_share: tuple = (1, 1)) -> PlanHandle:
         import re
+        if multicast and not self.multicast:
+            raise RuntimeFailure("multicast mapping requested but this communicator's heap has no NVLS binding")
         coll = re.search(r'coll="([a-z_]+)"', xml)
         collective = coll.group(1) if coll else "allreduce"
         key = (xml, nlanes, niters, elide, fuse, multicast, tuple(mc_share))
