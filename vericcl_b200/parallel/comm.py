@@ -209,7 +209,10 @@ class Communicator:
             have = self._scratch.get(key)
             if have is None or have[1] < need:
                 if have is not None:
+                    # launches already enqueued may still use the old scratch, and bound launches name it
+                    torch.cuda.synchronize()
                     self.heap.free(have[0])
+                    self._bound = {k: v for k, v in self._bound.items() if k[0] != key}
                 self._scratch[key] = (self.heap.alloc(need), need)
             return self._scratch[key][0]
 
@@ -302,9 +305,10 @@ class Communicator:
             self._run_oneshot(plan, inp, out, op, scale, stream, count_per_rank)
             return
         tl_ptr = 0 if timeline is None else timeline.data_ptr()
+        bound_key = (id(plan), inp.data_ptr(), out.data_ptr(), count_per_rank, inp.numel(), out.numel(), inp.dtype,
+                     op, scale, nbatch, in_stride, out_stride, tl_ptr)
         if trace is None:
-            fast = self._bound.get((id(plan), inp.data_ptr(), out.data_ptr(), count_per_rank, inp.dtype, op, scale,
-                                    nbatch, in_stride, out_stride, tl_ptr))
+            fast = self._bound.get(bound_key)
             if fast is not None:
                 fast.launch((torch.cuda.current_stream() if stream is None else stream).cuda_stream)
                 return
@@ -345,8 +349,7 @@ class Communicator:
             bound = plan.device_plan.bind(self.heap, in_off, out_off, scr_off, count, DTYPE_CODES[inp.dtype],
                                           REDOPS[op], float(factor), self.timeout_s, 512, nbatch, strides, tl_ptr,
                                           lean)
-            self._bound[(id(plan), inp.data_ptr(), out.data_ptr(), count_per_rank, inp.dtype, op, scale, nbatch,
-                         in_stride, out_stride, tl_ptr)] = bound
+            self._bound[bound_key] = bound
             bound.launch(stream.cuda_stream)
             return
         plan.device_plan.run(self.heap, in_off, out_off, scr_off, count, DTYPE_CODES[inp.dtype], REDOPS[op],
