@@ -164,3 +164,21 @@ def test_oneshot_kernel_single_rank(comm, dtype):
     assert comm.status()["ll_seq"] == seq0 + 6
     comm.free(x)
     comm.free(y)
+
+
+def test_bound_launch_follows_the_tensor_size(comm):
+    """The same plan and pointers with a longer view must not replay the shorter launch."""
+    from vericcl_b200.synthesis import schedule_xml
+    plan = comm.compile(schedule_xml("allreduce", 1, 1, inplace=False, datatype="float32"), nlanes=8)
+    n = 1 << 14
+    x = comm.empty(2 * n, torch.float32)
+    y = comm.empty(2 * n, torch.float32)
+    x.copy_(torch.randn(2 * n, device="cuda"))
+    y.zero_()
+    comm.run(plan, x[:n], y[:n], scale=2.0)
+    comm.run(plan, x, y, scale=2.0)
+    torch.cuda.synchronize()
+    comm.check_status()
+    assert torch.allclose(y, x * 2.0)
+    comm.free(x)
+    comm.free(y)
