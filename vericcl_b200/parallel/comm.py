@@ -268,6 +268,10 @@ class Communicator:
                 raise RuntimeFailure("one-shot plan holds %d bytes per rank, call has %d" % (plan.max_bytes, nbytes))
             if plan.collective == "allreduce_twoshot" and nbytes % (8 * self.world):
                 raise RuntimeFailure("two-shot AllReduce needs a payload of whole 8-byte units per rank")
+            need_out = count * (self.world if plan.collective == "allgather" else 1)
+            if inp.numel() < count or out.numel() < need_out:
+                raise RuntimeFailure("one-shot %s needs %d input and %d output elements, got %d and %d"
+                                     % (plan.collective, count, need_out, inp.numel(), out.numel()))
             in_off, out_off = self.offset_of(inp), self.offset_of(out)
             offsets = (in_off, out_off, nbytes)
             if offsets not in plan.checked:
@@ -319,6 +323,10 @@ class Communicator:
         esize = inp.element_size()
         scr_off = self.scratch_for(plan, count, inp.dtype, copies=nbatch)
         chunk, _ = plan.device_plan.geometry(count, DTYPE_CODES[inp.dtype])
+        if inp.numel() < plan.slots[0] * chunk or out.numel() < plan.slots[1] * chunk:
+            raise RuntimeFailure("%s plan reads %d and writes %d elements per instance; tensors hold %d and %d"
+                                 % (plan.collective, plan.slots[0] * chunk, plan.slots[1] * chunk, inp.numel(),
+                                    out.numel()))
         scr_stride = plan.slots[2] * chunk * esize
         strides = [in_stride * esize, out_stride * esize, scr_stride]
         key = (in_off, out_off, scr_off, count, nbatch, tuple(strides))
