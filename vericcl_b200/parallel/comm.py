@@ -109,8 +109,9 @@ class Communicator:
         self._plans: dict = {}
         self._scratch: dict = {}
         self._ll = None              # (offset, bytes per source) of the one-shot LL region
-        # VERICCL_LEAN=1: sum/avg launches use the interpreter instance with register-lean unrolls
-        self.lean = _env_flag("VERICCL_LEAN", False)
+        # Sum/avg launches use the register-lean interpreter instance when VERICCL_LEAN=1, and by default on a
+        # single rank, where every step is a one-source copy (its copies keep eight vectors in flight per thread)
+        self.lean = _env_flag("VERICCL_LEAN", self.world == 1)
         self._lock = threading.Lock()
         self._closed = False
 
