@@ -112,3 +112,31 @@ def test_experiment_report_tables(tmp_path):
     assert "| allreduce | 4 | graph | 1 KiB | one-shot NVLS | 6.1 |" in table
     cmds = matrix_commands([2, 8], graph=True)
     assert cmds[1][4] == "--nproc-per-node=8" and cmds[1][-1] == "--graph"
+
+
+def test_calibration_reuse_adopts_a_cached_model(tmp_path):
+    from vericcl_b200.execution.context import RunContext
+    from vericcl_b200.input.loader import load_request
+    from vericcl_b200.online.campaign import save_calibration
+    from vericcl_b200.workflow import PrimaryWorkflow
+    index = tmp_path / "calibrations.json"
+    d = example_documents("allgather", "hierarchy", 4, total_size_bytes=1 << 16, slice_size_bytes=1 << 14,
+                          calibration=True)
+    d["sketch"]["history"] = {"calibration_reuse": True, "calibration_index": str(index),
+                              "calibration_max_age_s": 3600}
+    files = write_documents(tmp_path / "in", d)
+    req = load_request(files)
+    ctx = RunContext.create(tmp_path, "c", "solve", run_id="r1", input_files=files)
+
+    def no_probes(job):
+        raise AssertionError("a fresh cached calibration must not run probes")
+    wf = PrimaryWorkflow(req, ctx, probe_executor=no_probes)
+    cached, _ = wf.model.with_updates("measured-cached")
+    save_calibration(index, wf._calibration_identity(), cached)
+    assert wf.calibration() is True and wf.model.version == "measured-cached"
+    # a different workload (datatype) has another identity and falls back to probing (none here: skipped)
+    d["sketch"]["collective"]["datatype"] = "bfloat16"
+    files2 = write_documents(tmp_path / "in2", d)
+    wf2 = PrimaryWorkflow(load_request(files2), RunContext.create(tmp_path, "c", "solve", run_id="r2",
+                                                                  input_files=files2))
+    assert wf2.calibration() is False and wf2.model.version != "measured-cached"

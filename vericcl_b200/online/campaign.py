@@ -103,10 +103,11 @@ def calibration_identity(request, device_names=(), driver: str = "") -> str:
 
 
 def save_calibration(index_path, identity: str, model) -> None:
+    from vericcl_b200.utils.jsonio import atomic_write_json
     path = Path(index_path)
     data = json.loads(path.read_text()) if path.exists() else {}
     data[identity] = {"model": model.as_json(), "saved": time.time()}
-    path.write_text(json.dumps(data, indent=2))
+    atomic_write_json(path, data)
 
 
 def lookup_calibration(index_path, identity: str, max_age_s: float):

@@ -231,8 +231,33 @@ class PrimaryWorkflow:
                                                 "reason": reason, "model_version": self.model.version})
         self.ctx.emit("candidate_adopted", id=bundle.candidate_id, t_pred_us=bundle.t_pred_us, reason=reason)
 
+    def _calibration_identity(self):
+        """Cache key of a calibration: the GPUs (UUIDs), driver, datatype, reduction and rank count."""
+        from vericcl_b200.execution.transport import machine_inventory
+        from vericcl_b200.online.campaign import calibration_identity
+        inv = machine_inventory()
+        return calibration_identity(self.request, [g["uuid"] for g in inv["gpus"]], inv.get("driver") or "")
+
+    def reuse_calibration(self) -> bool:
+        """Adopt a cached calibrated model of the same machine and workload when one is fresh enough."""
+        from vericcl_b200.online.campaign import lookup_calibration
+        hist = self.request.request_config["sketch"]["history"]
+        if not hist.get("calibration_reuse"):
+            return False
+        cached = lookup_calibration(hist["calibration_index"], self._calibration_identity(),
+                                    hist["calibration_max_age_s"])
+        if cached is None or dict(cached.context) != dict(self.model.context):
+            return False
+        self.model = cached
+        self.ctx.emit("calibration_reused", version=cached.version)
+        if self.incumbent is not None:
+            self.incumbent = self.reevaluate(self.incumbent)
+        return True
+
     def calibration(self):
-        from vericcl_b200.online.campaign import run_calibration
+        from vericcl_b200.online.campaign import run_calibration, save_calibration
+        if self.reuse_calibration():
+            return True
         if self.probe_executor is None:
             self.ctx.emit("calibration_skipped", reason="no probe executor (GPU runtime) available")
             return False
@@ -250,6 +275,9 @@ class PrimaryWorkflow:
             return False
         self.model = model
         self.ctx.emit("model_published", version=model.version, components=len(diff))
+        hist = self.request.request_config["sketch"]["history"]
+        if hist.get("calibration_reuse"):
+            save_calibration(hist["calibration_index"], self._calibration_identity(), model)
         if self.incumbent is not None:
             self.incumbent = self.reevaluate(self.incumbent)
         return True
