@@ -52,3 +52,10 @@ def test_emulated_two_groups_use_hierarchy():
     assert bundle.plan.mode.value == "hierarchy"
     ok, _ = check_program_numerics(parse_xml(bundle.xml), count_per_rank=8 * 16)
     assert ok
+
+
+def test_device_memory_budget_is_checked():
+    d = example_documents("allgather", "hierarchy", 4, total_size_bytes=4 * 4096, slice_size_bytes=4096)
+    d["runtime"]["device_memory_budget_bytes"] = 1024
+    bundle = synthesize(resolve_documents(d))
+    assert bundle.checks["storage"]["status"] != "valid" and "device bytes" in str(bundle.checks["storage"])

@@ -13,11 +13,11 @@ from vericcl_b200.execution.ownership import GPUOwnershipRegistry, local_gpu_uui
 from vericcl_b200.execution.transport import HostRunner, export_manifest, is_local, machine_inventory
 
 FAKE_DRIVER = """#!{py}
-import json, sys
+import json, os, sys
 cfg = json.load(open(sys.argv[1]))
 rank = cfg["rank"]
 with open(cfg["receipt"], "w") as f:
-    json.dump({{"rank": rank, "nranks": cfg["nranks"], "bad": 0,
+    json.dump({{"rank": rank, "nranks": cfg["nranks"], "bad": 0, "env": os.environ.get("VB_TEST_ENV"),
                "device_times_us": [10.0 + rank, 20.0 - rank, 30.0]}}, f)
 if "trace" in cfg:
     open(cfg["trace"], "wb").write(b"trace-of-rank-%d" % rank)
@@ -118,3 +118,22 @@ def test_inventory_and_manifest(tmp_path):
     doc = json.loads(Path(path).read_text())
     assert {f["path"] for f in doc["files"]} == {"schedule.xml", "process/events.jsonl"}
     assert all(len(f["sha256"]) == 64 for f in doc["files"]) and doc["inventory"] == {"host": "h"}
+
+
+def test_runtime_environment_reaches_every_rank(fakes, tmp_path, monkeypatch):
+    import json as _json
+    from vericcl_b200.execution import native as native_mod
+    root, ssh, scp, driver = fakes
+    seen = []
+    real = native_mod.combine_schedule_results
+
+    def spy(receipts):
+        seen.extend(r.get("env") for r in receipts)
+        return real(receipts)
+    monkeypatch.setattr(native_mod, "combine_schedule_results", spy)
+    drv = NativeScheduleDriver("<algo/>", 2, binary=driver, hosts=["localhost", "node-c.invalid"],
+                               environment={"VB_TEST_ENV": "x y"},
+                               runner_factory=lambda h: HostRunner(h, ssh=str(ssh), scp=str(scp)))
+    drv.measure(count=16, iters=1, timeout_s=20)
+    assert seen == ["x y", "x y"]
+    assert _json  # module used above

@@ -46,7 +46,7 @@ class NativeScheduleDriver:
     """
 
     def __init__(self, xml: str, nranks: int, *, devices=None, binary=None, port: int | None = None, hosts=None,
-                 registry=None, owner: str | None = None, runner_factory=None):
+                 registry=None, owner: str | None = None, runner_factory=None, environment=None):
         from vericcl_b200.execution.transport import HostRunner
         self.xml = xml
         self.nranks = nranks
@@ -63,6 +63,8 @@ class NativeScheduleDriver:
         self.runners = [factory(h) for h in self.hosts]
         self.registry = registry
         self.owner = owner or "native-%s" % secrets.token_hex(4)
+        # runtime.environment of the request: exported to every rank's process
+        self.environment = {str(k): str(v) for k, v in (environment or {}).items()}
 
     def _local_uuids(self):
         from vericcl_b200.execution.ownership import local_gpu_uuids
@@ -135,9 +137,13 @@ class NativeScheduleDriver:
                 path = tmp / ("config-%d.json" % rank)
                 path.write_text(json.dumps(cfg))
                 cfg_arg = str(path) if runner.local else runner.stage([path], session)[path]
-                argv = runner.command([where["binary"], cfg_arg])
+                if runner.local:
+                    argv, env = runner.command([where["binary"], cfg_arg]), dict(os.environ, **self.environment)
+                else:
+                    exports = ["%s=%s" % kv for kv in sorted(self.environment.items())]
+                    argv, env = runner.command((["env"] + exports if exports else []) + [where["binary"], cfg_arg]), None
                 p = subprocess.Popen(argv, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True,
-                                     start_new_session=True)
+                                     start_new_session=True, env=env)
                 procs.append((p, ProcessIdentity(p.pid, os.getpgid(p.pid), start_time(p.pid), boot_id()), where))
             deadline = time.monotonic() + timeout_s * 3 + 30
             codes = []

@@ -20,9 +20,13 @@ DTYPE_CODES = {"float32": 0, "bfloat16": 1, "float16": 2}
 def native_measure(xml: str, request, *, iters: int = 5, warmup: int = 2, nlanes: int = 32) -> float:
     elem = request.element_bytes
     count = request.hyperparameters.total_size_bytes // elem
-    ranks = sorted(request.request_config["runtime"]["rank_map"], key=lambda e: e["rank"])
+    runtime = request.request_config["runtime"]
+    ranks = sorted(runtime["rank_map"], key=lambda e: e["rank"])
+    paths = runtime.get("paths") or {}
     driver = NativeScheduleDriver(xml, request.rank_count, hosts=[e.get("host", "localhost") for e in ranks],
-                                  devices=[e.get("device", e["rank"]) for e in ranks])
+                                  devices=[e.get("device", e["rank"]) for e in ranks],
+                                  binary=paths.get("vericcl_native") or None,
+                                  environment=runtime.get("environment") or {})
     res = driver.measure(count=count, dtype=DTYPE_CODES.get(request.collective.datatype, 0), nlanes=nlanes,
                          warmup=warmup, iters=iters, timeout_s=60.0)
     if res["bad"]:

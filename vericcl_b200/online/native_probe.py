@@ -56,7 +56,8 @@ def _run_all(request):
         cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
                "--nproc-per-node=%d" % request.rank_count, "--master-addr", "127.0.0.1", "--master-port", "29621",
                "-m", "vericcl_b200.online.probe_worker", str(spec)]
-        env = dict(os.environ, PYTHONPATH=str(root) + os.pathsep + os.environ.get("PYTHONPATH", ""))
+        extra = {str(k): str(v) for k, v in (request.request_config["runtime"].get("environment") or {}).items()}
+        env = dict(os.environ, **extra, PYTHONPATH=str(root) + os.pathsep + os.environ.get("PYTHONPATH", ""))
         res = run_owned_process(cmd, timeout_s=float(cfg["job_timeout_s"]), env=env, cwd=str(root))
         if res.returncode != 0 or not out.exists():
             raise RuntimeFailure("probe job failed (%s): %s" % (res.returncode, res.stderr[-2000:]))

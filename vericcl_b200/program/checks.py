@@ -151,6 +151,14 @@ def check_storage(program, request):
     for rank, count in program.scratch_slots.items():
         if count * size > budget:
             issues.append("rank %d needs %d scratch bytes, budget %d" % (rank, count * size, budget))
+    device_budget = request.request_config["runtime"].get("device_memory_budget_bytes") or 0
+    if device_budget > 0:
+        # input, output and scratch buffers of the schedule, per rank (0 = no budget)
+        for rank in range(program.rank_count):
+            total = (program.input_slots.get(rank, 0) + program.output_slots.get(rank, 0)
+                     + program.scratch_slots.get(rank, 0)) * size
+            if total > device_budget:
+                issues.append("rank %d needs %d device bytes, budget %d" % (rank, total, device_budget))
     return issues
 
 

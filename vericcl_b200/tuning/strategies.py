@@ -181,8 +181,12 @@ class RepairOutcome:
     reason: str = ""
 
 
-def solve_repair(incumbent, strategies, *, lower, lease=None, max_channels: int = 16):
-    """Evaluate strategy variants; return the best strictly-improving bundle (if any)."""
+def solve_repair(incumbent, strategies, *, lower, lease=None, max_channels: int = 16, batch_size: int | None = None):
+    """Evaluate strategy variants; return the best strictly-improving bundle (if any).
+
+    The ``batch_size`` best improving variants (by exact T_pred) enter the
+    event-column combination model together (all of them when None).
+    """
     from vericcl_b200.tuning.event_columns import solve_event_columns
     network = incumbent.network
     if network is None:
@@ -210,8 +214,9 @@ def solve_repair(incumbent, strategies, *, lower, lease=None, max_channels: int 
                 improving.append((strategy, variant, bundle))
     if not improving:
         return RepairOutcome(False, incumbent, evaluated, [], "no strictly better variant")
-    best = min(improving, key=lambda item: item[2].t_pred_us)[2]
-    combined = solve_event_columns(incumbent, improving, lower=lower)
+    improving.sort(key=lambda item: item[2].t_pred_us)
+    best = improving[0][2]
+    combined = solve_event_columns(incumbent, improving[:batch_size] if batch_size else improving, lower=lower)
     if combined is not None and combined.t_pred_us < best.t_pred_us - 1e-9:
         best = combined
     return RepairOutcome(True, best, evaluated, [(s.strategy_id, b.t_pred_us) for s, _, b in improving])

@@ -317,7 +317,9 @@ class PrimaryWorkflow:
                     record["causes"] = [c.kind for c in analysis.causes][:20]
                     record["strategies"] = [s.as_json() for s in analysis.strategies]
                     lower = Lowerer(self.incumbent.request, self.topology, self.model)
-                    outcome = solve_repair(self.incumbent, analysis.strategies, lower=lower, lease=lease)
+                    outcome = solve_repair(self.incumbent, analysis.strategies, lower=lower, lease=lease,
+                                           batch_size=self.request.request_config["sketch"]["repair"][
+                                               "candidate_batch_size"])
                     candidates = [outcome.best] if outcome.improved else []
                     for branch in branches(self.incumbent.request, self.incumbent):
                         lease.check()
