@@ -141,7 +141,8 @@ class NativeScheduleDriver:
                     argv, env = runner.command([where["binary"], cfg_arg]), dict(os.environ, **self.environment)
                 else:
                     exports = ["%s=%s" % kv for kv in sorted(self.environment.items())]
-                    argv, env = runner.command((["env"] + exports if exports else []) + [where["binary"], cfg_arg]), None
+                    prefix = ["env"] + exports if exports else []
+                    argv, env = runner.command(prefix + [where["binary"], cfg_arg]), None
                 p = subprocess.Popen(argv, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True,
                                      start_new_session=True, env=env)
                 procs.append((p, ProcessIdentity(p.pid, os.getpgid(p.pid), start_time(p.pid), boot_id()), where))
@@ -155,7 +156,8 @@ class NativeScheduleDriver:
                 codes.append(p.returncode)
             errors = [p.stderr.read() if p.stderr else "" for p, _, _ in procs]
             if any(c != 0 for c in codes):
-                raise RuntimeFailure("native driver failed: codes %s; %s" % (codes, " | ".join(e[-400:] for e in errors)))
+                raise RuntimeFailure("native driver failed: codes %s; %s"
+                                     % (codes, " | ".join(e[-400:] for e in errors)))
             receipts = []
             for rank, (runner, (_, _, where)) in enumerate(zip(self.runners, procs)):
                 local_receipt = tmp / ("receipt-%d.json" % rank)
