@@ -137,3 +137,20 @@ def test_runtime_environment_reaches_every_rank(fakes, tmp_path, monkeypatch):
     drv.measure(count=16, iters=1, timeout_s=20)
     assert seen == ["x y", "x y"]
     assert _json  # module used above
+
+
+def test_hung_rank_is_terminated_and_reported(fakes, tmp_path):
+    """A rank that never finishes is killed at the deadline; the others' results are not combined."""
+    _, _, _, driver = fakes
+    hang = _script(tmp_path / "hang_driver", "#!/bin/sh\n"
+                   "case \"$(cat \"$1\")\" in *'\"rank\": 1'*) exec sleep 600;; esac\n"
+                   "exec \"%s\" \"$1\"\n" % driver)
+    reg = GPUOwnershipRegistry(tmp_path / "owners.json")
+    drv = NativeScheduleDriver("<algo/>", 2, binary=hang, registry=reg, owner="job-4")
+    import time
+    t0 = time.monotonic()
+    with pytest.raises(RuntimeFailure, match="codes"):
+        drv.measure(count=16, iters=1, timeout_s=0.5, grace_s=1.0)
+    assert time.monotonic() - t0 < 30
+    # the hung rank's group was terminated, so its GPU is released rather than quarantined
+    assert reg.unresolved("job-4") == []

@@ -75,9 +75,12 @@ class NativeScheduleDriver:
         return [uuids[d] for d in devices]
 
     def measure(self, *, count: int, dtype: int = 0, redop: int = 0, scale: float = 1.0, nlanes: int = 32,
-                niters: int = 1, warmup: int = 3, iters: int = 10, timeout_s: float = 60.0, trace_dir=None):
+                niters: int = 1, warmup: int = 3, iters: int = 10, timeout_s: float = 60.0, trace_dir=None,
+                grace_s: float = 30.0):
         """Device-timed invocations; with ``trace_dir`` every rank also writes
-        ``trace-rank<r>.bin`` (per-step trace of its last invocation)."""
+        ``trace-rank<r>.bin`` (per-step trace of its last invocation).  A rank
+        still running ``3 · timeout_s + grace_s`` after the launch has its
+        process group terminated and the measurement fails."""
         uuids = self._local_uuids() if self.registry is not None else []
         if uuids:
             self.registry.acquire(uuids, self.owner)
@@ -85,7 +88,7 @@ class NativeScheduleDriver:
         self.last_clean = True
         try:
             result = self._run(session, count, dtype, redop, scale, nlanes, niters, warmup, iters, timeout_s,
-                               trace_dir)
+                               trace_dir, grace_s)
         except Exception:
             if uuids:
                 if self.last_clean:
@@ -103,7 +106,8 @@ class NativeScheduleDriver:
                 self.registry.quarantine(uuids, self.owner, "a rank's process group outlived its deadline")
         return result
 
-    def _run(self, session, count, dtype, redop, scale, nlanes, niters, warmup, iters, timeout_s, trace_dir):
+    def _run(self, session, count, dtype, redop, scale, nlanes, niters, warmup, iters, timeout_s, trace_dir,
+             grace_s=30.0):
         from vericcl_b200.ops.build import OUT
         all_local = all(r.local for r in self.runners)
         control = "127.0.0.1" if all_local else self.hosts[0]
@@ -146,13 +150,17 @@ class NativeScheduleDriver:
                 p = subprocess.Popen(argv, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True,
                                      start_new_session=True, env=env)
                 procs.append((p, ProcessIdentity(p.pid, os.getpgid(p.pid), start_time(p.pid), boot_id()), where))
-            deadline = time.monotonic() + timeout_s * 3 + 30
+            deadline = time.monotonic() + timeout_s * 3 + grace_s
             codes = []
             for p, ident, _ in procs:
                 try:
                     p.wait(max(1.0, deadline - time.monotonic()))
                 except subprocess.TimeoutExpired:
                     self.last_clean = terminate_group(ident) and self.last_clean
+                    try:
+                        p.wait(5.0)            # reap it, so its exit status is known
+                    except subprocess.TimeoutExpired:
+                        self.last_clean = False
                 codes.append(p.returncode)
             errors = [p.stderr.read() if p.stderr else "" for p, _, _ in procs]
             if any(c != 0 for c in codes):

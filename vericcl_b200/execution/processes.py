@@ -25,12 +25,25 @@ def boot_id() -> str:
         return "unknown"
 
 
-def start_time(pid: int) -> int | None:
+def _stat(pid: int):
     try:
-        fields = Path("/proc/%d/stat" % pid).read_text().rsplit(")", 1)[1].split()
-        return int(fields[19])
-    except (OSError, IndexError, ValueError):
+        return Path("/proc/%d/stat" % pid).read_text().rsplit(")", 1)[1].split()
+    except (OSError, IndexError):
         return None
+
+
+def start_time(pid: int) -> int | None:
+    fields = _stat(pid)
+    try:
+        return int(fields[19]) if fields else None
+    except (IndexError, ValueError):
+        return None
+
+
+def is_zombie(pid: int) -> bool:
+    """True when the process has exited and only waits to be reaped by its parent."""
+    fields = _stat(pid)
+    return bool(fields) and fields[0] in ("Z", "X")
 
 
 @dataclass(frozen=True)
@@ -41,7 +54,9 @@ class ProcessIdentity:
     boot_id: str
 
     def alive(self) -> bool:
-        return boot_id() == self.boot_id and start_time(self.pid) == self.start_ticks and self.start_ticks is not None
+        """The recorded process still runs (an exited process awaiting its reaper counts as gone)."""
+        return (boot_id() == self.boot_id and self.start_ticks is not None and start_time(self.pid) == self.start_ticks
+                and not is_zombie(self.pid))
 
 
 @dataclass
