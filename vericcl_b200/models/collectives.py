@@ -28,16 +28,25 @@ MAX_ITERS = 8
 class CollectiveEngine:
     def __init__(self, comm, *, method: str = "hierarchy", slices_per_rank: int | None = None,
                  max_lanes: int | None = None, oneshot_max_bytes: int | None = None,
-                 twoshot_max_bytes: int | None = None):
+                 twoshot_max_bytes: int | None = None, ag_nvls_max_bytes: int | None = None,
+                 tuning: dict | None = None):
         self.comm = comm
         self.method = method
         self.slices_per_rank = slices_per_rank
+        explicit = {"oneshot_max_bytes": oneshot_max_bytes, "twoshot_max_bytes": twoshot_max_bytes,
+                    "ag_nvls_max_bytes": ag_nvls_max_bytes}
         if oneshot_max_bytes is None:
             oneshot_max_bytes = int(os.environ.get("VERICCL_ONESHOT_MAX", ONESHOT_MAX_BYTES))
         self.oneshot_max_bytes = oneshot_max_bytes
         if twoshot_max_bytes is None:
             twoshot_max_bytes = int(os.environ.get("VERICCL_TWOSHOT_MAX", 0))
         self.twoshot_max_bytes = twoshot_max_bytes
+        self.ag_nvls_max_bytes = AG_NVLS_MAX_BYTES if ag_nvls_max_bytes is None else ag_nvls_max_bytes
+        if tuning is not None:
+            # thresholds measured on this machine (vericcl_b200.models.tuner); explicit arguments still win
+            for name, given in explicit.items():
+                if given is None and name in tuning:
+                    setattr(self, name, int(tuning[name]))
         self._max_ctas = comm._mod.max_ctas(512)
         self.max_lanes = max_lanes or self._max_ctas
         self._staging: dict = {}
@@ -56,16 +65,16 @@ class CollectiveEngine:
     def use_multicast(self, collective: str, op: str, nbytes: int = 0) -> bool:
         """NVLS pays off from 4 ranks up (it cuts AllReduce NVLink traffic from 2(P-1)/P·M to about (1+1/P)·M).
 
-        AllGather moves (P-1)·M into every GPU either way; from ``AG_NVLS_MAX_BYTES``
-        per rank, peer pulls in rotated order (rank r reads r+1, r+2, … first) were
-        faster than owner multicast stores on 4 B200s (16 MiB: 117 vs 132 µs;
-        64 MiB: 364 vs 423 µs), so large AllGathers use them.
+        AllGather moves (P-1)·M into every GPU either way; from ``ag_nvls_max_bytes``
+        per rank (default ``AG_NVLS_MAX_BYTES``), peer pulls in rotated order (rank r
+        reads r+1, r+2, … first) were faster than owner multicast stores on 4 B200s
+        (16 MiB: 117 vs 132 µs; 64 MiB: 364 vs 423 µs), so large AllGathers use them.
         """
         if not self.comm.multicast or self.comm.world < 4:
             return False
         if collective == "allreduce":
             return op in ("sum", "avg")
-        return collective == "allgather" and nbytes < AG_NVLS_MAX_BYTES
+        return collective == "allgather" and nbytes < self.ag_nvls_max_bytes
 
     def use_oneshot(self, collective: str, count: int, dtype) -> bool:
         """Small AllReduce / AllGather payloads go through the one-shot kernel (one NVLink trip, no barrier)."""
