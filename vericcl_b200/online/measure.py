@@ -6,7 +6,8 @@ invocation).  ``measured_acceptance`` builds the workflow hook: for an
 (incumbent, candidate) pair it runs the pre-planned AB/BA pairs, draws the
 significance level from the task ledger and returns the comparison verdict.
 With ``VERICCL_EMULATE`` set, the interpreter paces inter-group steps, which
-is how the two-group online configuration is emulated on one NVSwitch box.
+is how the two-group online configuration is emulated on one NVSwitch box
+(reference: vericcl/online/acceptance.py:110-168 for the paired comparison).
 """
 from __future__ import annotations
 

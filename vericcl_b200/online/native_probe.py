@@ -7,7 +7,8 @@ size, for ``launches`` rounds of ``timed_iterations`` device-timed
 iterations after ``warmup_iterations``; the time of an iteration is the max
 over ranks.  The child runs as an owned process group with the calibration
 job deadline.  Returns ``None`` when no GPU is visible, so the workflow
-records calibration as skipped.
+records calibration as skipped (reference counterpart:
+vericcl/verification/online/remote.py:442, ``NativeProbeDriver``).
 """
 from __future__ import annotations
 

@@ -1,4 +1,11 @@
-"""torchrun worker that executes calibration probe jobs (one process per GPU)."""
+"""torchrun worker that executes calibration probe jobs (one process per GPU).
+
+Counterpart of the reference's ``vericcl-probe`` binary
+(runtime/probes/main.cu:130) launched per rank by
+vericcl/verification/online/remote.py:233 (``_probe_command``): here every
+job's probe XML runs through the same compiler and interpreter as real
+schedules.
+"""
 from __future__ import annotations
 
 import json

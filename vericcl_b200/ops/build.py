@@ -9,6 +9,8 @@
 Outputs live next to the package (``vericcl_b200/_native/``) so they travel
 with a source snapshot; a stamp file holding the hash of sources and flags
 decides whether a rebuild is needed.
+(reference counterparts: runtime/build_runtime.py:72, runtime/build_probes.py:45 and
+runtime/build_native.py:46, which build the patched MSCCL, the probe binary and the native driver).
 """
 from __future__ import annotations
 

@@ -7,10 +7,12 @@ directed graph whose links all belong to the sender's ``nvlink-tx`` and the
 receiver's ``nvlink-rx`` shared resources, plus one NVLS multicast group over
 all ranks when the switch supports in-network reduction.  Units follow the
 request schema: α in µs, β in µs per byte, capacities in bytes per µs.
+Shared per-GPU resources follow the reference's shared-NIC template
+(README.md:155-166 there), applied to NVLink ports.
 """
 from __future__ import annotations
 
-# Measured on this pool's B200s: peer copy ~770 GB/s per direction per GPU
+# Measured on B200s: peer copy ~770 GB/s per direction per GPU
 # (nominal 900 GB/s).  1 GB/s = 1000 bytes/us.
 B200_NVLINK_GBPS = 770.0
 B200_ALPHA_US = 1.5
