@@ -49,7 +49,9 @@ def example_documents(operator: str = "allreduce", method: str = "hierarchy", ra
         "trace_and_measure": {"enabled": False, "job_timeout_s": 300, "trace_capacity_bytes": 1 << 24},
     }
     atom = {"synthesis_method": method, "M_switch": 1 << 24}
-    runtime = {"rank_map": [{"rank": r, "host": "localhost", "device": r % 8} for r in range(topo["ranks"])],
+    # eight GPUs per host: ranks beyond the first eight go to further (named) hosts
+    hosts = ["localhost" if topo["ranks"] <= 8 else "node-%d" % (r // 8) for r in range(topo["ranks"])]
+    runtime = {"rank_map": [{"rank": r, "host": hosts[r], "device": r % 8} for r in range(topo["ranks"])],
                "environment": {"NCCL_BUFFSIZE": str(1 << 26)},
                "scratch_bytes_per_rank": scratch_bytes,
                "control": {"bind_address": "127.0.0.1", "port": 24950}}
