@@ -124,6 +124,13 @@ TOPOLOGY = obj({
                               doc="Rank sets that share an NVLS multicast object (NVSwitch in-switch reduction)."),
     "local_costs": array(obj({"rank": integer(), "copy": COST, "reduce": COST}, required=("rank",)),
                          default=[], doc="Initial local copy/reduce costs."),
+    "provenance": obj({
+        "legacy_format": string(enum=("taccl_topology_v2",), doc="Format of the converted source."),
+        "reference_slice_bytes": integer(minimum=1, doc="Chunk size the source durations refer to."),
+        "source_topology": string(doc="Canonical JSON of the source topology."),
+        "source_sketch": string(doc="Canonical JSON of the source sketch.")},
+        required=("legacy_format", "reference_slice_bytes", "source_topology", "source_sketch"),
+        doc="Sources of a topology converted from another format (topology/legacy.py)."),
 }, required=("ranks", "nodes", "directed_links"))
 
 BUDGETS = {k: positive() for k in (

@@ -43,8 +43,6 @@ def nvswitch_topology(ranks: int, *, alpha_us: float = B200_ALPHA_US, link_gbps:
                               "capacity_bytes_per_us": port * 1000.0, "links": tx[r]})
             resources.append({"id": "nvlink-rx-%d" % r, "kind": "nvlink_port",
                               "capacity_bytes_per_us": port * 1000.0, "links": rx[r]})
-    copy_beta = 2.0 / (hbm_gbps * 1000.0)   # a copy reads and writes every byte
-    reduce_beta = 3.0 / (hbm_gbps * 1000.0)  # two reads and one write
     return {
         "name": name or "nvswitch-b200-x%d" % ranks,
         "ranks": ranks,
@@ -53,9 +51,16 @@ def nvswitch_topology(ranks: int, *, alpha_us: float = B200_ALPHA_US, link_gbps:
         "shared_resources": resources,
         "groups": [],
         "multicast_groups": [list(range(ranks))] if nvls and ranks > 1 else [],
-        "local_costs": [{"rank": r, "copy": {"alpha_us": 1.0, "beta_us_per_byte": copy_beta},
-                         "reduce": {"alpha_us": 1.0, "beta_us_per_byte": reduce_beta}} for r in range(ranks)],
+        "local_costs": hbm_local_costs(ranks, hbm_gbps),
     }
+
+
+def hbm_local_costs(ranks: int, hbm_gbps: float = B200_HBM_GBPS) -> list:
+    """Local copy and reduce costs of HBM-bound kernels for every rank."""
+    copy_beta = 2.0 / (hbm_gbps * 1000.0)   # a copy reads and writes every byte
+    reduce_beta = 3.0 / (hbm_gbps * 1000.0)  # two reads and one write
+    return [{"rank": r, "copy": {"alpha_us": 1.0, "beta_us_per_byte": copy_beta},
+             "reduce": {"alpha_us": 1.0, "beta_us_per_byte": reduce_beta}} for r in range(ranks)]
 
 
 def multinode_topology(groups: int, per_group: int, *, intra_gbps: float = B200_NVLINK_GBPS,
