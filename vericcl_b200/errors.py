@@ -24,6 +24,14 @@ class SemanticError(VericclError):
     exit_code = 5
 
 
+class ScratchBudgetError(SemanticError):
+    """The scratch budget cannot hold a schedule's execution order; ``needed_bytes`` would."""
+
+    def __init__(self, message: str, needed_bytes: int):
+        super().__init__(message)
+        self.needed_bytes = needed_bytes
+
+
 class SolverError(VericclError):
     """The MILP backend failed or returned an unusable result."""
 

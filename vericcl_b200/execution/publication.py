@@ -25,6 +25,14 @@ def write_report(ctx, result: dict, best: dict | None) -> Path:
             for key, value in sorted(checks.items()):
                 detail = str(value.get("detail", ""))[:120].replace("|", "/")
                 lines.append("| %s | %s | %s |" % (key, value.get("status"), detail))
+    recs = result.get("recommendations") or []
+    if recs:
+        lines += ["", "## Recommended input changes", "", "| change | parameters | reasons | re-solve |",
+                  "|---|---|---|---|"]
+        for r in recs:
+            params = ", ".join("%s=%s" % kv for kv in sorted(r["parameters"].items()))
+            lines.append("| %s | %s | %s | %s |" % (r["kind"], params, ", ".join(r["reason_codes"]),
+                                                   "yes" if r["requires_resolve"] else "no"))
     for key in ("rounds", "proof", "measured", "issues"):
         if result.get(key):
             lines += ["", "## %s" % key.capitalize(), "", "```", str(result[key])[:4000], "```"]

@@ -37,15 +37,17 @@ def _divisors(m: int):
     return small + large[::-1]
 
 
-def initial_parameter_domain(request, *, max_candidates: int = 16):
+def initial_parameter_domain(request, *, max_candidates: int = 16, max_channels: int | None = None,
+                             scratch_bytes: int | None = None, free_slice: bool = False):
+    """Legal choices; the keywords relax the request's channel limit, scratch budget or fixed slice."""
     spec = request.collective
     p = request.rank_count
     m = request.hyperparameters.total_size_bytes
     elem = request.element_bytes
     limits = request.request_config["runtime"]["limits"]
-    scratch = request.request_config["runtime"]["scratch_bytes_per_rank"]
-    max_channels = request.solver.max_channels
-    fixed = request.hyperparameters.slice_size_bytes
+    scratch = request.request_config["runtime"]["scratch_bytes_per_rank"] if scratch_bytes is None else scratch_bytes
+    max_channels = request.solver.max_channels if max_channels is None else max_channels
+    fixed = None if free_slice else request.hyperparameters.slice_size_bytes
     out = []
     for n in sorted(_divisors(m // elem), reverse=True):
         s = m // n

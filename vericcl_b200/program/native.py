@@ -4,7 +4,8 @@ Each instruction becomes endpoints: a ``send`` is an ``s`` step on the sender
 and an ``r`` step on the receiver; an ``rrc`` is ``s`` + ``rrc``; a local
 ``copy`` is ``cpy``.  Endpoints go to thread blocks keyed by (rank,
 direction, peer, channel) — or (rank, fused, peer, channel) with the fused
-layout.  A step carries at most one cross-TB dependency, so extra waits become
+layout; a rank's copies share one TB, split round-robin over more when they
+exceed the steps-per-TB limit.  A step carries at most one cross-TB dependency, so extra waits become
 dependency-only ``nop`` steps; waits already implied by TB order or earlier
 waits are dropped using per-endpoint ancestor bitsets (reference:
 vericcl/xml/v5_program.py:15-94).  The XML uses the MSCCL attribute set
@@ -21,11 +22,11 @@ from vericcl_b200.program.model import NativeBlock, NativeProgram, NativeStep
 from vericcl_b200.semantics.collective import CollectiveKind, runtime_chunks
 
 
-def _endpoints(ins, storage):
+def _endpoints(ins, storage, lane=0):
     src = storage.addresses[ins.inputs[0]]
     dst = storage.addresses[ins.output]
     if ins.kind == "copy":
-        return ((ins.rank, "copy", -1, -1, "cpy", src, dst),)
+        return ((ins.rank, "copy", -1, -1 - lane, "cpy", src, dst),)
     recv_src = storage.addresses[ins.inputs[1]] if ins.kind == "rrc" else dst
     return ((src.rank, "send", dst.rank, ins.channel, "s", src, dst),
             (dst.rank, "recv", src.rank, ins.channel, "rrc" if ins.kind == "rrc" else "r", recv_src, dst))
@@ -39,8 +40,21 @@ def lower_program(storage, request, *, tb_layout: str | None = None, name: str =
     location, step_owner, dep_of = {}, {}, {}
     bits, ancestors, order = {}, {}, {}
     block_anc, seq = defaultdict(int), defaultdict(int)
+    # a rank's local copies share one TB unless they exceed the steps-per-TB limit; then they are dealt
+    # round-robin over as many copy TBs as the limit needs
+    limit = request.request_config["runtime"]["limits"]["steps_per_tb"]
+    copies = defaultdict(int)
     for ins in storage.instructions:
-        eps = _endpoints(ins, storage)
+        if ins.kind == "copy":
+            copies[ins.rank] += 1
+    lanes = {r: -(-c // limit) for r, c in copies.items()}
+    dealt = defaultdict(int)
+    for ins in storage.instructions:
+        lane = 0
+        if ins.kind == "copy":
+            lane = dealt[ins.rank] % lanes[ins.rank]
+            dealt[ins.rank] += 1
+        eps = _endpoints(ins, storage, lane)
         ranks = {e[0] for e in eps}
         assigned = defaultdict(list)
         for pred in sorted(ins.dependencies):

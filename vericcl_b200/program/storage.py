@@ -15,7 +15,7 @@ import heapq
 from collections import defaultdict
 from types import MappingProxyType
 
-from vericcl_b200.errors import SemanticError
+from vericcl_b200.errors import ScratchBudgetError, SemanticError
 from vericcl_b200.program.model import Address, Instruction, StoragePlan, Value
 from vericcl_b200.semantics.collective import CollectiveKind, input_ranks, required_outputs
 from vericcl_b200.semantics.versions import canonical
@@ -47,7 +47,8 @@ def _ordered(operations):
     return out
 
 
-def build_storage_plan(candidate, request, scratch_budget_bytes: int | None = None) -> StoragePlan:
+def build_storage_plan(candidate, request, scratch_budget_bytes: int | None = None, *,
+                       _probe: bool = False) -> StoragePlan:
     spec = request.collective
     p, n = candidate.rank_count, candidate.slice_count
     size = candidate.slice_size_bytes
@@ -177,7 +178,11 @@ def build_storage_plan(candidate, request, scratch_budget_bytes: int | None = No
             elif len(pool) < scratch_capacity:
                 slot_index = len(pool)
             else:
-                raise SemanticError("scratch budget (%d slots) cannot hold this execution order" % scratch_capacity)
+                if _probe:
+                    raise ScratchBudgetError("scratch budget too small", 0)
+                needed = _needed_scratch(candidate, request, scratch_capacity, size)
+                raise ScratchBudgetError("scratch budget (%d slots) cannot hold this execution order; %d bytes "
+                                         "per rank would" % (scratch_capacity, needed), needed)
             addresses[ins.output] = Address(ins.rank, "s", slot_index)
             pool[slot_index] = ins.output
         all_up = set(deps)
@@ -192,6 +197,19 @@ def build_storage_plan(candidate, request, scratch_budget_bytes: int | None = No
     return StoragePlan(MappingProxyType(states), tuple(initial), tuple(final), MappingProxyType(addresses),
                        MappingProxyType(outputs), MappingProxyType(input_slots), MappingProxyType(output_slots),
                        MappingProxyType({r: len(pools[r]) for r in range(p)}), tuple(reuse))
+
+
+def _needed_scratch(candidate, request, capacity: int, size: int) -> int:
+    """The smallest scratch budget (bytes per rank) that holds this execution order."""
+    unbounded = build_storage_plan(candidate, request, scratch_budget_bytes=1 << 62, _probe=True)
+    most = max(unbounded.scratch_slots.values(), default=0)
+    for slots in range(capacity + 1, most):
+        try:
+            build_storage_plan(candidate, request, scratch_budget_bytes=slots * size, _probe=True)
+            return slots * size
+        except ScratchBudgetError:
+            continue
+    return most * size
 
 
 def _a(address: Address):

@@ -28,7 +28,8 @@ from __future__ import annotations
 import time
 from dataclasses import dataclass, field, replace
 
-from vericcl_b200.errors import BudgetExhausted, SemanticError, SolverError
+from vericcl_b200.errors import (BudgetExhausted, InputValidationError, ScratchBudgetError, SemanticError,
+                                 SolverError)
 from vericcl_b200.execution.budget import BudgetManager
 from vericcl_b200.execution.checkpoint import save_checkpoint
 from vericcl_b200.execution.context import finalize_run
@@ -53,10 +54,12 @@ class RunResult:
     proof: dict | None = None
     timing: dict = field(default_factory=dict)
     issues: list = field(default_factory=list)
+    recommendations: list = field(default_factory=list)
 
     def as_json(self):
         return {"status": self.status, "stop_reason": self.stop_reason, "best": self.best, "rounds": self.rounds,
-                "proof": self.proof, "timing": self.timing, "issues": self.issues}
+                "proof": self.proof, "timing": self.timing, "issues": self.issues,
+                "recommendations": self.recommendations}
 
 
 def accept_candidate(incumbent, candidate, *, tolerance: float = 1e-9) -> bool:
@@ -85,6 +88,7 @@ class PrimaryWorkflow:
         self.measure = measure
         self.trace_provider = trace_provider   # bundle -> measured trace report (timeline with XML origins) or None
         self.measured_rejects: set = set()
+        self.failure_recommendations: list = []    # input changes derived from candidates that failed to lower
         budgets = dict(request.request_config["sketch"]["budgets"])
         self.budgets = BudgetManager(budgets, cpu_budget=request.solver.cpu_budget)
         self.candidates = []
@@ -169,7 +173,14 @@ class PrimaryWorkflow:
             if self.request.hyperparameters.slice_size_bytes is not None:
                 choices = [None]
             else:
-                choices = initial_parameter_domain(self.request)[:4]
+                try:
+                    choices = initial_parameter_domain(self.request)[:4]
+                except InputValidationError as error:
+                    from vericcl_b200.program.recommendations import describe, recommend_for_domain
+                    recs = recommend_for_domain(self.request)
+                    if not recs:
+                        raise
+                    raise InputValidationError("%s; recommended: %s" % (error, describe(recs))) from error
             methods = [self.request.selected_synthesis_method]
             if not self.request.request_config["atom"]["manual"]["enabled"]:
                 methods.append("constructive_trees" if methods[0] == "hierarchy" else "hierarchy")
@@ -193,6 +204,11 @@ class PrimaryWorkflow:
                                             channels=channels)
                     except (SemanticError, SolverError) as error:
                         self.ctx.emit("candidate_failed", method=method, error=str(error))
+                        if isinstance(error, ScratchBudgetError):
+                            self.failure_recommendations.append(
+                                {"kind": "increase_scratch_budget", "priority": 1,
+                                 "parameters": {"scratch_bytes_per_rank": error.needed_bytes},
+                                 "reason_codes": ["scratch"], "requires_resolve": False})
                         continue
                     self.store(bundle, "initial")
         self.stage_times["initial_s"] = time.monotonic() - t0
@@ -415,7 +431,8 @@ class PrimaryWorkflow:
                     "checks": self.incumbent.checks,
                     "slice_size_bytes": self.incumbent.request.hyperparameters.slice_size_bytes}
         status = "ok" if (best is not None or self.purpose == "calibrate") else "no_candidate"
-        result = RunResult(status, stop, best, self.rounds, self.proof, self.stage_times)
+        result = RunResult(status, stop, best, self.rounds, self.proof, self.stage_times,
+                           recommendations=self.recommendations())
         publish_results(self.ctx, xml=self.incumbent.xml if self.incumbent else None,
                         sidecar=to_sidecar(self.incumbent) if self.incumbent else None,
                         model=self.model.as_json(), result=result.as_json(), best=best)
@@ -425,6 +442,15 @@ class PrimaryWorkflow:
         self.checkpoint("finished")
         finalize_run(self.ctx, result.as_json())
         return result
+
+    def recommendations(self) -> list:
+        """Input changes for candidates that failed their launch or storage check (none when one runs)."""
+        if self.incumbent is not None and self.incumbent.can_execute:
+            return []
+        from vericcl_b200.program.recommendations import merge, recommend_for_program
+        groups = [recommend_for_program(b.program, b.request, b.checks or {}) for b in self.candidates
+                  if not b.can_execute and b.program is not None]
+        return merge(groups + [self.failure_recommendations])
 
     def restore_candidates(self):
         from vericcl_b200.program.sidecar import bundle_from_sidecar
