@@ -10,6 +10,7 @@ here is the ``signature`` of a demand).
 """
 from __future__ import annotations
 
+import heapq
 from collections import deque
 from dataclasses import dataclass, field
 
@@ -87,6 +88,40 @@ def _bfs_tree(topology, node, root, targets, allowed, sids, reverse=False):
     return edges, max(depth.values(), default=0)
 
 
+def _fastest_tree(topology, node, root, targets, allowed, sids, reverse=False):
+    """Arborescence of least per-byte time paths (sum of link β) from ``root`` (or into it)."""
+    best = {root: 0.0}
+    parent = {root: None}
+    heap = [(0.0, root)]
+    done = set()
+    while heap:
+        d, cur = heapq.heappop(heap)
+        if cur in done:
+            continue
+        done.add(cur)
+        nbrs = topology.in_neighbors(cur) if reverse else topology.out_neighbors(cur)
+        for nxt in nbrs:
+            if nxt not in allowed:
+                continue
+            a, b = (nxt, cur) if reverse else (cur, nxt)
+            if not _usable(topology, node, a, b, 0, sids):
+                continue
+            nd = d + topology.link(LinkKey(a, b)).beta_us_per_byte
+            if nd < best.get(nxt, float("inf")) - 1e-15:
+                best[nxt], parent[nxt] = nd, cur
+                heapq.heappush(heap, (nd, nxt))
+    if not set(targets) <= set(parent):
+        return None
+    needed = set()
+    for t in targets:
+        while t is not None and t != root:
+            needed.add(t)
+            t = parent[t]
+    order = sorted(needed, key=lambda r: (_dist(parent, r), r))
+    edges = [((r, parent[r]) if reverse else (parent[r], r)) for r in order]
+    return edges, max((_dist(parent, r) for r in needed), default=0)
+
+
 def _dist(parent, r):
     d = 0
     while parent[r] is not None:
@@ -121,6 +156,10 @@ def candidate_trees(topology: Topology, node: PlanNode, kind: str, root: int, me
     bfs = _bfs_tree(topology, node, root, members, allowed, sids, reverse)
     if bfs is not None and tuple(bfs[0]) not in {t.edges for t in out}:
         out.append(Tree("bfs", tuple(bfs[0]), bfs[1]))
+    # on links of unequal speed a relay can beat the direct hop
+    fast = _fastest_tree(topology, node, root, members, allowed, sids, reverse)
+    if fast is not None and tuple(fast[0]) not in {t.edges for t in out}:
+        out.append(Tree("fastest", tuple(fast[0]), fast[1]))
     if len(members) > 2:
         edges, depth = _binomial(root, sorted(members), reverse)
         if all(_usable(topology, node, a, b, 0, sids) for a, b in edges):

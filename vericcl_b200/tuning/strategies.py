@@ -70,8 +70,8 @@ def variant_order(candidate, topology, op_id, advance=1.0):
                             "repair:order", candidate.channels)
 
 
-def variant_path(candidate, topology, op_id, avoid=()):
-    """Reroute a send a→b through relay c (a→c then c→b), choosing the relay with the least load."""
+def variant_path(candidate, topology, op_id, avoid=(), via=None):
+    """Reroute a send a→b through relay c (a→c then c→b): ``via`` when given, else the least-loaded relay."""
     by_id = {op.operation_id: op for op in candidate.operations}
     op = by_id[op_id]
     if op.kind != "send":
@@ -82,6 +82,8 @@ def variant_path(candidate, topology, op_id, avoid=()):
         load[other.dst_rank] = load.get(other.dst_rank, 0) + 1
     relays = [c for c in range(candidate.rank_count) if c not in (op.src_rank, op.dst_rank)
               and topology.has_link(op.src_rank, c) and topology.has_link(c, op.dst_rank)]
+    if via is not None:
+        relays = [c for c in relays if c == via]
     if not relays:
         raise SemanticError("no relay available for " + op_id)
     c = min(relays, key=lambda r: (load.get(r, 0), r))
@@ -161,7 +163,7 @@ def implementations(strategy, candidate, topology, *, max_channels: int = 16):
             elif strategy.family == "order":
                 out.append(variant_order(candidate, topology, op_id, float(params.get("advance", 1))))
             elif strategy.family == "path":
-                out.append(variant_path(candidate, topology, op_id, params.get("avoid", ())))
+                out.append(variant_path(candidate, topology, op_id, params.get("avoid", ()), params.get("via")))
             elif strategy.family == "joint":
                 v = variant_channel(candidate, topology, op_id, params.get("channel", 0) % max_channels)
                 out.append(variant_path(v, topology, op_id, params.get("avoid", ())))

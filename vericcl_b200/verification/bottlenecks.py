@@ -8,7 +8,9 @@ classifies each link of it:
   shared resource (NVLink port, NIC) was split with concurrent flows;
 * ``tb_wait`` — the operation started later than its data was ready because
   its thread block was still busy with earlier work (TB order);
-* ``critical_service`` — the operation's own α + β·S dominates.
+* ``critical_service`` — the operation's own α + β·S dominates; for a send
+  whose link is slower than both hops of some relay a→c→b, the cause names
+  that relay and a ``path`` strategy moves the send onto it.
 
 Strategies are then generated lazily, round-robin over the eight families
 (path, allocation, order, channel, joint, internal_root, structure,
@@ -85,8 +87,37 @@ def causes_on_path(executable, prediction, model, path):
         elif start > ready + 1e-9:
             out.append(Cause("tb_wait", key, {"waited_us": start - ready}))
         else:
-            out.append(Cause("critical_service", key, {"alpha_us": cost.alpha_us if cost else None}))
+            detail = {"alpha_us": cost.alpha_us if cost else None}
+            relay = _faster_relay(model, op)
+            if relay is not None:
+                detail["relay"] = relay
+            out.append(Cause("critical_service", key, detail))
     return out
+
+
+def _faster_relay(model, op):
+    """A rank c whose two hops a→c→b each move this payload faster than the direct link a→b, or None."""
+    if not (op.cost_key or "").startswith("link:"):
+        return None
+    _, a, b = op.cost_key.split(":")
+    direct = model.service_for(op.cost_key, op.payload_bytes)
+    if direct is None:
+        return None
+    limit = direct.time_us(op.payload_bytes)
+    best = None
+    for key in model.services:
+        parts = key.split(":")
+        if parts[0] != "link" or parts[1] != a or parts[2] == b:
+            continue
+        c = parts[2]
+        first = model.service_for(key, op.payload_bytes)
+        second = model.service_for("link:%s:%s" % (c, b), op.payload_bytes)
+        if first is None or second is None:
+            continue
+        slower = max(first.time_us(op.payload_bytes), second.time_us(op.payload_bytes))
+        if slower < limit and (best is None or slower < best[0]):
+            best = (slower, int(c))
+    return None if best is None else best[1]
 
 
 def strategy_stream(causes, network, *, max_channels: int = 16):
@@ -111,6 +142,9 @@ def strategy_stream(causes, network, *, max_channels: int = 16):
             per_family["channel"].append(StrategyRecord("chan-%d" % index, "channel", (op.operation_id,),
                                                         (("channel", (op.channel + 1) % max_channels),)))
         else:
+            if op.kind == "send" and cause.detail.get("relay") is not None:
+                per_family["path"].append(StrategyRecord("relay-%d" % index, "path", (op.operation_id,),
+                                                         (("via", cause.detail["relay"]),)))
             if op.kind == "rrc":
                 per_family["internal_root"].append(StrategyRecord("root-%d" % index, "internal_root",
                                                                   (op.operation_id,), (("reshape", "binomial"),)))
