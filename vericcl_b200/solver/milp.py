@@ -10,9 +10,13 @@ Proven outcomes are cached by the model's content hash.
 """
 from __future__ import annotations
 
-import multiprocessing as mp
+import os
+import pickle
+import subprocess
+import sys
 import time
 from dataclasses import dataclass, field
+from pathlib import Path
 
 import numpy as np
 
@@ -181,50 +185,48 @@ def _solve_arrays(arrays, names, constant, time_limit, mip_gap) -> Solution:
 _CACHE: dict[str, Solution] = {}
 
 
-def _worker(conn, arrays, names, constant, time_limit, mip_gap):
+def _worker_main() -> None:
+    """Child side of an owned solve: a pickled problem on stdin, the pickled :class:`Solution` on stdout."""
+    arrays, names, constant, time_limit, mip_gap = pickle.load(sys.stdin.buffer)
     try:
-        conn.send(_solve_arrays(arrays, names, constant, time_limit, mip_gap))
+        result = _solve_arrays(arrays, names, constant, time_limit, mip_gap)
     except BaseException as error:  # pragma: no cover
-        conn.send(Solution("error", None, {}, None, 0.0, repr(error)))
-    finally:
-        conn.close()
+        result = Solution("error", None, {}, None, 0.0, repr(error))
+    sys.stdout.buffer.write(pickle.dumps(result))
+    sys.stdout.buffer.flush()
 
 
 def solve_owned(model: Model, *, time_limit: float = 60.0, mip_gap: float = 0.0, grace_s: float = 5.0,
                 use_cache: bool = True) -> Solution:
     """Solve in a fresh child process that is killed if it outlives its lease.
 
+    The child is a new interpreter running :func:`_worker_main`, not a fork: forking a process in which HiGHS has already run copies its
+    thread pool's locks in a held state and the child's solve never starts.
     Proven-optimal outcomes are cached by model fingerprint, so identical
     subproblems (isomorphic templates) are solved once.
     """
     key = model.fingerprint() + ":%g" % mip_gap
     if use_cache and key in _CACHE:
         return _CACHE[key]
-    ctx = mp.get_context("fork")
-    parent, child = ctx.Pipe(duplex=False)
-    proc = ctx.Process(target=_worker, args=(child, model.arrays(), [v.name for v in model.vars],
-                                             model.objective_constant, time_limit, mip_gap), daemon=True)
-    proc.start()
-    child.close()
-    deadline = time.monotonic() + time_limit + grace_s
-    result = None
-    while time.monotonic() < deadline:
-        if parent.poll(0.05):
-            try:
-                result = parent.recv()
-            except EOFError:
-                result = Solution("error", None, {}, None, 0.0, "solver worker exited without a result")
-            break
-        if not proc.is_alive() and not parent.poll(0):
-            result = Solution("error", None, {}, None, 0.0, "solver worker died (exit %s)" % proc.exitcode)
-            break
-    if result is None:
-        proc.terminate()
-        proc.join(2.0)
-        if proc.is_alive():
-            proc.kill()
-        result = Solution("timeout", None, {}, None, time_limit, "owned solver exceeded its lease")
-    proc.join(1.0)
+    payload = pickle.dumps((model.arrays(), [v.name for v in model.vars], model.objective_constant,
+                            time_limit, mip_gap))
+    root = str(Path(__file__).resolve().parents[2])
+    env = dict(os.environ, PYTHONPATH=root + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    proc = subprocess.Popen([sys.executable, "-c", "from vericcl_b200.solver.milp import _worker_main; "
+                             "_worker_main()"], stdin=subprocess.PIPE,
+                            stdout=subprocess.PIPE, stderr=subprocess.PIPE, env=env, start_new_session=True)
+    try:
+        out, err = proc.communicate(payload, timeout=time_limit + grace_s)
+    except subprocess.TimeoutExpired:
+        proc.kill()
+        proc.communicate()
+        return Solution("timeout", None, {}, None, time_limit, "owned solver exceeded its lease")
+    try:
+        result = pickle.loads(out)
+    except Exception:
+        tail = err.decode(errors="replace")[-300:]
+        result = Solution("error", None, {}, None, 0.0, "solver worker exited %s without a result: %s"
+                          % (proc.returncode, tail))
     if use_cache and result.status == "optimal":
         _CACHE[key] = result
     return result
