@@ -1,6 +1,9 @@
 // Small helper kernels: deterministic fills, a standalone scale pass (the
 // unfused baseline of the reference's post-collective average), an analytic
-// output checker and a %globaltimer reader.
+// output checker, a 2D pitched copy (staging of strided tensors; the
+// reference's stride copy is
+// third_party/msccl/src/collectives/device/stride_copy.cu:6-25) and a
+// %globaltimer reader.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -76,6 +79,20 @@ __global__ void timer_kernel(unsigned long long* dst) {
   *dst = t;
 }
 
+// 2D pitched copy: row r of ``rows`` rows of ``row_bytes`` bytes moves from
+// src + r*src_pitch to dst + r*dst_pitch.  V is the widest access that every
+// address, pitch and row length allows (16, 8, 4 or 1 bytes); the flat index
+// over (row, unit) is grid-strided so any shape fills the grid.
+template <typename V>
+__global__ void strided_copy_kernel(char* dst, long long dst_pitch, const char* src, long long src_pitch,
+                                    long long units_per_row, long long total) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    long long r = i / units_per_row, c = i - r * units_per_row;
+    *reinterpret_cast<V*>(dst + r * dst_pitch + c * (long long)sizeof(V)) =
+        *reinterpret_cast<const V*>(src + r * src_pitch + c * (long long)sizeof(V));
+  }
+}
+
 int grid_for(long long n) {
   long long g = (n + 255) / 256;
   return (int)(g > 4096 ? 4096 : (g < 1 ? 1 : g));
@@ -99,6 +116,29 @@ cudaError_t launch_check(const void* out, long long n, int dtype, int collective
                          cudaStream_t stream) {
   check_kernel<<<grid_for(n), 256, 0, stream>>>(out, n, dtype, collective, redop, nranks, rank, count_per_rank, atol,
                                                rtol, bad);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_strided_copy(void* dst, long long dst_pitch, const void* src, long long src_pitch,
+                                long long row_bytes, long long rows, cudaStream_t stream) {
+  if (rows <= 0 || row_bytes <= 0) return cudaSuccess;
+  if (row_bytes > dst_pitch && rows > 1) return cudaErrorInvalidValue;
+  if (row_bytes > src_pitch && rows > 1) return cudaErrorInvalidValue;
+  unsigned long long bits = reinterpret_cast<unsigned long long>(dst) | reinterpret_cast<unsigned long long>(src) |
+                            (unsigned long long)dst_pitch | (unsigned long long)src_pitch |
+                            (unsigned long long)row_bytes;
+  int width = (bits % 16 == 0) ? 16 : (bits % 8 == 0) ? 8 : (bits % 4 == 0) ? 4 : 1;
+  long long units = row_bytes / width, total = units * rows;
+  // at most 8 resident 256-thread blocks on each of the 148 SMs; fewer when there is less work
+  long long blocks = (total + 255) / 256;
+  int grid = (int)(blocks > 148 * 8 ? 148 * 8 : blocks);
+  char* d = static_cast<char*>(dst);
+  const char* sp = static_cast<const char*>(src);
+  if (width == 16) strided_copy_kernel<uint4><<<grid, 256, 0, stream>>>(d, dst_pitch, sp, src_pitch, units, total);
+  else if (width == 8) strided_copy_kernel<uint2><<<grid, 256, 0, stream>>>(d, dst_pitch, sp, src_pitch, units, total);
+  else if (width == 4) strided_copy_kernel<unsigned int><<<grid, 256, 0, stream>>>(d, dst_pitch, sp, src_pitch, units,
+                                                                                    total);
+  else strided_copy_kernel<unsigned char><<<grid, 256, 0, stream>>>(d, dst_pitch, sp, src_pitch, units, total);
   return cudaGetLastError();
 }
 

@@ -67,6 +67,8 @@ void apply_emulation_env(InterpArgs* a);
 cudaError_t launch_fill(void* dst, long long n, int dtype, int pattern, int rank, unsigned long long seed,
                         cudaStream_t stream);
 cudaError_t launch_scale(void* dst, const void* src, long long n, int dtype, float scale, cudaStream_t stream);
+cudaError_t launch_strided_copy(void* dst, long long dst_pitch, const void* src, long long src_pitch,
+                                long long row_bytes, long long rows, cudaStream_t stream);
 cudaError_t launch_check(const void* out, long long n, int dtype, int collective, int redop, int nranks,
                          int rank, long long count_per_rank, double atol, double rtol, unsigned long long* bad,
                          cudaStream_t stream);

@@ -425,6 +425,17 @@ PYBIND11_MODULE(_vbcuda, m) {
     cuda_check(launch_scale(dst.data_ptr(), src.data_ptr(), dst.numel(), dtype_code(dst.scalar_type()), s,
                             at::cuda::getCurrentCUDAStream().stream()), "scale");
   });
+  m.def("strided_copy", [](torch::Tensor dst, torch::Tensor src) {
+    // 2D tensors of one dtype and shape whose rows are contiguous (stride(1) == 1)
+    if (dst.dim() != 2 || src.dim() != 2 || dst.sizes() != src.sizes() || dst.scalar_type() != src.scalar_type())
+      throw std::runtime_error("strided_copy needs 2D tensors of the same shape and dtype");
+    if (!dst.is_cuda() || !src.is_cuda() || (dst.size(1) > 1 && (dst.stride(1) != 1 || src.stride(1) != 1)))
+      throw std::runtime_error("strided_copy needs CUDA tensors with contiguous rows");
+    int64_t es = dst.element_size();
+    cuda_check(launch_strided_copy(dst.data_ptr(), dst.stride(0) * es, src.data_ptr(), src.stride(0) * es,
+                                   dst.size(1) * es, dst.size(0), at::cuda::getCurrentCUDAStream().stream()),
+               "strided_copy");
+  }, py::arg("dst"), py::arg("src"));
   m.def("check", [](torch::Tensor out, int coll, int redop, int nranks, int rank, int64_t count, double atol, double rtol) {
     auto bad = torch::zeros({1}, torch::TensorOptions().dtype(torch::kInt64).device(out.device()));
     cuda_check(launch_check(out.data_ptr(), out.numel(), dtype_code(out.scalar_type()), coll, redop, nranks, rank, count,

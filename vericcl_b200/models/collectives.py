@@ -25,6 +25,12 @@ PIECE_TARGET_BYTES = 512 * 1024     # pipeline a lane's work in pieces of about 
 MAX_ITERS = 8
 
 
+def _pitched(tensor: torch.Tensor) -> bool:
+    """A 2D CUDA view with contiguous rows and a larger row pitch (a column slice of a matrix, for example)."""
+    return (tensor.is_cuda and tensor.dim() == 2 and tensor.size(0) > 1 and tensor.stride(1) == 1
+            and tensor.stride(0) >= tensor.size(1))
+
+
 class CollectiveEngine:
     def __init__(self, comm, *, method: str = "hierarchy", slices_per_rank: int | None = None,
                  max_lanes: int | None = None, oneshot_max_bytes: int | None = None,
@@ -114,6 +120,24 @@ class CollectiveEngine:
         return self.comm.compile(xml, nlanes=lanes, niters=iters,
                                  multicast=self.use_multicast(collective, op, count * esize), mc_share=share)
 
+    def _copy_in(self, flat: torch.Tensor, tensor: torch.Tensor) -> None:
+        """``flat`` (contiguous) ← ``tensor`` in row-major order; pitched 2D views go through the native copy."""
+        if tensor.is_contiguous():
+            flat.copy_(tensor.view(-1))
+        elif _pitched(tensor):
+            self.comm._mod.strided_copy(flat.view(tensor.shape), tensor)
+        else:
+            flat.view(tensor.shape).copy_(tensor)
+
+    def _copy_out(self, tensor: torch.Tensor, flat: torch.Tensor) -> None:
+        """``tensor`` ← ``flat`` (contiguous, row-major)."""
+        if tensor.is_contiguous():
+            tensor.view(-1).copy_(flat)
+        elif _pitched(tensor):
+            self.comm._mod.strided_copy(tensor, flat.view(tensor.shape))
+        else:
+            tensor.copy_(flat.view(tensor.shape))
+
     def _heap_copy(self, tensor: torch.Tensor, tag: str) -> torch.Tensor:
         key = (tag, tensor.numel(), tensor.dtype)
         buf = self._staging.get(key)
@@ -124,37 +148,37 @@ class CollectiveEngine:
 
     # -- collectives ---------------------------------------------------------
     def all_reduce(self, tensor: torch.Tensor, *, op: str = "sum", scale: float | None = None) -> torch.Tensor:
-        """In-place AllReduce of ``tensor`` (fused reduction, cast and scale)."""
-        flat = tensor.view(-1)
-        pad = self._padding(flat.numel(), flat.dtype, self.slices_per_rank or self.comm.world)
-        if self.comm.in_heap(flat) and pad == 0:
-            plan = self.plan("allreduce", flat.numel(), flat.dtype, inplace=True, op=op)
+        """In-place AllReduce of ``tensor`` (fused reduction, cast and scale); strided views are staged."""
+        n = tensor.numel()
+        pad = self._padding(n, tensor.dtype, self.slices_per_rank or self.comm.world)
+        if tensor.is_contiguous() and self.comm.in_heap(tensor.view(-1)) and pad == 0:
+            flat = tensor.view(-1)
+            plan = self.plan("allreduce", n, flat.dtype, inplace=True, op=op)
             self.comm.run(plan, flat, flat, op=op, scale=scale)
             return tensor
-        count = flat.numel() + pad
-        buf = self._heap_copy(torch.empty(count, dtype=flat.dtype, device="meta"), "ar")
-        buf[:flat.numel()].copy_(flat)
+        count = n + pad
+        buf = self._heap_copy(torch.empty(count, dtype=tensor.dtype, device="meta"), "ar")
+        self._copy_in(buf[:n], tensor)
         if pad:
-            buf[flat.numel():].zero_()
-        plan = self.plan("allreduce", count, flat.dtype, inplace=True, op=op)
+            buf[n:].zero_()
+        plan = self.plan("allreduce", count, tensor.dtype, inplace=True, op=op)
         self.comm.run(plan, buf, buf, op=op, scale=scale)
-        flat.copy_(buf[:flat.numel()])
+        self._copy_out(tensor, buf[:n])
         return tensor
 
     def all_gather(self, inp: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         world = self.comm.world
         if out.numel() != inp.numel() * world:
             raise RuntimeFailure("all_gather output must hold world × input elements")
-        if self.comm.in_heap(inp) and self.comm.in_heap(out):
+        if inp.is_contiguous() and out.is_contiguous() and self.comm.in_heap(inp) and self.comm.in_heap(out):
             plan = self.plan("allgather", inp.numel(), inp.dtype, inplace=False)
             self.comm.run(plan, inp.view(-1), out.view(-1))
             return out
-        src = self._heap_copy(inp.view(-1), "ag-in")
-        dst = self._heap_copy(out.view(-1), "ag-out")
-        src.copy_(inp.view(-1))
+        src = self._staged(inp, "ag-in", True)
+        dst = self._staged(out, "ag-out", False)
         plan = self.plan("allgather", inp.numel(), inp.dtype, inplace=False)
         self.comm.run(plan, src, dst)
-        out.view(-1).copy_(dst)
+        self._unstage(out, dst)
         return out
 
     def all_gather_fp8(self, inp: torch.Tensor, out: torch.Tensor, *, block: int = 128) -> torch.Tensor:
@@ -197,25 +221,25 @@ class CollectiveEngine:
         world = self.comm.world
         if inp.numel() != out.numel() * world:
             raise RuntimeFailure("reduce_scatter input must hold world × output elements")
-        src = inp.view(-1) if self.comm.in_heap(inp) else self._heap_copy(inp.view(-1), "rs-in")
-        dst = out.view(-1) if self.comm.in_heap(out) else self._heap_copy(out.view(-1), "rs-out")
-        if src.data_ptr() != inp.data_ptr():
-            src.copy_(inp.view(-1))
+        src, dst = self._staged(inp, "rs-in", True), self._staged(out, "rs-out", False)
         plan = self.plan("reduce_scatter", inp.numel(), inp.dtype, inplace=False)
         self.comm.run(plan, src, dst, op=op, scale=scale, count_per_rank=inp.numel())
-        if dst.data_ptr() != out.data_ptr():
-            out.view(-1).copy_(dst)
+        self._unstage(out, dst)
         return out
 
     def _staged(self, tensor: torch.Tensor, tag: str, copy_in: bool) -> torch.Tensor:
-        """The heap tensor to run on: ``tensor`` itself when it lives in the heap, else a staging buffer."""
-        flat = tensor.view(-1)
-        if self.comm.in_heap(flat):
-            return flat
-        buf = self._heap_copy(flat, tag)
+        """The heap tensor to run on: ``tensor`` itself when it is contiguous in the heap, else a staging buffer."""
+        if tensor.is_contiguous() and self.comm.in_heap(tensor.view(-1)):
+            return tensor.view(-1)
+        buf = self._heap_copy(torch.empty(tensor.numel(), dtype=tensor.dtype, device="meta"), tag)
         if copy_in:
-            buf.copy_(flat)
+            self._copy_in(buf, tensor)
         return buf
+
+    def _unstage(self, tensor: torch.Tensor, flat: torch.Tensor) -> None:
+        """Copy a staged result back unless ``flat`` is ``tensor``'s own storage."""
+        if not (tensor.is_contiguous() and flat.data_ptr() == tensor.data_ptr()):
+            self._copy_out(tensor, flat)
 
     def broadcast(self, inp: torch.Tensor, out: torch.Tensor, *, root: int = 0) -> torch.Tensor:
         """``out`` on every rank = ``inp`` of rank ``root`` (other ranks' ``inp`` is not read)."""
@@ -224,8 +248,7 @@ class CollectiveEngine:
         src, dst = self._staged(inp, "bc-in", True), self._staged(out, "bc-out", False)
         plan = self.plan("broadcast", inp.numel(), inp.dtype, inplace=False, root=root)
         self.comm.run(plan, src, dst)
-        if dst.data_ptr() != out.data_ptr():
-            out.view(-1).copy_(dst)
+        self._unstage(out, dst)
         return out
 
     def reduce(self, inp: torch.Tensor, out: torch.Tensor, *, root: int = 0, op: str = "sum",
@@ -240,8 +263,7 @@ class CollectiveEngine:
         src, dst = self._staged(inp, "rd-in", True), self._staged(out, "rd-out", False)
         plan = self.plan("reduce", inp.numel(), inp.dtype, inplace=False, op=op, root=root)
         self.comm.run(plan, src, dst, op=op, scale=scale)
-        if dst.data_ptr() != out.data_ptr():
-            out.view(-1).copy_(dst)
+        self._unstage(out, dst)
         return out
 
     def all_to_all(self, inp: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
@@ -252,8 +274,7 @@ class CollectiveEngine:
         src, dst = self._staged(inp, "a2a-in", True), self._staged(out, "a2a-out", False)
         plan = self.plan("alltoall", inp.numel(), inp.dtype, inplace=False)
         self.comm.run(plan, src, dst)
-        if dst.data_ptr() != out.data_ptr():
-            out.view(-1).copy_(dst)
+        self._unstage(out, dst)
         return out
 
     def _padding(self, count: int, dtype, slices: int) -> int:
