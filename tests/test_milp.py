@@ -81,3 +81,24 @@ def test_owned_solve_is_bounded_by_its_lease():
     m.minimize([(((i * 7 + j * 13) % 17) + 1, x) for (i, j), x in xs.items()])
     sol = solve_owned(m, time_limit=0.05, grace_s=5.0, use_cache=False)
     assert sol.status in ("optimal", "feasible", "timeout")
+
+
+def test_route_templates_balance_interchangeable_demands():
+    """Four identical broadcast demands share one template; the counts split them 2/2 and interleave."""
+    from vericcl_b200.solver.demands import TransferDemand, Tree
+    from vericcl_b200.solver.routing import _interleave, choose_trees
+    from vericcl_b200.topology import topology_from_document
+    from vericcl_b200.topology.nvswitch import nvswitch_topology
+    doc = nvswitch_topology(3, nvls=False)
+    for link in doc["directed_links"]:
+        link["resources"] = []
+    doc["shared_resources"] = []
+    topo = topology_from_document(doc)
+    direct = Tree("star", ((0, 1),), 1)
+    relay = Tree("relay", ((0, 2), (2, 1)), 2)
+    demands = [TransferDemand("d%d" % i, "n", 0, "broadcast", 0, (1,), i, candidates=(direct, relay))
+               for i in range(4)]
+    choice = choose_trees(demands, topo, 1 << 20)
+    assert [choice["d%d" % i].name for i in range(4)] in (["star", "relay"] * 2, ["relay", "star"] * 2)
+    assert _interleave({0: 3, 1: 1}) in ([0, 1, 0, 0], [0, 0, 1, 0])
+    assert sorted(_interleave({0: 2, 1: 3})) == [0, 0, 1, 1, 1]
