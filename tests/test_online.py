@@ -141,3 +141,15 @@ def test_trace_timeline_offsets():
     assert rows[(0, 0)]["start_us"] == 0.0 and rows[(0, 1)]["local_start_us"] == 4.0
     assert rows[(1, 0)]["start_us"] == 1.0 and rows[(1, 0)]["local_start_us"] == 0.0
     assert rows[(0, 0)]["duration_us"] == 2.0 and rows[(0, 0)]["wait_us"] == 0.5
+
+
+def test_step_counters_accumulate_over_launches():
+    from vericcl_b200.online.trace import TraceRecord, step_counters
+    recs = [TraceRecord(0, 0, 1, 0, 0, 2, 5, 100, 150, 30), TraceRecord(0, 1, 1, 1, 0, 2, 5, 300, 370, 10),
+            TraceRecord(0, 0, 1, 0, 0, 2, 5, 1000, 1040, 0), TraceRecord(1, 0, 0, 0, 0, 0, 1, 50, 60, 5)]
+    c = step_counters(recs)
+    a = c[(0, 1, 2)]
+    assert a["samples"] == 3 and a["service_ns"] == 50 + 70 + 40 and a["dependency_wait_ns"] == 40
+    assert a["max_service_ns"] == 70 and a["first_ns"] == 100 and a["last_ns"] == 1040
+    assert a["mean_service_ns"] == pytest.approx(160 / 3) and a["mean_wait_ns"] == pytest.approx(40 / 3)
+    assert c[(1, 0, 0)]["samples"] == 1

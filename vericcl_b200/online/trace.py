@@ -89,6 +89,38 @@ def records_from_buffer(rank, buffer, *, nblocks, nlanes, steps_per_iter, niters
     return out
 
 
+def step_counters(records) -> dict:
+    """Per-step counters over every captured launch, iteration and lane.
+
+    ``{(rank, block, step): {"samples", "service_ns", "dependency_wait_ns",
+    "mean_service_ns", "mean_wait_ns", "max_service_ns", "first_ns",
+    "last_ns"}}`` where service is end − start (data work after the waits)
+    and the wait is the time the step spent on its dependencies — the same
+    quantities as the reference's light probe counters
+    (runtime/msccl-trace/patches/0003 lines 62-78), accumulated on the host
+    from trace records instead of in a device table, so the interpreter's
+    hot loop carries no extra atomics.
+    """
+    out = {}
+    for r in records:
+        key = (r.rank, r.block, r.step)
+        c = out.get(key)
+        service = max(0, r.end_ns - r.start_ns)
+        if c is None:
+            c = out[key] = {"samples": 0, "service_ns": 0, "dependency_wait_ns": 0, "max_service_ns": 0,
+                            "first_ns": r.start_ns, "last_ns": r.end_ns}
+        c["samples"] += 1
+        c["service_ns"] += service
+        c["dependency_wait_ns"] += max(0, r.wait_ns)
+        c["max_service_ns"] = max(c["max_service_ns"], service)
+        c["first_ns"] = min(c["first_ns"], r.start_ns)
+        c["last_ns"] = max(c["last_ns"], r.end_ns)
+    for c in out.values():
+        c["mean_service_ns"] = c["service_ns"] / c["samples"]
+        c["mean_wait_ns"] = c["dependency_wait_ns"] / c["samples"]
+    return out
+
+
 def analyze_trace_causality(traces, clock_maps, *, tails: int = 5):
     """Span per rank, slowest steps, dominant waits and uncertain cross-rank orders."""
     spans, steps, waits = {}, [], []

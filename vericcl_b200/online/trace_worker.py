@@ -118,11 +118,13 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--steady", action="store_true",
                     help="trace a launch enqueued right behind the warm-up launches (no barrier before it)")
+    ap.add_argument("--repeat", type=int, default=1,
+                    help="captured launches; per-step counters accumulate over all of them")
     args = ap.parse_args(argv)
 
     import torch.distributed as dist
     from vericcl_b200.models import CollectiveEngine
-    from vericcl_b200.online.trace import analyze_trace_causality, capture_once, write_trace
+    from vericcl_b200.online.trace import analyze_trace_causality, capture_once, step_counters, write_trace
     from vericcl_b200.parallel import Communicator
     local = int(os.environ.get("LOCAL_RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -157,13 +159,17 @@ def main(argv=None) -> int:
     inp.normal_()
     out = inp if inplace else comm.empty(out_count, dtype)
     got = capture_once(comm, plan, inp, out, warmup=args.warmup, steady=args.steady)
+    counted = list(got["records"])
+    for _ in range(max(0, args.repeat - 1)):
+        counted += capture_once(comm, plan, inp, out, warmup=0, steady=args.steady)["records"]
     outdir = Path(args.out)
     outdir.mkdir(parents=True, exist_ok=True)
     write_trace(outdir / ("trace-rank%d.bin" % comm.rank), comm.rank, plan.device_plan.nblocks * plan.nlanes,
                 plan.device_plan.max_steps(), got["records"])
     origins = [[tuple(o) for o in blk] for blk in plan.device_plan.step_origins()]
+    counters = [dict(rank=k[0], block=k[1], step=k[2], **v) for k, v in sorted(step_counters(counted).items())]
     gathered = comm.all_gather_object({"rank": comm.rank, "records": got["records"], "clock": got["clock"],
-                                       "origins": origins})
+                                       "origins": origins, "counters": counters})
     if comm.rank == 0:
         traces = {g["rank"]: g["records"] for g in gathered}
         clocks = {g["rank"]: g["clock"] for g in gathered}
@@ -173,7 +179,9 @@ def main(argv=None) -> int:
                        "steady": args.steady,
                        "dtype": args.dtype, "lanes": plan.nlanes, "iters": plan.niters, "nvls": plan.multicast,
                        "clock_uncertainty_us": {r: round(c.uncertainty_ns / 1e3, 3) for r, c in clocks.items()},
-                       "timeline": timeline(traces, clocks, step_origins)})
+                       "timeline": timeline(traces, clocks, step_origins),
+                       "launches_counted": max(1, args.repeat),
+                       "counters": [c for g in gathered for c in g["counters"]]})
         (outdir / "trace.json").write_text(json.dumps(report, indent=1, default=str))
         print(json.dumps({"trace": str(outdir / "trace.json"), "global_span_us": report["global_span_us"],
                           "records": sum(len(v) for v in traces.values())}))
