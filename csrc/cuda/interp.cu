@@ -561,10 +561,17 @@ int interp_max_ctas(int threads) {
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && cached_threads[dev] == threads && cached_value[dev] > 0) return cached_value[dev];
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // the smallest residency over the instances a launch may pick (dtype, timeline, lean), so a cooperative
+  // grid sized from it is resident whichever instance runs
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, interp_kernel<DT_BF16, RED_SUM>, threads, 0);
-  int f32 = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&f32, interp_kernel<DT_F32, RED_SUM>, threads, 0);
-  if (f32 < per_sm) per_sm = f32;
+  const void* others[] = {
+      (const void*)interp_kernel<DT_F32, RED_SUM>, (const void*)interp_kernel<DT_BF16, RED_SUM, true, false>,
+      (const void*)interp_kernel<DT_BF16, RED_SUM, false, true>, (const void*)interp_kernel<DT_F32, RED_SUM, false, true>,
+      (const void*)interp_kernel<DT_BF16, RED_SUM, true, true>};
+  for (const void* fn : others) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, threads, 0) == cudaSuccess && n < per_sm) per_sm = n;
+  }
   if (dev >= 0 && dev < 64) {
     cached_threads[dev] = threads;
     cached_value[dev] = sms * per_sm;
