@@ -2,6 +2,7 @@
 
     python -m vericcl_b200.experiments matrix --gpus 2,4,8 [--colls allreduce,allgather] [--graph]
     python -m vericcl_b200.experiments report SWEEP_OUTPUT [SWEEP_OUTPUT ...] [--markdown]
+    python -m vericcl_b200.experiments overhead {solve,replay} --inputs DIR ... --out FILE
 
 ``matrix`` prints the ``torchrun … sweep.py`` command of every (GPU count,
 mode) cell of a message-size experiment (1 KiB … 1 GiB per rank, powers of
@@ -10,7 +11,8 @@ runs print (other lines are ignored) and tabulates, per collective, GPU
 count and size: time, bus bandwidth, the path that ran (one-shot or
 interpreter, NVLS or peer pulls), NCCL's time and the speedup, and the fp64
 check error (reference counterpart: vericcl/experiments/v100.py:929 and
-vericcl/experiments/report.py).
+vericcl/experiments/report.py).  ``overhead`` attributes the synthesis
+pipeline's wall clock to its phases (``vericcl_b200/overhead.py``).
 """
 from __future__ import annotations
 
@@ -95,7 +97,11 @@ def main(argv=None) -> int:
     r = sub.add_parser("report")
     r.add_argument("files", nargs="+")
     r.add_argument("--markdown", action="store_true")
+    from vericcl_b200 import overhead
+    overhead.add_arguments(sub.add_parser("overhead", help="pipeline wall-clock attribution or schedule replay"))
     args = ap.parse_args(argv)
+    if args.command == "overhead":
+        return overhead.run(args)
     if args.command == "matrix":
         for cmd in matrix_commands([int(g) for g in args.gpus.split(",")], colls=args.colls, graph=args.graph,
                                    max_bytes=args.max_bytes):
