@@ -44,26 +44,41 @@ __global__ void scale_kernel(void* dst, const void* src, long long n, int dt, fl
     st_elem(dst, i, dt, ld_elem(src, i, dt) * scale);
 }
 
-// Checks outputs of pattern-0 inputs analytically in fp64.
+// Analytic value of pattern 0 and the fp64 reduction of it over all ranks.
+__device__ __forceinline__ double pattern0(int rank, long long i) { return 1.0 + (double)((3 * rank + i) % 5); }
+
+__device__ double reduced0(long long i, int nranks, int redop) {
+  double acc = 0;
+  for (int r = 0; r < nranks; ++r) {
+    double v = pattern0(r, i);
+    if (r == 0) acc = v;
+    else if (redop == RED_PROD) acc *= v;
+    else if (redop == RED_MIN) acc = acc < v ? acc : v;
+    else if (redop == RED_MAX) acc = acc > v ? acc : v;
+    else acc += v;
+  }
+  return acc;
+}
+
+// Checks, in fp64, the output of a collective whose inputs follow pattern 0.
+// coll: 0 allreduce, 1 allgather, 2 reduce_scatter, 3 broadcast (root's input),
+// 4 reduce (the reduction, on the root), 5 alltoall (part s of rank r is part r
+// of rank s), 6 this rank's own input (a read-only re-check).  ``count`` is the
+// input elements per rank; reductions are multiplied by ``scale``.
 __global__ void check_kernel(const void* out, long long n, int dt, int coll, int redop, int nranks, int rank,
-                             long long count, double atol, double rtol, unsigned long long* bad) {
+                             long long count, double atol, double rtol, unsigned long long* bad, int root,
+                             double scale) {
   unsigned long long local = 0;
+  const long long part = nranks > 0 ? count / nranks : count;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     double expect;
-    if (coll == 1) {   // allgather: output i comes from rank i / count, element i % count
-      int src = (int)(i / count);
-      expect = 1.0 + (double)((3 * src + i % count) % 5);
-    } else {           // reductions over all ranks at element i
-      double acc = 0;
-      for (int r = 0; r < nranks; ++r) {
-        double v = 1.0 + (double)((3 * r + i) % 5);
-        if (r == 0) acc = v;
-        else if (redop == RED_PROD) acc *= v;
-        else if (redop == RED_MIN) acc = acc < v ? acc : v;
-        else if (redop == RED_MAX) acc = acc > v ? acc : v;
-        else acc += v;
-      }
-      expect = acc;
+    switch (coll) {
+      case 1: expect = pattern0((int)(i / count), i % count); break;
+      case 2: expect = reduced0((long long)rank * part + i, nranks, redop) * scale; break;
+      case 3: expect = pattern0(root, i); break;
+      case 5: expect = pattern0((int)(i / part), (long long)rank * part + i % part); break;
+      case 6: expect = pattern0(rank, i); break;
+      default: expect = reduced0(i, nranks, redop) * scale; break;   // 0 allreduce, 4 reduce
     }
     double got = ld_elem(out, i, dt);
     double err = got - expect;
@@ -113,9 +128,10 @@ cudaError_t launch_scale(void* dst, const void* src, long long n, int dtype, flo
 
 cudaError_t launch_check(const void* out, long long n, int dtype, int collective, int redop, int nranks, int rank,
                          long long count_per_rank, double atol, double rtol, unsigned long long* bad,
-                         cudaStream_t stream) {
+                         cudaStream_t stream, int root, double scale) {
+  if (n <= 0) return cudaSuccess;
   check_kernel<<<grid_for(n), 256, 0, stream>>>(out, n, dtype, collective, redop, nranks, rank, count_per_rank, atol,
-                                               rtol, bad);
+                                               rtol, bad, root, scale);
   return cudaGetLastError();
 }
 

@@ -69,9 +69,11 @@ cudaError_t launch_fill(void* dst, long long n, int dtype, int pattern, int rank
 cudaError_t launch_scale(void* dst, const void* src, long long n, int dtype, float scale, cudaStream_t stream);
 cudaError_t launch_strided_copy(void* dst, long long dst_pitch, const void* src, long long src_pitch,
                                 long long row_bytes, long long rows, cudaStream_t stream);
+// Counts outputs that differ from the analytic result of pattern-0 inputs.  collective: 0 allreduce,
+// 1 allgather, 2 reduce_scatter, 3 broadcast, 4 reduce (root), 5 alltoall, 6 the rank's own input.
 cudaError_t launch_check(const void* out, long long n, int dtype, int collective, int redop, int nranks,
                          int rank, long long count_per_rank, double atol, double rtol, unsigned long long* bad,
-                         cudaStream_t stream);
+                         cudaStream_t stream, int root = 0, double scale = 1.0);
 cudaError_t launch_read_timer(unsigned long long* dst, cudaStream_t stream);
 
 // Block-scaled FP8 (e4m3) payloads.

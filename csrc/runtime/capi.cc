@@ -30,7 +30,9 @@ struct vb_context {
   DevStep* steps = nullptr;
   DevSrc* srcs = nullptr;
   DevWait* waits = nullptr;
-  size_t stage_in = 0, stage_out = 0, stage_scr = 0, stage_bytes = 0;
+  size_t stage_in = 0, stage_out = 0, stage_scr = 0;               // heap offsets of the staging buffers
+  size_t cap_in = 0, cap_out = 0, cap_scr = 0;                      // their sizes
+  bool staged = false;
   std::atomic<bool> busy{false};
   bool unresolved = false;
   std::string error;
@@ -185,19 +187,35 @@ extern "C" vb_result vb_execute(vb_context* c, const void* in, void* out, size_t
   size_t in_bytes = (size_t)rp.i_chunks * chunk * esize(dtype);
   size_t out_bytes = (size_t)rp.o_chunks * chunk * esize(dtype);
   size_t scr_bytes = (size_t)c->plan.max_scratch_used() * chunk * esize(dtype) + 16;
+  // peers address each other's buffers by heap offset, so every rank allocates the largest input and output
+  // buffer of any rank (a reduce, for one, has an output buffer on its root only)
+  int max_i = 0, max_o = 0;
+  for (const RankProgram& r : c->plan.ranks) {
+    max_i = r.i_chunks > max_i ? r.i_chunks : max_i;
+    max_o = r.o_chunks > max_o ? r.o_chunks : max_o;
+  }
+  size_t in_alloc = (size_t)max_i * chunk * esize(dtype), out_alloc = (size_t)max_o * chunk * esize(dtype);
   try {
-    // staging buffers in the heap, sized identically on every rank
-    size_t want = in_bytes + out_bytes + scr_bytes;
-    if (want > c->stage_bytes) {
-      if (c->stage_bytes) { c->heap->free(c->stage_in); c->heap->free(c->stage_out); c->heap->free(c->stage_scr); }
-      c->stage_in = c->heap->alloc(in_bytes);
-      c->stage_out = c->heap->alloc(out_bytes);
-      c->stage_scr = c->heap->alloc(scr_bytes);
-      c->stage_bytes = want;
+    // staging buffers in the heap, sized identically on every rank; each grows on its own
+    if (!c->staged || in_alloc > c->cap_in || out_alloc > c->cap_out || scr_bytes > c->cap_scr) {
+      if (c->staged) { c->heap->free(c->stage_in); c->heap->free(c->stage_out); c->heap->free(c->stage_scr); }
+      c->cap_in = in_alloc > c->cap_in ? in_alloc : c->cap_in;
+      c->cap_out = out_alloc > c->cap_out ? out_alloc : c->cap_out;
+      c->cap_scr = scr_bytes > c->cap_scr ? scr_bytes : c->cap_scr;
+      c->stage_in = c->heap->alloc(c->cap_in);
+      c->stage_out = c->heap->alloc(c->cap_out);
+      c->stage_scr = c->heap->alloc(c->cap_scr);
+      c->staged = true;
     }
     size_t user_in = count * esize(dtype);
     size_t user_out = (coll == "allgather" ? count * c->nranks : coll == "reduce_scatter" ? count / c->nranks : count) * esize(dtype);
     if (c->plan.algo.inplace) return fail(c, VB_INVALID, "the C API runs out-of-place schedules");
+    // the staged copies must stay inside this rank's input and output buffers of the schedule; a reduce
+    // defines an output on its root only (the other ranks' schedules have no output buffer), so a rank
+    // without one leaves the user's output untouched
+    if (coll == "reduce" && out_bytes == 0) user_out = 0;
+    if (user_in > in_bytes || user_out > out_bytes)
+      return fail(c, VB_INVALID, "schedule buffers are smaller than the user buffers for this count");
     cudaMemcpyAsync(c->heap->base(c->rank) + c->stage_in, in, user_in, cudaMemcpyDeviceToDevice, stream);
     InterpArgs a = {};
     a.blocks = c->blocks; a.steps = c->steps; a.srcs = c->srcs; a.waits = c->waits;
@@ -237,7 +255,7 @@ extern "C" vb_result vb_execute(vb_context* c, const void* in, void* out, size_t
       c->trace_ready = (e == cudaSuccess);
     }
     if (e != cudaSuccess) return fail(c, VB_FAILED, cudaGetErrorString(e));
-    cudaMemcpyAsync(out, c->heap->base(c->rank) + c->stage_out, user_out, cudaMemcpyDeviceToDevice, stream);
+    if (user_out) cudaMemcpyAsync(out, c->heap->base(c->rank) + c->stage_out, user_out, cudaMemcpyDeviceToDevice, stream);
     cudaEvent_t done;
     cudaEventCreateWithFlags(&done, cudaEventDisableTiming);
     cudaEventRecord(done, stream);

@@ -4,9 +4,12 @@
 // config: {"xml": path, "rank": r, "nranks": p, "device": d, "control_address": "127.0.0.1",
 //          "control_port": port, "session": id, "count": elements per rank, "dtype": 0|1|2,
 //          "redop": 0..3, "scale": f, "nlanes": L, "niters": I, "warmup": W, "iters": K,
-//          "timeout_s": t, "receipt": path[, "trace": path of a per-step trace of the last invocation]}
+//          "timeout_s": t, "receipt": path[, "trace": path of a per-step trace of the last invocation]
+//          [, "root": r for broadcast / reduce]}
 // Inputs follow the analytic pattern value = 1 + ((3*rank + i) mod 5); outputs
-// are checked on the device in fp64 against the analytic collective result.
+// are checked on the device in fp64 against the analytic result of the
+// schedule's collective (scale applied to reductions), and the input buffer is
+// re-checked afterwards (it is read-only).  The receipt reports both counts.
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -54,14 +57,27 @@ int main(int argc, char** argv) {
   if (r != VB_OK) { fprintf(stderr, "vb_init failed: %d\n", r); return 8; }
   r = vb_prepare(ctx, xs.str().c_str(), (int)cfg.at("nlanes").as_int(), (int)cfg.at("niters").as_int(), timeout);
   if (r != VB_OK) { fprintf(stderr, "vb_prepare failed: %d %s\n", r, vb_last_error(ctx)); return 8; }
-  std::string coll = xs.str().find("coll=\"allgather\"") != std::string::npos ? "allgather" : "allreduce";
+  // the collective named by the <algo coll="..."> attribute
+  std::string coll = "allreduce";
+  {
+    const std::string& text = xs.str();
+    size_t at = text.find("coll=\"");
+    if (at != std::string::npos) {
+      size_t end = text.find('"', at + 6);
+      if (end != std::string::npos) coll = text.substr(at + 6, end - at - 6);
+    }
+  }
+  int check_code = coll == "allgather" ? 1 : coll == "reduce_scatter" ? 2 : coll == "broadcast" ? 3
+                   : coll == "reduce" ? 4 : coll == "alltoall" ? 5 : 0;
+  const Json* root_cfg = cfg.get("root");
+  int root = root_cfg ? (int)root_cfg->as_int() : 0;
   size_t esz = dtype == 0 ? 4 : 2;
-  size_t out_count = coll == "allgather" ? count * nranks : count;
+  size_t out_count = coll == "allgather" ? count * nranks : coll == "reduce_scatter" ? count / nranks : count;
   void *in = nullptr, *out = nullptr;
   unsigned long long* bad = nullptr;
   cudaMalloc(&in, count * esz);
   cudaMalloc(&out, out_count * esz);
-  cudaMalloc(&bad, sizeof(unsigned long long));
+  cudaMalloc(&bad, 2 * sizeof(unsigned long long));
   cudaStream_t s;
   cudaStreamCreate(&s);
   launch_fill(in, (long long)count, dtype, 0, rank, 0, s);
@@ -90,19 +106,23 @@ int main(int argc, char** argv) {
     fprintf(stderr, "vb_trace_write failed: %s\n", vb_last_error(ctx));
     return 8;
   }
-  cudaMemsetAsync(bad, 0, sizeof(unsigned long long), s);
-  launch_check(out, (long long)out_count, dtype, coll == "allgather" ? 1 : 0, redop, nranks, rank, (long long)count,
-               1e-2, 1e-2, bad, s);
-  unsigned long long nbad = 0;
-  cudaMemcpyAsync(&nbad, bad, sizeof nbad, cudaMemcpyDeviceToHost, s);
+  cudaMemsetAsync(bad, 0, 2 * sizeof(unsigned long long), s);
+  // a reduce defines the output on its root only
+  long long checked = (check_code == 4 && rank != root) ? 0 : (long long)out_count;
+  launch_check(out, checked, dtype, check_code, redop, nranks, rank, (long long)count, 1e-2, 1e-2, bad, s, root,
+               (double)scale);
+  // the input is read-only: it must still hold this rank's pattern
+  launch_check(in, (long long)count, dtype, 6, redop, nranks, rank, (long long)count, 0.0, 0.0, bad + 1, s);
+  unsigned long long nbad[2] = {0, 0};
+  cudaMemcpyAsync(nbad, bad, sizeof nbad, cudaMemcpyDeviceToHost, s);
   cudaStreamSynchronize(s);
   std::ofstream receipt(cfg.at("receipt").as_string());
-  receipt << "{\"rank\":" << rank << ",\"nranks\":" << nranks << ",\"count\":" << count << ",\"bad\":" << nbad
-          << ",\"device_times_us\":[";
+  receipt << "{\"rank\":" << rank << ",\"nranks\":" << nranks << ",\"count\":" << count << ",\"coll\":\"" << coll
+          << "\",\"bad\":" << nbad[0] << ",\"bad_input\":" << nbad[1] << ",\"device_times_us\":[";
   for (size_t i = 0; i < times.size(); ++i) receipt << (i ? "," : "") << times[i];
   receipt << "],\"abi\":" << vb_abi_version() << "}\n";
   receipt.close();
   vb_close(ctx, timeout);
   vb_destroy(ctx);
-  return nbad ? 5 : 0;
+  return (nbad[0] || nbad[1]) ? 5 : 0;
 }

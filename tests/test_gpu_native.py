@@ -38,3 +38,18 @@ def test_native_driver_writes_step_traces(tmp_path):
         doc = parse_trace((tmp_path / ("trace-rank%d.bin" % rank)).read_bytes(), partial_ok=False)
         assert doc["rank"] == rank and doc["complete"] and doc["records"]
         assert all(r.end_ns >= r.start_ns > 0 for r in doc["records"])
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+@pytest.mark.parametrize("coll,root", [("reduce_scatter", 0), ("alltoall", 0), ("broadcast", 1), ("reduce", 1),
+                                       ("allgather", 0)])
+def test_native_driver_checks_every_collective(coll, root):
+    """The driver's analytic check and read-only input re-check cover each collective kind."""
+    if _gpus() < 2:
+        pytest.skip("needs two GPUs")
+    from vericcl_b200.execution.native import NativeScheduleDriver
+    slices = 2
+    xml = schedule_xml(coll, 2, slices, root=root if coll in ("broadcast", "reduce") else 0)
+    res = NativeScheduleDriver(xml, 2).measure(count=1 << 14, nlanes=4, iters=2, timeout_s=20, root=root)
+    assert res["bad"] == 0 and res["bad_input"] == 0

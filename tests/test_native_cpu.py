@@ -27,3 +27,7 @@ def test_native_contract_and_control_plane(tmp_path):
 def test_combine_takes_slowest_rank_per_invocation():
     out = combine_schedule_results([{"device_times_us": [1, 5, 3], "bad": 0}, {"device_times_us": [2, 4, 3], "bad": 0}])
     assert out["per_invocation_us"] == [2, 5, 3] and out["mean_us"] == 10 / 3
+    assert out["bad"] == 0 and out["bad_input"] == 0
+    changed = combine_schedule_results([{"device_times_us": [1], "bad": 0, "bad_input": 3},
+                                        {"device_times_us": [1], "bad": 2, "bad_input": 0}])
+    assert changed["bad"] == 2 and changed["bad_input"] == 3

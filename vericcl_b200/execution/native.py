@@ -29,7 +29,7 @@ def combine_schedule_results(receipts):
         raise RuntimeFailure("ranks reported different invocation counts")
     per_invocation = [max(ts) for ts in zip(*times)]
     return {"mean_us": statistics.fmean(per_invocation), "per_invocation_us": per_invocation,
-            "bad": sum(r["bad"] for r in receipts)}
+            "bad": sum(r["bad"] for r in receipts), "bad_input": sum(r.get("bad_input", 0) for r in receipts)}
 
 
 class NativeScheduleDriver:
@@ -76,7 +76,7 @@ class NativeScheduleDriver:
 
     def measure(self, *, count: int, dtype: int = 0, redop: int = 0, scale: float = 1.0, nlanes: int = 32,
                 niters: int = 1, warmup: int = 3, iters: int = 10, timeout_s: float = 60.0, trace_dir=None,
-                grace_s: float = 30.0):
+                grace_s: float = 30.0, root: int = 0):
         """Device-timed invocations; with ``trace_dir`` every rank also writes
         ``trace-rank<r>.bin`` (per-step trace of its last invocation).  A rank
         still running ``3 · timeout_s + grace_s`` after the launch has its
@@ -88,7 +88,7 @@ class NativeScheduleDriver:
         self.last_clean = True
         try:
             result = self._run(session, count, dtype, redop, scale, nlanes, niters, warmup, iters, timeout_s,
-                               trace_dir, grace_s)
+                               trace_dir, grace_s, root)
         except Exception:
             if uuids:
                 if self.last_clean:
@@ -107,7 +107,7 @@ class NativeScheduleDriver:
         return result
 
     def _run(self, session, count, dtype, redop, scale, nlanes, niters, warmup, iters, timeout_s, trace_dir,
-             grace_s=30.0):
+             grace_s=30.0, root=0):
         from vericcl_b200.ops.build import OUT
         all_local = all(r.local for r in self.runners)
         control = "127.0.0.1" if all_local else self.hosts[0]
@@ -134,7 +134,8 @@ class NativeScheduleDriver:
                 cfg = {"xml": where["xml"], "rank": rank, "nranks": self.nranks, "device": self.devices[rank],
                        "control_address": control, "control_port": self.port, "session": session, "count": count,
                        "dtype": dtype, "redop": redop, "scale": scale, "nlanes": nlanes, "niters": niters,
-                       "warmup": warmup, "iters": iters, "timeout_s": timeout_s, "receipt": where["receipt"]}
+                       "warmup": warmup, "iters": iters, "timeout_s": timeout_s, "receipt": where["receipt"],
+                       "root": root}
                 if trace_dir is not None:
                     Path(trace_dir).mkdir(parents=True, exist_ok=True)
                     cfg["trace"] = where["trace"]

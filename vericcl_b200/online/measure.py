@@ -29,9 +29,10 @@ def native_measure(xml: str, request, *, iters: int = 5, warmup: int = 2, nlanes
                                   binary=paths.get("vericcl_native") or None,
                                   environment=runtime.get("environment") or {})
     res = driver.measure(count=count, dtype=DTYPE_CODES.get(request.collective.datatype, 0), nlanes=nlanes,
-                         warmup=warmup, iters=iters, timeout_s=60.0)
-    if res["bad"]:
-        raise RuntimeError("measured schedule produced wrong results")
+                         warmup=warmup, iters=iters, timeout_s=60.0, root=request.collective.root or 0)
+    if res["bad"] or res.get("bad_input"):
+        raise RuntimeError("measured schedule produced wrong results (%d outputs, %d inputs changed)"
+                           % (res["bad"], res.get("bad_input", 0)))
     return res["mean_us"]
 
 
