@@ -31,3 +31,16 @@ def test_combine_takes_slowest_rank_per_invocation():
     changed = combine_schedule_results([{"device_times_us": [1], "bad": 0, "bad_input": 3},
                                         {"device_times_us": [1], "bad": 2, "bad_input": 0}])
     assert changed["bad"] == 2 and changed["bad_input"] == 3
+
+
+def test_capi_execute_path_on_cpu_stand_ins(tmp_path):
+    """vb_execute staging symmetry and unresolved-execution ownership, two ranks as threads (no GPU)."""
+    from vericcl_b200.ops.build import build_capi_cpu_tests
+    from vericcl_b200.synthesis import schedule_xml
+    binary = build_capi_cpu_tests()
+    ar, rd = tmp_path / "allreduce.xml", tmp_path / "reduce.xml"
+    ar.write_text(schedule_xml("allreduce", 2, 2))
+    rd.write_text(schedule_xml("reduce", 2, 2, root=1))
+    proc = subprocess.run([str(binary), str(ar), str(rd)], capture_output=True, text=True, timeout=120)
+    assert proc.returncode == 0, proc.stdout + proc.stderr
+    assert "capi cpu tests passed" in proc.stdout

@@ -209,12 +209,32 @@ def build_native_tests(force: bool = False) -> Path:
     return target
 
 
+def build_capi_cpu_tests(force: bool = False) -> Path:
+    """The C API's execute path built with g++ against host stand-ins of the CUDA runtime and the heap."""
+    OUT.mkdir(parents=True, exist_ok=True)
+    target = OUT / "capi_cpu_tests"
+    stubs = ROOT / "tests" / "native" / "cpu_stubs"
+    sources = [CSRC / s for s in CAPI_SOURCES + RUNTIME_SOURCES] + [CSRC / "plan" / "xml_parse.cc",
+                                                                     CSRC / "plan" / "compile.cc"] + \
+        [stubs / "stubs.cc", ROOT / "tests" / "native" / "test_capi_cpu.cc"]
+    headers = [stubs / "cuda_runtime.h", stubs / "cuda.h"]
+    flags = ["-O1", "-std=c++17", "-pthread", "-I", str(stubs), "-I", str(CSRC / "include")]
+    stamp = _digest(sources + headers, flags)
+    if not force and _fresh(target, stamp):
+        return target
+    _run(["g++", *flags, *map(str, sources), "-o", str(target) + ".tmp"], "C API CPU test build")
+    os.replace(str(target) + ".tmp", target)
+    _mark(target, stamp)
+    return target
+
+
 def build_all(force: bool = False) -> dict:
     out = {"plan": str(build_plan_module(force))}
     out["cuda"] = str(build_cuda_module(force))
     out["capi"] = str(build_capi(force))
     out["driver"] = str(build_driver(force))
     out["native_tests"] = str(build_native_tests(force))
+    out["capi_cpu_tests"] = str(build_capi_cpu_tests(force))
     return out
 
 
