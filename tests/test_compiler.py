@@ -125,3 +125,19 @@ def test_rooted_and_alltoall_programs_on_the_oracle(coll, root, lanes, iters, me
     for r in range(p):
         if exp[r] is not None:
             np.testing.assert_allclose(outs[r][:len(exp[r])], exp[r], atol=1e-5)
+
+
+def test_device_blocks_must_fit_the_resident_ctas(monkeypatch):
+    from vericcl_b200.examples import example_documents
+    from vericcl_b200.input.loader import resolve_documents
+    from vericcl_b200.program import checks
+    req = resolve_documents(example_documents("allreduce", "hierarchy", 4, total_size_bytes=4 * 1024,
+                                              slice_size_bytes=1024))
+    from vericcl_b200.synthesis import synthesize
+    bundle = synthesize(req)
+    assert bundle.checks["compatibility"]["status"] == "valid"
+    assert 1 <= bundle.checks["compatibility"]["detail"]["device_blocks"] <= checks.B200_RESIDENT_CTAS
+    monkeypatch.setattr(checks, "B200_RESIDENT_CTAS", 0)
+    from vericcl_b200.topology import load_topology
+    again = checks.evaluate_program(bundle, load_topology(req))
+    assert again["compatibility"]["status"] == "invalid" and "co-resident" in again["compatibility"]["detail"]

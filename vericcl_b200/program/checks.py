@@ -16,8 +16,9 @@ ones are valid and compatibility is valid or not run.
 * launch — runtime structural limits (steps per TB, TBs per rank, channels,
   dependency ids, buffer offsets) and the interpreter's device-block limit.
 * compatibility — the native compiler accepts the program under pull
-  semantics (no reliance on FIFO buffering); not run when the native module
-  cannot be built.
+  semantics (no reliance on FIFO buffering) and its device blocks (after
+  block merging) fit the 148 co-resident CTAs of a B200; not run when the
+  native module cannot be built.
 * prediction — exact T_pred exists with no missing cost component.
 """
 from __future__ import annotations
@@ -31,6 +32,9 @@ from vericcl_b200.semantics.collective import CollectiveKind, required_outputs
 from vericcl_b200.semantics.versions import canonical
 
 MAX_DEVICE_BLOCKS = 512
+# The interpreter is a cooperative launch of 512-thread CTAs using up to 128 registers each, so one CTA is
+# resident per SM: a rank's device blocks (each with at least one lane) must fit the 148 SMs of a B200.
+B200_RESIDENT_CTAS = 148
 
 
 def _ok(detail=None):
@@ -222,7 +226,13 @@ def evaluate_program(bundle, topology) -> dict:
         try:
             from vericcl_b200.program.device import compile_xml
             compiled = compile_xml(bundle.xml, nlanes=1, niters=1)
-            checks["compatibility"] = _ok(dict(compiled.stats))
+            blocks = compiled.max_blocks
+            if blocks > B200_RESIDENT_CTAS:
+                checks["compatibility"] = _bad("%d device blocks on one rank exceed the %d CTAs that are co-resident "
+                                               "on a B200 (one 512-thread interpreter CTA per SM)"
+                                               % (blocks, B200_RESIDENT_CTAS))
+            else:
+                checks["compatibility"] = _ok(dict(compiled.stats, device_blocks=blocks))
         except SemanticError as error:
             checks["compatibility"] = _bad(error)
         except Exception as error:  # native module unavailable
