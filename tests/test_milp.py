@@ -102,3 +102,34 @@ def test_route_templates_balance_interchangeable_demands():
     assert [choice["d%d" % i].name for i in range(4)] in (["star", "relay"] * 2, ["relay", "star"] * 2)
     assert _interleave({0: 3, 1: 1}) in ([0, 1, 0, 0], [0, 0, 1, 0])
     assert sorted(_interleave({0: 2, 1: 3})) == [0, 0, 1, 1, 1]
+
+
+def test_owned_result_survives_solver_output():
+    """Text the solver library writes to standard output does not corrupt the owned worker's result."""
+    import os
+    import pickle
+    import subprocess
+    import sys
+    from pathlib import Path
+    m = knapsack()
+    code = """
+import os
+from vericcl_b200.solver import milp
+real = milp._solve_arrays
+
+
+def noisy(*args):
+    os.write(1, b"solver chatter\\n")
+    return real(*args)
+
+
+milp._solve_arrays = noisy
+milp._worker_main()
+"""
+    payload = pickle.dumps((m.arrays(), [v.name for v in m.vars], m.objective_constant, 10.0, 0.0))
+    root = str(Path(__file__).resolve().parents[1])
+    proc = subprocess.run([sys.executable, "-c", code], input=payload, capture_output=True, timeout=60,
+                          env=dict(os.environ, PYTHONPATH=root))
+    assert proc.returncode == 0, proc.stderr.decode()[-1000:]
+    got = pickle.loads(proc.stdout)
+    assert got.status == "optimal" and b"solver chatter" in proc.stderr

@@ -188,12 +188,15 @@ _CACHE: dict[str, Solution] = {}
 def _worker_main() -> None:
     """Child side of an owned solve: a pickled problem on stdin, the pickled :class:`Solution` on stdout."""
     arrays, names, constant, time_limit, mip_gap = pickle.load(sys.stdin.buffer)
+    # the solver library may print to file descriptor 1: keep the result channel to ourselves
+    result_fd = os.dup(1)
+    os.dup2(2, 1)
     try:
         result = _solve_arrays(arrays, names, constant, time_limit, mip_gap)
     except BaseException as error:  # pragma: no cover
         result = Solution("error", None, {}, None, 0.0, repr(error))
-    sys.stdout.buffer.write(pickle.dumps(result))
-    sys.stdout.buffer.flush()
+    with os.fdopen(result_fd, "wb") as channel:
+        channel.write(pickle.dumps(result))
 
 
 def solve_owned(model: Model, *, time_limit: float = 60.0, mip_gap: float = 0.0, grace_s: float = 5.0,
