@@ -133,3 +133,23 @@ milp._worker_main()
     assert proc.returncode == 0, proc.stderr.decode()[-1000:]
     got = pickle.loads(proc.stdout)
     assert got.status == "optimal" and b"solver chatter" in proc.stderr
+
+
+def test_in_process_solves_keep_standard_output_clean(capfd):
+    """Solver library text goes to standard error, so a command's JSON lines stay parseable."""
+    import os
+    from vericcl_b200.solver import milp
+    real = milp._solve_arrays
+
+    def noisy(*args):
+        os.write(1, b"solver chatter\n")
+        return real(*args)
+
+    milp._solve_arrays = noisy
+    try:
+        assert knapsack().solve().status == "optimal"
+    finally:
+        milp._solve_arrays = real
+    print('{"ok": true}')
+    out, err = capfd.readouterr()
+    assert out.strip() == '{"ok": true}' and "solver chatter" in err

@@ -14,7 +14,9 @@ import os
 import pickle
 import subprocess
 import sys
+import threading
 import time
+from contextlib import contextmanager
 from dataclasses import dataclass, field
 from pathlib import Path
 
@@ -158,8 +160,41 @@ class Model:
         return c, lb, ub, integrality, None, None, None
 
     def solve(self, *, time_limit: float = 60.0, mip_gap: float = 0.0, threads: int = 1) -> Solution:
-        return _solve_arrays(self.arrays(), [v.name for v in self.vars], self.objective_constant,
-                             time_limit, mip_gap)
+        with _solver_output_to_stderr():
+            return _solve_arrays(self.arrays(), [v.name for v in self.vars], self.objective_constant,
+                                 time_limit, mip_gap)
+
+
+_QUIET_LOCK = threading.Lock()
+_QUIET = {"depth": 0, "saved": None}
+
+
+@contextmanager
+def _solver_output_to_stderr():
+    """Send what the solver library prints on file descriptor 1 to standard error for the block.
+
+    The package's commands print JSON lines on standard output; the HiGHS
+    library writes progress text straight to descriptor 1.  Nested and
+    concurrent blocks share one redirection, restored when the last one ends.
+    """
+    with _QUIET_LOCK:
+        if _QUIET["depth"] == 0:
+            try:
+                sys.stdout.flush()
+                _QUIET["saved"] = os.dup(1)
+                os.dup2(2, 1)
+            except (OSError, ValueError):
+                _QUIET["saved"] = None
+        _QUIET["depth"] += 1
+    try:
+        yield
+    finally:
+        with _QUIET_LOCK:
+            _QUIET["depth"] -= 1
+            if _QUIET["depth"] == 0 and _QUIET["saved"] is not None:
+                os.dup2(_QUIET["saved"], 1)
+                os.close(_QUIET["saved"])
+                _QUIET["saved"] = None
 
 
 def _solve_arrays(arrays, names, constant, time_limit, mip_gap) -> Solution:
