@@ -153,3 +153,37 @@ def test_in_process_solves_keep_standard_output_clean(capfd):
     print('{"ok": true}')
     out, err = capfd.readouterr()
     assert out.strip() == '{"ok": true}' and "solver chatter" in err
+
+
+def test_template_counts_reach_the_per_demand_optimum():
+    """Aggregating interchangeable demands into counts loses nothing: the max link load equals brute force."""
+    import itertools
+    import random
+    from vericcl_b200.solver.demands import TransferDemand, Tree
+    from vericcl_b200.solver.routing import choose_trees
+    from vericcl_b200.topology import topology_from_document
+    from vericcl_b200.topology.model import LinkKey
+    from vericcl_b200.topology.nvswitch import nvswitch_topology
+    rng = random.Random(5)
+    for trial in range(6):
+        doc = nvswitch_topology(3, nvls=False)
+        for link in doc["directed_links"]:
+            link["resources"] = []
+            link["beta_us_per_byte"] = rng.choice([0.001, 0.002, 0.004])
+        doc["shared_resources"] = []
+        topo = topology_from_document(doc)
+        trees = (Tree("direct", ((0, 1),), 1), Tree("relay", ((0, 2), (2, 1)), 2))
+        k = rng.randint(1, 6)
+        demands = [TransferDemand("d%d" % i, "n", 0, "broadcast", 0, (1,), i, candidates=trees) for i in range(k)]
+        size = 1000
+
+        def max_load(assign):
+            load = {}
+            for t in assign:
+                for a, b in t.edges:
+                    load[(a, b)] = load.get((a, b), 0.0) + size * topo.link(LinkKey(a, b)).beta_us_per_byte
+            return max(load.values())
+
+        best = min(max_load(c) for c in itertools.product(trees, repeat=k))
+        got = choose_trees(demands, topo, size)
+        assert max_load([got["d%d" % i] for i in range(k)]) == pytest.approx(best), trial
