@@ -22,7 +22,9 @@ def test_build_sources_are_tracked():
     rel = []
     for name in ("RUNTIME_SOURCES", "CUDA_SOURCES", "PLAN_SOURCES", "CAPI_SOURCES"):
         rel += ["csrc/" + s for s in getattr(build, name, [])]
-    rel += ["csrc/cuda/noalloc.cu", "csrc/runtime/driver.cc", "tests/native/test_control_and_contract.cc"]
+    rel += ["csrc/cuda/noalloc.cu", "csrc/runtime/driver.cc", "tests/native/test_control_and_contract.cc",
+            "tests/native/test_capi_cpu.cc", "tests/native/cpu_stubs/stubs.cc", "tests/native/cpu_stubs/cuda.h",
+            "tests/native/cpu_stubs/cuda_runtime.h", "tests/requirements.json"]
     headers = [str(p.relative_to(ROOT)) for p in (ROOT / "csrc" / "include").rglob("*.h")]
     missing = [p for p in rel + headers if p not in tracked]
     assert not missing, missing
