@@ -94,8 +94,8 @@ def torch_flags():
     return inc, libs
 
 
-CUDA_SOURCES = ["cuda/interp.cu", "cuda/oneshot.cu", "cuda/helpers.cu", "cuda/direct.cu", "cuda/probes.cu", "cuda/fp8.cu",
-                "runtime/symheap.cc", "runtime/cuda_ext.cc"]
+CUDA_SOURCES = ["cuda/interp.cu", "cuda/oneshot.cu", "cuda/helpers.cu", "cuda/direct.cu", "cuda/probes.cu",
+                "cuda/fp8.cu", "runtime/symheap.cc", "runtime/cuda_ext.cc"]
 
 
 def build_cuda_module(force: bool = False, jobs: int | None = None) -> Path:

@@ -206,7 +206,8 @@ def evaluate_program(bundle, topology) -> dict:
     except SemanticError as error:
         checks["semantic"] = _bad(error)
     issues = check_storage(program, request)
-    checks["storage"] = _ok({"scratch_slots": dict(program.scratch_slots)}) if not issues else _bad("; ".join(issues[:5]))
+    checks["storage"] = (_ok({"scratch_slots": dict(program.scratch_slots)}) if not issues
+                         else _bad("; ".join(issues[:5])))
     try:
         deps, members = execution_dependencies(program)
         checks["endpoint"] = _ok({"operations": len(members)})

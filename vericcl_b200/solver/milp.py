@@ -238,10 +238,11 @@ def solve_owned(model: Model, *, time_limit: float = 60.0, mip_gap: float = 0.0,
                 use_cache: bool = True) -> Solution:
     """Solve in a fresh child process that is killed if it outlives its lease.
 
-    The child is a new interpreter running :func:`_worker_main`, not a fork: forking a process in which HiGHS has already run copies its
-    thread pool's locks in a held state and the child's solve never starts.
-    Proven-optimal outcomes are cached by model fingerprint, so identical
-    subproblems (isomorphic templates) are solved once.
+    The child is a new interpreter running :func:`_worker_main`, not a fork:
+    forking a process in which HiGHS has already run copies its thread pool's
+    locks in a held state and the child's solve never starts.  Proven-optimal
+    outcomes are cached by model fingerprint, so identical subproblems
+    (isomorphic templates) are solved once.
     """
     key = model.fingerprint() + ":%g" % mip_gap
     if use_cache and key in _CACHE:
