@@ -67,6 +67,7 @@ struct RankProgram {
 struct CompileStats {
   int xml_steps = 0, device_steps = 0, elided_blocks = 0, fused_reduces = 0, multicast_ops = 0;
   int waits = 0, remote_waits = 0, scale_steps = 0, deferred_waits = 0, dropped_nops = 0;
+  int staged_forwards = 0;   // 'rrs' steps given a scratch store so the next hop can pull the value
 };
 
 struct CompiledPlan {

@@ -23,6 +23,7 @@ py::dict stats_dict(const CompileStats& s) {
   d["scale_steps"] = s.scale_steps;
   d["deferred_waits"] = s.deferred_waits;
   d["dropped_nops"] = s.dropped_nops;
+  d["staged_forwards"] = s.staged_forwards;
   return d;
 }
 

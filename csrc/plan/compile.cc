@@ -142,7 +142,6 @@ class Compiler {
           ++stats_.xml_steps;
           if (has_send(st.kind) && b.send < 0) fail(std::string("step '") + kname(st.kind) + "' in a TB without a send peer");
           if (has_recv(st.kind) && b.recv < 0) fail(std::string("step '") + kname(st.kind) + "' in a TB without a receive peer");
-          if (st.kind == X_RRS) fail("'rrs' (reduce-and-forward without a local store) needs a staging buffer; not supported");
           if (st.kind == X_S || st.kind == X_CPY || st.kind == X_RRC || st.kind == X_RE) check_region(r, st.srcbuf, st.srcoff, st.cnt, "source");
           if (writes_dst(st.kind)) check_region(r, st.dstbuf, st.dstoff, st.cnt, "destination");
           if (st.depid >= 0) {
@@ -1060,9 +1059,29 @@ class Compiler {
 
 }  // namespace
 
-CompiledPlan compile_plan(const XAlgo& algo, const CompileOptions& options) {
-  if (options.nlanes < 1 || options.nlanes > kMaxFlagLanes) throw CompileError("nlanes must be in [1, 256]");
-  if (options.niters < 1) throw CompileError("niters must be positive");
+namespace {
+
+// Under pull semantics the next hop reads a forwarded value out of the forwarding rank's memory, so an
+// 'rrs' (receive, reduce with a local operand, send on, without a local store) becomes an 'rrcs' whose
+// store goes to a scratch region of its own, appended to that rank's scratch buffer.
+XAlgo stage_forwarded_reductions(const XAlgo& algo, int* staged) {
+  XAlgo out = algo;
+  *staged = 0;
+  for (XGpu& g : out.gpus)
+    for (XTB& b : g.tbs)
+      for (XStep& st : b.steps) {
+        if (st.kind != X_RRS) continue;
+        if (st.cnt < 1) throw CompileError("an 'rrs' step needs a positive count");
+        st.kind = X_RRCS;
+        st.dstbuf = BUF_SCR;
+        st.dstoff = g.s_chunks;
+        g.s_chunks += st.cnt;
+        ++*staged;
+      }
+  return out;
+}
+
+CompiledPlan compile_staged(const XAlgo& algo, const CompileOptions& options) {
   if (options.fuse_chains) {
     try {
       Compiler c(algo, options);
@@ -1078,6 +1097,18 @@ CompiledPlan compile_plan(const XAlgo& algo, const CompileOptions& options) {
   }
   Compiler c(algo, options);
   return c.run();
+}
+
+}  // namespace
+
+CompiledPlan compile_plan(const XAlgo& algo, const CompileOptions& options) {
+  if (options.nlanes < 1 || options.nlanes > kMaxFlagLanes) throw CompileError("nlanes must be in [1, 256]");
+  if (options.niters < 1) throw CompileError("niters must be positive");
+  int staged = 0;
+  XAlgo prepared = stage_forwarded_reductions(algo, &staged);
+  CompiledPlan plan = compile_staged(prepared, options);
+  plan.stats.staged_forwards = staged;
+  return plan;
 }
 
 std::string describe_rank(const CompiledPlan& plan, int rank) {

@@ -313,6 +313,7 @@ class DevicePlan {
     d["multicast_ops"] = plan_.stats.multicast_ops;
     d["deferred_waits"] = plan_.stats.deferred_waits;
     d["dropped_nops"] = plan_.stats.dropped_nops;
+    d["staged_forwards"] = plan_.stats.staged_forwards;
     return d;
   }
 

@@ -141,3 +141,35 @@ def test_device_blocks_must_fit_the_resident_ctas(monkeypatch):
     from vericcl_b200.topology import load_topology
     again = checks.evaluate_program(bundle, load_topology(req))
     assert again["compatibility"]["status"] == "invalid" and "co-resident" in again["compatibility"]["detail"]
+
+
+RRS_CHAIN = """<algo name="chain" nchannels="1" nchunksperloop="1" proto="Simple" coll="reduce" inplace="0" redop="sum" ngpus="3">
+  <gpu id="0" i_chunks="1" o_chunks="0" s_chunks="0">
+    <tb id="0" send="1" recv="-1" chan="0">
+      <step s="0" type="s" srcbuf="i" srcoff="0" dstbuf="i" dstoff="0" cnt="1" depid="-1" deps="-1" hasdep="0"/>
+    </tb>
+  </gpu>
+  <gpu id="1" i_chunks="1" o_chunks="0" s_chunks="0">
+    <tb id="0" send="2" recv="0" chan="0">
+      <step s="0" type="rrs" srcbuf="i" srcoff="0" dstbuf="i" dstoff="0" cnt="1" depid="-1" deps="-1" hasdep="0"/>
+    </tb>
+  </gpu>
+  <gpu id="2" i_chunks="1" o_chunks="1" s_chunks="0">
+    <tb id="0" send="-1" recv="1" chan="0">
+      <step s="0" type="rrc" srcbuf="i" srcoff="0" dstbuf="o" dstoff="0" cnt="1" depid="-1" deps="-1" hasdep="0"/>
+    </tb>
+  </gpu>
+</algo>
+"""
+
+
+@pytest.mark.parametrize("lanes,iters", [(1, 1), (3, 2)])
+def test_reduce_and_forward_is_staged_in_scratch(lanes, iters):
+    """An 'rrs' forwards a partial sum it never stores; under pulls it gets a scratch store of its own."""
+    compiled = compile_xml(RRS_CHAIN, nlanes=lanes, niters=iters)
+    assert compiled.stats["staged_forwards"] == 1
+    assert compiled.slots(1)[2] == 1 and compiled.slots(0)[2] == 0
+    rng = np.random.default_rng(4)
+    inputs = [rng.standard_normal(96).astype(np.float32) for _ in range(3)]
+    outs = run_cpu(compiled, inputs, seed=7)
+    np.testing.assert_allclose(outs[2][:96], inputs[0] + inputs[1] + inputs[2], rtol=1e-6, atol=1e-6)
