@@ -1,0 +1,83 @@
+"""AllGather ↔ ReduceScatter duality: a ReduceScatter schedule from an AllGather one.
+
+An AllGather moves every slice ``sid = s·q + j`` from its owner ``s`` to all
+ranks along a broadcast tree.  Reversing every edge of that tree gives a
+reduction tree into ``s`` — exactly what a ReduceScatter needs for its output
+``sid`` (owned by rank ``s``), over the same links and channels.  Each AG
+``send a→b`` becomes an ``rrc b→a`` carrying the sum of ``b``'s subtree;
+a rank forwards only after all of its subtree arrived, and reductions into
+one rank chain through its accumulator, children taken in reverse AG time
+order (the branch the AllGather served last is reduced first).  Start times
+come from the same list schedule as composed candidates (reference:
+vericcl/composer/dual.py:412, ``reverse_allgather_schedule``).
+
+The AllGather candidate has ``q`` slices per rank; the ReduceScatter
+candidate has ``p·q`` slices per rank of the same slice size, so its request
+is the AllGather's with ``p`` times the bytes per rank.
+"""
+from __future__ import annotations
+
+from collections import defaultdict
+
+from vericcl_b200.composer.compose import NetworkCandidate, NetworkOperation, list_schedule
+from vericcl_b200.errors import SemanticError
+
+
+def reverse_allgather(ag: NetworkCandidate, topology, *, origin: str = "dual") -> NetworkCandidate:
+    p, q = ag.rank_count, ag.slice_count
+    n = p * q
+    trees = defaultdict(list)
+    for op in ag.operations:
+        if op.kind != "send" or len(op.contributors) != 1:
+            raise SemanticError("only broadcast-tree AllGather schedules can be reversed")
+        trees[next(iter(op.contributors))].append(op)
+    if set(trees) != set(range(n)):
+        raise SemanticError("the AllGather schedule does not move every slice")
+    ops = []
+    for sid in sorted(trees):
+        root = sid // q
+        children = defaultdict(list)
+        seen = set()
+        for op in trees[sid]:
+            if op.dst_rank in seen or op.dst_rank == root:
+                raise SemanticError("slice %d reaches a rank twice; not a tree" % sid)
+            seen.add(op.dst_rank)
+            children[op.src_rank].append(op)
+        if seen != set(range(p)) - {root}:
+            raise SemanticError("slice %d does not reach every rank" % sid)
+        subtree = {}
+
+        def value_of(rank):
+            if rank not in subtree:
+                total = frozenset({rank * n + sid})
+                for child_op in children.get(rank, ()):
+                    total |= value_of(child_op.dst_rank)
+                subtree[rank] = total
+            return subtree[rank]
+
+        if value_of(root) != frozenset(r * n + sid for r in range(p)):
+            raise SemanticError("slice %d's tree is not connected to its owner" % sid)
+        accumulator = {}
+
+        def emit(rank):
+            # the branch the AllGather served last is reduced first
+            for child_op in sorted(children.get(rank, ()), key=lambda o: (-o.priority_time, o.operation_id)):
+                child = child_op.dst_rank
+                emit(child)
+                deps = set()
+                if child in accumulator:
+                    deps.add(accumulator[child][0])
+                if rank in accumulator:
+                    deps.add(accumulator[rank][0])
+                    base = accumulator[rank][1]
+                else:
+                    base = frozenset({rank * n + sid})
+                carried = subtree[child]
+                op_id = "dual:" + child_op.operation_id
+                ops.append(NetworkOperation(op_id, "rrc", child, rank, child_op.channel, child_op.stage_id, carried,
+                                            base | carried, frozenset(deps), 0.0, sid))
+                accumulator[rank] = (op_id, base | carried)
+
+        emit(root)
+    timed = list_schedule(ops, topology, ag.slice_size_bytes)
+    return NetworkCandidate(p, n, ag.slice_size_bytes, tuple(timed), origin, ag.channels)

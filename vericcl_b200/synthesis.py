@@ -93,6 +93,45 @@ def synthesize(request, model=None, *, channels: int = 1) -> CandidateBundle:
     return lower_candidate(request, topology, network, model, plan=plan, origin=plan.mode.value)
 
 
+def allgather_request_for(request):
+    """The AllGather request whose slices a ReduceScatter request reduces (same slice size, 1/P the bytes)."""
+    import json
+    from vericcl_b200.input.loader import resolve_documents
+    p = request.rank_count
+    n = request.hyperparameters.slice_count
+    if n is None or n % p:
+        raise SemanticError("the ReduceScatter slice count must be a multiple of the rank count")
+    docs = json.loads(json.dumps(dict(request.request_config), default=dict))
+    coll = docs["sketch"]["collective"]
+    coll["operator"] = "allgather"
+    for key in ("reduction_op", "scale", "root"):
+        coll.pop(key, None)
+    hyper = docs["sketch"]["hyperparameters"]
+    hyper["total_size_bytes"] = request.hyperparameters.total_size_bytes // p
+    hyper["slice_size_bytes"] = request.hyperparameters.slice_size_bytes
+    hyper.pop("reference_slice_size_bytes", None)
+    return resolve_documents(docs, purpose=request.purpose)
+
+
+def synthesize_reduce_scatter_dual(request, model=None, *, channels: int = 1) -> CandidateBundle:
+    """A ReduceScatter candidate made by reversing the AllGather schedule of the same slices.
+
+    The AllGather is synthesized for the same topology, slice size and
+    method; every broadcast tree is reversed into a reduction tree
+    (``composer/dual.py``); the result is lowered, checked and predicted
+    like any ReduceScatter candidate.
+    """
+    from vericcl_b200.composer.dual import reverse_allgather
+    if request.collective.kind.value != "reduce_scatter":
+        raise SemanticError("the AllGather dual builds ReduceScatter candidates only")
+    topology = load_topology(request)
+    # the AllGather's own cost context (no reduction); routes come from the topology, and the reversed
+    # schedule is predicted under ``model`` below
+    ag = synthesize(allgather_request_for(request), None, channels=channels)
+    network = reverse_allgather(ag.network, topology, origin="dual:" + ag.origin)
+    return lower_candidate(request, topology, network, model, origin="allgather_dual")
+
+
 @lru_cache(maxsize=256)
 def schedule_xml(collective: str, ranks: int, slices_per_rank: int, *, inplace: bool = False,
                  datatype: str = "float32", method: str = "hierarchy", channels: int = 1, root: int = 0) -> str:

@@ -40,7 +40,7 @@ from vericcl_b200.performance.simulation import predict
 from vericcl_b200.planner.parameters import initial_parameter_domain
 from vericcl_b200.program.sidecar import to_sidecar
 from vericcl_b200.solver.bounds import dependency_lower_bound
-from vericcl_b200.synthesis import Lowerer, synthesize
+from vericcl_b200.synthesis import Lowerer, synthesize, synthesize_reduce_scatter_dual
 from vericcl_b200.topology import load_topology
 from vericcl_b200.utils.jsonio import atomic_write_json, atomic_write_text
 
@@ -211,6 +211,15 @@ class PrimaryWorkflow:
                                  "reason_codes": ["scratch"], "requires_resolve": False})
                         continue
                     self.store(bundle, "initial")
+                if req.collective.kind.value == "reduce_scatter":
+                    # the reversed AllGather schedule of the same slices is another candidate
+                    lease.check()
+                    try:
+                        bundle = synthesize_reduce_scatter_dual(req, self.model, channels=channels)
+                    except (SemanticError, SolverError, InputValidationError) as error:
+                        self.ctx.emit("candidate_failed", method="allgather_dual", error=str(error))
+                    else:
+                        self.store(bundle, "initial")
         self.stage_times["initial_s"] = time.monotonic() - t0
         self.checkpoint("initial_done")
 
