@@ -32,7 +32,7 @@ def test_build_sources_are_tracked():
 
 def test_entry_points_and_no_build_outputs_tracked():
     tracked = _tracked()
-    for path in ("__graft_entry__.py", "bench.py", "sweep.py", "README.md", "DESIGN.md", "pytest.ini"):
+    for path in ("__graft_entry__.py", "bench.py", "sweep.py", "README.md", "pytest.ini"):
         assert path in tracked
     built = [p for p in tracked if p.endswith((".so", ".o", ".stamp", ".ncu-rep")) or p.startswith("_work/")]
     assert not built, built

@@ -20,7 +20,6 @@ JUNIT = """<?xml version="1.0"?>
 def test_every_inventory_row_is_mapped_to_existing_tests():
     reqs = json.loads(DEFAULT_REQUIREMENTS.read_text())
     survey_rows = set()
-    design = (ROOT / "DESIGN.md").read_text()
     for row in reqs:
         for f in reqs[row]:
             assert (ROOT / f).exists(), (row, f)
@@ -29,7 +28,6 @@ def test_every_inventory_row_is_mapped_to_existing_tests():
     expected = {"P%d" % i for i in range(1, 37)} | {"P5L", "P20L", "P24L"} | {"N%d" % i for i in range(1, 13)} \
         | {"N1e"} | {"M%d" % i for i in range(1, 10)} | {"K%d" % i for i in range(1, 15)}
     assert survey_rows == expected
-    assert "K8 stride copy" in design
 
 
 def test_report_statuses(tmp_path):
