@@ -19,15 +19,15 @@ JUNIT = """<?xml version="1.0"?>
 
 def test_every_inventory_row_is_mapped_to_existing_tests():
     reqs = json.loads(DEFAULT_REQUIREMENTS.read_text())
-    survey_rows = set()
+    inventory_rows = set()
     for row in reqs:
         for f in reqs[row]:
             assert (ROOT / f).exists(), (row, f)
-        survey_rows.add(row)
+        inventory_rows.add(row)
     # the K, M, N and P rows of the component inventory
     expected = {"P%d" % i for i in range(1, 37)} | {"P5L", "P20L", "P24L"} | {"N%d" % i for i in range(1, 13)} \
         | {"N1e"} | {"M%d" % i for i in range(1, 10)} | {"K%d" % i for i in range(1, 15)}
-    assert survey_rows == expected
+    assert inventory_rows == expected
 
 
 def test_report_statuses(tmp_path):
