@@ -67,3 +67,18 @@ def test_workflow_offers_the_dual_candidate(tmp_path):
     assert main(args) == 0
     meta = json.loads((tmp_path / "examples" / "d" / "output" / "s" / "run.json").read_text())
     assert meta["best"]["origin"] == "allgather_dual"
+
+
+@pytest.mark.parametrize("groups,p", [(1, 4), (2, 8)])
+def test_allreduce_from_reduce_scatter_then_allgather(groups, p):
+    from vericcl_b200.synthesis import synthesize_allreduce_rs_ag
+    s, q = 1024, 2
+    topo = multinode_topology(groups, p // groups, inter_gbps=25.0) if groups > 1 else None
+    ar = resolve_documents(example_documents("allreduce", "hierarchy", p, total_size_bytes=p * q * s,
+                                             slice_size_bytes=s, topology=topo, scale=0.25))
+    bundle = synthesize_allreduce_rs_ag(ar)
+    assert bundle.can_execute, bundle.checks
+    ok, err = check_program_numerics(parse_xml(bundle.xml), count_per_rank=p * q * 16, seed=5)
+    assert ok, err
+    kinds = [op.kind for op in bundle.network.operations]
+    assert kinds.count("rrc") == kinds.count("send") > 0

@@ -81,3 +81,34 @@ def reverse_allgather(ag: NetworkCandidate, topology, *, origin: str = "dual") -
         emit(root)
     timed = list_schedule(ops, topology, ag.slice_size_bytes)
     return NetworkCandidate(p, n, ag.slice_size_bytes, tuple(timed), origin, ag.channels)
+
+
+def allreduce_from_allgather(ag: NetworkCandidate, topology, *, origin: str = "rs_ag") -> NetworkCandidate:
+    """An AllReduce as the reversed AllGather (a ReduceScatter) followed by the AllGather itself.
+
+    Slice ``sid`` is reduced into its owner along the reversed tree, then
+    broadcast from the owner along the original tree; the broadcast of a slice
+    waits only for that slice's reduction, so the two phases overlap slice by
+    slice.  The AllReduce request has ``p·q`` slices per rank.
+    """
+    rs = reverse_allgather(ag, topology, origin=origin)
+    p, q = ag.rank_count, ag.slice_count
+    n = p * q
+    final = {}
+    for op in rs.operations:
+        if op.dst_rank == op.index // q and len(op.target_contributors) == p:
+            final[op.index] = op.operation_id
+    ops = list(rs.operations)
+    for op in ag.operations:
+        sid = next(iter(op.contributors))
+        full = frozenset(r * n + sid for r in range(p))
+        deps = {"bcast:" + d for d in op.dependencies}
+        if op.src_rank == sid // q:
+            if p > 1 and sid not in final:
+                raise SemanticError("slice %d has no completed reduction at its owner" % sid)
+            if sid in final:
+                deps.add(final[sid])
+        ops.append(NetworkOperation("bcast:" + op.operation_id, "send", op.src_rank, op.dst_rank, op.channel,
+                                    op.stage_id + 1, full, full, frozenset(deps), 0.0, sid))
+    timed = list_schedule(ops, topology, ag.slice_size_bytes)
+    return NetworkCandidate(p, n, ag.slice_size_bytes, tuple(timed), origin, ag.channels)

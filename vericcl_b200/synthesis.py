@@ -94,13 +94,14 @@ def synthesize(request, model=None, *, channels: int = 1) -> CandidateBundle:
 
 
 def allgather_request_for(request):
-    """The AllGather request whose slices a ReduceScatter request reduces (same slice size, 1/P the bytes)."""
+    """The AllGather request over the same slices (same slice size, 1/P the bytes) of a ReduceScatter or an
+    AllReduce request."""
     import json
     from vericcl_b200.input.loader import resolve_documents
     p = request.rank_count
     n = request.hyperparameters.slice_count
     if n is None or n % p:
-        raise SemanticError("the ReduceScatter slice count must be a multiple of the rank count")
+        raise SemanticError("the slice count must be a multiple of the rank count")
     docs = json.loads(json.dumps(dict(request.request_config), default=dict))
     coll = docs["sketch"]["collective"]
     coll["operator"] = "allgather"
@@ -130,6 +131,17 @@ def synthesize_reduce_scatter_dual(request, model=None, *, channels: int = 1) ->
     ag = synthesize(allgather_request_for(request), None, channels=channels)
     network = reverse_allgather(ag.network, topology, origin="dual:" + ag.origin)
     return lower_candidate(request, topology, network, model, origin="allgather_dual")
+
+
+def synthesize_allreduce_rs_ag(request, model=None, *, channels: int = 1) -> CandidateBundle:
+    """An AllReduce candidate: the reversed AllGather schedule (a ReduceScatter) then the AllGather itself."""
+    from vericcl_b200.composer.dual import allreduce_from_allgather
+    if request.collective.kind.value != "allreduce":
+        raise SemanticError("the ReduceScatter + AllGather composition builds AllReduce candidates only")
+    topology = load_topology(request)
+    ag = synthesize(allgather_request_for(request), None, channels=channels)
+    network = allreduce_from_allgather(ag.network, topology, origin="rs_ag:" + ag.origin)
+    return lower_candidate(request, topology, network, model, origin="reduce_scatter_allgather")
 
 
 @lru_cache(maxsize=256)

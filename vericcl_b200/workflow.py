@@ -40,7 +40,8 @@ from vericcl_b200.performance.simulation import predict
 from vericcl_b200.planner.parameters import initial_parameter_domain
 from vericcl_b200.program.sidecar import to_sidecar
 from vericcl_b200.solver.bounds import dependency_lower_bound
-from vericcl_b200.synthesis import Lowerer, synthesize, synthesize_reduce_scatter_dual
+from vericcl_b200.synthesis import (Lowerer, synthesize, synthesize_allreduce_rs_ag,
+                                    synthesize_reduce_scatter_dual)
 from vericcl_b200.topology import load_topology
 from vericcl_b200.utils.jsonio import atomic_write_json, atomic_write_text
 
@@ -211,13 +212,17 @@ class PrimaryWorkflow:
                                  "reason_codes": ["scratch"], "requires_resolve": False})
                         continue
                     self.store(bundle, "initial")
-                if req.collective.kind.value == "reduce_scatter":
-                    # the reversed AllGather schedule of the same slices is another candidate
+                # candidates built from the AllGather schedule of the same slices: reversed (a ReduceScatter),
+                # or reversed and then run forward (an AllReduce)
+                dual = {"reduce_scatter": ("allgather_dual", synthesize_reduce_scatter_dual),
+                        "allreduce": ("reduce_scatter_allgather", synthesize_allreduce_rs_ag)}.get(
+                            req.collective.kind.value)
+                if dual is not None and req.hyperparameters.slice_count % req.rank_count == 0:
                     lease.check()
                     try:
-                        bundle = synthesize_reduce_scatter_dual(req, self.model, channels=channels)
+                        bundle = dual[1](req, self.model, channels=channels)
                     except (SemanticError, SolverError, InputValidationError) as error:
-                        self.ctx.emit("candidate_failed", method="allgather_dual", error=str(error))
+                        self.ctx.emit("candidate_failed", method=dual[0], error=str(error))
                     else:
                         self.store(bundle, "initial")
         self.stage_times["initial_s"] = time.monotonic() - t0
