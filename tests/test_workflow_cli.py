@@ -140,3 +140,13 @@ def test_calibration_reuse_adopts_a_cached_model(tmp_path):
     wf2 = PrimaryWorkflow(load_request(files2), RunContext.create(tmp_path, "c", "solve", run_id="r2",
                                                                   input_files=files2))
     assert wf2.calibration() is False and wf2.model.version != "measured-cached"
+
+
+def test_tuning_with_a_slice_chosen_by_the_parameter_domain(tmp_path):
+    """No fixed slice size: the domain picks it, and the tuning round's cut bound uses the incumbent's slices."""
+    d = example_documents("reduce_scatter", "hierarchy", 4, total_size_bytes=256 << 10, slice_size_bytes=None,
+                          tuning_rounds=1, calibration=False)
+    write_documents(tmp_path / "in", d)
+    assert main(["solve"] + _args(tmp_path / "in", tmp_path, "c", "auto-slice")) == 0
+    meta = json.loads((tmp_path / "examples" / "c" / "output" / "auto-slice" / "run.json").read_text())
+    assert meta["best"]["slice_size_bytes"] > 0 and meta["result"]["rounds"]

@@ -324,7 +324,7 @@ class PrimaryWorkflow:
                 return "no incumbent"
             self.budgets.new_round()
             record = {"round": index, "start_t_pred_us": self.incumbent.t_pred_us}
-            bound = certify_global_cut(self.request, self.topology, self.model)
+            bound = certify_global_cut(self.incumbent.request, self.topology, self.model)
             if bound is not None:
                 record["cut_lower_bound_us"] = bound.lower_bound_us
                 if check_global_cut(bound, self.incumbent.t_pred_us):
