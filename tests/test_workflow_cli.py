@@ -150,3 +150,22 @@ def test_tuning_with_a_slice_chosen_by_the_parameter_domain(tmp_path):
     assert main(["solve"] + _args(tmp_path / "in", tmp_path, "c", "auto-slice")) == 0
     meta = json.loads((tmp_path / "examples" / "c" / "output" / "auto-slice" / "run.json").read_text())
     assert meta["best"]["slice_size_bytes"] > 0 and meta["result"]["rounds"]
+
+
+def test_history_lookup_without_a_fixed_slice(tmp_path):
+    from vericcl_b200.input.loader import resolve_documents
+    from vericcl_b200.solver.history import find_schedules, save_schedule
+    from vericcl_b200.synthesis import synthesize
+    from vericcl_b200.topology import load_topology
+    fixed = resolve_documents(example_documents("allgather", "hierarchy", 4, total_size_bytes=64 << 10,
+                                                slice_size_bytes=16 << 10))
+    bundle = synthesize(fixed)
+    index = tmp_path / "index.json"
+    save_schedule(index, fixed, load_topology(fixed), bundle.xml, bundle.t_pred_us)
+    auto = resolve_documents(example_documents("allgather", "hierarchy", 4, total_size_bytes=64 << 10,
+                                               slice_size_bytes=None))
+    found = find_schedules(index, auto, load_topology(auto), tolerance=0.01, limit=4)
+    assert len(found) == 1 and found[0]["t_pred_us"] == bundle.t_pred_us
+    other = resolve_documents(example_documents("allgather", "hierarchy", 4, total_size_bytes=64 << 10,
+                                                slice_size_bytes=8 << 10))
+    assert find_schedules(index, other, load_topology(other), tolerance=0.01, limit=4) == []

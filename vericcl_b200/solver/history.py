@@ -44,7 +44,14 @@ def find_schedules(index_path, request, topology, *, tolerance: float, limit: in
     inverse = {new: old for old, new in mapping.items()}
     current = sorted(1.0 / l.beta_us_per_byte for l in topology.links.values())
     out = []
-    for entry in json.loads(path.read_text()).get(_key(request, sig), []):
+    data = json.loads(path.read_text())
+    if request.hyperparameters.slice_size_bytes is None:
+        # no fixed slice size: schedules saved for any slice size of this problem qualify
+        prefix = _key(request, sig).rsplit("|", 1)[0] + "|"
+        entries = [e for k in sorted(data) if k.startswith(prefix) for e in data[k]]
+    else:
+        entries = data.get(_key(request, sig), [])
+    for entry in entries:
         scales = [a / b for a, b in zip(current, entry["bandwidth"]) if b]
         if scales and max(scales) / min(scales) - 1.0 > tolerance:
             continue
