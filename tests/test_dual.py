@@ -82,3 +82,27 @@ def test_allreduce_from_reduce_scatter_then_allgather(groups, p):
     assert ok, err
     kinds = [op.kind for op in bundle.network.operations]
     assert kinds.count("rrc") == kinds.count("send") > 0
+
+
+@pytest.mark.parametrize("groups,p", [(1, 4), (2, 8)])
+def test_reduce_scatter_reverses_into_an_allgather_and_round_trips(groups, p):
+    from vericcl_b200.composer.dual import reverse_reduce_scatter
+    from vericcl_b200.performance.initial import initial_cost_model
+    from vericcl_b200.synthesis import Lowerer
+    s, q = 1024, 2
+    topo_doc = multinode_topology(groups, p // groups, inter_gbps=25.0) if groups > 1 else None
+    ag_req = resolve_documents(example_documents("allgather", "hierarchy", p, total_size_bytes=q * s,
+                                                 slice_size_bytes=s, topology=topo_doc))
+    rs_req = resolve_documents(example_documents("reduce_scatter", "hierarchy", p, total_size_bytes=p * q * s,
+                                                 slice_size_bytes=s, topology=topo_doc))
+    topo = load_topology(ag_req)
+    rs = synthesize(rs_req)
+    back = Lowerer(ag_req, topo, initial_cost_model(ag_req))(reverse_reduce_scatter(rs.network, topo))
+    assert back.can_execute, back.checks
+    ok, err = check_program_numerics(parse_xml(back.xml), count_per_rank=q * 16, seed=3)
+    assert ok, err
+    # AllGather → ReduceScatter → AllGather keeps every edge and channel
+    ag = synthesize(ag_req)
+    again = reverse_reduce_scatter(reverse_allgather(ag.network, load_topology(rs_req)), topo)
+    key = lambda ops: sorted((o.src_rank, o.dst_rank, o.channel, min(o.contributors)) for o in ops)
+    assert key(again.operations) == key(ag.network.operations)

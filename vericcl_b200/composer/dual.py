@@ -1,4 +1,4 @@
-"""AllGather ↔ ReduceScatter duality: a ReduceScatter schedule from an AllGather one.
+"""AllGather ↔ ReduceScatter duality: each schedule reversed into the other.
 
 An AllGather moves every slice ``sid = s·q + j`` from its owner ``s`` to all
 ranks along a broadcast tree.  Reversing every edge of that tree gives a
@@ -112,3 +112,49 @@ def allreduce_from_allgather(ag: NetworkCandidate, topology, *, origin: str = "r
                                     op.stage_id + 1, full, full, frozenset(deps), 0.0, sid))
     timed = list_schedule(ops, topology, ag.slice_size_bytes)
     return NetworkCandidate(p, n, ag.slice_size_bytes, tuple(timed), origin, ag.channels)
+
+
+def reverse_reduce_scatter(rs: NetworkCandidate, topology, *, origin: str = "dual") -> NetworkCandidate:
+    """The other direction: every reduction tree of a ReduceScatter reversed into a broadcast tree.
+
+    The ReduceScatter has ``p·q`` slices per rank; output ``idx`` is reduced
+    into rank ``idx // q``.  Reversed, that rank broadcasts its slice ``idx``
+    (``q`` slices per rank) to every rank over the same links and channels, a
+    relay forwarding only after it received.
+    """
+    p, n = rs.rank_count, rs.slice_count
+    if n % p:
+        raise SemanticError("the ReduceScatter slice count must be a multiple of the rank count")
+    q = n // p
+    parent_of = defaultdict(dict)        # idx -> child -> op
+    for op in rs.operations:
+        if op.kind != "rrc":
+            raise SemanticError("only reduction-tree ReduceScatter schedules can be reversed")
+        if op.src_rank in parent_of[op.index]:
+            raise SemanticError("slice %d leaves rank %d twice; not a tree" % (op.index, op.src_rank))
+        parent_of[op.index][op.src_rank] = op
+    ops = []
+    for idx in range(n):
+        owner = idx // q
+        edges = parent_of.get(idx, {})
+        if set(edges) != set(range(p)) - {owner}:
+            raise SemanticError("slice %d is not reduced from every rank" % idx)
+        delivered = {}
+
+        def deliver(rank):
+            """Id of the broadcast op that brings slice idx to ``rank`` (None at the owner)."""
+            if rank == owner:
+                return None
+            if rank not in delivered:
+                op = edges[rank]
+                dep = deliver(op.dst_rank)
+                delivered[rank] = "dual:" + op.operation_id
+                ops.append(NetworkOperation(delivered[rank], "send", op.dst_rank, rank, op.channel, op.stage_id,
+                                            frozenset({idx}), frozenset({idx}),
+                                            frozenset({dep}) if dep else frozenset(), -op.priority_time, idx % q))
+            return delivered[rank]
+
+        for child in sorted(edges, key=lambda r: (-edges[r].priority_time, r)):
+            deliver(child)
+    timed = list_schedule(ops, topology, rs.slice_size_bytes)
+    return NetworkCandidate(p, q, rs.slice_size_bytes, tuple(timed), origin, rs.channels)
