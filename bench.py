@@ -9,9 +9,18 @@ Launch: ``python bench.py`` (1 GPU) or ``torchrun --nproc-per-node N bench.py
 --gpus N``.  Timing: W untimed warm-up steps, then K steps bracketed by a
 barrier and a device synchronize, measured with CUDA events on the launching
 stream; the reported time is the max over ranks.  The 16 GB buffer is larger
-than the 126 MB L2, so no flush is needed between steps.  ``value`` is the
-whole-job aggregate bus bandwidth: the sum over GPUs of the NCCL-convention
-bus bandwidth (2(P-1)/P × bytes / time; with one GPU the bytes count once).
+than the 126 MB L2, so no flush is needed between steps.
+
+Units.  ``busbw_per_gpu_gbs`` is the nccl-tests bus bandwidth of one GPU
+(2(P-1)/P × bytes / time).  ``value`` is the whole-job aggregate: that figure
+summed over the N GPUs.  With one GPU an AllReduce moves nothing between GPUs;
+the bytes are then counted once and the figure is the rate of the in-place
+scale pass (an HBM read and write), labelled as such.  ``nvlink`` gives the
+bytes each GPU really sends per direction on the path the plan takes and
+their fraction of 900 GB/s (nominal) and 770 GB/s (measured peer copy).
+
+``--impl reference`` runs the reference's own MSCCL/NCCL 2.12.12 build instead
+(``baseline/reference_arm.py``), without PyTorch or this package.
 """
 from __future__ import annotations
 
@@ -22,8 +31,6 @@ import statistics
 import subprocess
 import sys
 import time
-
-import torch
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
@@ -47,29 +54,6 @@ def parse():
     ap.add_argument("--per-bucket", action="store_true", help="one launch per bucket instead of one batched launch")
     ap.add_argument("--slices", type=int, default=None, help="slices per rank of the synthesized schedule")
     return ap.parse_args()
-
-
-def reference_unavailable(reason: str):
-    # under torchrun every rank runs this; only rank 0 prints the line
-    if os.environ.get("RANK", "0") == "0":
-        print(json.dumps({"impl": "reference", "unavailable": reason}), flush=True)
-
-
-def reference_reason() -> str:
-    ref = os.path.join(ROOT, "baseline", "_ref")
-    if not os.path.isdir(os.path.join(ref, "vericcl")):
-        return "reference package is not installed in baseline/_ref"
-    missing = []
-    for mod in ("pyscipopt", "gmpy2", "dd", "lxml"):
-        try:
-            __import__(mod)
-        except ImportError:
-            missing.append(mod)
-    mpi = any(os.path.exists(os.path.join(d, "mpirun")) for d in os.environ.get("PATH", "").split(os.pathsep))
-    return ("reference installed in baseline/_ref (--no-deps) but its public API cannot run here: "
-            "its synthesis imports %s (absent offline) and its GPU path executes schedules only through "
-            "its patched MSCCL 0.1 / NCCL 2.12.12 runtime launched with Open MPI (%s); NCCL 2.12 predates "
-            "sm_100" % (", ".join(missing) or "nothing missing", "mpirun present" if mpi else "no mpirun"))
 
 
 class ClockSampler:
@@ -142,11 +126,28 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def timed(fn, steps, stream, barrier):
+    """Device time of ``steps`` calls of ``fn`` on ``stream`` (ms per call), bracketed by barriers."""
+    import torch
+    barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        fn()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    return t0.elapsed_time(t1) / steps
+
+
 def main():
     args = parse()
     if args.impl == "reference":
-        reference_unavailable(reference_reason())
-        return 0
+        sys.path.insert(0, os.path.join(ROOT, "baseline"))
+        import reference_arm
+        return reference_arm.run(args, ClockSampler, METRIC, MODEL)
+    import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if world != args.gpus:
         raise SystemExit("--gpus %d but WORLD_SIZE=%d (launch N>1 with torchrun)" % (args.gpus, world))
@@ -176,6 +177,7 @@ def main():
         part = flat[lo:lo + step]
         part.copy_(torch.randn(part.numel(), generator=gen, device="cuda", dtype=torch.float32).mul_(0.02))
     stream = torch.cuda.current_stream()
+    batched = not args.per_bucket
 
     def barrier():
         if world > 1:
@@ -188,10 +190,10 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=comm.control_group)
         return float(t.item())
 
-    # correctness of the first and last bucket of one full (batched) sync against NCCL, untimed
+    # correctness of the first and last bucket of one full sync against an fp32 sum of every rank's data, untimed
     first, last = ar.bucket(0), ar.bucket(ar.buckets - 1)
     saved = [first.clone(), last.clone()]
-    ar.sync(stream, batched=not args.per_bucket)
+    ar.sync(stream, batched=batched)
     torch.cuda.synchronize()
     comm.check_status()
     err, tol_fail = 0.0, False
@@ -207,50 +209,68 @@ def main():
     del saved
 
     for _ in range(args.warmup):
-        ar.sync(stream, batched=not args.per_bucket)
+        ar.sync(stream, batched=batched)
     torch.cuda.synchronize()
     comm.check_status()
-    barrier()
-    torch.cuda.synchronize()
     with ClockSampler([local] if world == 1 else list(range(world)), enabled=rank == 0) as clocks:
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier()
-        torch.cuda.synchronize()
-        start.record(stream)
-        for _ in range(args.steps):
-            ar.sync(stream, batched=not args.per_bucket)
-        end.record(stream)
-        torch.cuda.synchronize()
-        barrier()
-    ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+        ms = timed(lambda: ar.sync(stream, batched=batched), args.steps, stream, barrier)
+    ms = max_over_ranks(ms)
     comm.check_status()
     clock_info = clocks.summary() if rank == 0 else None
     bus = ar.bus_bytes_per_rank()
     busbw = bus / (ms * 1e-3) / 1e9
     value = busbw * world
     launches = args.steps * (ar.buckets if args.per_bucket else ar.launches_per_sync)
+    link_bytes = ar.nvlink_bytes_per_rank()
+    link_gbs = link_bytes / (ms * 1e-3) / 1e9
+    nvlink = {"bytes_per_gpu_per_direction": int(link_bytes), "gbs_per_direction": round(link_gbs, 2),
+              "pct_of_900_nominal": round(100 * link_gbs / 900.0, 2),
+              "pct_of_770_measured_peer_copy": round(100 * link_gbs / 770.0, 2),
+              "path": ("none (one GPU)" if world == 1 else
+                       "NVLS multimem.ld_reduce + multimem.st: (1+1/P) x bytes each way" if ar.plan.multicast else
+                       "peer pulls (reduce-scatter + all-gather): 2(P-1)/P x bytes each way")}
+
+    # the same product API with one launch per bucket (how data-parallel training fires buckets as they fill)
+    other = None
+    if world > 1 and not args.no_nccl:
+        alt = not batched
+        for _ in range(2):
+            ar.sync(stream, batched=alt)
+        oms = max_over_ranks(timed(lambda: ar.sync(stream, batched=alt), max(2, args.steps // 4), stream, barrier))
+        comm.check_status()
+        other = {"mode": "batched" if alt else "per-bucket", "ms_per_step": round(oms, 4),
+                 "busbw_per_gpu_gbs": round(bus / (oms * 1e-3) / 1e9, 2),
+                 "launches_per_step": ar.launches_per_sync if alt else ar.buckets}
 
     nccl = None
     if world > 1 and not args.no_nccl:
         premul = dist._make_nccl_premul_sum(args.scale)
         bufs = [ar.bucket(i) for i in range(ar.buckets)]
-        for _ in range(max(1, args.warmup)):
+        flat_all = ar.grads
+
+        def per_bucket():
             for b in bufs:
                 dist.all_reduce(b, op=premul)
-        torch.cuda.synchronize()
-        barrier()
-        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s2.record(stream)
-        for _ in range(args.steps):
-            for b in bufs:
-                dist.all_reduce(b, op=premul)
-        e2.record(stream)
-        torch.cuda.synchronize()
-        nms = max_over_ranks(s2.elapsed_time(e2) / args.steps)
-        nccl = {"ms_per_step": round(nms, 4), "busbw_gbs": round(bus / (nms * 1e-3) / 1e9, 2),
-                "aggregate_gbs": round(bus / (nms * 1e-3) / 1e9 * world, 2),
-                "op": "ncclAllReduce PREMUL_SUM (torch %s, NCCL %s)" % (torch.__version__,
-                                                                       ".".join(map(str, torch.cuda.nccl.version())))}
+
+        def grouped():
+            with dist._coalescing_manager(device=torch.device("cuda", local)):
+                for b in bufs:
+                    dist.all_reduce(b, op=premul)
+
+        def flat_call():
+            dist.all_reduce(flat_all, op=premul)
+
+        nccl = {"library": "torch %s, NCCL %s" % (torch.__version__, ".".join(map(str, torch.cuda.nccl.version()))),
+                "op": "ncclAllReduce PREMUL_SUM (scale fused)"}
+        for name, fn in (("per_bucket", per_bucket), ("per_bucket_grouped", grouped), ("flat_16GB", flat_call)):
+            try:
+                for _ in range(max(1, min(2, args.warmup))):
+                    fn()
+                torch.cuda.synchronize()
+                nms = max_over_ranks(timed(fn, max(2, args.steps // 4), stream, barrier))
+                nccl[name] = {"ms_per_step": round(nms, 4), "busbw_per_gpu_gbs": round(bus / (nms * 1e-3) / 1e9, 2)}
+            except Exception as e:     # a comparator that fails does not void the product's line
+                nccl[name] = {"error": str(e)[:200]}
 
     e2e = None
     if not args.no_e2e:
@@ -262,30 +282,25 @@ def main():
             host = None
         if host is not None:
             out_host = torch.empty(32768, dtype=dtype, pin_memory=True)
-            for _ in range(1):
+
+            def e2e_step():
                 flat.copy_(host, non_blocking=True)
-                ar.sync(stream, batched=not args.per_bucket)
-                out_host.copy_(ar.grads[:32768], non_blocking=True)
-            torch.cuda.synchronize()
-            barrier()
-            s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s3.record(stream)
-            for _ in range(args.e2e_steps):
-                flat.copy_(host, non_blocking=True)
-                ar.sync(stream, batched=not args.per_bucket)
+                ar.sync(stream, batched=batched)
                 out_host.copy_(ar.grads[:32768], non_blocking=True)
                 stream.synchronize()
                 _ = float(out_host[0])
-            e3.record(stream)
-            torch.cuda.synchronize()
-            ems = max_over_ranks(s3.elapsed_time(e3) / args.e2e_steps)
-            e2e = {"value": round(bus / (ems * 1e-3) / 1e9 * world, 2), "unit": "GB/s",
+
+            e2e_step()
+            ems = max_over_ranks(timed(e2e_step, args.e2e_steps, stream, barrier))
+            e2e = {"value": round(bus / (ems * 1e-3) / 1e9 * world, 2),
+                   "unit": "GB/s (sum over GPUs of per-GPU bus bandwidth)",
                    "ms_per_step": round(ems, 3), "h2d_bytes_per_step": int(total_bytes),
                    "d2h_bytes_per_step": int(out_host.numel() * esize),
                    "api": "GradBucketAllReduce.sync after a pinned host->heap copy of all gradients"}
             del host
     if rank == 0:
-        line = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        line = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s (sum over GPUs of per-GPU bus bandwidth)",
+                "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,0.02) gradients, random init",
                 "impl": "vericcl_b200",
@@ -299,8 +314,12 @@ def main():
                                     "stats": ar.plan.device_plan.stats() if ar.plan.device_plan is not None
                                     else {"path": ar.plan.kind}},
                            "l2": "inputs (16 GB) larger than the 126 MB L2; no flush needed"},
-                "busbw_per_gpu_gbs": round(busbw, 2), "pct_of_900": round(100 * busbw / 900.0, 2),
-                "check": {"first_last_bucket_max_err": err, "ok": bool(check_ok), "reference": "NCCL all_reduce x scale"},
+                "busbw_per_gpu_gbs": round(busbw, 2),
+                "busbw_note": ("one GPU: no inter-GPU traffic; bytes counted once, i.e. the in-place scale pass "
+                               "rate (HBM read + write)") if world == 1 else "nccl-tests bus bandwidth, 2(P-1)/P",
+                "nvlink": nvlink, "other_launch_mode": other,
+                "check": {"first_last_bucket_max_err": err, "ok": bool(check_ok),
+                          "reference": "fp32 sum over ranks (torch) x scale"},
                 "clocks": clock_info, "e2e": e2e, "gpu_launches": launches, "nccl": nccl}
         print(json.dumps(line), flush=True)
     comm.close()

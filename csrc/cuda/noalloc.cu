@@ -5,6 +5,7 @@
 // staged chunk onto itself with the fused scale", exactly what the schedule
 // compiler emits for a one-rank in-place AllReduce - with every piece of the
 // interpreter's working memory taken from the static array below.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstring>
@@ -33,6 +34,7 @@ static_assert(sizeof(vb::Control) <= kFlagOff, "control block overlaps the flag 
 
 std::mutex g_setup_mutex;
 unsigned char* g_base[kMaxDevices] = {};    // device address of the array, per device
+CUcontext g_ctx[kMaxDevices] = {};          // the context that address belongs to
 thread_local std::string g_last_error;
 
 int fail(int code, const std::string& why) {
@@ -42,12 +44,19 @@ int fail(int code, const std::string& why) {
 
 // Once per device, with that device current: look the array up, clear the
 // control block and flag table, write the epoch and the one-step program.
+//
+// The set-up is keyed by (device, current context): after cudaDeviceReset the
+// runtime creates a new primary context whose copy of the array holds no
+// control block or program, so a changed context redoes the set-up.
 int setup_device(int device, unsigned char** base) {
   std::lock_guard<std::mutex> lock(g_setup_mutex);
-  if (g_base[device]) {
+  CUcontext ctx = nullptr;
+  if (cuCtxGetCurrent(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+  if (g_base[device] && g_ctx[device] == ctx) {
     *base = g_base[device];
     return VB_NOALLOC_OK;
   }
+  g_base[device] = nullptr;
   void* ptr = nullptr;
   cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
   if (e != cudaSuccess) return fail(VB_NOALLOC_CUDA_ERROR, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
@@ -75,8 +84,16 @@ int setup_device(int device, unsigned char** base) {
   e = cudaMemcpy(p + kTableOff, &t, sizeof t, cudaMemcpyHostToDevice);
   if (e != cudaSuccess) return fail(VB_NOALLOC_CUDA_ERROR, std::string("write program: ") + cudaGetErrorString(e));
   g_base[device] = p;
+  g_ctx[device] = ctx;
   *base = p;
   return VB_NOALLOC_OK;
+}
+
+int current_base(unsigned char** base) {
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess || device < 0 || device >= kMaxDevices) return fail(VB_NOALLOC_CUDA_ERROR, "no current device");
+  return setup_device(device, base);
 }
 
 }  // namespace
@@ -94,12 +111,10 @@ extern "C" int vb_allreduce_local_noalloc(const void* in, void* out, size_t coun
     return fail(VB_NOALLOC_TOO_LARGE, "count * element size = " + std::to_string(count * esize) +
                                           " bytes exceeds the " + std::to_string(VB_NOALLOC_MAX_BYTES) +
                                           "-byte static staging buffer");
-  int device = 0;
-  cudaError_t e = cudaGetDevice(&device);
-  if (e != cudaSuccess || device < 0 || device >= kMaxDevices) return fail(VB_NOALLOC_CUDA_ERROR, "no current device");
   unsigned char* base = nullptr;
-  int rc = setup_device(device, &base);
+  int rc = current_base(&base);
   if (rc != VB_NOALLOC_OK) return rc;
+  cudaError_t e = cudaSuccess;
   cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
   vb::Control* ctl = reinterpret_cast<vb::Control*>(base);
   // status words that must start at zero for every call
@@ -117,7 +132,11 @@ extern "C" int vb_allreduce_local_noalloc(const void* in, void* out, size_t coun
   a.nblocks = 1;
   size_t bytes = padded * esize;
   size_t lanes = bytes / (64u << 10);
-  a.nlanes = (int)(lanes < 1 ? 1 : lanes > kMaxLanes ? kMaxLanes : lanes);
+  // at most one CTA per co-resident slot of the cooperative launch (fewer SMs under MPS or a partitioned GPU)
+  size_t max_lanes = (size_t)vb::interp_max_ctas(512);
+  if (max_lanes > (size_t)kMaxLanes) max_lanes = kMaxLanes;
+  if (max_lanes < 1) return fail(VB_NOALLOC_CUDA_ERROR, "the interpreter kernel cannot be resident on this device");
+  a.nlanes = (int)(lanes < 1 ? 1 : lanes > max_lanes ? max_lanes : lanes);
   a.niters = 1;
   a.nbatch = 1;
   a.rank = 0;
@@ -140,5 +159,22 @@ extern "C" int vb_allreduce_local_noalloc(const void* in, void* out, size_t coun
   if (e != cudaSuccess) return fail(VB_NOALLOC_CUDA_ERROR, std::string("launch: ") + cudaGetErrorString(e));
   e = cudaMemcpyAsync(out, base + kStageOff, count * esize, cudaMemcpyDeviceToDevice, stream);
   if (e != cudaSuccess) return fail(VB_NOALLOC_CUDA_ERROR, std::string("copy result: ") + cudaGetErrorString(e));
+  return VB_NOALLOC_OK;
+}
+
+extern "C" int vb_noalloc_status(int* status, int detail[4]) {
+  if (!status) return fail(VB_NOALLOC_INVALID, "null status pointer");
+  unsigned char* base = nullptr;
+  int rc = current_base(&base);
+  if (rc != VB_NOALLOC_OK) return rc;
+  const vb::Control* ctl = reinterpret_cast<const vb::Control*>(base);
+  int words[5] = {};
+  // a synchronous copy: it waits for the work already enqueued on the legacy default stream, but the
+  // caller must synchronise its own stream first (the header says so)
+  cudaError_t e = cudaMemcpy(words, &ctl->status, sizeof words, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return fail(VB_NOALLOC_CUDA_ERROR, std::string("read status: ") + cudaGetErrorString(e));
+  *status = words[0];
+  if (detail)
+    for (int i = 0; i < 4; ++i) detail[i] = words[1 + i];
   return VB_NOALLOC_OK;
 }

@@ -35,6 +35,13 @@
  *    contents between calls (each call clears the status words that must
  *    start at zero).  Calls whose GPU work overlaps - for example on two
  *    streams at once - race on the array; serialise them on one stream.
+ *  - The kernel never hangs: its waits are bounded and a failure is written
+ *    to a status word in the array instead of trapping.  After synchronising
+ *    the stream, vb_noalloc_status() reports it; on a failure `out` holds
+ *    the unscaled input and must not be used.
+ *  - The set-up belongs to the device's current CUDA context.  A call made
+ *    under a different context (after cudaDeviceReset, for example) repeats
+ *    the set-up for that context.
  */
 #ifndef VERICCL_B200_NOALLOC_H
 #define VERICCL_B200_NOALLOC_H
@@ -58,6 +65,13 @@ enum {
 
 /* dtype: 0 float32, 1 bfloat16, 2 float16.  in/out are device pointers (may be equal). */
 int vb_allreduce_local_noalloc(const void* in, void* out, size_t count, int dtype, float scale, void* cuda_stream);
+
+/* The kernel status of the last call on the current device: *status is 0 when
+ * it completed, 1 when a wait ran out of time, 2 when it was aborted, 3 for a
+ * bad geometry; detail (may be NULL) receives rank, block, lane and wait index
+ * of the failure.  Synchronise the call's stream first.  Returns VB_NOALLOC_OK
+ * or VB_NOALLOC_CUDA_ERROR. */
+int vb_noalloc_status(int* status, int detail[4]);
 
 /* Human-readable reason of the calling thread's last failed call. */
 const char* vb_noalloc_last_error(void);

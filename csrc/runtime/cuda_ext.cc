@@ -7,6 +7,7 @@
 
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <memory>
 #include <stdexcept>
 #include <string>
@@ -448,6 +449,74 @@ PYBIND11_MODULE(_vbcuda, m) {
     cuda_check(launch_copy_probe(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), bytes, ctas, threads,
                                  unroll, at::cuda::getCurrentCUDAStream().stream()), "copy probe");
   });
+  // dst = scale? * op(srcs[0], ..., srcs[K-1]) on this GPU through the interpreter kernel: a one-rank,
+  // one-step program whose step reads K chunks of `srcs` ([K, n], contiguous).  This is the n-ary local reduce
+  // of a single-rank schedule (the reference's onerank reduce, third_party/msccl/src/collectives/device/
+  // onerank_reduce.cu:13-41, generalised to K sources); it runs the same move paths as a K-source pull reduce.
+  m.def("local_reduce", [](torch::Tensor dst, torch::Tensor srcs, int redop, double scale, bool do_scale, int lanes,
+                           int iters, bool lean) {
+    TORCH_CHECK(srcs.is_cuda() && dst.is_cuda() && srcs.is_contiguous() && dst.is_contiguous(), "contiguous CUDA tensors");
+    TORCH_CHECK(srcs.dim() == 2 && srcs.size(1) == dst.numel() && srcs.scalar_type() == dst.scalar_type(),
+                "srcs must be [K, dst.numel()] of dst's dtype");
+    const int dtype = dtype_code(dst.scalar_type());
+    const int64_t k = srcs.size(0), n = dst.numel(), vec = 16 / elem_bytes(dtype);
+    TORCH_CHECK(k >= 1 && k <= 16 && n > 0 && n % vec == 0, "1..16 sources of a multiple of 16 bytes each");
+    TORCH_CHECK(lanes >= 1 && iters >= 1 && redop >= RED_SUM && redop <= RED_MAX, "bad geometry or reduction");
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(srcs.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(dst.data_ptr()) % 16 == 0,
+                "16-byte aligned buffers");
+    TORCH_CHECK(lanes <= interp_max_ctas(512) && lanes <= kMaxFlagLanes, "more lanes than co-resident CTAs");
+    // workspace: [0, 256) control | [256, ...) flags of one block | [8192, ...) program tables
+    const int64_t table_off = 8192;
+    const int64_t bytes = table_off + sizeof(DevBlock) + sizeof(DevStep) + k * sizeof(DevSrc);
+    auto ws = torch::zeros({(bytes + 255) / 256 * 256}, torch::TensorOptions().dtype(torch::kUInt8).device(dst.device()));
+    char* w = reinterpret_cast<char*>(ws.data_ptr());
+    std::vector<char> host(bytes - table_off);
+    DevBlock blk{0, 1, -1, 0, 0};
+    DevStep st{};
+    st.op = k == 1 ? OP_COPY : OP_REDUCE;
+    st.dst_buf = BUF_OUT;
+    st.flags = do_scale ? F_SCALE : 0;
+    st.cnt = 1;
+    st.nsrc = (int32_t)k;
+    std::vector<DevSrc> src(k);
+    for (int64_t i = 0; i < k; ++i) src[i] = DevSrc{0, BUF_IN, 0, (int32_t)i};
+    std::memcpy(host.data(), &blk, sizeof blk);
+    std::memcpy(host.data() + sizeof blk, &st, sizeof st);
+    std::memcpy(host.data() + sizeof blk + sizeof st, src.data(), k * sizeof(DevSrc));
+    auto stream = at::cuda::getCurrentCUDAStream().stream();
+    const unsigned long long epoch = 1;
+    cuda_check(cudaMemcpyAsync(w + offsetof(Control, epoch), &epoch, sizeof epoch, cudaMemcpyHostToDevice, stream), "epoch");
+    cuda_check(cudaMemcpyAsync(w + table_off, host.data(), host.size(), cudaMemcpyHostToDevice, stream), "tables");
+    InterpArgs a{};
+    a.blocks = reinterpret_cast<const DevBlock*>(w + table_off);
+    a.steps = reinterpret_cast<const DevStep*>(w + table_off + sizeof(DevBlock));
+    a.srcs = reinterpret_cast<const DevSrc*>(w + table_off + sizeof(DevBlock) + sizeof(DevStep));
+    a.nblocks = 1;
+    a.nlanes = lanes;
+    a.niters = iters;
+    a.nbatch = 1;
+    a.rank = 0;
+    a.nranks = 1;
+    a.dtype = dtype;
+    a.redop = redop;
+    a.scale = (float)scale;
+    a.chunk_elems = n;
+    const int64_t pieces = (int64_t)lanes * iters;
+    a.piece_elems = ((n + pieces - 1) / pieces + vec - 1) / vec * vec;
+    // offsets are relative to the workspace, which stands in for this rank's heap base
+    a.buf_off[BUF_IN] = (long long)(reinterpret_cast<char*>(srcs.data_ptr()) - w);
+    a.buf_off[BUF_OUT] = (long long)(reinterpret_cast<char*>(dst.data_ptr()) - w);
+    a.buf_off[BUF_SCR] = a.buf_off[BUF_OUT];
+    a.flag_off = 256;
+    a.start_slot = kMaxFlagLanes;
+    a.base[0] = w;
+    a.control = reinterpret_cast<Control*>(w);
+    a.timeout_ns = 10ull * 1000000000ull;
+    a.lean = lean ? 1 : 0;
+    cuda_check(launch_interp(a, stream, 512), "local reduce launch");
+    return ws;   // keeps the workspace alive until the caller drops it; its first int words hold the status
+  }, py::arg("dst"), py::arg("srcs"), py::arg("redop") = 0, py::arg("scale") = 1.0, py::arg("do_scale") = false,
+     py::arg("lanes") = 1, py::arg("iters") = 1, py::arg("lean") = false);
   m.def("reduce_probe", [](uint64_t dst, std::vector<uint64_t> srcs, int64_t bytes, int ctas, int threads) {
     std::vector<const void*> p;
     for (auto s : srcs) p.push_back(reinterpret_cast<const void*>(s));

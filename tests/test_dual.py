@@ -106,3 +106,20 @@ def test_reduce_scatter_reverses_into_an_allgather_and_round_trips(groups, p):
     again = reverse_reduce_scatter(reverse_allgather(ag.network, load_topology(rs_req)), topo)
     key = lambda ops: sorted((o.src_rank, o.dst_rank, o.channel, min(o.contributors)) for o in ops)
     assert key(again.operations) == key(ag.network.operations)
+
+
+def test_reduce_scatter_cycle_among_non_owners_is_refused():
+    """Two non-owner ranks that reduce a slice into each other never reach the owner."""
+    from dataclasses import replace
+    from vericcl_b200.composer.dual import reverse_reduce_scatter
+    p, s = 4, 1024
+    req = resolve_documents(example_documents("reduce_scatter", "hierarchy", p, total_size_bytes=p * s,
+                                              slice_size_bytes=s))
+    rs = synthesize(req).network
+    ops = list(rs.operations)
+    # slice 0 is owned by rank 0; send rank 1's and rank 2's contributions to each other instead
+    for i, op in enumerate(ops):
+        if op.index == 0 and op.src_rank in (1, 2):
+            ops[i] = replace(op, dst_rank=2 if op.src_rank == 1 else 1)
+    with pytest.raises(SemanticError, match="not connected to its owner"):
+        reverse_reduce_scatter(replace(rs, operations=tuple(ops)), load_topology(req))

@@ -217,3 +217,69 @@ def test_bound_launch_follows_the_tensor_size(comm):
     assert torch.allclose(y, x * 2.0)
     comm.free(x)
     comm.free(y)
+
+
+REDOPS = {"sum": 0, "prod": 1, "min": 2, "max": 3}
+
+
+def _reference(stack: torch.Tensor, op: str) -> torch.Tensor:
+    x = stack.float()
+    if op == "sum":
+        return x.sum(0)
+    if op == "prod":
+        return x.prod(0)
+    return x.amin(0) if op == "min" else x.amax(0)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("op", ["sum", "prod", "min", "max"])
+@pytest.mark.parametrize("k", [1, 2, 3, 4, 5, 6, 7, 8, 9, 12])
+def test_local_multi_source_reduce_matches_fp32_reference(comm, dtype, op, k):
+    """The interpreter's K-source move paths (fixed K = 1..8, generic above) for every reduction and dtype."""
+    n = 3 * 4096 + 64
+    gen = torch.Generator(device="cuda").manual_seed(100 * k + REDOPS[op])
+    if op == "prod":
+        srcs = (0.5 + torch.rand(k, n, device="cuda", generator=gen)).to(dtype)
+    else:
+        srcs = torch.randn(k, n, device="cuda", generator=gen).to(dtype)
+    dst = torch.empty(n, device="cuda", dtype=dtype)
+    scale = 0.37 if op == "sum" else 1.0
+    ws = comm._mod.local_reduce(dst, srcs, REDOPS[op], scale, op == "sum", 7, 2, False)
+    torch.cuda.synchronize()
+    assert int(ws[12:16].view(torch.int32).item()) == 0          # the control block's status word
+    ref = _reference(srcs, op) * scale
+    tol = {torch.float32: 1e-5, torch.bfloat16: 1e-2, torch.float16: 2e-3}[dtype]
+    assert torch.allclose(dst.float(), ref, atol=tol * max(1.0, k ** 0.5), rtol=tol)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("k", [1, 2, 3, 8])
+def test_lean_instance_local_reduce(comm, dtype, k):
+    """The register-lean interpreter instance (sum and copies) on the same one-step programs."""
+    n = 1 << 16
+    srcs = torch.randn(k, n, device="cuda").to(dtype)
+    dst = torch.empty(n, device="cuda", dtype=dtype)
+    ws = comm._mod.local_reduce(dst, srcs, 0, 0.5, True, 64, 1, True)
+    torch.cuda.synchronize()
+    assert int(ws[12:16].view(torch.int32).item()) == 0
+    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    assert torch.allclose(dst.float(), srcs.float().sum(0) * 0.5, atol=tol * 2, rtol=tol)
+
+
+@pytest.mark.parametrize("k", [1, 2, 5, 8])
+def test_reduce_probe_matches_torch(comm, k):
+    n = 1 << 18
+    srcs = [torch.randn(n, device="cuda") for _ in range(k)]
+    dst = torch.empty(n, device="cuda")
+    comm._mod.reduce_probe(dst.data_ptr(), [s.data_ptr() for s in srcs], n * 4, 64, 256)
+    torch.cuda.synchronize()
+    assert torch.allclose(dst, torch.stack(srcs).sum(0), atol=1e-5, rtol=1e-5)
+
+
+def test_copy_probe_matches_source(comm):
+    n = 1 << 18
+    src = torch.randn(n, device="cuda")
+    dst = torch.zeros_like(src)
+    comm._mod.copy_probe(dst.data_ptr(), src.data_ptr(), n * 4, 32, 256, 4)
+    torch.cuda.synchronize()
+    assert torch.equal(dst, src)

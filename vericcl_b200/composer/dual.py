@@ -139,6 +139,14 @@ def reverse_reduce_scatter(rs: NetworkCandidate, topology, *, origin: str = "dua
         edges = parent_of.get(idx, {})
         if set(edges) != set(range(p)) - {owner}:
             raise SemanticError("slice %d is not reduced from every rank" % idx)
+        for start in edges:
+            # every parent chain must end at the owner; a cycle among non-owners never delivers
+            seen, rank = set(), start
+            while rank != owner:
+                if rank in seen:
+                    raise SemanticError("slice %d's tree is not connected to its owner" % idx)
+                seen.add(rank)
+                rank = edges[rank].dst_rank
         delivered = {}
 
         def deliver(rank):

@@ -69,3 +69,21 @@ class GradBucketAllReduce:
         world = self.comm.world
         nbytes = self.numel * self.grads.element_size()
         return nbytes * (2.0 * (world - 1) / world if world > 1 else 1.0)
+
+    def nvlink_bytes_per_rank(self) -> float:
+        """Bytes one GPU sends (and receives) over NVLink in one full sync, for the path the plan takes.
+
+        Peer pulls (reduce-scatter, then all-gather of the reduced slices) move
+        2(P-1)/P × bytes each way.  The NVLS path reads every GPU's copy of each
+        slice once through the switch (multimem.ld_reduce, bytes out of every GPU)
+        and multicasts each reduced slice once (bytes/P into the switch per GPU,
+        bytes out of the switch into every GPU): about (1 + 1/P) × bytes each way.
+        One GPU moves nothing over NVLink.
+        """
+        world = self.comm.world
+        nbytes = self.numel * self.grads.element_size()
+        if world == 1:
+            return 0.0
+        if self.plan.kind != "oneshot" and self.plan.multicast:
+            return nbytes * (1.0 + 1.0 / world)
+        return nbytes * 2.0 * (world - 1) / world
