@@ -37,6 +37,7 @@ class CandidateBundle:
     prediction: object
     checks: dict = field(default_factory=dict)
     origin: str = "direct"
+    timing: dict | None = None        # seed vs solver-timed T_pred when the timing MILP ran
 
     @property
     def t_pred_us(self):
@@ -74,7 +75,8 @@ def lower_candidate(request, topology, network, model=None, *, plan=None, origin
     return bundle
 
 
-def synthesize(request, model=None, *, channels: int = 1) -> CandidateBundle:
+def synthesize(request, model=None, *, channels: int = 1, timing: bool = True, plan=None) -> CandidateBundle:
+    """Synthesize, lower, check and predict one candidate (``plan``: a given stage plan, else the method's)."""
     topology = load_topology(request)
     if request.hyperparameters.slice_count is None:
         raise SemanticError("synthesize needs a resolved slice size; use the parameter domain first")
@@ -84,13 +86,22 @@ def synthesize(request, model=None, *, channels: int = 1) -> CandidateBundle:
         from vericcl_b200.solver.trees.construct import construct_network
         network = construct_network(request, topology, model or initial_cost_model(request), channels=channels)
         return lower_candidate(request, topology, network, model, origin="constructive_trees")
-    plan = plan_for(request, topology)
+    plan = plan if plan is not None else plan_for(request, topology)
     demands = build_demands(plan, topology)
     trees = choose_trees(demands, topology, slice_bytes, time_limit=request.solver.per_model_timeout_s)
     network = compose_routes(plan, demands, trees, topology, slice_bytes, channels=channels, origin=plan.mode.value)
-    from vericcl_b200.solver.timing import optimize_fixed_routes
-    network = optimize_fixed_routes(network, topology, time_limit=min(20.0, request.solver.per_model_timeout_s))
-    return lower_candidate(request, topology, network, model, plan=plan, origin=plan.mode.value)
+    from vericcl_b200.solver.timing import keep_better, optimize_fixed_routes
+    seed = lower_candidate(request, topology, network, model, plan=plan, origin=plan.mode.value)
+    if not timing:
+        return seed
+    timed_network = optimize_fixed_routes(network, topology, time_limit=min(6.0, request.solver.per_model_timeout_s))
+    if timed_network is network:
+        return seed
+    timed = lower_candidate(request, topology, timed_network, model, plan=plan, origin=plan.mode.value + "+timing")
+    best = keep_better(seed, timed)
+    best.timing = {"seed_t_pred_us": seed.t_pred_us, "timed_t_pred_us": timed.t_pred_us,
+                   "kept": "timed" if best is timed else "seed", "network_origin": timed_network.origin}
+    return best
 
 
 def allgather_request_for(request):
@@ -161,7 +172,9 @@ def schedule_xml(collective: str, ranks: int, slices_per_rank: int, *, inplace: 
                              max_channels=channels, scratch_bytes=slice_bytes * slices_per_rank * ranks,
                              root=root)
     request = resolve_documents(docs)
-    bundle = synthesize(request, channels=channels)
+    # the runtime path skips the timing MILP: on one NVSwitch domain it never beat the list schedule's
+    # T_pred (every link is uncontended and the ports are shared symmetrically) and costs seconds per shape
+    bundle = synthesize(request, channels=channels, timing=False)
     if not bundle.can_execute:
         failed = {k: v for k, v in bundle.checks.items() if v.get("status") not in ("valid", "not_run")}
         raise SemanticError("synthesized schedule failed admission checks: %s" % failed)

@@ -73,13 +73,39 @@ def multinode_topology(groups: int, per_group: int, *, intra_gbps: float = B200_
     Each group's outbound and inbound inter-group traffic shares one NIC-like
     resource of ``inter_gbps``.
     """
-    ranks = groups * per_group
-    doc = nvswitch_topology(ranks, nvls=False, name="emulated-%dx%d" % (groups, per_group))
-    doc["nodes"] = [{"id": g, "ranks": list(range(g * per_group, (g + 1) * per_group)),
-                     "gateways": list(range(g * per_group, (g + 1) * per_group))} for g in range(groups)]
+    return grouped_topology([per_group] * groups, inter_gbps=inter_gbps, inter_alpha_us=inter_alpha_us,
+                            name="emulated-%dx%d" % (groups, per_group))
+
+
+def grouped_topology(sizes, *, inter_gbps: float = 25.0, inter_alpha_us: float = 5.0, gateways=None,
+                     name: str | None = None) -> dict:
+    """NVSwitch groups of the given sizes (they may differ) joined by slow shared inter-group links.
+
+    ``gateways``: per group, the ranks that own the group's inter-group
+    links (default: every member); links between non-gateway members of
+    different groups are left out, as on nodes whose NICs hang off some GPUs.
+    """
+    ranks = sum(sizes)
+    starts = [sum(sizes[:i]) for i in range(len(sizes))]
+    group = {}
+    for g, (lo, n) in enumerate(zip(starts, sizes)):
+        for r in range(lo, lo + n):
+            group[r] = g
+    gws = [list(range(lo, lo + n)) for lo, n in zip(starts, sizes)] if gateways is None else \
+        [sorted(g) for g in gateways]
+    doc = nvswitch_topology(ranks, nvls=False, name=name or "emulated-" + "+".join(map(str, sizes)))
+    doc["nodes"] = [{"id": g, "ranks": list(range(lo, lo + n)), "gateways": gws[g]}
+                    for g, (lo, n) in enumerate(zip(starts, sizes))]
+    if gateways is not None:
+        keep = [e for e in doc["directed_links"] if group[e["src"]] == group[e["dst"]] or
+                (e["src"] in gws[group[e["src"]]] and e["dst"] in gws[group[e["dst"]]])]
+        doc["directed_links"] = keep
+        for res in doc["shared_resources"]:
+            res["links"] = [pair for pair in res["links"] if group[pair[0]] == group[pair[1]] or
+                            (pair[0] in gws[group[pair[0]]] and pair[1] in gws[group[pair[1]]])]
     nic = {}
     for edge in doc["directed_links"]:
-        gs, gd = edge["src"] // per_group, edge["dst"] // per_group
+        gs, gd = group[edge["src"]], group[edge["dst"]]
         if gs == gd:
             continue
         edge["alpha_us"] = inter_alpha_us
@@ -92,7 +118,7 @@ def multinode_topology(groups: int, per_group: int, *, intra_gbps: float = B200_
         doc["shared_resources"].append({"id": rid, "kind": "nic", "capacity_bytes_per_us": inter_gbps * 1000.0,
                                         "links": members})
     doc["groups"] = [node["ranks"] for node in doc["nodes"]]
-    doc["multicast_groups"] = [node["ranks"] for node in doc["nodes"] if per_group > 1]
+    doc["multicast_groups"] = [node["ranks"] for node in doc["nodes"] if len(node["ranks"]) > 1]
     return doc
 
 

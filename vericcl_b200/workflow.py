@@ -198,11 +198,19 @@ class PrimaryWorkflow:
                     self.ctx.emit("choice_pruned", slice_size_bytes=req.hyperparameters.slice_size_bytes,
                                   lower_bound_us=bound, best_t_pred_us=best)
                     continue
+                jobs = []
                 for method in methods:
+                    if method == "hierarchy" and not req.request_config["atom"]["manual"]["enabled"]:
+                        # the two best hierarchy plans by coarse score, then the direct plan
+                        from vericcl_b200.planner.hierarchy import enumerate_hierarchy_plans
+                        jobs.extend((method, plan) for plan in enumerate_hierarchy_plans(req, self.topology, 2))
+                    else:
+                        jobs.append((method, None))
+                for method, plan in jobs:
                     lease.check()
                     try:
                         bundle = synthesize(replace(req, selected_synthesis_method=method), self.model,
-                                            channels=channels)
+                                            channels=channels, plan=plan)
                     except (SemanticError, SolverError) as error:
                         self.ctx.emit("candidate_failed", method=method, error=str(error))
                         if isinstance(error, ScratchBudgetError):
