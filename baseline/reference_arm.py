@@ -196,6 +196,10 @@ def run(args, clock_sampler_cls, metric: str, model: str) -> int:
         return 0
     if world != args.gpus:
         raise SystemExit("--gpus %d but WORLD_SIZE=%d (launch N>1 with torchrun)" % (args.gpus, world))
+    # NCCL 2.12 bootstraps over TCP on the first non-loopback interface; on a box without a routable network
+    # that connect fails ("unhandled system error" in its socket layer), and every rank of this launch is on
+    # this host, so the loopback interface carries the bootstrap (an NCCL setting, the library is unchanged)
+    os.environ.setdefault("NCCL_SOCKET_IFNAME", "lo")
     rt = CudaRT()
     rt.call("cudaSetDevice", local)
     nccl = RefNccl()
@@ -331,6 +335,7 @@ def run(args, clock_sampler_cls, metric: str, model: str) -> int:
                            "schedule": "reference MSCCL/NCCL %s ncclAllReduce SUM per bucket + vericcl_scale_output"
                                        % vs,
                            "nccl_algo": os.environ.get("NCCL_ALGO", "library default"),
+                           "nccl_socket_ifname": os.environ.get("NCCL_SOCKET_IFNAME"),
                            "library": os.path.relpath(NCCL_SO, os.path.dirname(HERE)),
                            "l2": "inputs (16 GB) larger than the 126 MB L2; no flush needed"},
                 "busbw_per_gpu_gbs": round(busbw, 2),

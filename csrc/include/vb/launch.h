@@ -23,7 +23,10 @@ struct Control {
   int abort_request;              // host-set abort flag (mapped memory or device write)
   unsigned int ll_arrive;         // CTAs finished in the current one-shot launch
   unsigned long long ll_seq;      // one-shot launch counter (tags the flag-in-data lines)
-  unsigned long long pad[3];
+  unsigned long long fp8_seq;     // fused fp8 AllGather launch counter (its staging parity and flag values)
+  unsigned int fp8_arrive;        // CTAs finished in the current fused fp8 AllGather launch
+  unsigned int pad32;
+  unsigned long long pad[1];
 };
 
 struct InterpArgs {
@@ -103,6 +106,25 @@ struct OneShotArgs {
 long long oneshot_region_bytes(int nranks, long long max_bytes);
 cudaError_t launch_oneshot(const OneShotArgs& args, cudaStream_t stream);
 int oneshot_max_ctas();
+
+// Fused block-scaled FP8 AllGather: one launch quantizes this rank's input into its staging area
+// (e4m3 bytes + one fp32 scale per 128 elements), publishes per-CTA flags, pulls every peer's staging
+// over NVLink and dequantizes it straight into the output.  Staging and flags live in the symmetric
+// heap at the same offsets on every rank; the staging area holds two parities of fp8_stage_bytes(n).
+struct Fp8AgArgs {
+  char* base[kMaxRanks];     // heap base of every rank in this process's address space
+  const void* in;            // this rank's n input elements (any device memory)
+  void* out;                 // nranks * n output elements (any device memory)
+  long long n;               // elements per rank (multiple of 16)
+  long long stage_off;       // heap offset of the two staging parities
+  long long flag_off;        // heap offset of the per-CTA flags ([ctas] u64 per rank)
+  int rank, nranks, dtype, ctas;
+  Control* control;
+  unsigned long long timeout_ns;
+};
+long long fp8_stage_bytes(long long n);        // bytes of one staging parity for n elements
+cudaError_t launch_fp8_allgather(const Fp8AgArgs& args, cudaStream_t stream);
+int fp8_allgather_max_ctas();
 
 // Calibration probes.
 cudaError_t launch_copy_probe(void* dst, const void* src, long long bytes, int ctas, int threads, int unroll,

@@ -157,9 +157,10 @@ BoundOneShot bind_oneshot(Heap& heap, size_t in_off, size_t out_off, size_t ll_o
 class DevicePlan {
  public:
   DevicePlan(const std::string& xml, int rank, int nlanes, int niters, bool elide, bool fuse, bool multicast,
-             bool reducing, int mc_keep, int mc_period)
+             bool reducing, int mc_keep, int mc_period, bool merge)
       : rank_(rank) {
     CompileOptions o;
+    o.merge_blocks = merge;
     o.nlanes = nlanes;
     o.niters = niters;
     o.elide_sends = elide;
@@ -353,10 +354,43 @@ PYBIND11_MODULE(_vbcuda, m) {
         py::arg("ll_src_bytes"), py::arg("bytes"), py::arg("dtype"), py::arg("redop"), py::arg("coll"),
         py::arg("scale"), py::arg("do_scale"), py::arg("timeout_s"), py::arg("multicast") = false);
   m.def("oneshot_region_bytes", [](int nranks, int64_t max_bytes) { return oneshot_region_bytes(nranks, max_bytes); });
+  m.def("fp8_stage_bytes", [](int64_t n) { return fp8_stage_bytes(n); });
+  m.def("fp8_allgather_max_ctas", []() { return fp8_allgather_max_ctas(); });
+  // Fused block-scaled FP8 AllGather over the heap's peer mappings: `in` (n elements) and `out`
+  // (nranks * n) may be any device tensors; the staging parities and the per-CTA flags are heap regions
+  // reserved at the same offsets on every rank.
+  m.def("fp8_allgather", [](Heap& heap, torch::Tensor in, torch::Tensor out, size_t stage_off, size_t flag_off,
+                            int ctas, double timeout_s) {
+    SymHeap& h = heap.get();
+    TORCH_CHECK(in.is_cuda() && out.is_cuda() && in.is_contiguous() && out.is_contiguous(), "contiguous CUDA tensors");
+    TORCH_CHECK(in.scalar_type() == out.scalar_type(), "input and output dtypes differ");
+    TORCH_CHECK(out.numel() == in.numel() * h.nranks(), "output must hold nranks x input elements");
+    const int64_t n = in.numel();
+    TORCH_CHECK(n > 0 && n % 16 == 0, "fp8 AllGather needs a positive multiple of 16 elements per rank");
+    TORCH_CHECK(stage_off >= kReservedBytes && flag_off >= kReservedBytes, "region overlaps the control block");
+    TORCH_CHECK(stage_off + 2 * (size_t)fp8_stage_bytes(n) <= h.size() && flag_off + 8 * (size_t)ctas <= h.size(),
+                "fp8 staging or flags exceed the heap");
+    Fp8AgArgs a{};
+    for (int r = 0; r < h.nranks(); ++r) a.base[r] = h.base(r);
+    a.in = in.data_ptr();
+    a.out = out.data_ptr();
+    a.n = n;
+    a.stage_off = (long long)stage_off;
+    a.flag_off = (long long)flag_off;
+    a.rank = h.rank();
+    a.nranks = h.nranks();
+    a.dtype = dtype_code(in.scalar_type());
+    a.ctas = ctas;
+    a.control = heap.control();
+    a.timeout_ns = (unsigned long long)(timeout_s * 1e9);
+    cuda_check(launch_fp8_allgather(a, at::cuda::getCurrentCUDAStream().stream()), "fp8 AllGather launch");
+  }, py::arg("heap"), py::arg("inp"), py::arg("out"), py::arg("stage_off"), py::arg("flag_off"), py::arg("ctas"),
+     py::arg("timeout_s") = 10.0);
   py::class_<DevicePlan>(m, "DevicePlan")
-      .def(py::init<const std::string&, int, int, int, bool, bool, bool, bool, int, int>(), py::arg("xml"),
+      .def(py::init<const std::string&, int, int, int, bool, bool, bool, bool, int, int, bool>(), py::arg("xml"),
            py::arg("rank"), py::arg("nlanes"), py::arg("niters"), py::arg("elide"), py::arg("fuse"),
-           py::arg("multicast"), py::arg("reducing"), py::arg("mc_keep") = 1, py::arg("mc_period") = 1)
+           py::arg("multicast"), py::arg("reducing"), py::arg("mc_keep") = 1, py::arg("mc_period") = 1,
+           py::arg("merge") = true)
       .def("run", &DevicePlan::run, py::arg("heap"), py::arg("in_off"), py::arg("out_off"), py::arg("scr_off"),
            py::arg("count_per_rank"), py::arg("dtype"), py::arg("redop"), py::arg("scale"), py::arg("stream"),
            py::arg("timeout_s") = 10.0, py::arg("threads") = 512, py::arg("nbatch") = 1,

@@ -46,6 +46,9 @@ def main():
                     help="record kernel entry/exit per interpreter launch and report durations and gaps")
     ap.add_argument("--oneshot-max", type=int, default=None,
                     help="largest per-rank payload of the one-shot path (0: always the interpreter)")
+    ap.add_argument("--variants", default="",
+                    help="';'-separated engine settings to compare in one run, each a ','-separated list of "
+                         "NAME=VALUE (VERICCL_ prefix implied), e.g. 'MERGE=1;MERGE=0;MERGE=0,LANES=21'")
     args = ap.parse_args()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -115,6 +118,24 @@ def main():
         return float((got - want).abs().max() / max(1e-12, float(want.abs().max())))
 
     results = []
+    variants = [v for v in args.variants.split(";") if v.strip()] or [""]
+    for variant in variants:
+        settings = dict(kv.split("=", 1) for kv in variant.split(",") if kv.strip())
+        for k, v in settings.items():
+            os.environ["VERICCL_" + k.strip()] = v.strip()
+        if "LEAN" in settings:
+            comm.lean = settings["LEAN"] not in ("0", "")
+        run_sizes(args, variant, comm, eng, world, rank, dtype, esize, timed, check, host_us, results)
+        for k in settings:
+            os.environ.pop("VERICCL_" + k.strip(), None)
+    if rank == 0:
+        print(json.dumps({"summary": True, "points": len(results)}), flush=True)
+    comm.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_sizes(args, variant, comm, eng, world, rank, dtype, esize, timed, check, host_us, results):
     size = args.min_bytes
     while size <= args.max_bytes:
         count = size // esize
@@ -133,6 +154,26 @@ def main():
                 factor = 2.0 * (world - 1) / world if world > 1 else 1.0
                 nbytes = size
                 comm.free(buf)
+            elif coll == "allgather_fp8":
+                # the fused block-scaled fp8 AllGather; busbw counts the logical (input dtype) bytes
+                inp = comm.empty(count, dtype)
+                out = comm.empty(count * world, dtype)
+                inp.normal_()
+                err = None
+                tl, gaps = None, None
+
+                class _Fused:
+                    kind, nlanes, niters, multicast = "fp8_fused", 0, 1, False
+                plan = _Fused()
+                ours = timed(lambda: eng.all_gather_fp8(inp, out))
+                ours_host = host_us[0]
+                comm.check_status()
+                nccl = None if (args.no_nccl or world == 1) else timed(
+                    lambda: dist.all_gather_into_tensor(out, inp))
+                factor = (world - 1) / world if world > 1 else 1.0
+                nbytes = size * world
+                comm.free(inp)
+                comm.free(out)
             else:
                 inp = comm.empty(count, dtype)
                 out = comm.empty(count * world, dtype)
@@ -165,15 +206,12 @@ def main():
                 point.update({"nccl_time_us": round(nccl, 3),
                               "nccl_busbw_gbs": round(nbytes / nccl / 1e3 * factor, 2),
                               "speedup_vs_nccl": round(nccl / ours, 3)})
+            if variant:
+                point["variant"] = variant
             results.append(point)
             if rank == 0:
                 print(json.dumps(point), flush=True)
         size *= 4
-    if rank == 0:
-        print(json.dumps({"summary": True, "points": len(results)}), flush=True)
-    comm.close()
-    if world > 1:
-        dist.destroy_process_group()
 
 
 if __name__ == "__main__":

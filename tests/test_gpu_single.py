@@ -178,6 +178,27 @@ def test_engine_all_gather_fp8_single_rank(comm):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("n", [4096, 10240 + 48, 1 << 20])
+def test_fused_fp8_all_gather_matches_three_pass_path(comm, dtype, n):
+    """One rank: the fused kernel (quantize, publish, dequantize) gives the three-pass path's values."""
+    from vericcl_b200.models import CollectiveEngine
+    eng = CollectiveEngine(comm)
+    x = (torch.randn(n, device="cuda") * 2).to(dtype)
+    slow = torch.empty_like(x)
+    eng.all_gather_fp8(x, slow, fused=False)
+    for _ in range(3):                                  # both staging parities, then the first again
+        out = torch.full_like(x, float("nan"))
+        eng.all_gather_fp8(x, out, fused=True)
+        torch.cuda.synchronize()
+        comm.check_status()
+        assert not torch.isnan(out.float()).any()
+        xf = torch.nn.functional.pad(x.float(), (0, (-n) % 128)).view(-1, 128)
+        amax = xf.abs().amax(dim=1).repeat_interleave(128)[:n]
+        assert ((out.float() - x.float()).abs() / amax.clamp_min(1e-6)).max().item() < 0.07
+        assert (out.float() - slow.float()).abs().max().item() <= 1e-2 * float(amax.max()) / 448
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 def test_oneshot_kernel_single_rank(comm, dtype):
     """The one-shot kernel on one rank: AllReduce is the scaled copy, AllGather the copy; the tag counter advances."""
     n = 4096

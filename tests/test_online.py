@@ -153,3 +153,24 @@ def test_step_counters_accumulate_over_launches():
     assert a["max_service_ns"] == 70 and a["first_ns"] == 100 and a["last_ns"] == 1040
     assert a["mean_service_ns"] == pytest.approx(160 / 3) and a["mean_wait_ns"] == pytest.approx(40 / 3)
     assert c[(1, 0, 0)]["samples"] == 1
+
+
+def test_bracket_fit_recovers_offset_and_drift_and_drops_a_contradicting_sample():
+    import random
+    from vericcl_b200.online.clock_sync import fit_transform
+    rng = random.Random(3)
+    offset, drift = 12_345.0, 3e-6
+    samples = []
+    for i in range(24):
+        g = 1_000_000.0 + i * 50_000.0
+        true = offset + g * (1 + drift)
+        samples.append((true - rng.uniform(50, 400), g, true + rng.uniform(50, 400)))
+    m = fit_transform(samples)
+    assert m.method == "bracket-lp" and m.samples_used == 24
+    for lo, g, hi in samples:
+        assert lo - 1e-6 <= m.to_host(g) <= hi + 1e-6          # inside every bracket
+    assert abs(m.to_host(2_000_000.0) - (offset + 2_000_000.0 * (1 + drift))) <= m.uncertainty_ns + 400
+    # a sample whose GPU read came 5 µs late contradicts the rest and is dropped
+    bad = samples + [(offset + 1_500_000.0, 1_500_000.0 + 5_000.0, offset + 1_500_000.0 + 2_000.0)]
+    m2 = fit_transform(bad)
+    assert m2.method == "bracket-lp" and m2.samples_used == 24

@@ -80,7 +80,8 @@ class CollectiveEngine:
             return False
         if collective == "allreduce":
             return op in ("sum", "avg")
-        return collective == "allgather" and nbytes < self.ag_nvls_max_bytes
+        limit = int(os.environ.get("VERICCL_AG_NVLS_MAX", self.ag_nvls_max_bytes))
+        return collective == "allgather" and nbytes < limit
 
     def use_oneshot(self, collective: str, count: int, dtype) -> bool:
         """Small AllReduce / AllGather payloads go through the one-shot kernel (one NVLink trip, no barrier)."""
@@ -110,7 +111,8 @@ class CollectiveEngine:
         dname = str(dtype).split(".")[-1]
         xml = schedule_xml(collective, world, slices, inplace=inplace, datatype=dname, method=self.method,
                            root=root if collective in ("broadcast", "reduce") else 0)
-        probe = self.comm.compile(xml, nlanes=1, niters=1)
+        merge = self.merge_blocks(collective, count * torch.tensor([], dtype=dtype).element_size())
+        probe = self.comm.compile(xml, nlanes=1, niters=1, merge=merge)
         esize = torch.tensor([], dtype=dtype).element_size()
         runtime = count * (world if collective == "allgather" else 1)
         nchunks = slices * (world if collective == "allgather" else 1)
@@ -118,7 +120,17 @@ class CollectiveEngine:
         lanes, iters = self.geometry(probe.device_plan.nblocks, chunk_bytes)
         share = tuple(int(v) for v in os.environ.get("VERICCL_MC_SHARE", "1/1").split("/"))
         return self.comm.compile(xml, nlanes=lanes, niters=iters,
-                                 multicast=self.use_multicast(collective, op, count * esize), mc_share=share)
+                                 multicast=self.use_multicast(collective, op, count * esize), mc_share=share,
+                                 merge=merge)
+
+    def merge_blocks(self, collective: str, nbytes: int) -> bool:
+        """Run a rank's steps as one CTA group in one order (default) or each XML block on its own CTAs.
+
+        ``VERICCL_MERGE=0`` keeps the XML blocks apart: an AllGather then pulls
+        from every peer at once, each peer's chunk on its own share of the CTAs.
+        """
+        env = os.environ.get("VERICCL_MERGE")
+        return True if env is None else env not in ("0", "")
 
     def _copy_in(self, flat: torch.Tensor, tensor: torch.Tensor) -> None:
         """``flat`` (contiguous) ← ``tensor`` in row-major order; pitched 2D views go through the native copy."""
@@ -181,19 +193,35 @@ class CollectiveEngine:
         self._unstage(out, dst)
         return out
 
-    def all_gather_fp8(self, inp: torch.Tensor, out: torch.Tensor, *, block: int = 128) -> torch.Tensor:
+    def all_gather_fp8(self, inp: torch.Tensor, out: torch.Tensor, *, block: int = 128,
+                       fused: bool | None = None) -> torch.Tensor:
         """AllGather with block-scaled FP8 (e4m3) payloads.
 
-        Each rank quantizes its input (one fp32 scale per ``block`` elements),
-        gathers the packed [fp8 bytes | scales] payloads with the synthesized
-        AllGather schedule, and dequantizes every rank's part into ``out``.
-        Moves about a quarter (fp32) or half (bf16) of the bytes of a plain
-        AllGather; values carry e4m3 precision.
+        Each rank's input is quantized with one fp32 scale per ``block``
+        elements; only the e4m3 bytes and the scales cross NVLink (about a
+        quarter of an fp32, half of a bf16 AllGather's bytes) and every rank's
+        part of ``out`` is dequantized; values carry e4m3 precision and every
+        rank, the owner included, sees the same values.
+
+        With 128-element blocks and a multiple of 16 elements per rank one
+        fused kernel does it all (quantize into the heap, per-CTA ready flags,
+        pull and dequantize straight into ``out``: ``fp8_allgather`` in
+        csrc/cuda/fp8.cu).  Otherwise (or with ``fused=False``) three passes
+        run: a quantize kernel, the synthesized AllGather of the packed
+        payload bytes, a dequantize kernel per rank.
         """
         world = self.comm.world
         n = inp.numel()
         if out.numel() != n * world:
             raise RuntimeFailure("all_gather_fp8 output must hold world × input elements")
+        can_fuse = block == 128 and n % 16 == 0 and inp.dtype in (torch.float32, torch.bfloat16, torch.float16) \
+            and out.dtype == inp.dtype
+        if fused is None:
+            fused = can_fuse
+        if fused:
+            if not can_fuse:
+                raise RuntimeFailure("the fused fp8 AllGather needs 128-element blocks and 16-element multiples")
+            return self._fp8_fused(inp, out)
         nblocks = -(-n // block)
         packed = -(-(n + 4 * nblocks) // 16) * 16        # bytes per rank, 16-byte aligned
         key = ("fp8", n, block)
@@ -214,6 +242,30 @@ class CollectiveEngine:
         for r in range(world):
             part = gathered[r]
             self.comm._mod.dequantize_fp8(part[:n], part[n:n + 4 * nblocks].view(torch.float32), flat_out[r], block)
+        return out
+
+    def _fp8_fused(self, inp: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        mod, n = self.comm._mod, inp.numel()
+        key = ("fp8-fused", n)
+        regions = self._staging.get(key)
+        if regions is None:
+            blocks = -(-n // 128)
+            ctas = max(1, min(mod.fp8_allgather_max_ctas(), 2 * 148, -(-blocks // 16)))
+            # heap tensors are float-typed; the regions are raw bytes
+            stage = self.comm.empty(mod.fp8_stage_bytes(n), torch.float16)          # 2 parities = 2 x bytes / 2
+            flags = self.comm.empty(4 * ctas, torch.float16)                         # ctas x 8 bytes
+            flags.zero_()
+            torch.cuda.synchronize()
+            self.comm.barrier()            # every rank's flags are zero before any launch reads them
+            regions = (stage, flags, ctas)
+            self._staging[key] = regions
+        stage, flags, ctas = regions
+        src = inp.contiguous().view(-1)
+        dst = out if out.is_contiguous() else torch.empty_like(out)
+        mod.fp8_allgather(self.comm.heap, src, dst.view(-1), self.comm.offset_of(stage), self.comm.offset_of(flags),
+                          ctas, self.comm.timeout_s)
+        if dst is not out:
+            out.copy_(dst)
         return out
 
     def reduce_scatter(self, inp: torch.Tensor, out: torch.Tensor, *, op: str = "sum",

@@ -58,15 +58,34 @@ def _components(ranks: int, joined) -> tuple:
     return tuple(sorted(tuple(sorted(c)) for c in comps.values()))
 
 
+def _strongly_connected(topology, group) -> bool:
+    """Every member reaches every other over links inside the group (a stage stays inside its group)."""
+    members = set(group)
+    for start in (group[0],):
+        for reverse in (False, True):
+            seen, todo = {start}, [start]
+            while todo:
+                v = todo.pop()
+                nbrs = topology.in_neighbors(v) if reverse else topology.out_neighbors(v)
+                for w in nbrs:
+                    if w in members and w not in seen:
+                        seen.add(w)
+                        todo.append(w)
+            if seen != members:
+                return False
+    return True
+
+
 def partition_candidates(topology) -> list:
-    """Distinct partitions into at least two groups, most structured first (sizes may differ)."""
+    """Distinct partitions into at least two strongly connected groups, most structured first (sizes may differ)."""
     out = []
 
     def add(part):
         part = tuple(tuple(sorted(g)) for g in part)
         part = tuple(sorted(part))
         if 1 < len(part) < topology.rank_count + 1 and part not in out and \
-                sorted(r for g in part for r in g) == list(range(topology.rank_count)):
+                sorted(r for g in part for r in g) == list(range(topology.rank_count)) and \
+                all(_strongly_connected(topology, g) for g in part):
             out.append(part)
 
     if len(topology.nodes) > 1:
@@ -288,6 +307,8 @@ class CandidateStream:
             for mode, rails_of in (("rails", discover_rails), ("gateways", gateway_rails)):
                 rails = rails_of(topology, groups, range(p))
                 score = coarse_score(request, topology, groups, rails)
+                if score == float("inf"):
+                    continue          # some stage would need a link the topology does not have
                 heapq.heappush(self._heap, _Coarse(score, seq, groups, mode, rails))
                 seq += 1
 

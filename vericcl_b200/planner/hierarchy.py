@@ -16,8 +16,14 @@ from vericcl_b200.planner.group_search import CandidateStream, partition_candida
 
 
 def plan_hierarchy(request, topology):
-    """The hierarchy plan with the best coarse score, else the direct plan."""
+    """The hierarchy plan with the best coarse score whose stages all have route trees, else the direct plan."""
+    from vericcl_b200.errors import SemanticError
+    from vericcl_b200.solver.demands import build_demands
     for plan in CandidateStream(request, topology):
+        try:
+            build_demands(plan, topology)
+        except SemanticError:
+            continue
         return plan
     return build_direct_plan(request, topology, reason="single_group")
 

@@ -146,7 +146,7 @@ def _binomial(root, members, reverse):
 
 
 def candidate_trees(topology: Topology, node: PlanNode, kind: str, root: int, members, sids, *,
-                    limit: int = 4):
+                    limit: int = 4, slice_bytes: int | None = None):
     allowed = set(node.group) | set(node.relay_ranks)
     reverse = kind == "reduce"
     out = []
@@ -172,13 +172,28 @@ def candidate_trees(topology: Topology, node: PlanNode, kind: str, root: int, me
         edges = list(zip(seq, seq[1:]))
         if all(_usable(topology, node, a, b, 0, sids) for a, b in edges):
             out.append(Tree("chain", tuple(edges), len(edges)))
+    if len(members) > 1 and slice_bytes and not _uniform(topology):
+        # the fine MILP's tree over every usable link (it can find relays the menu above does not hold)
+        from vericcl_b200.solver.flow_milp import solve_tree_milp
+        found = solve_tree_milp(topology, root, members, allowed, reverse=reverse, slice_bytes=slice_bytes,
+                                usable=lambda a, b: _usable(topology, node, a, b, 0, sids))
+        if found is not None and tuple(found[0]) not in {t.edges for t in out}:
+            out.insert(min(len(out), limit - 1), Tree("milp", tuple(found[0]), found[1]))
     if not out:
         raise SemanticError("no legal route tree for node %s (root %d)" % (node.node_id, root))
     return tuple(out[:limit])
 
 
-def build_demands(plan: PlanDAG, topology: Topology):
-    """Return the transfer demands of every plan node, in plan order."""
+def _uniform(topology: Topology) -> bool:
+    """Every rank linked to every other with the same α and β (one switch): the star is already optimal."""
+    if not topology.is_complete():
+        return False
+    costs = {(l.alpha_us, l.beta_us_per_byte) for l in topology.links.values()}
+    return len(costs) <= 1
+
+
+def build_demands(plan: PlanDAG, topology: Topology, slice_bytes: int | None = None):
+    """Return the transfer demands of every plan node, in plan order (``slice_bytes`` enables the fine MILP)."""
     n = plan.slice_count
     demands = []
     for node in plan.nodes:
@@ -190,7 +205,8 @@ def build_demands(plan: PlanDAG, topology: Topology):
             members = tuple(sorted({s.rank for s in inputs} - {slot.rank}))
             contributors = {s.rank: c for s, c in inputs.items()}
             sids = sorted(target)
-            trees = candidate_trees(topology, node, "reduce", slot.rank, members, sids) if members else ()
+            trees = candidate_trees(topology, node, "reduce", slot.rank, members, sids,
+                                    slice_bytes=slice_bytes) if members else ()
             demands.append(TransferDemand("d-" + node.node_id, node.node_id, node.stage_id, "reduce", slot.rank,
                                           members, min(target) % n, contributors, frozenset(target),
                                           candidates=trees))
@@ -201,7 +217,8 @@ def build_demands(plan: PlanDAG, topology: Topology):
             (src_slot, value), = node.logical_input.values.items()
             dests = tuple(sorted({s.rank for s in node.logical_output.values} - {src_slot.rank}))
             sids = sorted(value)
-            trees = candidate_trees(topology, node, "broadcast", src_slot.rank, dests, sids) if dests else ()
+            trees = candidate_trees(topology, node, "broadcast", src_slot.rank, dests, sids,
+                                    slice_bytes=slice_bytes) if dests else ()
             demands.append(TransferDemand("d-" + node.node_id, node.node_id, node.stage_id, "broadcast",
                                           src_slot.rank, dests, min(value) % n, {src_slot.rank: value},
                                           frozenset(value), local=not dests, candidates=trees))

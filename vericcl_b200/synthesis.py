@@ -87,7 +87,7 @@ def synthesize(request, model=None, *, channels: int = 1, timing: bool = True, p
         network = construct_network(request, topology, model or initial_cost_model(request), channels=channels)
         return lower_candidate(request, topology, network, model, origin="constructive_trees")
     plan = plan if plan is not None else plan_for(request, topology)
-    demands = build_demands(plan, topology)
+    demands = build_demands(plan, topology, slice_bytes)
     trees = choose_trees(demands, topology, slice_bytes, time_limit=request.solver.per_model_timeout_s)
     network = compose_routes(plan, demands, trees, topology, slice_bytes, channels=channels, origin=plan.mode.value)
     from vericcl_b200.solver.timing import keep_better, optimize_fixed_routes
@@ -97,7 +97,14 @@ def synthesize(request, model=None, *, channels: int = 1, timing: bool = True, p
     timed_network = optimize_fixed_routes(network, topology, time_limit=min(6.0, request.solver.per_model_timeout_s))
     if timed_network is network:
         return seed
-    timed = lower_candidate(request, topology, timed_network, model, plan=plan, origin=plan.mode.value + "+timing")
+    try:
+        timed = lower_candidate(request, topology, timed_network, model, plan=plan,
+                                origin=plan.mode.value + "+timing")
+    except SemanticError as error:
+        # the re-timed order can need more scratch than the budget holds: the seed stands
+        seed.timing = {"seed_t_pred_us": seed.t_pred_us, "timed_t_pred_us": None, "kept": "seed",
+                       "network_origin": timed_network.origin, "timed_failed": str(error)[:200]}
+        return seed
     best = keep_better(seed, timed)
     best.timing = {"seed_t_pred_us": seed.t_pred_us, "timed_t_pred_us": timed.t_pred_us,
                    "kept": "timed" if best is timed else "seed", "network_origin": timed_network.origin}
