@@ -115,7 +115,8 @@ class CudaRT:
 
 
 class UniqueId(ctypes.Structure):
-    _fields_ = [("internal", ctypes.c_char * 128)]
+    # raw bytes: a c_char array would read back only up to its first zero byte
+    _fields_ = [("internal", ctypes.c_ubyte * 128)]
 
 
 class RefNccl:
@@ -143,8 +144,9 @@ class RefNccl:
 
     def init_rank(self, nranks, uid: bytes, rank):
         comm = ctypes.c_void_p()
-        u = UniqueId()
-        ctypes.memmove(ctypes.byref(u), uid, 128)
+        if len(uid) != 128:
+            raise ValueError("an ncclUniqueId has 128 bytes, got %d" % len(uid))
+        u = UniqueId.from_buffer_copy(uid)
         self.check(self.lib.ncclCommInitRank(ctypes.byref(comm), nranks, u, rank), "ncclCommInitRank")
         return comm.value
 
@@ -196,9 +198,8 @@ def run(args, clock_sampler_cls, metric: str, model: str) -> int:
         return 0
     if world != args.gpus:
         raise SystemExit("--gpus %d but WORLD_SIZE=%d (launch N>1 with torchrun)" % (args.gpus, world))
-    # NCCL 2.12 bootstraps over TCP on the first non-loopback interface; on a box without a routable network
-    # that connect fails ("unhandled system error" in its socket layer), and every rank of this launch is on
-    # this host, so the loopback interface carries the bootstrap (an NCCL setting, the library is unchanged)
+    # every rank of this launch is on this host: NCCL's TCP bootstrap goes over the loopback interface
+    # (an NCCL setting; the library is unchanged)
     os.environ.setdefault("NCCL_SOCKET_IFNAME", "lo")
     rt = CudaRT()
     rt.call("cudaSetDevice", local)
@@ -311,7 +312,7 @@ def run(args, clock_sampler_cls, metric: str, model: str) -> int:
         rt.call("cudaEventSynchronize", ctypes.c_void_p(e1))
         ems = all_max(rt.elapsed_ms(e0, e1) / args.e2e_steps)
         bus = total * esize * (2.0 * (world - 1) / world if world > 1 else 1.0)
-        e2e = {"value": round(bus / (ems * 1e-3) / 1e9 * world, 2), "unit": "GB/s",
+        e2e = {"value": round(bus / (ems * 1e-3) / 1e9 * world, 2), "unit": "GB/s (sum over GPUs of per-GPU bus bandwidth)",
                "ms_per_step": round(ems, 3), "h2d_bytes_per_step": int(nbytes), "d2h_bytes_per_step": 65536,
                "api": "ncclAllReduce + vericcl_scale_output per bucket after a pinned host->device copy"}
         rt.call("cudaFreeHost", ctypes.c_void_p(host))

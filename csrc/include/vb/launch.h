@@ -25,8 +25,8 @@ struct Control {
   unsigned long long ll_seq;      // one-shot launch counter (tags the flag-in-data lines)
   unsigned long long fp8_seq;     // fused fp8 AllGather launch counter (its staging parity and flag values)
   unsigned int fp8_arrive;        // CTAs finished in the current fused fp8 AllGather launch
-  unsigned int pad32;
-  unsigned long long pad[1];
+  unsigned int push_arrive;       // CTAs finished in the current push AllGather launch
+  unsigned long long push_seq;    // push AllGather launch counter (its start and done flag values)
 };
 
 struct InterpArgs {
@@ -125,6 +125,22 @@ struct Fp8AgArgs {
 long long fp8_stage_bytes(long long n);        // bytes of one staging parity for n elements
 cudaError_t launch_fp8_allgather(const Fp8AgArgs& args, cudaStream_t stream);
 int fp8_allgather_max_ctas();
+
+// Push AllGather: every rank stores its chunk straight into every peer's output (NVLink writes, no read
+// requests travelling against the data), after the peer has entered the same launch; per-CTA done flags tell
+// each receiver when the matching range of every part has landed.
+struct PushAgArgs {
+  char* base[kMaxRanks];     // heap base of every rank in this process's address space
+  const void* in;            // this rank's chunk (local device memory)
+  long long out_off;         // heap offset of the output (nranks * bytes), identical on every rank
+  long long bytes;           // bytes per rank (multiple of 16)
+  long long flag_off;        // heap offset of the flags: [0] start flag, [1 + c] done flag of CTA c
+  int rank, nranks, ctas;
+  Control* control;
+  unsigned long long timeout_ns;
+};
+cudaError_t launch_push_allgather(const PushAgArgs& args, cudaStream_t stream);
+int push_allgather_max_ctas();
 
 // Calibration probes.
 cudaError_t launch_copy_probe(void* dst, const void* src, long long bytes, int ctas, int threads, int unroll,

@@ -101,13 +101,16 @@ def main():
         g = torch.Generator().manual_seed(1234 + r)
         return torch.randn(count, generator=g, dtype=torch.float64)
 
-    def check(coll, plan, count, inp, out):
+    def check(coll, plan, count, inp, out, run=None):
         """One run on seeded N(0,1) inputs against an fp64 host reference; returns the max relative error."""
         mine = seeded(rank, count)
         inp.copy_(mine.to(dtype))
         torch.cuda.synchronize()
         comm.barrier()
-        comm.run(plan, inp, out)
+        if run is None:
+            comm.run(plan, inp, out)
+        else:
+            run()
         torch.cuda.synchronize()
         comm.check_status()
         if coll == "allreduce":
@@ -178,10 +181,18 @@ def run_sizes(args, variant, comm, eng, world, rank, dtype, esize, timed, check,
                 inp = comm.empty(count, dtype)
                 out = comm.empty(count * world, dtype)
                 plan = eng.plan("allgather", count, dtype, inplace=False)
-                err = check(coll, plan, count, inp, out) if size <= args.check_max_bytes else None
+                push = eng.use_push(size)
+                if push:
+                    class _Push:
+                        kind, nlanes, niters, multicast = "push", 0, 1, False
+                    plan = _Push()
+                    run = lambda: eng.all_gather(inp, out)          # noqa: E731
+                else:
+                    run = None
+                err = check(coll, plan, count, inp, out, run) if size <= args.check_max_bytes else None
                 inp.normal_()
                 tl = comm.timeline_buffer() if args.timeline and plan.kind == "interp" else None
-                ours = timed(lambda: comm.run(plan, inp, out, timeline=tl))
+                ours = timed(run if push else (lambda: comm.run(plan, inp, out, timeline=tl)))
                 ours_host = host_us[0]
                 gaps = comm.launch_gaps(tl, args.iters) if tl is not None else None
                 comm.check_status()

@@ -228,6 +228,26 @@ def main():
             print(json.dumps({"rank": rank, "coll": coll, "root": root, "path": "engine", "max_err": err, "ok": ok}),
                   flush=True)
     cases += extra
+    # push AllGather (every rank stores into every peer's heap output), three calls in a row per size
+    push_eng = CollectiveEngine(comm)
+    push_eng.ag_push_min_bytes = 0
+    for dt, n in ((torch.float32, 1 << 16), (torch.bfloat16, (1 << 16) + 8), (torch.float16, 24)):
+        x = inputs_for(rank, n, dt, 777).cuda()
+        ref = torch.cat([inputs_for(r, n, dt, 777) for r in range(world)]).cuda()
+        out = comm.empty(n * world, dt)
+        for call in range(3):
+            out.fill_(float("nan"))
+            torch.cuda.synchronize()
+            comm.barrier()
+            push_eng.all_gather(x, out)
+            torch.cuda.synchronize()
+            comm.check_status()
+            ok = bool(torch.equal(out, ref))
+            failures += 0 if ok else 1
+            if rank == 0 or not ok:
+                print(json.dumps({"rank": rank, "coll": "allgather", "path": "push", "dtype": str(dt), "n": n,
+                                  "call": call, "ok": ok}), flush=True)
+        comm.free(out)
     # block-scaled FP8 AllGather through the engine: the fused kernel (three calls in a row, so both staging
     # parities are reused) against the three-pass path and against the fp64 inputs
     for dt, n in ((torch.float32, 1 << 14), (torch.bfloat16, (1 << 14) + 48), (torch.float16, 4096)):

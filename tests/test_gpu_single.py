@@ -304,3 +304,22 @@ def test_copy_probe_matches_source(comm):
     comm._mod.copy_probe(dst.data_ptr(), src.data_ptr(), n * 4, 32, 256, 4)
     torch.cuda.synchronize()
     assert torch.equal(dst, src)
+
+
+def test_push_allgather_kernel_single_rank(comm):
+    """One rank: the push kernel copies the chunk into part 0 of the heap output; its counter advances."""
+    mod = comm._mod
+    ctas = max(1, min(mod.push_allgather_max_ctas(), 148))
+    flags = comm.empty(4 * (ctas + 1), torch.float16)
+    flags.zero_()
+    x = torch.randn(4096 * 3 + 4, device="cuda")
+    out = comm.empty(x.numel())
+    before = comm.heap.status()
+    for _ in range(2):
+        out.zero_()
+        mod.push_allgather(comm.heap, x.data_ptr(), comm.offset_of(out), x.numel() * 4, comm.offset_of(flags), ctas)
+        torch.cuda.synchronize()
+        comm.check_status()
+        assert torch.equal(out, x)
+    comm.free(out)
+    comm.free(flags)

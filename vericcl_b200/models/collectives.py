@@ -48,6 +48,7 @@ class CollectiveEngine:
             twoshot_max_bytes = int(os.environ.get("VERICCL_TWOSHOT_MAX", 0))
         self.twoshot_max_bytes = twoshot_max_bytes
         self.ag_nvls_max_bytes = AG_NVLS_MAX_BYTES if ag_nvls_max_bytes is None else ag_nvls_max_bytes
+        self.ag_push_min_bytes = None      # push AllGather threshold (None: off); VERICCL_AG_PUSH_MIN overrides
         if tuning is not None:
             # thresholds measured on this machine (vericcl_b200.models.tuner); explicit arguments still win
             for name, given in explicit.items():
@@ -178,10 +179,38 @@ class CollectiveEngine:
         self._copy_out(tensor, buf[:n])
         return tensor
 
+    def use_push(self, nbytes: int) -> bool:
+        """AllGathers of at least ``VERICCL_AG_PUSH_MIN`` bytes per rank run the push kernel (off unless set)."""
+        env = os.environ.get("VERICCL_AG_PUSH_MIN")
+        limit = self.ag_push_min_bytes if env is None else int(env)
+        return self.comm.world > 1 and limit is not None and nbytes >= limit and nbytes % 16 == 0
+
+    def _push_all_gather(self, inp: torch.Tensor, out: torch.Tensor) -> None:
+        """Every rank stores its chunk into every peer's heap output (csrc/cuda/push.cu)."""
+        mod = self.comm._mod
+        flags = self._staging.get("push-flags")
+        if flags is None:
+            ctas = max(1, min(mod.push_allgather_max_ctas(), 148))
+            flags = (self.comm.empty(4 * (ctas + 1), torch.float16), ctas)
+            flags[0].zero_()
+            torch.cuda.synchronize()
+            self.comm.barrier()
+            self._staging["push-flags"] = flags
+        region, ctas = flags
+        mod.push_allgather(self.comm.heap, inp.data_ptr(), self.comm.offset_of(out), inp.numel() * inp.element_size(),
+                           self.comm.offset_of(region), ctas, self.comm.timeout_s)
+
     def all_gather(self, inp: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         world = self.comm.world
         if out.numel() != inp.numel() * world:
             raise RuntimeFailure("all_gather output must hold world × input elements")
+        nbytes = inp.numel() * inp.element_size()
+        if self.use_push(nbytes) and inp.is_contiguous() and out.is_contiguous():
+            dst = out.view(-1) if self.comm.in_heap(out.view(-1)) else self._heap_copy(out, "ag-push-out")
+            self._push_all_gather(inp.view(-1), dst)
+            if dst.data_ptr() != out.data_ptr():
+                self._copy_out(out, dst)
+            return out
         if inp.is_contiguous() and out.is_contiguous() and self.comm.in_heap(inp) and self.comm.in_heap(out):
             plan = self.plan("allgather", inp.numel(), inp.dtype, inplace=False)
             self.comm.run(plan, inp.view(-1), out.view(-1))

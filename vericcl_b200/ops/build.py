@@ -94,7 +94,7 @@ def torch_flags():
     return inc, libs
 
 
-CUDA_SOURCES = ["cuda/interp.cu", "cuda/oneshot.cu", "cuda/helpers.cu", "cuda/probes.cu",
+CUDA_SOURCES = ["cuda/interp.cu", "cuda/oneshot.cu", "cuda/helpers.cu", "cuda/probes.cu", "cuda/push.cu",
                 "cuda/fp8.cu", "runtime/symheap.cc", "runtime/cuda_ext.cc"]
 
 
