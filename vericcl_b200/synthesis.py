@@ -92,6 +92,16 @@ def synthesize(request, model=None, *, channels: int = 1, timing: bool = True, p
     network = compose_routes(plan, demands, trees, topology, slice_bytes, channels=channels, origin=plan.mode.value)
     from vericcl_b200.solver.timing import keep_better, optimize_fixed_routes
     seed = lower_candidate(request, topology, network, model, plan=plan, origin=plan.mode.value)
+    if channels > 1:
+        # channels chosen for the whole schedule at once instead of round-robin per link
+        from vericcl_b200.solver.global_scheduler import assign_channels
+        global_net = assign_channels(network, topology, channels)
+        try:
+            alt = lower_candidate(request, topology, global_net, model, plan=plan, origin=global_net.origin)
+        except SemanticError:
+            alt = None
+        if alt is not None and keep_better(seed, alt) is alt:
+            seed, network = alt, global_net
     if not timing:
         return seed
     timed_network = optimize_fixed_routes(network, topology, time_limit=min(6.0, request.solver.per_model_timeout_s))
@@ -99,7 +109,7 @@ def synthesize(request, model=None, *, channels: int = 1, timing: bool = True, p
         return seed
     try:
         timed = lower_candidate(request, topology, timed_network, model, plan=plan,
-                                origin=plan.mode.value + "+timing")
+                                origin=seed.origin + "+timing")
     except SemanticError as error:
         # the re-timed order can need more scratch than the budget holds: the seed stands
         seed.timing = {"seed_t_pred_us": seed.t_pred_us, "timed_t_pred_us": None, "kept": "seed",
