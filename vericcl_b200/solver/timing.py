@@ -137,7 +137,7 @@ def optimize_fixed_routes(candidate, topology, *, window: int = WINDOW, time_lim
     hold = _holds(ops, topology, candidate.slice_size_bytes)
     order = _topological(ops)
     chunks = [order[i:i + window] for i in range(0, len(order), window)]
-    per_window = max(0.2, time_limit / len(chunks))
+    per_window = max(0.1, time_limit / len(chunks))
     start, end, conn_free, res_free = {}, {}, {}, {}
     solved = 0
     for chunk in chunks:

@@ -104,7 +104,7 @@ def synthesize(request, model=None, *, channels: int = 1, timing: bool = True, p
             seed, network = alt, global_net
     if not timing:
         return seed
-    timed_network = optimize_fixed_routes(network, topology, time_limit=min(6.0, request.solver.per_model_timeout_s))
+    timed_network = optimize_fixed_routes(network, topology, time_limit=min(3.0, request.solver.per_model_timeout_s))
     if timed_network is network:
         return seed
     try:
