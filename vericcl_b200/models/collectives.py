@@ -19,6 +19,9 @@ from vericcl_b200.errors import RuntimeFailure
 from vericcl_b200.synthesis import schedule_xml
 
 ONESHOT_MAX_BYTES = 1 << 20          # per-rank payloads up to this size take the one-shot flag-in-data path
+# world sizes whose one-shot / two-shot runs have passed the multi-GPU fp64 checks on B200s; other sizes take the
+# interpreter unless VERICCL_ONESHOT_ANY_WORLD=1 (or an explicit threshold) says otherwise
+ONESHOT_VERIFIED_WORLDS = frozenset({2, 4})
 AG_NVLS_MAX_BYTES = 8 << 20          # larger AllGathers pull from peers (measured faster than multicast stores)
 PIECE_MIN_BYTES = 8 * 1024          # smallest useful piece per CTA per iteration
 PIECE_TARGET_BYTES = 512 * 1024     # pipeline a lane's work in pieces of about this size
@@ -41,6 +44,9 @@ class CollectiveEngine:
         self.slices_per_rank = slices_per_rank
         explicit = {"oneshot_max_bytes": oneshot_max_bytes, "twoshot_max_bytes": twoshot_max_bytes,
                     "ag_nvls_max_bytes": ag_nvls_max_bytes}
+        # an explicit threshold (argument or environment) is the caller's choice at any world size
+        self._explicit_oneshot = (oneshot_max_bytes is not None or twoshot_max_bytes is not None or
+                                  "VERICCL_ONESHOT_MAX" in os.environ or "VERICCL_TWOSHOT_MAX" in os.environ)
         if oneshot_max_bytes is None:
             oneshot_max_bytes = int(os.environ.get("VERICCL_ONESHOT_MAX", ONESHOT_MAX_BYTES))
         self.oneshot_max_bytes = oneshot_max_bytes
@@ -54,6 +60,7 @@ class CollectiveEngine:
             for name, given in explicit.items():
                 if given is None and name in tuning:
                     setattr(self, name, int(tuning[name]))
+            self._explicit_oneshot |= "oneshot_max_bytes" in tuning or "twoshot_max_bytes" in tuning
         self._max_ctas = comm._mod.max_ctas(512)
         self.max_lanes = max_lanes or self._max_ctas
         self._staging: dict = {}
@@ -84,18 +91,22 @@ class CollectiveEngine:
         limit = int(os.environ.get("VERICCL_AG_NVLS_MAX", self.ag_nvls_max_bytes))
         return collective == "allgather" and nbytes < limit
 
+    def _oneshot_world_ok(self) -> bool:
+        return (self.comm.world in ONESHOT_VERIFIED_WORLDS or self._explicit_oneshot
+                or os.environ.get("VERICCL_ONESHOT_ANY_WORLD") == "1")
+
     def use_oneshot(self, collective: str, count: int, dtype) -> bool:
         """Small AllReduce / AllGather payloads go through the one-shot kernel (one NVLink trip, no barrier)."""
         nbytes = count * torch.tensor([], dtype=dtype).element_size()
         return (collective in ("allreduce", "allgather") and self.comm.world > 1 and 0 < nbytes
-                <= self.oneshot_max_bytes and nbytes % 8 == 0)
+                <= self.oneshot_max_bytes and nbytes % 8 == 0 and self._oneshot_world_ok())
 
     def use_twoshot(self, collective: str, count: int, dtype) -> bool:
         """Mid-size AllReduce (above the one-shot range, up to ``twoshot_max_bytes``; off unless set)."""
         nbytes = count * torch.tensor([], dtype=dtype).element_size()
         world = self.comm.world
         return (collective == "allreduce" and world > 1 and self.oneshot_max_bytes < nbytes <= self.twoshot_max_bytes
-                and nbytes % (8 * world) == 0)
+                and nbytes % (8 * world) == 0 and self._oneshot_world_ok())
 
     def plan(self, collective: str, count: int, dtype, *, inplace: bool, op: str = "sum", root: int = 0):
         world = self.comm.world
