@@ -84,3 +84,33 @@ def test_measured_trace_tails_become_causes():
     analysis = analyze(bundle, model, trace=report)
     assert analysis.causes[0].kind == "trace_tail"
     assert any(causes[0].operation_id in s.operations for s in analysis.strategies)
+
+
+def test_joint_repair_keeps_only_merges_the_exact_replay_confirms():
+    """Column gains do not add: the greedy pass re-predicts every merge and drops the ones that do not help."""
+    from dataclasses import replace
+    from types import SimpleNamespace
+    from vericcl_b200.composer.compose import NetworkCandidate, NetworkOperation
+    from vericcl_b200.tuning.event_columns import solve_event_columns
+    ops = tuple(NetworkOperation("op%d" % i, "send", 0, 1, 0, 0, frozenset({i}), frozenset({i}), frozenset(),
+                                 float(i), i) for i in range(4))
+    base = NetworkCandidate(2, 4, 1024, ops, "base")
+    gain = {"op0": 3.0, "op1": 2.0, "op2": 1.5, "op3": 1.0}
+    hurts = {("op0", "op2")}                  # these two changes collide when merged
+
+    def lower(candidate):
+        changed = sorted(op.operation_id for op in candidate.operations if op.channel == 1)
+        t = 20.0 - sum(gain[k] for k in changed)
+        if any(a in changed and b in changed for a, b in hurts):
+            t += 10.0
+        return SimpleNamespace(network=candidate, t_pred_us=t, can_execute=True)
+
+    incumbent = SimpleNamespace(network=base, t_pred_us=20.0)
+    improving = []
+    for op in ops:
+        variant = replace(base, operations=tuple(replace(o, channel=1) if o is op else o for o in ops))
+        improving.append(("s", variant, lower(variant)))
+    best = solve_event_columns(incumbent, improving, lower=lower)
+    assert best is not None
+    # op0 + op1 + op3 (op2 would cost 10 more): 20 - 3 - 2 - 1 = 14
+    assert best.t_pred_us == pytest.approx(14.0)

@@ -4,9 +4,15 @@ Every improving variant is a column with its measured exact gain (incumbent
 T_pred minus the variant's).  A MILP chooses a set of pairwise-compatible
 columns (disjoint repair domains) maximising the summed gain; the chosen
 changes are merged into one network candidate, which is lowered, checked and
-predicted exactly — it is accepted only when its exact T_pred beats every
-single variant (reference: vericcl/tuning/event_columns.py:24-111, where the
-columns carry exact active-mode rates inside a SCIP disjunction model).
+predicted exactly.  Gains do not simply add up — merged changes share ports
+and thread blocks — so the MILP's choice is only a starting point: a greedy
+pass then adds compatible columns one at a time, best single gain first, and
+keeps an addition only when the exact replay of the merged schedule (the
+event simulator: operations start as soon as their dependencies finish, at
+the rates of the sharing mode that is active) improves.  The best merged
+candidate is accepted only when it beats every single variant (reference:
+vericcl/tuning/event_columns.py:24-111, where the columns carry exact
+active-mode rates inside a SCIP disjunction model).
 """
 from __future__ import annotations
 
@@ -23,9 +29,56 @@ def _changes(base, variant):
         set(old) - {op.operation_id for op in variant.operations}
 
 
+def _merge(base, variants):
+    merged = {op.operation_id: op for op in base.operations}
+    for variant in variants:
+        changed, removed = _changes(base, variant)
+        for key in removed:
+            merged.pop(key, None)
+        merged.update(changed)
+    return NetworkCandidate(base.rank_count, base.slice_count, base.slice_size_bytes, tuple(merged.values()),
+                            "repair:joint", base.channels)
+
+
+def _lowered(lower, candidate):
+    try:
+        bundle = lower(candidate)
+    except SemanticError:
+        return None
+    return bundle if bundle.can_execute and bundle.t_pred_us is not None else None
+
+
+def greedy_exact(incumbent, improving, *, lower, limit: int = 8):
+    """Add compatible columns best-first while the exact T_pred of the merged schedule keeps dropping."""
+    base = incumbent.network
+    order = sorted(range(len(improving)), key=lambda i: improving[i][2].t_pred_us)
+    touched = []
+    for _, variant, _ in improving:
+        changed, removed = _changes(base, variant)
+        touched.append(set(changed) | removed)
+    chosen, best = [order[0]], improving[order[0]][2]
+    used = set(touched[order[0]])
+    for i in order[1:limit]:
+        if touched[i] & used:
+            continue
+        trial = _lowered(lower, _merge(base, [improving[j][1] for j in chosen + [i]]))
+        if trial is not None and trial.t_pred_us < best.t_pred_us:
+            chosen.append(i)
+            used |= touched[i]
+            best = trial
+    return best if len(chosen) > 1 else None
+
+
 def solve_event_columns(incumbent, improving, *, lower):
     if len(improving) < 2:
         return None
+    greedy = greedy_exact(incumbent, improving, lower=lower)
+    milp = _solve_selection(incumbent, improving, lower=lower)
+    found = [b for b in (greedy, milp) if b is not None]
+    return min(found, key=lambda b: b.t_pred_us) if found else None
+
+
+def _solve_selection(incumbent, improving, *, lower):
     base = incumbent.network
     model = Model("event-columns")
     x = []
