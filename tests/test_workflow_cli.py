@@ -109,7 +109,14 @@ def test_experiment_report_tables(tmp_path):
     rows = report_rows(load_points([log]))
     assert len(rows) == 1 and rows[0]["path"] == "one-shot NVLS" and rows[0]["size"] == "1 KiB"
     table = markdown(rows)
-    assert "| allreduce | 4 | graph | 1 KiB | one-shot NVLS | 6.1 |" in table
+    assert "| allreduce | 4 | graph | 1 KiB | one-shot NVLS |  | 6.1 |" in table
+    # one-shot NVLS lines: 2 bytes of line per payload byte, multicast into all 4 GPUs: 8 KiB in 6.1 µs
+    assert rows[0]["nvlink_gbs"] == round(8192 / 6.1e-6 / 1e9, 1)
+    # a reference sweep point of the same (collective, GPUs, size) fills the reference columns
+    log.write_text(log.read_text() + '{"impl": "reference", "coll": "allreduce", "bytes_per_rank": 1024, '
+                   '"ranks": 4, "us": 30.5, "busbw_gbs": 0.05}\n')
+    rows = report_rows(load_points([log]))
+    assert len(rows) == 1 and rows[0]["ref_us"] == 30.5 and rows[0]["x_ref"] == 5.0
     cmds = matrix_commands([2, 8], graph=True)
     assert cmds[1][4] == "--nproc-per-node=8" and cmds[1][-1] == "--graph"
 

@@ -35,6 +35,27 @@ def matrix_commands(gpus, *, colls: str = "allreduce,allgather", graph: bool = F
     return out
 
 
+NVLINK_MEASURED_GBS = 770.0      # peer copy per direction per GPU measured on B200s (900 nominal)
+
+
+def nvlink_bytes(point) -> int | None:
+    """Bytes the busier direction of one GPU's NVLink ports carries for this point's path."""
+    p, m = point["n_gpus"], point["bytes_per_rank"]
+    if p < 2:
+        return None
+    coll, kind, nvls = point["coll"], point.get("path", "interp"), bool(point.get("nvls"))
+    if coll == "allreduce":
+        if kind == "oneshot":
+            return 2 * m * p if nvls else 2 * m * (p - 1)          # 16-byte lines carry 8 payload bytes
+        return int(m * (1 + 1 / p)) if nvls else int(2 * m * (p - 1) / p)
+    if coll == "allgather_fp8":
+        esize = 4 if point.get("dtype") == "float32" else 2
+        return int((p - 1) * (m // esize) * (1 + 4 / 128))
+    if kind == "oneshot":
+        return 2 * m * p if nvls else 2 * m * (p - 1)
+    return m * p if nvls else m * (p - 1)                           # multicast stores also land on the sender
+
+
 def load_points(paths) -> list:
     points = []
     for path in paths:
@@ -48,6 +69,8 @@ def load_points(paths) -> list:
                 continue
             if "coll" in doc and "bytes_per_rank" in doc and "time_us" in doc:
                 points.append(doc)
+            elif doc.get("impl") == "reference" and "coll" in doc and "us" in doc:
+                points.append(dict(doc, reference=True))
     return points
 
 
@@ -62,26 +85,41 @@ def _path(p) -> str:
     kind = p.get("path", "interp")
     if kind == "oneshot":
         return "one-shot" + (" NVLS" if p.get("nvls") else "")
+    if kind in ("push", "fp8_fused"):
+        return {"push": "push", "fp8_fused": "fp8 fused"}[kind]
     return ("NVLS" if p.get("nvls") else "P2P") + (" %s" % p["method"] if p.get("method") not in (None, "hierarchy")
                                                    else "")
 
 
 def report_rows(points) -> list:
+    """One row per product point, with the reference library's time of the same (collective, GPUs, size)."""
+    ref = {(p["coll"], p["ranks"], p["bytes_per_rank"]): p["us"] for p in points if p.get("reference")}
     rows = []
-    for p in sorted(points, key=lambda d: (d["coll"], d["n_gpus"], bool(d.get("graph")), d["bytes_per_rank"])):
+    mine = [p for p in points if not p.get("reference")]
+    for p in sorted(mine, key=lambda d: (d["coll"], d["n_gpus"], bool(d.get("graph")), d.get("variant", ""),
+                                         d["bytes_per_rank"])):
+        link = nvlink_bytes(p)
+        link_gbs = None if link is None else link / (p["time_us"] * 1e-6) / 1e9
+        ref_us = ref.get((p["coll"], p["n_gpus"], p["bytes_per_rank"]))
         rows.append({"coll": p["coll"], "gpus": p["n_gpus"], "mode": "graph" if p.get("graph") else "eager",
-                     "size": human_bytes(p["bytes_per_rank"]), "path": _path(p), "time_us": p["time_us"],
-                     "busbw_gbs": p.get("busbw_gbs"), "nccl_us": p.get("nccl_time_us"),
-                     "x_nccl": p.get("speedup_vs_nccl"), "err": p.get("max_rel_err_vs_fp64")})
+                     "size": human_bytes(p["bytes_per_rank"]), "path": _path(p), "variant": p.get("variant", ""),
+                     "time_us": p["time_us"], "busbw_gbs": p.get("busbw_gbs"), "nccl_us": p.get("nccl_time_us"),
+                     "x_nccl": p.get("speedup_vs_nccl"), "ref_us": ref_us,
+                     "x_ref": None if ref_us is None else round(ref_us / p["time_us"], 3),
+                     "nvlink_gbs": None if link_gbs is None else round(link_gbs, 1),
+                     "frac_770": None if link_gbs is None else round(link_gbs / NVLINK_MEASURED_GBS, 3),
+                     "err": p.get("max_rel_err_vs_fp64")})
     return rows
 
 
 def markdown(rows) -> str:
-    head = ["coll", "GPUs", "mode", "bytes/rank", "path", "µs", "busbw GB/s", "NCCL µs", "× NCCL", "fp64 rel err"]
+    head = ["coll", "GPUs", "mode", "bytes/rank", "path", "variant", "µs", "busbw GB/s", "NCCL 2.28 µs", "× NCCL",
+            "ref 2.12 µs", "× ref", "NVLink GB/s/dir", "of 770", "fp64 rel err"]
     lines = ["| " + " | ".join(head) + " |", "|" + "---|" * len(head)]
     for r in rows:
-        vals = [r["coll"], r["gpus"], r["mode"], r["size"], r["path"], r["time_us"], r["busbw_gbs"], r["nccl_us"],
-                r["x_nccl"], "" if r["err"] is None else "%.1e" % r["err"]]
+        vals = [r["coll"], r["gpus"], r["mode"], r["size"], r["path"], r["variant"], r["time_us"], r["busbw_gbs"],
+                r["nccl_us"], r["x_nccl"], r["ref_us"], r["x_ref"], r["nvlink_gbs"], r["frac_770"],
+                "" if r["err"] is None else "%.1e" % r["err"]]
         lines.append("| " + " | ".join("" if v is None else str(v) for v in vals) + " |")
     return "\n".join(lines) + "\n"
 
