@@ -348,7 +348,7 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
   const unsigned long long stride = 2ull * (unsigned long long)blk.nsteps;
   unsigned long long* my_flag = flag_ptr(a, a.rank, (long long)block * kMaxFlagLanes + lane);
   __shared__ const char* s_src[16];
-  bool mc_pending = false;   // multimem stores of this thread not yet fenced
+  bool mc_pending = false;   // multimem or remote (push) stores of this thread not yet fenced
   const int total_iters = a.niters * a.nbatch;
   for (int it = 0; it < total_iters; ++it) {
     const int batch = it / a.niters;
@@ -421,9 +421,12 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
                                  ((long long)(sr.chunk + k) * a.chunk_elems + pr.lo) * esize;
           }
           __syncthreads();
-          char* dst = s_rank_base[a.rank] + s_buf_off[st.dst_buf] + batch * a.batch_stride[st.dst_buf] +
+          // a push writes the receiver's buffer through its peer mapping
+          const int dr = (st.dst_rank >= 0 && st.dst_rank < a.nranks) ? st.dst_rank : a.rank;
+          char* dst = s_rank_base[dr] + s_buf_off[st.dst_buf] + batch * a.batch_stride[st.dst_buf] +
                       ((long long)(st.dst_chunk + k) * a.chunk_elems + pr.lo) * esize;
           move_piece<DT, RED, LEAN>(dst, s_src, st.nsrc, nvec, (st.flags & F_SCALE) != 0, a.scale);
+          if (dr != a.rank) mc_pending = true;   // remote stores: fenced at system scope before the done flag
           __syncthreads();
         }
       }

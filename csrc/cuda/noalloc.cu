@@ -73,6 +73,7 @@ int setup_device(int device, unsigned char** base) {
   } t;
   std::memset(&t, 0, sizeof t);
   t.block = vb::DevBlock{0, 1, -1, 0, 0};
+  t.step.dst_rank = -1;
   t.step.op = vb::OP_COPY;
   t.step.dst_buf = vb::BUF_OUT;
   t.step.flags = vb::F_SCALE;

@@ -3,8 +3,9 @@
 // The schedule's thread blocks become CTA groups ("blocks"); every block runs
 // on `nlanes` CTAs, and each lane owns a fixed sub-range (a "piece") of every
 // chunk, so the whole program is instantiated nlanes x niters times over
-// disjoint element ranges.  Steps are pull-based: a receive loads the
-// sender's source region directly from the sender's peer-mapped memory.
+// disjoint element ranges.  Steps are pull-based (a receive loads the
+// sender's source region directly from the sender's peer-mapped memory) or,
+// in push mode, a send stores into the receiver's peer-mapped buffer.
 // Cross-CTA and cross-rank ordering uses monotone 64-bit flags, one per
 // (block, lane) per rank: step s of iteration it publishes
 //   base + it * stride + 2*s + 1   when it arrives (its waits are satisfied)
@@ -54,6 +55,7 @@ struct DevStep {
   int32_t nsrc;
   int32_t wait_begin;   // index into the wait table
   int32_t wait_count;
+  int32_t dst_rank;     // rank whose buffer the step writes: < 0 (or the own rank) local; else a push into a peer
 };
 
 struct DevWait {

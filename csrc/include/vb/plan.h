@@ -48,6 +48,7 @@ struct CompileOptions {
   bool fuse_chains = true;   // fold chains of receive-reduce steps into one n-ary reduce
   bool multicast = false;    // map whole-group reduce/broadcast patterns to NVLS multimem ops
   bool merge_blocks = true;  // run each rank's steps as one CTA group in a global topological order
+  bool push = false;         // a plain send/receive pair becomes a store into the receiver's memory
   int mc_keep = 1, mc_period = 1;  // map a reduce chunk to NVLS when chunk % mc_period < mc_keep (rest stays P2P)
   bool reducing = false;     // the collective reduces (enables scale placement)
 };
@@ -68,6 +69,7 @@ struct CompileStats {
   int xml_steps = 0, device_steps = 0, elided_blocks = 0, fused_reduces = 0, multicast_ops = 0;
   int waits = 0, remote_waits = 0, scale_steps = 0, deferred_waits = 0, dropped_nops = 0;
   int staged_forwards = 0;   // 'rrs' steps given a scratch store so the next hop can pull the value
+  int pushes = 0;            // send/receive pairs carried out as stores into the receiver's memory
 };
 
 struct CompiledPlan {

@@ -24,6 +24,7 @@ py::dict stats_dict(const CompileStats& s) {
   d["deferred_waits"] = s.deferred_waits;
   d["dropped_nops"] = s.dropped_nops;
   d["staged_forwards"] = s.staged_forwards;
+  d["pushes"] = s.pushes;
   return d;
 }
 
@@ -94,8 +95,9 @@ PYBIND11_MODULE(_vbplan, m) {
       });
   m.def("parse_and_compile",
         [](const std::string& xml, int nlanes, int niters, bool elide, bool fuse, bool multicast, bool reducing,
-           bool merge) {
+           bool merge, bool push) {
           CompileOptions o;
+          o.push = push;
           o.nlanes = nlanes;
           o.niters = niters;
           o.elide_sends = elide;
@@ -106,7 +108,8 @@ PYBIND11_MODULE(_vbplan, m) {
           return compile_plan(parse_xml(xml), o);
         },
         py::arg("xml"), py::arg("nlanes") = 1, py::arg("niters") = 1, py::arg("elide") = true,
-        py::arg("fuse") = true, py::arg("multicast") = false, py::arg("reducing") = false, py::arg("merge") = true);
+        py::arg("fuse") = true, py::arg("multicast") = false, py::arg("reducing") = false, py::arg("merge") = true,
+        py::arg("push") = false);
   m.def("cpu_interpret",
         [](const CompiledPlan& plan, py::list in, py::list out, py::list scr, int dtype, int redop, float scale,
            long long chunk_elems, long long piece_elems, unsigned seed, int launches) {

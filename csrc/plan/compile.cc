@@ -17,6 +17,15 @@
 //      waits for all of its sends to be consumed before the kernel ends;
 //   6. optional chain fusion (receive-reduce chains into one n-ary reduce);
 //   7. a final deadlock check of the device event graph.
+// Push mode (CompileOptions::push) turns every plain send/receive pair into a
+// store by the sender into the receiver's buffer: the sender's step waits for
+// everything the receive would have waited for on the receiving rank (its
+// predecessor in its thread block, its explicit dependency, the readers of the
+// destination it overwrites, the receiver's start flag), the receive becomes a
+// NOP that waits for the push.  The data leaves the sender when the send runs,
+// as with MSCCL's FIFO connections, so overwriting the send's source only
+// waits for the push itself, and NVLink carries stores instead of the read
+// requests of pulls.  Reductions keep pulling; push mode excludes NVLS mapping.
 #include <algorithm>
 #include <deque>
 #include <functional>
@@ -80,7 +89,7 @@ class Compiler {
     assign_blocks();
     build_waits_and_hazards();
     if (o_.merge_blocks) merge_blocks();
-    if (o_.multicast && merged_ && P_ > 1) map_multicast();
+    if (o_.multicast && !o_.push && merged_ && P_ > 1) map_multicast();
     dedupe_start_waits();
     if (merged_) drop_idle_nops();
     emit();
@@ -308,9 +317,13 @@ class Compiler {
       dblock_[r].assign(g.tbs.size(), -1);
       int next = 0;
       for (int t = 0; t < (int)g.tbs.size(); ++t) {
-        bool only_sends = true;
-        for (auto& st : g.tbs[t].steps) if (st.kind != X_S && st.kind != X_NOP) only_sends = false;
-        if (o_.elide_sends && only_sends) { ++stats_.elided_blocks; continue; }
+        bool only_sends = true, pushes = false;
+        for (int s = 0; s < (int)g.tbs[t].steps.size(); ++s) {
+          const XStep& st = g.tbs[t].steps[s];
+          if (st.kind != X_S && st.kind != X_NOP) only_sends = false;
+          if (pushed(SRef{r, t, s})) pushes = true;
+        }
+        if (o_.elide_sends && only_sends && !pushes) { ++stats_.elided_blocks; continue; }
         dblock_[r][t] = next++;
       }
       out_[r].i_chunks = g.i_chunks;
@@ -323,13 +336,28 @@ class Compiler {
 
   bool elided(const SRef& x) const { return dblock_[x.rank][x.tb] < 0; }
 
+  // Push mode: a plain send whose receive is a plain receive is carried out by the sender.
+  bool pushed(const SRef& x) const {
+    if (!o_.push) return false;
+    const XStep& st = step(x);
+    if (st.kind != X_S) return false;
+    auto it = match_recv_.find(x);
+    return it != match_recv_.end() && step(it->second).kind == X_R;
+  }
+  bool pushed_recv(const SRef& y) const {
+    auto it = match_send_.find(y);
+    return it != match_send_.end() && pushed(it->second);
+  }
+
   // Event set that is complete once step x is complete under pull semantics.
   EventSet completion(const SRef& x) {
     auto it = completion_memo_.find(x);
     if (it != completion_memo_.end()) return it->second;
     EventSet e;
     const XStep& st = step(x);
-    if (st.kind == X_S) {
+    if (pushed(x)) {
+      e[{x.rank, dblock_[x.rank][x.tb]}] = 2 * x.step + 2;   // the push is done: the data left the source
+    } else if (st.kind == X_S) {
       SRef rv = match_recv_.at(x);
       e[{rv.rank, redirect_block(rv)}] = 2 * redirect_step(rv) + 2;
     } else if (elided(x)) {
@@ -448,7 +476,7 @@ class Compiler {
   }
 
   struct PendingStep {
-    DevStep st;
+    DevStep st{};
     std::vector<DevSrc> srcs;
     EventSet waits;
     int prio = 0;
@@ -457,6 +485,7 @@ class Compiler {
     int xml_step = -1;         // index of the originating step in its XML thread block (-1: compiler-made)
     bool mc_peer = false;      // a copy replaced by the owner's multicast store
     int mc_buf = -1, mc_chunk = -1;
+    PendingStep() { st.dst_rank = -1; }
   };
 
   void build_waits_and_hazards() {
@@ -503,7 +532,28 @@ class Compiler {
       if (st.depid >= 0) merge(ps.waits, completion(SRef{x.rank, tb_index_[x.rank].at(st.depid), st.deps}));
       for (auto& s : acks[x]) merge(ps.waits, completion(s));
       auto fused = fused_into_.find(x);
-      if (fused != fused_into_.end()) {
+      if (pushed(x)) {
+        // the sender stores into the receiver's destination once the receive could have run there: after
+        // its predecessor in its thread block, its explicit dependency and the readers of what it overwrites
+        const SRef y = match_recv_.at(x);
+        const XStep& ry = step(y);
+        Region src = pull_source(x);
+        Region d = canon(y.rank, ry.dstbuf, ry.dstoff);
+        ps.st.op = OP_COPY;
+        ps.srcs.push_back(DevSrc{(int16_t)x.rank, (uint8_t)src.buf, 0, src.chunk});
+        ps.st.dst_buf = (uint8_t)d.buf;
+        ps.st.dst_chunk = d.chunk;
+        ps.st.dst_rank = y.rank;
+        if (y.step > 0) merge(ps.waits, completion(SRef{y.rank, y.tb, y.step - 1}));
+        if (ry.depid >= 0) merge(ps.waits, completion(SRef{y.rank, tb_index_[y.rank].at(ry.depid), ry.deps}));
+        for (auto& s : acks[y]) merge(ps.waits, completion(s));
+        merge(ps.waits, EventSet{{{y.rank, -1}, 1}});   // the receiver's kernel has started
+        if (scale_steps_.count(y)) ps.st.flags |= F_SCALE;
+        ++stats_.pushes;
+      } else if (pushed_recv(x)) {
+        ps.st.op = OP_NOP;                                // the push into this rank does the work
+        merge(ps.waits, completion(match_send_.at(x)));
+      } else if (fused != fused_into_.end()) {
         ps.st.op = OP_NOP;   // work moves to the chain's final step
       } else if (chains_.count(x)) {
         const auto& chain = chains_[x];
@@ -564,7 +614,7 @@ class Compiler {
           ps.st.dst_chunk = d.chunk;
         }
       }
-      if (scale_steps_.count(x)) ps.st.flags |= F_SCALE;
+      if (scale_steps_.count(x) && !pushed_recv(x)) ps.st.flags |= F_SCALE;
       // drop waits implied by this CTA's own sequential order
       auto own = ps.waits.find({x.rank, db});
       if (own != ps.waits.end()) {
@@ -611,7 +661,7 @@ class Compiler {
     end_waits_.resize(P_);
     for (const SRef& x : all_) {
       const XStep& st = step(x);
-      if (!has_send(st.kind)) continue;
+      if (!has_send(st.kind) || pushed(x)) continue;   // a push is over when its own step is
       SRef rv = match_recv_.at(x);
       merge(end_waits_[x.rank], EventSet{{{rv.rank, redirect_block(rv)}, 2 * redirect_step(rv) + 2}});
     }
@@ -645,6 +695,7 @@ class Compiler {
     auto rotation = [&](const Node& n) {
       const PendingStep& ps = pending_[std::get<0>(n)][std::get<1>(n)][std::get<2>(n)];
       const int r = std::get<0>(n);
+      if (ps.st.dst_rank >= 0 && ps.st.dst_rank != r) return (ps.st.dst_rank - r + P_) % P_;   // push target
       for (auto& sr : ps.srcs)
         if (sr.rank != r) return (sr.rank - r + P_) % P_;
       return 0;
@@ -1121,7 +1172,11 @@ std::string describe_rank(const CompiledPlan& plan, int rank) {
     for (int s = 0; s < blk.nsteps; ++s) {
       const DevStep& st = rp.steps[blk.step_begin + s];
       o << "  " << s << ": " << ops[st.op];
-      if (st.op != OP_NOP) o << " -> " << "ios"[st.dst_buf] << "[" << st.dst_chunk << "]";
+      if (st.op != OP_NOP) {
+        o << " -> ";
+        if (st.dst_rank >= 0 && st.dst_rank != rank) o << "r" << st.dst_rank << ":";
+        o << "ios"[st.dst_buf] << "[" << st.dst_chunk << "]";
+      }
       for (int i = 0; i < st.nsrc; ++i) {
         const DevSrc& sr = rp.srcs[st.src_begin + i];
         o << (i ? ", " : " <- ") << "r" << sr.rank << ":" << "ios"[sr.buf] << "[" << sr.chunk << "]";

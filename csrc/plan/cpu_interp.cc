@@ -5,7 +5,8 @@
 // waits are satisfied, exactly as on the GPU, and a pull reads the peer's
 // buffer at the moment the step runs.  Element arithmetic mirrors the kernel:
 // sources are widened to fp32, combined left to right, scaled once when the
-// step carries F_SCALE, and rounded back to the storage type.
+// step carries F_SCALE, and rounded back to the storage type.  A push step
+// writes the receiving rank's buffer at the moment it runs.
 #include <algorithm>
 #include <cmath>
 #include <cstring>
@@ -163,13 +164,14 @@ InterpResult cpu_interpret(const CompiledPlan& plan, HostBuffers& bufs, int dtyp
           if (st.flags & F_PUB_ARRIVE) publish(2 * c.s + 1, c.it);
           if (st.op == OP_COPY || st.op == OP_REDUCE) {
             PieceRange pr = piece_range(chunk_elems, piece_elems, c.it, L, c.lane);
+            const int dr = (st.dst_rank >= 0 && st.dst_rank < P) ? st.dst_rank : c.rank;   // push target
             for (int k = 0; k < st.cnt; ++k) {
               long long dst_off = (long long)(st.dst_chunk + k) * chunk_elems;
-              if (dst_off + pr.hi > buf_elems(c.rank, st.dst_buf)) {
+              if (dst_off + pr.hi > buf_elems(dr, st.dst_buf)) {
                 res.error = "destination out of range";
                 return res;
               }
-              unsigned char* dst = base_ptr(c.rank, st.dst_buf);
+              unsigned char* dst = base_ptr(dr, st.dst_buf);
               for (long long e = pr.lo; e < pr.hi; ++e) {
                 float acc = 0.f;
                 for (int si = 0; si < st.nsrc; ++si) {

@@ -157,10 +157,11 @@ BoundOneShot bind_oneshot(Heap& heap, size_t in_off, size_t out_off, size_t ll_o
 class DevicePlan {
  public:
   DevicePlan(const std::string& xml, int rank, int nlanes, int niters, bool elide, bool fuse, bool multicast,
-             bool reducing, int mc_keep, int mc_period, bool merge)
+             bool reducing, int mc_keep, int mc_period, bool merge, bool push)
       : rank_(rank) {
     CompileOptions o;
     o.merge_blocks = merge;
+    o.push = push;
     o.nlanes = nlanes;
     o.niters = niters;
     o.elide_sends = elide;
@@ -316,6 +317,7 @@ class DevicePlan {
     d["deferred_waits"] = plan_.stats.deferred_waits;
     d["dropped_nops"] = plan_.stats.dropped_nops;
     d["staged_forwards"] = plan_.stats.staged_forwards;
+    d["pushes"] = plan_.stats.pushes;
     return d;
   }
 
@@ -410,10 +412,10 @@ PYBIND11_MODULE(_vbcuda, m) {
   }, py::arg("heap"), py::arg("inp"), py::arg("out"), py::arg("stage_off"), py::arg("flag_off"), py::arg("ctas"),
      py::arg("timeout_s") = 10.0);
   py::class_<DevicePlan>(m, "DevicePlan")
-      .def(py::init<const std::string&, int, int, int, bool, bool, bool, bool, int, int, bool>(), py::arg("xml"),
+      .def(py::init<const std::string&, int, int, int, bool, bool, bool, bool, int, int, bool, bool>(), py::arg("xml"),
            py::arg("rank"), py::arg("nlanes"), py::arg("niters"), py::arg("elide"), py::arg("fuse"),
            py::arg("multicast"), py::arg("reducing"), py::arg("mc_keep") = 1, py::arg("mc_period") = 1,
-           py::arg("merge") = true)
+           py::arg("merge") = true, py::arg("push") = false)
       .def("run", &DevicePlan::run, py::arg("heap"), py::arg("in_off"), py::arg("out_off"), py::arg("scr_off"),
            py::arg("count_per_rank"), py::arg("dtype"), py::arg("redop"), py::arg("scale"), py::arg("stream"),
            py::arg("timeout_s") = 10.0, py::arg("threads") = 512, py::arg("nbatch") = 1,
@@ -453,6 +455,7 @@ PYBIND11_MODULE(_vbcuda, m) {
     blocks[0] = DevBlock{0, 1, -1, 0, 0};
     std::vector<DevStep> steps(1);
     steps[0] = DevStep{};
+    steps[0].dst_rank = -1;
     steps[0].op = OP_NOP;
     steps[0].cnt = 1;
     steps[0].wait_begin = 0;
@@ -530,6 +533,7 @@ PYBIND11_MODULE(_vbcuda, m) {
     std::vector<char> host(bytes - table_off);
     DevBlock blk{0, 1, -1, 0, 0};
     DevStep st{};
+    st.dst_rank = -1;
     st.op = k == 1 ? OP_COPY : OP_REDUCE;
     st.dst_buf = BUF_OUT;
     st.flags = do_scale ? F_SCALE : 0;

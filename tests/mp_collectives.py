@@ -64,12 +64,19 @@ def main():
                 for slices in ((1, world) if coll != "reduce_scatter" else (world,)):
                     for lanes, iters in ((1, 1), (4, 2), (16, 1)):
                         for count in ((world * 4096, world * 1 << 18) if not quick else (world * 4096,)):
-                            cases.append((coll, dtype, inplace, slices, lanes, iters, count))
-    for coll, dtype, inplace, slices, lanes, iters, count in cases:
+                            cases.append((coll, dtype, inplace, slices, lanes, iters, count, False))
+    # push steps (stores into the receiver's heap buffer) on the plain-transfer collectives, no NVLS
+    for coll in ("allgather", "allreduce"):
+        for inplace in (False, True):
+            for lanes, iters in ((1, 1), (8, 2)):
+                cases.append((coll, torch.float32, inplace, world if coll == "allreduce" else 1, lanes, iters,
+                              world * 4096, True))
+    for coll, dtype, inplace, slices, lanes, iters, count, push in cases:
         dname = str(dtype).split(".")[-1]
         xml = schedule_xml(coll, world, slices, inplace=inplace, datatype=dname)
         op = "avg" if coll == "allreduce" and lanes == 4 else "sum"
-        plan = comm.compile(xml, nlanes=lanes, niters=iters, multicast=comm.multicast and coll in ("allreduce", "allgather"))
+        plan = comm.compile(xml, nlanes=lanes, niters=iters, push=push,
+                            multicast=comm.multicast and not push and coll in ("allreduce", "allgather"))
         seed = zlib.crc32(repr((coll, dname, inplace, slices, lanes, iters, count)).encode()) % 100000
         x = inputs_for(rank, count, dtype, seed).cuda()
         out_n = count * world if coll == "allgather" else count // world if coll == "reduce_scatter" else count
@@ -111,8 +118,8 @@ def main():
             failures += 1
         if rank == 0 or not ok:
             print(json.dumps({"rank": rank, "coll": coll, "dtype": dname, "inplace": inplace, "slices": slices,
-                              "lanes": lanes, "iters": iters, "count": count, "op": op, "max_err": err, "ok": ok}),
-                  flush=True)
+                              "lanes": lanes, "iters": iters, "count": count, "op": op, "push": push,
+                              "max_err": err, "ok": ok}), flush=True)
         dist.barrier()
         for t in ([buf] if inplace else [inp, out]):
             comm.free(t)

@@ -173,3 +173,34 @@ def test_reduce_and_forward_is_staged_in_scratch(lanes, iters):
     inputs = [rng.standard_normal(96).astype(np.float32) for _ in range(3)]
     outs = run_cpu(compiled, inputs, seed=7)
     np.testing.assert_allclose(outs[2][:96], inputs[0] + inputs[1] + inputs[2], rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("coll", ["allgather", "allreduce", "broadcast", "alltoall"])
+@pytest.mark.parametrize("p", [2, 4, 8])
+@pytest.mark.parametrize("lanes,iters,merge", [(1, 1, True), (3, 2, True), (2, 1, False)])
+def test_push_programs_match_reference(coll, p, lanes, iters, merge):
+    """Push mode: plain transfers become stores into the receiver; the randomized oracle still finds every result."""
+    inplace = coll in ("allgather", "allreduce")
+    slices = p if coll in ("allreduce", "alltoall") else 1
+    xml = schedule_xml(coll, p, slices, inplace=inplace)
+    plan = compile_xml(xml, nlanes=lanes, niters=iters, merge=merge, push=True)
+    assert plan.stats["pushes"] > 0
+    pulled = compile_xml(xml, nlanes=lanes, niters=iters, merge=merge)
+    assert pulled.stats["pushes"] == 0
+    count = p * 16 * slices
+    rng = np.random.default_rng(p + lanes)
+    ins = [rng.uniform(-1, 1, count).astype(np.float32) for _ in range(p)]
+    exp = reference_result(coll, [a.astype(np.float64) for a in ins], rank_count=p)
+    for seed in range(3):
+        outs = run_cpu(plan, ins, seed=seed)
+        for r in range(p):
+            if exp[r] is not None:
+                np.testing.assert_allclose(outs[r][:len(exp[r])], exp[r], atol=1e-5)
+
+
+def test_push_steps_write_the_receiver_and_receives_wait_for_them():
+    plan = compile_xml(schedule_xml("allgather", 4, 1), push=True)
+    text = plan.describe(0)
+    assert "-> r1:o[" in text or "-> r1:" in text          # rank 0 stores into a peer's output
+    # a push waits for the receiver's start flag (block -1 is the per-rank start flag)
+    assert "wait(r1,b-1,e1)" in text or "wait(r2,b-1,e1)" in text or "wait(r3,b-1,e1)" in text

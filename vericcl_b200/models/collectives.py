@@ -55,6 +55,7 @@ class CollectiveEngine:
         self.twoshot_max_bytes = twoshot_max_bytes
         self.ag_nvls_max_bytes = AG_NVLS_MAX_BYTES if ag_nvls_max_bytes is None else ag_nvls_max_bytes
         self.ag_push_min_bytes = None      # push AllGather threshold (None: off); VERICCL_AG_PUSH_MIN overrides
+        self.push_collectives = frozenset()   # interpreter collectives compiled with push steps
         if tuning is not None:
             # thresholds measured on this machine (vericcl_b200.models.tuner); explicit arguments still win
             for name, given in explicit.items():
@@ -123,17 +124,32 @@ class CollectiveEngine:
         dname = str(dtype).split(".")[-1]
         xml = schedule_xml(collective, world, slices, inplace=inplace, datatype=dname, method=self.method,
                            root=root if collective in ("broadcast", "reduce") else 0)
-        merge = self.merge_blocks(collective, count * torch.tensor([], dtype=dtype).element_size())
-        probe = self.comm.compile(xml, nlanes=1, niters=1, merge=merge)
+        nbytes = count * torch.tensor([], dtype=dtype).element_size()
+        merge = self.merge_blocks(collective, nbytes)
+        multicast = self.use_multicast(collective, op, nbytes)
+        push = not multicast and self.push_steps(collective, nbytes)
+        probe = self.comm.compile(xml, nlanes=1, niters=1, merge=merge, push=push)
         esize = torch.tensor([], dtype=dtype).element_size()
         runtime = count * (world if collective == "allgather" else 1)
         nchunks = slices * (world if collective == "allgather" else 1)
         chunk_bytes = runtime * esize // nchunks
         lanes, iters = self.geometry(probe.device_plan.nblocks, chunk_bytes)
         share = tuple(int(v) for v in os.environ.get("VERICCL_MC_SHARE", "1/1").split("/"))
-        return self.comm.compile(xml, nlanes=lanes, niters=iters,
-                                 multicast=self.use_multicast(collective, op, count * esize), mc_share=share,
-                                 merge=merge)
+        return self.comm.compile(xml, nlanes=lanes, niters=iters, multicast=multicast, mc_share=share,
+                                 merge=merge, push=push)
+
+    def push_steps(self, collective: str, nbytes: int) -> bool:
+        """Compile plain transfers as pushes (stores into the receiver) instead of pulls.
+
+        Pushes keep read requests off the links, which matters when every GPU
+        sends and receives at once.  ``VERICCL_PUSH=1`` turns it on for every
+        interpreter collective, ``VERICCL_PUSH=0`` off; the default follows
+        ``push_collectives`` (empty until the 8-GPU measurements decide).
+        """
+        env = os.environ.get("VERICCL_PUSH")
+        if env is not None:
+            return env not in ("0", "")
+        return self.comm.world > 1 and collective in self.push_collectives
 
     def merge_blocks(self, collective: str, nbytes: int) -> bool:
         """Run a rank's steps as one CTA group in one order (default) or each XML block on its own CTAs.

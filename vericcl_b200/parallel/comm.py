@@ -184,18 +184,21 @@ class Communicator:
 
     # -- plans ----------------------------------------------------------------
     def compile(self, xml: str, *, nlanes: int = 1, niters: int = 1, elide: bool = True, fuse: bool = True,
-                multicast: bool = False, mc_share: tuple = (1, 1), merge: bool = True) -> PlanHandle:
+                multicast: bool = False, mc_share: tuple = (1, 1), merge: bool = True,
+                push: bool = False) -> PlanHandle:
+        """Compile ``xml`` for this rank (cached).  ``push``: plain send/receive pairs become stores by the sender
+        into the receiver's heap buffer instead of pulls (see csrc/plan/compile.cc)."""
         import re
         if multicast and not self.multicast:
             raise RuntimeFailure("multicast mapping requested but this communicator's heap has no NVLS binding")
         coll = re.search(r'coll="([a-z_]+)"', xml)
         collective = coll.group(1) if coll else "allreduce"
-        key = (xml, nlanes, niters, elide, fuse, multicast, tuple(mc_share), merge)
+        key = (xml, nlanes, niters, elide, fuse, multicast, tuple(mc_share), merge, push)
         with self._lock:
             if key in self._plans:
                 return self._plans[key]
             plan = self._mod.DevicePlan(xml, self.rank, nlanes, niters, elide, fuse, multicast,
-                                        collective in REDUCING, int(mc_share[0]), int(mc_share[1]), merge)
+                                        collective in REDUCING, int(mc_share[0]), int(mc_share[1]), merge, push)
             handle = PlanHandle(plan, xml, collective, nlanes, niters, tuple(plan.slots()), set(), multicast)
             self._plans[key] = handle
             return handle

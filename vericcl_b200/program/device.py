@@ -48,14 +48,15 @@ def geometry(collective: str, ranks: int, nchunks: int, count_per_rank: int, ele
 
 
 def compile_xml(xml: str, *, nlanes: int = 1, niters: int = 1, elide: bool = True, fuse: bool = True,
-                multicast: bool = False, collective: str | None = None, merge: bool = True):
+                multicast: bool = False, collective: str | None = None, merge: bool = True, push: bool = False):
     mod = native.plan()
     if collective is None:
         import re
         found = re.search(r'coll="([a-z_]+)"', xml)
         collective = found.group(1) if found else "allreduce"
     try:
-        return mod.parse_and_compile(xml, nlanes, niters, elide, fuse, multicast, collective in REDUCING, merge)
+        return mod.parse_and_compile(xml, nlanes, niters, elide, fuse, multicast, collective in REDUCING, merge,
+                                     push)
     except mod.CompileError as error:
         raise SemanticError(str(error)) from error
 
