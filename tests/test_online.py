@@ -174,3 +174,27 @@ def test_bracket_fit_recovers_offset_and_drift_and_drops_a_contradicting_sample(
     bad = samples + [(offset + 1_500_000.0, 1_500_000.0 + 5_000.0, offset + 1_500_000.0 + 2_000.0)]
     m2 = fit_transform(bad)
     assert m2.method == "bracket-lp" and m2.samples_used == 24
+
+
+def test_link_class_probing_measures_representatives_and_covers_every_link():
+    """On 2 x 4 groups, 16 probe jobs (two links per class, one rank per node, one shared mode per resource kind)
+    stand in for the 168 of per-link probing; every link and local component ends up measured."""
+    from vericcl_b200.online.loop import loop_documents
+    from vericcl_b200.online.probe_jobs import link_classes, plan_probes
+    docs = loop_documents(groups=2, per_group=4, inter_gbps=25.0, size_bytes=8 << 20, rounds=1,
+                          datatype="float32", pairs=2)
+    req = resolve_documents(docs)
+    topo = load_topology(req)
+    assert docs["sketch"]["calibration"]["probe_scope"] == "link_classes"
+    jobs = plan_probes(req, topo)
+    every = dict(docs)
+    every["sketch"] = dict(docs["sketch"], calibration=dict(docs["sketch"]["calibration"], probe_scope="every_link"))
+    assert len(jobs) < len(plan_probes(resolve_documents(every), topo)) // 5
+    assert len(link_classes(topo)) == 2                 # intra-group and inter-group links
+    model = initial_cost_model(req)
+    executor = campaign.simulated_executor(topo, source="native_interpreter", noise=0.001)
+    new_model, _, report = campaign.run_calibration(req, topo, model, executor)
+    for key in new_model.services:
+        if key.split(":")[0] in ("link", "rrc", "copy", "reduce"):
+            assert new_model.services[key][0].source == "measured", key
+    assert report["represented"]

@@ -170,6 +170,10 @@ SKETCH = obj({
         "max_rounds": integer(minimum=1, default=3), "max_cv": positive(default=0.05),
         "max_relative_fit_error": number(minimum=0), "job_timeout_s": positive(),
         "payload_sizes": array(integer(minimum=1), default=[]),
+        "probe_scope": string(default="every_link", enum=("every_link", "link_classes"),
+                              doc="every_link probes each directed link; link_classes probes two links of every "
+                                  "class of interchangeable links (same α, β, placement and shared-resource kinds) "
+                                  "and one rank per node, and gives the fit to the whole class"),
     }),
     "trace_and_measure": section({
         "enabled": boolean(False), "pairs": integer(minimum=1, default=20),

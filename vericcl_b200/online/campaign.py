@@ -85,6 +85,24 @@ def run_calibration(request, topology, model, executor, *, lease=None, max_chann
             report["rejected"][job.job_id] = "fit error above the limit"
             continue
         fitted[flow.component] = segments
+    if cfg.get("probe_scope", "every_link") == "link_classes" and fitted:
+        # a class representative's fit stands for every member of its class (and a node's probed rank for
+        # the node's other ranks); the report names what stood for what
+        from vericcl_b200.online.probe_jobs import representatives
+        _, stands_for, local_ranks = representatives(topology)
+        extended = dict(fitted)
+        for component, segments in fitted.items():
+            kind, _, suffix = component.partition(":")
+            if kind in ("link", "rrc"):
+                for member in stands_for.get(suffix, ()):
+                    extended.setdefault("%s:%s" % (kind, member), segments)
+            elif kind in ("copy", "reduce"):
+                rank = int(suffix)
+                node = topology.node_of(rank)
+                for other in node.ranks:
+                    extended.setdefault("%s:%d" % (kind, other), segments)
+        report["represented"] = sorted(set(extended) - set(fitted))
+        fitted = extended
     if not fitted and not profiles:
         return model, [], report
     new_model, diff = publish_model(model, fitted, profiles)

@@ -39,7 +39,8 @@ def loop_documents(*, groups: int, per_group: int, inter_gbps: float, size_bytes
     docs["sketch"]["trace_and_measure"].update({"enabled": True, "pairs": pairs, "max_rounds": 2,
                                                 "max_cv": 0.05, "warmup_iterations": 2, "timed_iterations": 5})
     docs["sketch"]["calibration"].update({"warmup_iterations": 2, "timed_iterations": 5, "launches": 2,
-                                          "payload_sizes": [2 << 20, 8 << 20, 32 << 20]})
+                                          "payload_sizes": [2 << 20, 8 << 20, 32 << 20],
+                                          "probe_scope": "link_classes"})
     return docs
 
 

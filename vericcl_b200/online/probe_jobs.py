@@ -68,11 +68,55 @@ def payload_sizes(request, explicit=()):
     return tuple(sorted(sizes))
 
 
+def link_classes(topology) -> dict:
+    """Interchangeable links: same α, β, same/other node, and the same kinds of shared resources on them.
+
+    Returns ``{class key: [LinkKey, ...]}`` with members in (src, dst) order.
+    """
+    classes = {}
+    for key, link in sorted(topology.links.items()):
+        kinds = tuple(sorted(topology.resources[r].kind if r in topology.resources else r.split("-")[0]
+                             for r in link.resource_ids))
+        same_node = topology.node_of(key.src).node_id == topology.node_of(key.dst).node_id
+        classes.setdefault((same_node, link.alpha_us, link.beta_us_per_byte, kinds), []).append(key)
+    return classes
+
+
+def representatives(topology, per_class: int = 2) -> tuple:
+    """(links to probe, {probed component suffix "s:d": [suffixes it stands for]}, ranks to probe).
+
+    Representatives of a class are spread over different source ranks; each
+    stands for the members nearest to it in the class order.  One rank per
+    node represents the node's local copy/reduce.
+    """
+    chosen, stands_for = [], {}
+    for members in link_classes(topology).values():
+        picks, seen_src = [], set()
+        for key in members:
+            if key.src not in seen_src:
+                picks.append(key)
+                seen_src.add(key.src)
+            if len(picks) == per_class:
+                break
+        for i, key in enumerate(members):
+            rep = picks[i * len(picks) // len(members)]
+            stands_for.setdefault("%d:%d" % (rep.src, rep.dst), []).append("%d:%d" % (key.src, key.dst))
+        chosen.extend(picks)
+    ranks = sorted({node.ranks[0] for node in topology.nodes if node.ranks})
+    return tuple(chosen), stands_for, tuple(ranks)
+
+
 def plan_probes(request, topology, *, max_channels: int = 1, include_shared: bool = True):
-    sizes = payload_sizes(request, request.request_config["sketch"]["calibration"]["payload_sizes"])
+    cfg = request.request_config["sketch"]["calibration"]
+    sizes = payload_sizes(request, cfg["payload_sizes"])
     jobs = []
     reducing = request.collective.reducing
-    for key, link in sorted(topology.links.items()):
+    if cfg.get("probe_scope", "every_link") == "link_classes":
+        links, _, local_ranks = representatives(topology)
+        link_items = [(k, topology.links[k]) for k in sorted(links)]
+    else:
+        link_items, local_ranks = sorted(topology.links.items()), tuple(range(topology.rank_count))
+    for key, link in link_items:
         same_node = topology.node_of(key.src).node_id == topology.node_of(key.dst).node_id
         group = "link_intra" if same_node else "link_inter"
         for c in range(1, max_channels + 1):
@@ -81,15 +125,20 @@ def plan_probes(request, topology, *, max_channels: int = 1, include_shared: boo
             if reducing:
                 jobs.append(ProbeJob("rrc-%d-%d-c%d" % (key.src, key.dst, c), group,
                                      (ProbeFlow("rrc", key.src, key.dst, c),), sizes))
-    for r in range(topology.rank_count):
+    for r in local_ranks:
         jobs.append(ProbeJob("copy-%d" % r, "local", (ProbeFlow("copy", r, r),), sizes))
         if reducing:
             jobs.append(ProbeJob("reduce-%d" % r, "local", (ProbeFlow("reduce", r, r),), sizes))
     if include_shared:
+        kinds_done = set()
         for rid, res in sorted(topology.resources.items()):
             members = sorted(res.links)
             if len(members) < 2:
                 continue
+            if cfg.get("probe_scope", "every_link") == "link_classes":
+                if res.kind in kinds_done:
+                    continue               # one resource of each kind stands for the others
+                kinds_done.add(res.kind)
             pairs = list(combinations(members, 2))[:2]
             for i, (a, b) in enumerate(pairs):
                 jobs.append(ProbeJob("shared-%s-%d" % (rid, i), "shared",
