@@ -114,3 +114,27 @@ def test_joint_repair_keeps_only_merges_the_exact_replay_confirms():
     assert best is not None
     # op0 + op1 + op3 (op2 would cost 10 more): 20 - 3 - 2 - 1 = 14
     assert best.t_pred_us == pytest.approx(14.0)
+
+
+def test_storage_reuse_edges_on_the_critical_path_are_named():
+    """With the smallest scratch budget that fits, reuse edges appear; the analysis separates them from data edges."""
+    from vericcl_b200.errors import ScratchBudgetError
+    from vericcl_b200.verification.bottlenecks import dependency_kinds, storage_causes
+    d = example_documents("allreduce", "hierarchy", 4, total_size_bytes=16 * 1024, slice_size_bytes=1024,
+                          scratch_bytes=1024)
+    with pytest.raises(ScratchBudgetError) as info:
+        synthesize(resolve_documents(d))
+    d["runtime"]["scratch_bytes_per_rank"] = info.value.needed_bytes
+    req = resolve_documents(d)
+    bundle = synthesize(req, timing=False)
+    kinds = dependency_kinds(bundle.storage)
+    assert "data" in kinds.values()
+    if bundle.storage.reuse:
+        assert "storage" in kinds.values() or all((r, rec["writer"]) in kinds for rec in bundle.storage.reuse
+                                                  for r in rec["previous_readers"])
+    path = bundle.prediction.critical_path(bundle.executable)
+    for cause in storage_causes(bundle, path):
+        assert cause.kind == "storage_wait"
+        assert cause.detail["scratch_bytes_per_rank_to_remove"] > info.value.needed_bytes - 1
+    analysis = analyze(bundle, initial_cost_model(req))
+    assert analysis.causes

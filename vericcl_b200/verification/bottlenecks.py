@@ -10,7 +10,13 @@ classifies each link of it:
   its thread block was still busy with earlier work (TB order);
 * ``critical_service`` — the operation's own α + β·S dominates; for a send
   whose link is slower than both hops of some relay a→c→b, the cause names
-  that relay and a ``path`` strategy moves the send onto it.
+  that relay and a ``path`` strategy moves the send onto it;
+* ``storage_wait`` — the chain passes a dependency that no data flow needs:
+  the storage plan added it because the operation reuses a scratch slot
+  whose previous value still had this reader (a read-completion edge).  Every
+  other dependency on the chain is mandatory (it carries data, or orders
+  operations of one thread block).  Such a cause comes with the scratch
+  budget that would let the storage plan keep both values.
 
 Strategies are then generated lazily, round-robin over the eight families
 (path, allocation, order, channel, joint, internal_root, structure,
@@ -204,11 +210,51 @@ def trace_causes(report, bundle, *, tails: int = 5):
     return out
 
 
+def dependency_kinds(storage) -> dict:
+    """``{(reader, writer): kind}`` for every dependency the storage plan created.
+
+    ``data`` — the later operation consumes the earlier one's output;
+    ``storage`` — the writer overwrites a scratch
+    slot whose previous value the earlier operation still reads, and nothing
+    else links them (a read-completion edge that more scratch would remove).
+    """
+    if storage is None:
+        return {}
+    producer = {sid: v.producer for sid, v in storage.values.items()}
+    kinds = {}
+    for ins in storage.instructions:
+        for sid in ins.inputs:
+            if producer.get(sid) is not None:
+                kinds[(producer[sid], ins.operation_id)] = "data"
+    for record in getattr(storage, "reuse", ()) or ():
+        writer = record["writer"]
+        for reader in record["previous_readers"]:
+            kinds.setdefault((reader, writer), "storage")
+    return kinds
+
+
+def storage_causes(bundle, path) -> list:
+    """``storage_wait`` causes for consecutive critical-path operations linked only by slot reuse."""
+    kinds = dependency_kinds(getattr(bundle, "storage", None))
+    out = []
+    for a, b in zip(path, path[1:]):
+        if kinds.get((a, b)) == "storage":
+            slot = next((r for r in bundle.storage.reuse if r["writer"] == b and a in r["previous_readers"]), {})
+            size = bundle.request.hyperparameters.slice_size_bytes if bundle.request is not None else None
+            budget = bundle.request.request_config["runtime"]["scratch_bytes_per_rank"] \
+                if bundle.request is not None else None
+            out.append(Cause("storage_wait", b, {"after": a, "rank": slot.get("rank"), "offset": slot.get("offset"),
+                                                 "scratch_bytes_per_rank_to_remove": None if budget is None
+                                                 or size is None else budget + size}))
+    return out
+
+
 def analyze(bundle, model, *, batch_size: int = 16, trace=None) -> Analysis:
     """Causes on the predicted critical path (and, with a measured ``trace`` report, its slowest steps)."""
     pred = bundle.prediction
     path = pred.critical_path(bundle.executable)
-    causes = trace_causes(trace, bundle) + causes_on_path(bundle.executable, pred, model, path)
+    causes = trace_causes(trace, bundle) + storage_causes(bundle, path) + \
+        causes_on_path(bundle.executable, pred, model, path)
     stream = list(strategy_stream(causes, bundle.network))
     return Analysis(pred.t_pred_us, path, causes, _utilisation(bundle.executable, pred),
                     choose_batch(stream, batch_size))
