@@ -86,3 +86,14 @@ def test_partitions_of_a_three_level_topology():
     parts = partition_candidates(load_topology(req))
     assert ((0, 1, 2, 3), (4, 5, 6, 7)) in parts
     assert ((0, 1), (2, 3), (4, 5), (6, 7)) in parts
+
+
+def test_resynthesis_offers_the_other_groupings_of_the_hierarchy():
+    from vericcl_b200.tuning.resynthesis import branches, resynthesize_branch
+    from vericcl_b200.performance.initial import initial_cost_model
+    req = _request("allreduce", multinode_topology(2, 4, inter_gbps=25.0), 8, 8)
+    bundle = synthesize(req, timing=False)
+    alts = [b for b in branches(req, bundle) if b.plan_reason is not None]
+    assert alts and all(b.plan_reason != bundle.plan.reason for b in alts)
+    other = resynthesize_branch(req, alts[0], initial_cost_model(req))
+    assert other is not None and other.can_execute and other.plan.reason == alts[0].plan_reason
