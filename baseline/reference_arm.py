@@ -188,6 +188,33 @@ def bf16_to_f32(b: np.ndarray) -> np.ndarray:
 
 
 def run(args, clock_sampler_cls, metric: str, model: str) -> int:
+    """The arm, guarded: any failure prints the ``unavailable`` line (rank 0) instead of a traceback, and a
+    watchdog ends a process whose NCCL calls never return (VB_REF_DEADLINE_S, default 1200 s)."""
+    import threading
+    rank = int(os.environ.get("RANK", "0"))
+    deadline = float(os.environ.get("VB_REF_DEADLINE_S", "1200"))
+
+    def expire():
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the reference library did not finish within "
+                              "%.0f s (stopped by the arm's watchdog)" % deadline}), flush=True)
+        os._exit(0)
+
+    watchdog = threading.Timer(deadline, expire)
+    watchdog.daemon = True
+    watchdog.start()
+    try:
+        return _run(args, clock_sampler_cls, metric, model)
+    except Exception as error:          # noqa: BLE001 - reported as the arm's outcome
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "reference run failed: %s: %s"
+                              % (type(error).__name__, str(error)[:300])}), flush=True)
+        return 0
+    finally:
+        watchdog.cancel()
+
+
+def _run(args, clock_sampler_cls, metric: str, model: str) -> int:
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
