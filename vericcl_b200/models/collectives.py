@@ -306,7 +306,7 @@ class CollectiveEngine:
         regions = self._staging.get(key)
         if regions is None:
             blocks = -(-n // 128)
-            ctas = max(1, min(mod.fp8_allgather_max_ctas(), 2 * 148, -(-blocks // 16)))
+            ctas = max(1, min(mod.fp8_allgather_max_ctas(), 4 * 148, -(-blocks // 16)))
             # heap tensors are float-typed; the regions are raw bytes
             stage = self.comm.empty(mod.fp8_stage_bytes(n), torch.float16)          # 2 parities = 2 x bytes / 2
             flags = self.comm.empty(4 * ctas, torch.float16)                         # ctas x 8 bytes
