@@ -91,6 +91,34 @@ __device__ __forceinline__ void mc_st(char* p, const uint4& v) {
                "r"(v.w) : "memory");
 }
 
+// ---- TMA bulk staging (cp.async.bulk + mbarrier) ---------------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("{\n .reg .b64 state;\n mbarrier.arrive.expect_tx.shared::cta.b64 state, [%0], %1;\n}"
+               ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(done) : "r"(bar), "r"(parity) : "memory");
+  return done != 0;
+}
+
+// global (local or peer-mapped, 16-byte aligned) -> shared, completion counted on `bar`
+__device__ __forceinline__ void bulk_load(uint32_t dst_smem, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(dst_smem), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+
 template <int DT>
 struct VecT;
 
@@ -270,6 +298,113 @@ __device__ void mc_store_piece(char* mc_dst, const char* src, long long nvec) {
   }
 }
 
+__device__ void record_failure(const InterpArgs& a, int code, int block, int lane, int wait);
+
+// Staging state of one CTA: the mbarriers, the shared buffers and the running count of staged tiles (the same
+// in every thread; a tile's buffer is count % kBulkStages and its mbarrier phase parity (count / kBulkStages) & 1).
+struct BulkState {
+  unsigned char* buf;
+  uint32_t bar0;        // shared address of the first mbarrier (8 bytes apart)
+  unsigned int issued;  // tiles whose loads thread 0 has issued
+  unsigned int used;    // tiles consumed
+};
+
+// Waits (every thread) for tile `t`'s loads; false when the wait ran out of time or the launch is stopping.
+__device__ bool bulk_wait(const InterpArgs& a, BulkState& bs, unsigned int t) {
+  const uint32_t bar = bs.bar0 + 8u * (t % kBulkStages);
+  const uint32_t parity = (t / kBulkStages) & 1u;
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  unsigned int spins = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if ((++spins & 255u) == 0) {
+      if (ld_volatile_int(&a.control->status) != ST_OK || ld_volatile_int(&a.control->abort_request)) return false;
+      if (globaltimer() - t0 > a.timeout_ns) return false;
+    }
+  }
+  return true;
+}
+
+// After a failure: wait (bounded) for every tile whose loads are still in flight, so nothing lands in
+// shared memory after the CTA has moved on.
+__device__ void bulk_drain(const InterpArgs& a, BulkState& bs) {
+  for (unsigned int t = bs.used; t < bs.issued; ++t) {
+    const uint32_t bar = bs.bar0 + 8u * (t % kBulkStages);
+    const uint32_t parity = (t / kBulkStages) & 1u;
+    const unsigned long long t0 = globaltimer();
+    while (!mbar_try_wait(bar, parity))
+      if (globaltimer() - t0 > a.timeout_ns) break;
+  }
+  bs.used = bs.issued;
+}
+
+// dst[v] = scale? * op(src0[v], ..., src{K-1}[v]) over `bytes` bytes (a multiple of 16), the sources staged in
+// shared memory by TMA bulk copies, kBulkStages - 1 tiles ahead of the tile being combined.  Thread 0 issues
+// the copies; all threads combine and store.  Returns false (after draining) when a wait failed.
+template <int DT, int RED>
+__device__ bool move_bulk(char* dst, const char* const* src, int nsrc, long long bytes, bool do_scale, float scale,
+                          const InterpArgs& a, BulkState& bs) {
+  using V = VecT<DT>;
+  // bytes of one source per tile: the stage split evenly over the sources, in 1 KiB units
+  const long long tile = (long long)((kBulkStageBytes / nsrc) & ~1023);
+  const unsigned int tiles = (unsigned int)((bytes + tile - 1) / tile);
+  const unsigned int first = bs.issued;   // tile numbers of this call: first .. first + tiles - 1
+  auto issue = [&](unsigned int i) {      // thread 0 only
+    const unsigned int t = first + i;
+    const long long off = (long long)i * tile;
+    const uint32_t n = (uint32_t)(bytes - off < tile ? bytes - off : tile);
+    const uint32_t bar = bs.bar0 + 8u * (t % kBulkStages);
+    unsigned char* stage = bs.buf + (size_t)(t % kBulkStages) * kBulkStageBytes;
+    // the buffer was last read through the generic proxy; order those reads before the async-proxy writes
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_expect_tx(bar, n * (uint32_t)nsrc);
+    for (int k = 0; k < nsrc; ++k) bulk_load(smem_addr(stage + (size_t)k * tile), src[k] + off, n, bar);
+  };
+  if (threadIdx.x == 0)
+    for (unsigned int i = 0; i < tiles && i < (unsigned int)(kBulkStages - 1); ++i) issue(i);
+  bs.issued += tiles < (unsigned int)(kBulkStages - 1) ? tiles : (unsigned int)(kBulkStages - 1);
+  for (unsigned int i = 0; i < tiles; ++i) {
+    const unsigned int t = first + i;
+    if (i + kBulkStages - 1 < tiles) {
+      if (threadIdx.x == 0) issue(i + kBulkStages - 1);
+      ++bs.issued;
+    }
+    if (!__syncthreads_and(bulk_wait(a, bs, t))) {   // one decision for the whole CTA
+      // a wait ran out of time: record it, let the loads in flight land, stop
+      if (threadIdx.x == 0 && ld_volatile_int(&a.control->status) == ST_OK) record_failure(a, ST_TIMEOUT, -1, -1, -2);
+      bs.used = t;
+      bulk_drain(a, bs);
+      return false;
+    }
+    const unsigned char* stage = bs.buf + (size_t)(t % kBulkStages) * kBulkStageBytes;
+    const long long off = (long long)i * tile;
+    const long long n = bytes - off < tile ? bytes - off : tile;
+    char* out = dst + off;
+    for (long long v = threadIdx.x; v < n / 16; v += blockDim.x) {
+      uint4 r0 = *reinterpret_cast<const uint4*>(stage + v * 16);
+      if (nsrc == 1 && !do_scale) {
+        st_vec(out + v * 16, r0);
+        continue;
+      }
+      float acc[V::N], tmp[V::N];
+      V::unpack(r0, acc);
+      for (int k = 1; k < nsrc; ++k) {
+        V::unpack(*reinterpret_cast<const uint4*>(stage + (size_t)k * tile + v * 16), tmp);
+#pragma unroll
+        for (int e = 0; e < V::N; ++e) acc[e] = combine<RED>(acc[e], tmp[e]);
+      }
+      if (do_scale) {
+#pragma unroll
+        for (int e = 0; e < V::N; ++e) acc[e] *= scale;
+      }
+      st_vec(out + v * 16, V::pack(acc));
+    }
+    bs.used = t + 1;
+    __syncthreads();   // every thread is done with this buffer before it is refilled
+  }
+  return true;
+}
+
 // LEAN selects the register-lean unrolls (2 and 3 sources one vector deep, copies eight deep) that build
 // without spills.
 template <int DT, int RED, bool LEAN>
@@ -340,9 +475,9 @@ __device__ bool wait_events(const InterpArgs& a, const DevWait* w, int n, int it
   return __all_sync(0xffffffffu, ok);
 }
 
-template <int DT, int RED, bool LEAN>
+template <int DT, int RED, bool LEAN, bool BULK>
 __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long long base, int* s_stop,
-                        char* const* s_rank_base, const long long* s_buf_off) {
+                        char* const* s_rank_base, const long long* s_buf_off, BulkState& bs) {
   const DevBlock blk = a.blocks[block];
   const int esize = DT == DT_F32 ? 4 : 2;
   const unsigned long long stride = 2ull * (unsigned long long)blk.nsteps;
@@ -425,7 +560,15 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
           const int dr = (st.dst_rank >= 0 && st.dst_rank < a.nranks) ? st.dst_rank : a.rank;
           char* dst = s_rank_base[dr] + s_buf_off[st.dst_buf] + batch * a.batch_stride[st.dst_buf] +
                       ((long long)(st.dst_chunk + k) * a.chunk_elems + pr.lo) * esize;
-          move_piece<DT, RED, LEAN>(dst, s_src, st.nsrc, nvec, (st.flags & F_SCALE) != 0, a.scale);
+          if (BULK && nvec * 16 >= kBulkMinBytes && st.nsrc <= 16) {
+            if (!move_bulk<DT, RED>(dst, s_src, st.nsrc, nvec * 16, (st.flags & F_SCALE) != 0, a.scale, a, bs)) {
+              if (threadIdx.x == 0) *s_stop = 1;
+              __syncthreads();
+              return;
+            }
+          } else {
+            move_piece<DT, RED, LEAN>(dst, s_src, st.nsrc, nvec, (st.flags & F_SCALE) != 0, a.scale);
+          }
           if (dr != a.rank) mc_pending = true;   // remote stores: fenced at system scope before the done flag
           __syncthreads();
         }
@@ -474,15 +617,22 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
   }
 }
 
-// TL: record the launch timeline; LEAN: register-lean unrolls (see move_piece).
-template <int DT, int RED, bool TL = false, bool LEAN = false>
+// TL: record the launch timeline; LEAN: register-lean unrolls (see move_piece); BULK: copy and reduce steps
+// stage their sources in shared memory with TMA bulk copies (move_bulk), kBulkSmemBytes of dynamic shared memory.
+template <int DT, int RED, bool TL = false, bool LEAN = false, bool BULK = false>
 __global__ void __launch_bounds__(512, 1) interp_kernel(const InterpArgs a) {
   __shared__ unsigned long long s_base;
   __shared__ int s_stop;
   __shared__ char* s_rank_base[kMaxRanks];
   __shared__ long long s_buf_off[BUF_COUNT];
+  extern __shared__ __align__(1024) unsigned char s_dyn[];   // kBulkSmemBytes when a.bulk, else empty
   if (threadIdx.x < kMaxRanks) s_rank_base[threadIdx.x] = a.base[threadIdx.x];
   if (threadIdx.x < BUF_COUNT) s_buf_off[threadIdx.x] = a.buf_off[threadIdx.x];
+  BulkState bs{s_dyn, smem_addr(s_dyn + (size_t)kBulkStages * kBulkStageBytes), 0u, 0u};
+  if (BULK && threadIdx.x == 0) {
+    for (int i = 0; i < kBulkStages; ++i) mbar_init(bs.bar0 + 8u * i, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
   const int block = blockIdx.x / a.nlanes;
   const int lane = blockIdx.x % a.nlanes;
   if (threadIdx.x == 0) {
@@ -492,7 +642,9 @@ __global__ void __launch_bounds__(512, 1) interp_kernel(const InterpArgs a) {
     st_release_sys(flag_ptr(a, a.rank, a.start_slot), s_base + 1);
   }
   __syncthreads();
-  if (block < a.nblocks) run_cta<DT, RED, LEAN>(a, block, lane, s_base, &s_stop, s_rank_base, s_buf_off);
+  // staged instances keep the lean unrolls for the pieces below kBulkMinBytes (fewer registers beside move_bulk)
+  if (block < a.nblocks)
+    run_cta<DT, RED, LEAN || BULK, BULK>(a, block, lane, s_base, &s_stop, s_rank_base, s_buf_off, bs);
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
@@ -506,24 +658,46 @@ __global__ void __launch_bounds__(512, 1) interp_kernel(const InterpArgs a) {
   }
 }
 
+// Cooperative launch of one interpreter instance; with TMA staging the instance gets its dynamic shared memory.
+cudaError_t coop(const void* fn, dim3 grid, dim3 block, void** args, bool bulk, cudaStream_t stream) {
+  size_t smem = 0;
+  if (bulk) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kBulkSmemBytes);
+    if (e != cudaSuccess) return e;
+    smem = kBulkSmemBytes;
+  }
+  return cudaLaunchCooperativeKernel(fn, grid, block, args, smem, stream);
+}
+
 template <int DT>
 cudaError_t launch_red(const InterpArgs& a, cudaStream_t stream, int threads) {
   void* args[] = {const_cast<InterpArgs*>(&a)};
   dim3 grid(a.nblocks * a.nlanes), block(threads);
+  const bool b = a.bulk != 0;
+  if (b) {
+    // the staged instances: every reduction, no timeline, the lean unrolls do not apply
+    if (a.timeline) return cudaErrorInvalidValue;
+    switch (a.redop) {
+      case RED_PROD: return coop((void*)interp_kernel<DT, RED_PROD, false, false, true>, grid, block, args, b, stream);
+      case RED_MIN: return coop((void*)interp_kernel<DT, RED_MIN, false, false, true>, grid, block, args, b, stream);
+      case RED_MAX: return coop((void*)interp_kernel<DT, RED_MAX, false, false, true>, grid, block, args, b, stream);
+      default: return coop((void*)interp_kernel<DT, RED_SUM, false, false, true>, grid, block, args, b, stream);
+    }
+  }
   if (a.timeline || a.lean) {
     // the instrumented and the lean instances exist for sum (and average) reductions and copies only
     if (a.redop != RED_SUM) return cudaErrorInvalidValue;
     if (a.timeline && a.lean)
-      return cudaLaunchCooperativeKernel((void*)interp_kernel<DT, RED_SUM, true, true>, grid, block, args, 0, stream);
+      return coop((void*)interp_kernel<DT, RED_SUM, true, true>, grid, block, args, b, stream);
     if (a.timeline)
-      return cudaLaunchCooperativeKernel((void*)interp_kernel<DT, RED_SUM, true, false>, grid, block, args, 0, stream);
-    return cudaLaunchCooperativeKernel((void*)interp_kernel<DT, RED_SUM, false, true>, grid, block, args, 0, stream);
+      return coop((void*)interp_kernel<DT, RED_SUM, true, false>, grid, block, args, b, stream);
+    return coop((void*)interp_kernel<DT, RED_SUM, false, true>, grid, block, args, b, stream);
   }
   switch (a.redop) {
-    case RED_PROD: return cudaLaunchCooperativeKernel((void*)interp_kernel<DT, RED_PROD>, grid, block, args, 0, stream);
-    case RED_MIN: return cudaLaunchCooperativeKernel((void*)interp_kernel<DT, RED_MIN>, grid, block, args, 0, stream);
-    case RED_MAX: return cudaLaunchCooperativeKernel((void*)interp_kernel<DT, RED_MAX>, grid, block, args, 0, stream);
-    default: return cudaLaunchCooperativeKernel((void*)interp_kernel<DT, RED_SUM>, grid, block, args, 0, stream);
+    case RED_PROD: return coop((void*)interp_kernel<DT, RED_PROD>, grid, block, args, b, stream);
+    case RED_MIN: return coop((void*)interp_kernel<DT, RED_MIN>, grid, block, args, b, stream);
+    case RED_MAX: return coop((void*)interp_kernel<DT, RED_MAX>, grid, block, args, b, stream);
+    default: return coop((void*)interp_kernel<DT, RED_SUM>, grid, block, args, b, stream);
   }
 }
 
@@ -566,14 +740,20 @@ int interp_max_ctas(int threads) {
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   // the smallest residency over the instances a launch may pick (dtype, timeline, lean), so a cooperative
   // grid sized from it is resident whichever instance runs
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, interp_kernel<DT_BF16, RED_SUM>, threads, 0);
+  // sized for the staged (TMA) launches too, which add kBulkSmemBytes of dynamic shared memory
+  cudaFuncSetAttribute((const void*)interp_kernel<DT_BF16, RED_SUM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       kBulkSmemBytes);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, interp_kernel<DT_BF16, RED_SUM>, threads, kBulkSmemBytes);
   const void* others[] = {
       (const void*)interp_kernel<DT_F32, RED_SUM>, (const void*)interp_kernel<DT_BF16, RED_SUM, true, false>,
       (const void*)interp_kernel<DT_BF16, RED_SUM, false, true>, (const void*)interp_kernel<DT_F32, RED_SUM, false, true>,
-      (const void*)interp_kernel<DT_BF16, RED_SUM, true, true>};
+      (const void*)interp_kernel<DT_BF16, RED_SUM, true, true>, (const void*)interp_kernel<DT_BF16, RED_SUM, false, false, true>,
+      (const void*)interp_kernel<DT_F32, RED_SUM, false, false, true>};
   for (const void* fn : others) {
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, threads, 0) == cudaSuccess && n < per_sm) per_sm = n;
+    cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kBulkSmemBytes);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, threads, kBulkSmemBytes) == cudaSuccess && n < per_sm)
+      per_sm = n;
   }
   if (dev >= 0 && dev < 64) {
     cached_threads[dev] = threads;

@@ -56,7 +56,15 @@ struct InterpArgs {
   // finish), indexed by launch epoch modulo kTimelineSlots; nullptr disables it (separate kernel instance).
   unsigned long long* timeline;
   int lean;                          // 1: run the register-lean kernel instance (sum reductions and copies)
+  int bulk;                          // 1: copy and reduce steps stage their sources in shared memory with TMA
+                                     //    bulk copies (cp.async.bulk) instead of per-thread vector loads
 };
+
+// TMA staging of copy/reduce sources: kBulkStages buffers of kBulkStageBytes each, one mbarrier per buffer.
+constexpr int kBulkStages = 3;
+constexpr int kBulkStageBytes = 64 * 1024;
+constexpr int kBulkSmemBytes = kBulkStages * kBulkStageBytes + 128;
+constexpr long long kBulkMinBytes = 32 * 1024;   // smaller pieces keep the per-thread vector path
 
 constexpr int kTimelineSlots = 256;
 

@@ -126,9 +126,13 @@ def main():
         settings = dict(kv.split("=", 1) for kv in variant.split(",") if kv.strip())
         for k, v in settings.items():
             os.environ["VERICCL_" + k.strip()] = v.strip()
+        saved = (comm.lean, comm.bulk)
         if "LEAN" in settings:
             comm.lean = settings["LEAN"] not in ("0", "")
+        if "BULK" in settings:
+            comm.bulk = settings["BULK"] not in ("0", "")
         run_sizes(args, variant, comm, eng, world, rank, dtype, esize, timed, check, host_us, results)
+        comm.lean, comm.bulk = saved
         for k in settings:
             os.environ.pop("VERICCL_" + k.strip(), None)
     if rank == 0:

@@ -323,3 +323,48 @@ def test_push_allgather_kernel_single_rank(comm):
         assert torch.equal(out, x)
     comm.free(out)
     comm.free(flags)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("op", ["sum", "prod", "min", "max"])
+@pytest.mark.parametrize("k", [1, 2, 3, 5, 8, 12])
+def test_tma_staged_reduce_matches_fp32_reference(comm, dtype, op, k):
+    """The TMA-staged instance: sources reach shared memory by cp.async.bulk (several tiles per piece, a partial
+    last tile), are combined in fp32 and stored; same results as the fp32 reference."""
+    n = (1 << 20) + 96
+    gen = torch.Generator(device="cuda").manual_seed(7 * k + REDOPS[op])
+    if op == "prod":
+        srcs = (0.9 + 0.2 * torch.rand(k, n, device="cuda", generator=gen)).to(dtype)
+    else:
+        srcs = torch.randn(k, n, device="cuda", generator=gen).to(dtype)
+    dst = torch.full((n,), float("nan"), device="cuda", dtype=dtype)
+    scale = 0.37 if op == "sum" else 1.0
+    ws = comm._mod.local_reduce(dst, srcs, REDOPS[op], scale, op == "sum", 4, 2, False, True)
+    torch.cuda.synchronize()
+    assert int(ws[12:16].view(torch.int32).item()) == 0
+    ref = _reference(srcs, op) * scale
+    tol = {torch.float32: 1e-5, torch.bfloat16: 1e-2, torch.float16: 2e-3}[dtype]
+    assert torch.allclose(dst.float(), ref, atol=tol * max(1.0, k ** 0.5), rtol=tol)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_tma_staged_single_rank_allreduce_through_the_engine(comm, dtype):
+    from vericcl_b200.synthesis import schedule_xml
+    dname = str(dtype).split(".")[-1]
+    plan = comm.compile(schedule_xml("allreduce", 1, 1, inplace=False, datatype=dname), nlanes=16, niters=2)
+    n = 1 << 22
+    x, y = comm.empty(n, dtype), comm.empty(n, dtype)
+    x.copy_(torch.randn(n, device="cuda"))
+    comm.bulk = True
+    try:
+        for _ in range(2):
+            y.fill_(float("nan"))
+            comm.run(plan, x, y, scale=0.25)
+            torch.cuda.synchronize()
+            comm.check_status()
+            tol = 1e-6 if dtype == torch.float32 else 1e-2
+            assert torch.allclose(y.float(), x.float() * 0.25, atol=tol, rtol=tol)
+    finally:
+        comm.bulk = False
+        comm.free(x)
+        comm.free(y)

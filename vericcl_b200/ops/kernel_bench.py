@@ -39,6 +39,7 @@ def main(argv=None) -> int:
     ap.add_argument("--k", type=int, default=4, help="sources of the local reduce")
     ap.add_argument("--dtype", default="bfloat16", choices=sorted(DTYPES))
     ap.add_argument("--lanes", type=int, default=0, help="CTAs of the local reduce (0: every SM)")
+    ap.add_argument("--bulk", action="store_true", help="local reduce: the TMA-staged kernel instance")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
     args = ap.parse_args(argv)
@@ -56,9 +57,9 @@ def main(argv=None) -> int:
         dst = torch.empty(n, device="cuda", dtype=dtype)
         lanes = args.lanes or min(148, mod.max_ctas(512))
         keep = []
-        fn = lambda: keep.append(mod.local_reduce(dst, srcs, 0, 0.5, True, lanes, 1, False))   # noqa: E731
+        fn = lambda: keep.append(mod.local_reduce(dst, srcs, 0, 0.5, True, lanes, 1, False, args.bulk))  # noqa: E731
         nbytes = (args.k + 1) * n * esize
-        label = "interp_kernel local reduce K=%d" % args.k
+        label = "interp_kernel local reduce K=%d%s" % (args.k, " (TMA-staged)" if args.bulk else "")
     elif args.kernel == "fp8_allgather":
         eng = CollectiveEngine(comm)
         x = torch.randn(n, device="cuda").to(dtype)

@@ -112,6 +112,8 @@ class Communicator:
         # Sum/avg launches use the register-lean interpreter instance when VERICCL_LEAN=1, and by default on a
         # single rank, where every step is a one-source copy (its copies keep eight vectors in flight per thread)
         self.lean = _env_flag("VERICCL_LEAN", self.world == 1)
+        # copy and reduce steps stage their sources in shared memory with TMA bulk copies (VERICCL_BULK=1)
+        self.bulk = _env_flag("VERICCL_BULK", False)
         self._lock = threading.Lock()
         self._closed = False
 
@@ -314,7 +316,7 @@ class Communicator:
             return
         tl_ptr = 0 if timeline is None else timeline.data_ptr()
         bound_key = (id(plan), inp.data_ptr(), out.data_ptr(), count_per_rank, inp.numel(), out.numel(), inp.dtype,
-                     op, scale, nbatch, in_stride, out_stride, tl_ptr)
+                     op, scale, nbatch, in_stride, out_stride, tl_ptr, self.bulk, self.lean)
         if trace is None:
             fast = self._bound.get(bound_key)
             if fast is not None:
@@ -358,9 +360,10 @@ class Communicator:
                                          or not timeline.is_cuda):
                 raise RuntimeFailure("timeline buffer needs %d int64 elements on the device" % (2 * TIMELINE_SLOTS))
             lean = self.lean and REDOPS[op] == 0
+            bulk = self.bulk and not tl_ptr
             bound = plan.device_plan.bind(self.heap, in_off, out_off, scr_off, count, DTYPE_CODES[inp.dtype],
                                           REDOPS[op], float(factor), self.timeout_s, 512, nbatch, strides, tl_ptr,
-                                          lean)
+                                          lean, bulk)
             self._bound[bound_key] = bound
             bound.launch(stream.cuda_stream)
             return
