@@ -19,6 +19,11 @@ scale pass (an HBM read and write), labelled as such.  ``nvlink`` gives the
 bytes each GPU really sends per direction on the path the plan takes and
 their fraction of 900 GB/s (nominal) and 770 GB/s (measured peer copy).
 
+``cta_budget`` times the same sync restricted to 16, 32 and 64 CTAs per GPU
+(``--cta-budgets``): the interpreter otherwise takes one CTA on every SM, and
+in data-parallel training the SMs it leaves free are what the overlapping
+backward pass gets.
+
 ``--impl reference`` runs the reference's own MSCCL/NCCL 2.12.12 build instead
 (``baseline/reference_arm.py``), without PyTorch or this package.
 """
@@ -53,6 +58,8 @@ def parse():
     ap.add_argument("--no-nccl", action="store_true")
     ap.add_argument("--per-bucket", action="store_true", help="one launch per bucket instead of one batched launch")
     ap.add_argument("--slices", type=int, default=None, help="slices per rank of the synthesized schedule")
+    ap.add_argument("--cta-budgets", default="16,32,64",
+                    help="also time the sync restricted to these CTAs per GPU (comma list; empty: skip)")
     return ap.parse_args()
 
 
@@ -242,6 +249,22 @@ def main():
                  "busbw_per_gpu_gbs": round(bus / (oms * 1e-3) / 1e9, 2),
                  "launches_per_step": ar.launches_per_sync if alt else ar.buckets}
 
+    # the same sync on a CTA budget: the SMs left over are what overlapping backward compute gets
+    budgets = None
+    if args.cta_budgets:
+        budgets = {"full": {"ctas": ar.ctas_of(ar.plan), "ms_per_step": round(ms, 4),
+                            "busbw_per_gpu_gbs": round(busbw, 2)}}
+        for want in [int(v) for v in args.cta_budgets.split(",") if v.strip()]:
+            bplan = ar.plan_with_budget(want)
+            for _ in range(2):
+                ar.sync(stream, batched=batched, plan=bplan)
+            bms = max_over_ranks(timed(lambda: ar.sync(stream, batched=batched, plan=bplan),
+                                       max(2, args.steps // 4), stream, barrier))
+            comm.check_status()
+            budgets[str(want)] = {"ctas": ar.ctas_of(bplan), "sms_free": max(0, 148 - ar.ctas_of(bplan)),
+                                  "ms_per_step": round(bms, 4), "busbw_per_gpu_gbs": round(bus / (bms * 1e-3) / 1e9, 2)}
+            del bplan
+
     nccl = None
     if world > 1 and not args.no_nccl:
         premul = dist._make_nccl_premul_sum(args.scale)
@@ -317,7 +340,7 @@ def main():
                 "busbw_per_gpu_gbs": round(busbw, 2),
                 "busbw_note": ("one GPU: no inter-GPU traffic; bytes counted once, i.e. the in-place scale pass "
                                "rate (HBM read + write)") if world == 1 else "nccl-tests bus bandwidth, 2(P-1)/P",
-                "nvlink": nvlink, "other_launch_mode": other,
+                "nvlink": nvlink, "other_launch_mode": other, "cta_budget": budgets,
                 "check": {"first_last_bucket_max_err": err, "ok": bool(check_ok),
                           "reference": "fp32 sum over ranks (torch) x scale"},
                 "clocks": clock_info, "e2e": e2e, "gpu_launches": launches, "nccl": nccl}

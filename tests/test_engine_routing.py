@@ -54,3 +54,13 @@ def test_twoshot_window_is_opt_in():
     assert not on.use_twoshot("allgather", 1 << 21, torch.bfloat16)
     plan = on.plan("allreduce", 1 << 21, torch.bfloat16, inplace=True)
     assert plan.collective == "allreduce_twoshot" and comm.requests[-1] == ("allreduce_twoshot", 8 << 20)
+
+
+def test_cta_budget_caps_the_interpreter_grid():
+    """A budget of B CTAs gives at most max(1, B // blocks) lanes per schedule block; no budget fills the GPU."""
+    full = CollectiveEngine(_Comm(8))
+    assert full.geometry(8, 64 << 20)[0] == 148 // 8
+    small = CollectiveEngine(_Comm(8), cta_budget=32)
+    assert small.geometry(8, 64 << 20)[0] == 4
+    assert small.geometry(64, 64 << 20)[0] == 1            # below the block count: one lane per block
+    assert CollectiveEngine(_Comm(8), cta_budget=4096).geometry(8, 64 << 20)[0] == 148 // 8

@@ -38,8 +38,11 @@ class CollectiveEngine:
     def __init__(self, comm, *, method: str = "hierarchy", slices_per_rank: int | None = None,
                  max_lanes: int | None = None, oneshot_max_bytes: int | None = None,
                  twoshot_max_bytes: int | None = None, ag_nvls_max_bytes: int | None = None,
-                 tuning: dict | None = None):
+                 tuning: dict | None = None, cta_budget: int | None = None):
         self.comm = comm
+        # interpreter CTAs per GPU this engine may launch (None: every co-resident CTA); the rest of the
+        # SMs stay free for compute that overlaps the collective (a data-parallel backward pass)
+        self.cta_budget = cta_budget
         self.method = method
         self.slices_per_rank = slices_per_rank
         explicit = {"oneshot_max_bytes": oneshot_max_bytes, "twoshot_max_bytes": twoshot_max_bytes,
@@ -68,7 +71,8 @@ class CollectiveEngine:
 
     # -- geometry ---------------------------------------------------------------
     def geometry(self, plan_blocks: int, chunk_bytes: int):
-        lanes = max(1, min(self.max_lanes, 256, self._max_ctas // max(1, plan_blocks)))
+        cap = self._max_ctas if self.cta_budget is None else max(1, min(self._max_ctas, self.cta_budget))
+        lanes = max(1, min(self.max_lanes, 256, cap // max(1, plan_blocks)))
         lanes = max(1, min(lanes, chunk_bytes // PIECE_MIN_BYTES))
         iters = max(1, min(MAX_ITERS, chunk_bytes // (lanes * PIECE_TARGET_BYTES)))
         if os.environ.get("VERICCL_LANES"):

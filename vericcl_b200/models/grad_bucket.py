@@ -19,7 +19,7 @@ DEFAULT_BUCKET_BYTES = 25 * 1024 * 1024
 
 class GradBucketAllReduce:
     def __init__(self, comm, numel: int, *, dtype=torch.bfloat16, bucket_bytes: int = DEFAULT_BUCKET_BYTES,
-                 scale: float | None = None, slices_per_rank: int | None = None):
+                 scale: float | None = None, slices_per_rank: int | None = None, cta_budget: int | None = None):
         self.comm = comm
         self.dtype = dtype
         self.numel = numel
@@ -32,8 +32,24 @@ class GradBucketAllReduce:
         self.scale = 1.0 / world if scale is None else scale
         self.grads = comm.empty(self.buckets * self.bucket_elems, dtype)
         self.grads[numel:].zero_()
-        self.engine = CollectiveEngine(comm, slices_per_rank=slices)
+        self.engine = CollectiveEngine(comm, slices_per_rank=slices, cta_budget=cta_budget)
         self.plan = self.engine.plan("allreduce", self.bucket_elems, dtype, inplace=True)
+
+    def plan_with_budget(self, ctas: int):
+        """The bucket plan launched on about ``ctas`` CTAs per GPU, leaving the other SMs to overlapping compute.
+
+        The grid is (thread blocks of the schedule) × lanes, so a budget below the
+        schedule's block count still launches one lane per block.
+        """
+        eng = CollectiveEngine(self.comm, slices_per_rank=self.engine.slices_per_rank, cta_budget=ctas)
+        return eng.plan("allreduce", self.bucket_elems, self.dtype, inplace=True)
+
+    @staticmethod
+    def ctas_of(plan) -> int:
+        """CTAs per GPU one launch of ``plan`` occupies (one-shot plans report their own grid)."""
+        if plan.device_plan is None:
+            return int(getattr(plan, "nlanes", 0) or 0)
+        return plan.device_plan.nblocks * plan.nlanes
 
     @property
     def flat(self) -> torch.Tensor:
@@ -43,22 +59,24 @@ class GradBucketAllReduce:
     def bucket(self, i: int) -> torch.Tensor:
         return self.grads[i * self.bucket_elems:(i + 1) * self.bucket_elems]
 
-    def sync(self, stream=None, *, batched: bool = True) -> None:
+    def sync(self, stream=None, *, batched: bool = True, plan=None) -> None:
         """AllReduce every bucket in place with the fused scale (asynchronous on ``stream``).
 
         By default all buckets run in one persistent launch (the bucket index is an
         outer pipeline dimension of the replayed schedule); ``batched=False`` issues one
         launch per bucket.  Buckets small enough for the one-shot path are launched one by
         one (that kernel has no batched form; each launch is a few microseconds).
+        ``plan`` replaces the default bucket plan (for example one from :meth:`plan_with_budget`).
         """
-        if batched and self.plan.kind != "oneshot":
+        plan = plan or self.plan
+        if batched and plan.kind != "oneshot":
             b = self.bucket(0)
-            self.comm.run(self.plan, b, b, op="sum", scale=self.scale, stream=stream, nbatch=self.buckets,
+            self.comm.run(plan, b, b, op="sum", scale=self.scale, stream=stream, nbatch=self.buckets,
                           in_stride=self.bucket_elems, out_stride=self.bucket_elems)
             return
         for i in range(self.buckets):
             b = self.bucket(i)
-            self.comm.run(self.plan, b, b, op="sum", scale=self.scale, stream=stream)
+            self.comm.run(plan, b, b, op="sum", scale=self.scale, stream=stream)
 
     @property
     def launches_per_sync(self) -> int:
