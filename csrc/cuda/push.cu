@@ -16,7 +16,11 @@
 //  2. CTA c owns bytes [c·B/C, (c+1)·B/C) of the chunk (16-byte units): it
 //     copies them into its own output part, then for every peer q (rank + 1,
 //     rank + 2, ...) waits until q's start flag reaches seq + 1 and stores them
-//     into part `rank` of q's output.
+//     into part `rank` of q's output.  In fan-out mode the CTA first waits for
+//     every peer's start flag, then reads each vector of its range once and
+//     stores it into every rank's output (own first, then rank + 1, ...): one
+//     HBM read per byte instead of one per peer, and all of the GPU's links
+//     busy from the first vector on.
 //  3. Each thread fences its stores at system scope; after a CTA barrier,
 //     thread 0 publishes this CTA's done flag = seq + 1 with st.release.sys.
 //  4. CTA c then waits until the done flag of CTA c on every peer reaches
@@ -83,6 +87,28 @@ __device__ __forceinline__ void copy_range(char* dst, const char* src, long long
   }
 }
 
+// Fan-out: each vector of [0, nvec) read once and stored into part `rank` of every rank's output.
+__device__ __forceinline__ void fanout_range(const PushAgArgs& a, long long part, const char* src, long long nvec) {
+  const long long stride = (long long)kPushThreads * kPushUnroll;
+  for (long long v0 = threadIdx.x; v0 < nvec; v0 += stride) {
+    uint4 r[kPushUnroll];
+#pragma unroll
+    for (int u = 0; u < kPushUnroll; ++u) {
+      const long long v = v0 + (long long)u * kPushThreads;
+      if (v < nvec) r[u] = push_ld(src + v * 16);
+    }
+    for (int step = 0; step < a.nranks; ++step) {
+      const int q = a.rank + step < a.nranks ? a.rank + step : a.rank + step - a.nranks;
+      char* dst = a.base[q] + a.out_off + part;
+#pragma unroll
+      for (int u = 0; u < kPushUnroll; ++u) {
+        const long long v = v0 + (long long)u * kPushThreads;
+        if (v < nvec) push_st(dst + v * 16, r[u]);
+      }
+    }
+  }
+}
+
 __device__ void push_fail(const PushAgArgs& a, int peer, int what) {
   if (atomicCAS(&a.control->status, ST_OK, ST_TIMEOUT) == ST_OK) {
     a.control->detail[0] = a.rank;
@@ -126,16 +152,31 @@ __global__ void __launch_bounds__(kPushThreads, 1) push_allgather_kernel(const P
   const long long v0 = nvec * blockIdx.x / a.ctas, v1 = nvec * (blockIdx.x + 1) / a.ctas;
   const char* src = static_cast<const char*>(a.in) + v0 * 16;
   const long long part = (long long)a.rank * a.bytes + v0 * 16;
-  copy_range(a.base[a.rank] + a.out_off + part, src, v1 - v0);
-  for (int step = 1; step < a.nranks; ++step) {
-    const int q = (a.rank + step) % a.nranks;
+  if (a.fanout) {
     if (threadIdx.x == 0) {
-      const unsigned long long* start = reinterpret_cast<const unsigned long long*>(a.base[q] + a.flag_off);
-      if (!push_wait(a, start, seq + 1, q, 0)) s_ok = 0;
+      for (int step = 1; step < a.nranks; ++step) {
+        const int q = (a.rank + step) % a.nranks;
+        const unsigned long long* start = reinterpret_cast<const unsigned long long*>(a.base[q] + a.flag_off);
+        if (!push_wait(a, start, seq + 1, q, 0)) {
+          s_ok = 0;
+          break;
+        }
+      }
     }
     __syncthreads();
-    if (!s_ok) break;
-    copy_range(a.base[q] + a.out_off + part, src, v1 - v0);
+    if (s_ok) fanout_range(a, part, src, v1 - v0);
+  } else {
+    copy_range(a.base[a.rank] + a.out_off + part, src, v1 - v0);
+    for (int step = 1; step < a.nranks; ++step) {
+      const int q = (a.rank + step) % a.nranks;
+      if (threadIdx.x == 0) {
+        const unsigned long long* start = reinterpret_cast<const unsigned long long*>(a.base[q] + a.flag_off);
+        if (!push_wait(a, start, seq + 1, q, 0)) s_ok = 0;
+      }
+      __syncthreads();
+      if (!s_ok) break;
+      copy_range(a.base[q] + a.out_off + part, src, v1 - v0);
+    }
   }
   // every thread's remote stores reach their targets before this CTA's done flag does
   asm volatile("fence.acq_rel.sys;" ::: "memory");

@@ -144,6 +144,7 @@ struct PushAgArgs {
   long long bytes;           // bytes per rank (multiple of 16)
   long long flag_off;        // heap offset of the flags: [0] start flag, [1 + c] done flag of CTA c
   int rank, nranks, ctas;
+  int fanout;                // 0: one peer after another (re-reading the chunk); 1: each loaded vector to every rank
   Control* control;
   unsigned long long timeout_ns;
 };

@@ -359,7 +359,7 @@ PYBIND11_MODULE(_vbcuda, m) {
   m.def("push_allgather_max_ctas", []() { return push_allgather_max_ctas(); });
   // Push AllGather: `inp` (bytes per rank, local device memory) into the heap output at out_off on every rank.
   m.def("push_allgather", [](Heap& heap, uint64_t in_ptr, size_t out_off, int64_t bytes, size_t flag_off, int ctas,
-                             double timeout_s) {
+                             double timeout_s, bool fanout) {
     SymHeap& h = heap.get();
     TORCH_CHECK(bytes > 0 && bytes % 16 == 0, "push AllGather needs a positive multiple of 16 bytes per rank");
     TORCH_CHECK(out_off >= kReservedBytes && flag_off >= kReservedBytes, "region overlaps the control block");
@@ -374,11 +374,12 @@ PYBIND11_MODULE(_vbcuda, m) {
     a.rank = h.rank();
     a.nranks = h.nranks();
     a.ctas = ctas;
+    a.fanout = fanout ? 1 : 0;
     a.control = heap.control();
     a.timeout_ns = (unsigned long long)(timeout_s * 1e9);
     cuda_check(launch_push_allgather(a, at::cuda::getCurrentCUDAStream().stream()), "push AllGather launch");
   }, py::arg("heap"), py::arg("in_ptr"), py::arg("out_off"), py::arg("bytes"), py::arg("flag_off"), py::arg("ctas"),
-     py::arg("timeout_s") = 10.0);
+     py::arg("timeout_s") = 10.0, py::arg("fanout") = false);
   m.def("fp8_stage_bytes", [](int64_t n) { return fp8_stage_bytes(n); });
   m.def("fp8_allgather_max_ctas", []() { return fp8_allgather_max_ctas(); });
   // Fused block-scaled FP8 AllGather over the heap's peer mappings: `in` (n elements) and `out`

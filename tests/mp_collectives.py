@@ -238,7 +238,9 @@ def main():
     # push AllGather (every rank stores into every peer's heap output), three calls in a row per size
     push_eng = CollectiveEngine(comm)
     push_eng.ag_push_min_bytes = 0
-    for dt, n in ((torch.float32, 1 << 16), (torch.bfloat16, (1 << 16) + 8), (torch.float16, 24)):
+    for dt, n, fanout in ((torch.float32, 1 << 16, False), (torch.bfloat16, (1 << 16) + 8, False),
+                          (torch.float16, 24, False), (torch.float32, 1 << 16, True), (torch.bfloat16, 4104, True)):
+        push_eng.ag_push_fanout = fanout
         x = inputs_for(rank, n, dt, 777).cuda()
         ref = torch.cat([inputs_for(r, n, dt, 777) for r in range(world)]).cuda()
         out = comm.empty(n * world, dt)
@@ -253,7 +255,7 @@ def main():
             failures += 0 if ok else 1
             if rank == 0 or not ok:
                 print(json.dumps({"rank": rank, "coll": "allgather", "path": "push", "dtype": str(dt), "n": n,
-                                  "call": call, "ok": ok}), flush=True)
+                                  "fanout": fanout, "call": call, "ok": ok}), flush=True)
         comm.free(out)
     # block-scaled FP8 AllGather through the engine: the fused kernel (three calls in a row, so both staging
     # parities are reused) against the three-pass path and against the fp64 inputs

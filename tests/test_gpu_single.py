@@ -315,9 +315,10 @@ def test_push_allgather_kernel_single_rank(comm):
     x = torch.randn(4096 * 3 + 4, device="cuda")
     out = comm.empty(x.numel())
     before = comm.heap.status()
-    for _ in range(2):
+    for fanout in (False, False, True, True):
         out.zero_()
-        mod.push_allgather(comm.heap, x.data_ptr(), comm.offset_of(out), x.numel() * 4, comm.offset_of(flags), ctas)
+        mod.push_allgather(comm.heap, x.data_ptr(), comm.offset_of(out), x.numel() * 4, comm.offset_of(flags), ctas,
+                           10.0, fanout)
         torch.cuda.synchronize()
         comm.check_status()
         assert torch.equal(out, x)

@@ -58,6 +58,7 @@ class CollectiveEngine:
         self.twoshot_max_bytes = twoshot_max_bytes
         self.ag_nvls_max_bytes = AG_NVLS_MAX_BYTES if ag_nvls_max_bytes is None else ag_nvls_max_bytes
         self.ag_push_min_bytes = None      # push AllGather threshold (None: off); VERICCL_AG_PUSH_MIN overrides
+        self.ag_push_fanout = False        # push kernel stores each loaded vector to every rank; VERICCL_AG_PUSH_FANOUT
         self.push_collectives = frozenset()   # interpreter collectives compiled with push steps
         if tuning is not None:
             # thresholds measured on this machine (vericcl_b200.models.tuner); explicit arguments still win
@@ -228,8 +229,10 @@ class CollectiveEngine:
             self.comm.barrier()
             self._staging["push-flags"] = flags
         region, ctas = flags
+        env = os.environ.get("VERICCL_AG_PUSH_FANOUT")
+        fanout = self.ag_push_fanout if env is None else env not in ("0", "")
         mod.push_allgather(self.comm.heap, inp.data_ptr(), self.comm.offset_of(out), inp.numel() * inp.element_size(),
-                           self.comm.offset_of(region), ctas, self.comm.timeout_s)
+                           self.comm.offset_of(region), ctas, self.comm.timeout_s, fanout)
 
     def all_gather(self, inp: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         world = self.comm.world

@@ -40,6 +40,7 @@ def main(argv=None) -> int:
     ap.add_argument("--dtype", default="bfloat16", choices=sorted(DTYPES))
     ap.add_argument("--lanes", type=int, default=0, help="CTAs of the local reduce (0: every SM)")
     ap.add_argument("--bulk", action="store_true", help="local reduce: the TMA-staged kernel instance")
+    ap.add_argument("--fanout", action="store_true", help="push AllGather: the fan-out mode")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
     args = ap.parse_args(argv)
@@ -75,9 +76,9 @@ def main(argv=None) -> int:
         x = torch.randn(n, device="cuda").to(dtype)
         out = comm.empty(n, dtype)
         fn = lambda: mod.push_allgather(comm.heap, x.data_ptr(), comm.offset_of(out), n * esize,   # noqa: E731
-                                        comm.offset_of(flags), ctas)
+                                        comm.offset_of(flags), ctas, 10.0, args.fanout)
         nbytes = 2 * n * esize
-        label = "push_allgather_kernel (one rank: own part copy)"
+        label = "push_allgather_kernel (one rank: own part copy%s)" % (", fan-out" if args.fanout else "")
     for _ in range(args.warmup):
         fn()
     torch.cuda.synchronize()
