@@ -119,6 +119,23 @@ __device__ __forceinline__ void bulk_load(uint32_t dst_smem, const void* src, ui
                ::"r"(dst_smem), "l"(src), "r"(bytes), "r"(bar) : "memory");
 }
 
+// shared -> this GPU's global memory (16-byte aligned, a multiple of 16 bytes), one bulk group per call
+__device__ __forceinline__ void bulk_store(void* dst, uint32_t src_smem, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n"
+               "cp.async.bulk.commit_group;" ::"l"(dst), "r"(src_smem), "r"(bytes) : "memory");
+}
+
+// the issuing thread's bulk stores have read their shared-memory sources
+__device__ __forceinline__ void bulk_store_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+// the issuing thread's bulk stores are complete, and ordered before its later generic-proxy accesses
+__device__ __forceinline__ void bulk_store_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;\n"
+               "fence.proxy.async.global;" ::: "memory");
+}
+
 template <int DT>
 struct VecT;
 
@@ -340,10 +357,13 @@ __device__ void bulk_drain(const InterpArgs& a, BulkState& bs) {
 
 // dst[v] = scale? * op(src0[v], ..., src{K-1}[v]) over `bytes` bytes (a multiple of 16), the sources staged in
 // shared memory by TMA bulk copies, kBulkStages - 1 tiles ahead of the tile being combined.  Thread 0 issues
-// the copies; all threads combine and store.  Returns false (after draining) when a wait failed.
+// the copies; all threads combine and store.  A plain copy into this GPU's memory (`tma_store`: one source, no
+// scale, local destination) leaves the store to TMA as well: thread 0 writes each staged tile back with a bulk
+// store, and waits for those stores to have read a buffer before it refills it and for all of them to have
+// completed before it returns.  Returns false (after draining) when a wait failed.
 template <int DT, int RED>
 __device__ bool move_bulk(char* dst, const char* const* src, int nsrc, long long bytes, bool do_scale, float scale,
-                          const InterpArgs& a, BulkState& bs) {
+                          const InterpArgs& a, BulkState& bs, bool tma_store) {
   using V = VecT<DT>;
   // bytes of one source per tile: the stage split evenly over the sources, in 1 KiB units
   const long long tile = (long long)((kBulkStageBytes / nsrc) & ~1023);
@@ -355,7 +375,9 @@ __device__ bool move_bulk(char* dst, const char* const* src, int nsrc, long long
     const uint32_t n = (uint32_t)(bytes - off < tile ? bytes - off : tile);
     const uint32_t bar = bs.bar0 + 8u * (t % kBulkStages);
     unsigned char* stage = bs.buf + (size_t)(t % kBulkStages) * kBulkStageBytes;
-    // the buffer was last read through the generic proxy; order those reads before the async-proxy writes
+    // the buffer was last read by a bulk store (copy mode) or through the generic proxy; either way those
+    // reads come before the async-proxy writes that refill it
+    if (tma_store) bulk_store_wait_read();
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     mbar_expect_tx(bar, n * (uint32_t)nsrc);
     for (int k = 0; k < nsrc; ++k) bulk_load(smem_addr(stage + (size_t)k * tile), src[k] + off, n, bar);
@@ -372,6 +394,7 @@ __device__ bool move_bulk(char* dst, const char* const* src, int nsrc, long long
     if (!__syncthreads_and(bulk_wait(a, bs, t))) {   // one decision for the whole CTA
       // a wait ran out of time: record it, let the loads in flight land, stop
       if (threadIdx.x == 0 && ld_volatile_int(&a.control->status) == ST_OK) record_failure(a, ST_TIMEOUT, -1, -1, -2);
+      if (tma_store && threadIdx.x == 0) bulk_store_wait_all();
       bs.used = t;
       bulk_drain(a, bs);
       return false;
@@ -380,6 +403,14 @@ __device__ bool move_bulk(char* dst, const char* const* src, int nsrc, long long
     const long long off = (long long)i * tile;
     const long long n = bytes - off < tile ? bytes - off : tile;
     char* out = dst + off;
+    if (tma_store) {
+      if (threadIdx.x == 0) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        bulk_store(out, smem_addr(stage), (uint32_t)n);
+      }
+      bs.used = t + 1;
+      continue;   // no thread touches the buffer; thread 0 alone orders its reuse
+    }
     for (long long v = threadIdx.x; v < n / 16; v += blockDim.x) {
       uint4 r0 = *reinterpret_cast<const uint4*>(stage + v * 16);
       if (nsrc == 1 && !do_scale) {
@@ -402,6 +433,7 @@ __device__ bool move_bulk(char* dst, const char* const* src, int nsrc, long long
     bs.used = t + 1;
     __syncthreads();   // every thread is done with this buffer before it is refilled
   }
+  if (tma_store && threadIdx.x == 0) bulk_store_wait_all();
   return true;
 }
 
@@ -561,7 +593,9 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
           char* dst = s_rank_base[dr] + s_buf_off[st.dst_buf] + batch * a.batch_stride[st.dst_buf] +
                       ((long long)(st.dst_chunk + k) * a.chunk_elems + pr.lo) * esize;
           if (BULK && nvec * 16 >= kBulkMinBytes && st.nsrc <= 16) {
-            if (!move_bulk<DT, RED>(dst, s_src, st.nsrc, nvec * 16, (st.flags & F_SCALE) != 0, a.scale, a, bs)) {
+            const bool scaled = (st.flags & F_SCALE) != 0;
+            const bool tma_store = (a.bulk & 2) != 0 && st.nsrc == 1 && !scaled && dr == a.rank;
+            if (!move_bulk<DT, RED>(dst, s_src, st.nsrc, nvec * 16, scaled, a.scale, a, bs, tma_store)) {
               if (threadIdx.x == 0) *s_stop = 1;
               __syncthreads();
               return;

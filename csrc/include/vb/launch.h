@@ -56,8 +56,9 @@ struct InterpArgs {
   // finish), indexed by launch epoch modulo kTimelineSlots; nullptr disables it (separate kernel instance).
   unsigned long long* timeline;
   int lean;                          // 1: run the register-lean kernel instance (sum reductions and copies)
-  int bulk;                          // 1: copy and reduce steps stage their sources in shared memory with TMA
-                                     //    bulk copies (cp.async.bulk) instead of per-thread vector loads
+  int bulk;                          // bit 0: copy and reduce steps stage their sources in shared memory with TMA
+                                     //    bulk copies (cp.async.bulk) instead of per-thread vector loads;
+                                     // bit 1: staged plain copies into local memory are also written back by TMA
 };
 
 // TMA staging of copy/reduce sources: kBulkStages buffers of kBulkStageBytes each, one mbarrier per buffer.

@@ -424,20 +424,20 @@ PYBIND11_MODULE(_vbcuda, m) {
            py::arg("trace_stride") = 0)
       .def("bind", [](DevicePlan& p, Heap& heap, size_t in_off, size_t out_off, size_t scr_off, int64_t count, int dtype,
                       int redop, float scale, double timeout_s, int threads, int nbatch,
-                      std::vector<long long> strides, uint64_t timeline_ptr, bool lean, bool bulk) {
+                      std::vector<long long> strides, uint64_t timeline_ptr, bool lean, int bulk) {
         InterpArgs a = p.bind(heap, in_off, out_off, scr_off, count, dtype, redop, scale, timeout_s, threads, nbatch,
                               strides, 0, 0);
         if ((timeline_ptr || lean) && redop != RED_SUM)
           throw std::runtime_error("the launch timeline and the lean kernel cover sum/avg reductions and copies");
         a.timeline = reinterpret_cast<unsigned long long*>(timeline_ptr);
         a.lean = lean ? 1 : 0;
-        a.bulk = bulk ? 1 : 0;
+        a.bulk = bulk & 3;
         if (bulk && timeline_ptr) throw std::runtime_error("the launch timeline has no TMA-staged kernel instance");
         return BoundLaunch{a, threads};
       }, py::arg("heap"), py::arg("in_off"), py::arg("out_off"), py::arg("scr_off"), py::arg("count"),
          py::arg("dtype"), py::arg("redop"), py::arg("scale"), py::arg("timeout_s"), py::arg("threads"),
          py::arg("nbatch"), py::arg("strides"), py::arg("timeline_ptr") = 0, py::arg("lean") = false,
-         py::arg("bulk") = false)
+         py::arg("bulk") = 0)
       .def("geometry", &DevicePlan::geometry)
       .def("slots", &DevicePlan::slots)
       .def("describe", &DevicePlan::describe)
@@ -518,7 +518,7 @@ PYBIND11_MODULE(_vbcuda, m) {
   // of a single-rank schedule (the reference's onerank reduce, third_party/msccl/src/collectives/device/
   // onerank_reduce.cu:13-41, generalised to K sources); it runs the same move paths as a K-source pull reduce.
   m.def("local_reduce", [](torch::Tensor dst, torch::Tensor srcs, int redop, double scale, bool do_scale, int lanes,
-                           int iters, bool lean, bool bulk) {
+                           int iters, bool lean, int bulk) {
     TORCH_CHECK(srcs.is_cuda() && dst.is_cuda() && srcs.is_contiguous() && dst.is_contiguous(), "contiguous CUDA tensors");
     TORCH_CHECK(srcs.dim() == 2 && srcs.size(1) == dst.numel() && srcs.scalar_type() == dst.scalar_type(),
                 "srcs must be [K, dst.numel()] of dst's dtype");
@@ -578,11 +578,11 @@ PYBIND11_MODULE(_vbcuda, m) {
     a.control = reinterpret_cast<Control*>(w);
     a.timeout_ns = 10ull * 1000000000ull;
     a.lean = lean ? 1 : 0;
-    a.bulk = bulk ? 1 : 0;
+    a.bulk = bulk & 3;
     cuda_check(launch_interp(a, stream, 512), "local reduce launch");
     return ws;   // keeps the workspace alive until the caller drops it; its first int words hold the status
   }, py::arg("dst"), py::arg("srcs"), py::arg("redop") = 0, py::arg("scale") = 1.0, py::arg("do_scale") = false,
-     py::arg("lanes") = 1, py::arg("iters") = 1, py::arg("lean") = false, py::arg("bulk") = false);
+     py::arg("lanes") = 1, py::arg("iters") = 1, py::arg("lean") = false, py::arg("bulk") = 0);
   m.def("reduce_probe", [](uint64_t dst, std::vector<uint64_t> srcs, int64_t bytes, int ctas, int threads) {
     std::vector<const void*> p;
     for (auto s : srcs) p.push_back(reinterpret_cast<const void*>(s));

@@ -130,7 +130,8 @@ def main():
         if "LEAN" in settings:
             comm.lean = settings["LEAN"] not in ("0", "")
         if "BULK" in settings:
-            comm.bulk = settings["BULK"] not in ("0", "")
+            from vericcl_b200.parallel.comm import _bulk_mode
+            comm.bulk = _bulk_mode(settings["BULK"])
         run_sizes(args, variant, comm, eng, world, rank, dtype, esize, timed, check, host_us, results)
         comm.lean, comm.bulk = saved
         for k in settings:

@@ -340,7 +340,7 @@ def test_tma_staged_reduce_matches_fp32_reference(comm, dtype, op, k):
         srcs = torch.randn(k, n, device="cuda", generator=gen).to(dtype)
     dst = torch.full((n,), float("nan"), device="cuda", dtype=dtype)
     scale = 0.37 if op == "sum" else 1.0
-    ws = comm._mod.local_reduce(dst, srcs, REDOPS[op], scale, op == "sum", 4, 2, False, True)
+    ws = comm._mod.local_reduce(dst, srcs, REDOPS[op], scale, op == "sum", 4, 2, False, 1)
     torch.cuda.synchronize()
     assert int(ws[12:16].view(torch.int32).item()) == 0
     ref = _reference(srcs, op) * scale
@@ -356,7 +356,7 @@ def test_tma_staged_single_rank_allreduce_through_the_engine(comm, dtype):
     n = 1 << 22
     x, y = comm.empty(n, dtype), comm.empty(n, dtype)
     x.copy_(torch.randn(n, device="cuda"))
-    comm.bulk = True
+    comm.bulk = 1
     try:
         for _ in range(2):
             y.fill_(float("nan"))
@@ -366,6 +366,41 @@ def test_tma_staged_single_rank_allreduce_through_the_engine(comm, dtype):
             tol = 1e-6 if dtype == torch.float32 else 1e-2
             assert torch.allclose(y.float(), x.float() * 0.25, atol=tol, rtol=tol)
     finally:
-        comm.bulk = False
+        comm.bulk = 0
+        comm.free(x)
+        comm.free(y)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("n", [(1 << 20) + 96, 3 * (1 << 16) + 8])
+def test_tma_store_copy_is_exact(comm, dtype, n):
+    """Staged plain copy written back by TMA bulk stores (mode 3): bit-exact, twice in a row on one workspace."""
+    gen = torch.Generator(device="cuda").manual_seed(n)
+    src = torch.randn(1, n, device="cuda", generator=gen).to(dtype)
+    for _ in range(2):
+        dst = torch.full((n,), float("nan"), device="cuda", dtype=dtype)
+        ws = comm._mod.local_reduce(dst, src, 0, 1.0, False, 8, 2, False, 3)
+        torch.cuda.synchronize()
+        assert int(ws[12:16].view(torch.int32).item()) == 0
+        assert torch.equal(dst, src[0])
+
+
+def test_tma_store_engine_allgather_single_rank(comm):
+    """A one-rank AllGather through the engine with TMA loads and stores: the output equals the input."""
+    from vericcl_b200.synthesis import schedule_xml
+    plan = comm.compile(schedule_xml("allgather", 1, 1, inplace=False, datatype="bfloat16"), nlanes=16, niters=2)
+    n = 1 << 22
+    x, y = comm.empty(n, torch.bfloat16), comm.empty(n, torch.bfloat16)
+    x.copy_(torch.randn(n, device="cuda"))
+    comm.bulk = 3
+    try:
+        for _ in range(2):
+            y.fill_(float("nan"))
+            comm.run(plan, x, y)
+            torch.cuda.synchronize()
+            comm.check_status()
+            assert torch.equal(y, x)
+    finally:
+        comm.bulk = 0
         comm.free(x)
         comm.free(y)

@@ -39,7 +39,9 @@ def main(argv=None) -> int:
     ap.add_argument("--k", type=int, default=4, help="sources of the local reduce")
     ap.add_argument("--dtype", default="bfloat16", choices=sorted(DTYPES))
     ap.add_argument("--lanes", type=int, default=0, help="CTAs of the local reduce (0: every SM)")
-    ap.add_argument("--bulk", action="store_true", help="local reduce: the TMA-staged kernel instance")
+    ap.add_argument("--bulk", type=int, default=0, choices=(0, 1, 3),
+                    help="local reduce: 1 the TMA-staged kernel instance, 3 also TMA stores for plain copies")
+    ap.add_argument("--no-scale", action="store_true", help="local reduce: no scale (K=1 is then a plain copy)")
     ap.add_argument("--fanout", action="store_true", help="push AllGather: the fan-out mode")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
@@ -58,9 +60,12 @@ def main(argv=None) -> int:
         dst = torch.empty(n, device="cuda", dtype=dtype)
         lanes = args.lanes or min(148, mod.max_ctas(512))
         keep = []
-        fn = lambda: keep.append(mod.local_reduce(dst, srcs, 0, 0.5, True, lanes, 1, False, args.bulk))  # noqa: E731
+        scaled = not args.no_scale
+        fn = lambda: keep.append(mod.local_reduce(dst, srcs, 0, 0.5 if scaled else 1.0, scaled, lanes, 1,  # noqa: E731
+                                                  False, args.bulk))
         nbytes = (args.k + 1) * n * esize
-        label = "interp_kernel local reduce K=%d%s" % (args.k, " (TMA-staged)" if args.bulk else "")
+        label = "interp_kernel local reduce K=%d%s%s" % (args.k, "" if scaled else " no scale",
+                                                         {0: "", 1: " (TMA-staged)", 3: " (TMA loads + stores)"}[args.bulk])
     elif args.kernel == "fp8_allgather":
         eng = CollectiveEngine(comm)
         x = torch.randn(n, device="cuda").to(dtype)

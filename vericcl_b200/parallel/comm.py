@@ -32,6 +32,18 @@ DEFAULT_HEAP_BYTES = 1 << 30
 TIMELINE_SLOTS = 256      # launch timeline slots (matches the device-side constant)
 
 
+def _bulk_mode(value) -> int:
+    """The staged-instance mode: 0 off, 1 TMA loads, 3 TMA loads and (for local plain copies) TMA stores."""
+    if value in (None, "", "0", "false", "False"):
+        return 0
+    if value in ("true", "True"):
+        return 1
+    mode = int(value)
+    if mode not in (1, 3):
+        raise ValueError("VERICCL_BULK must be 0, 1 or 3, not %r" % value)
+    return mode
+
+
 def _env_flag(name: str, default: bool) -> bool:
     value = os.environ.get(name)
     if value is None:
@@ -112,8 +124,9 @@ class Communicator:
         # Sum/avg launches use the register-lean interpreter instance when VERICCL_LEAN=1, and by default on a
         # single rank, where every step is a one-source copy (its copies keep eight vectors in flight per thread)
         self.lean = _env_flag("VERICCL_LEAN", self.world == 1)
-        # copy and reduce steps stage their sources in shared memory with TMA bulk copies (VERICCL_BULK=1)
-        self.bulk = _env_flag("VERICCL_BULK", False)
+        # copy and reduce steps stage their sources in shared memory with TMA bulk copies (VERICCL_BULK=1); with
+        # VERICCL_BULK=3 staged plain copies into local memory are written back by TMA too (a bit mask, 0..3)
+        self.bulk = _bulk_mode(os.environ.get("VERICCL_BULK"))
         self._lock = threading.Lock()
         self._closed = False
 
@@ -360,7 +373,7 @@ class Communicator:
                                          or not timeline.is_cuda):
                 raise RuntimeFailure("timeline buffer needs %d int64 elements on the device" % (2 * TIMELINE_SLOTS))
             lean = self.lean and REDOPS[op] == 0
-            bulk = self.bulk and not tl_ptr
+            bulk = int(self.bulk) if not tl_ptr else 0
             bound = plan.device_plan.bind(self.heap, in_off, out_off, scr_off, count, DTYPE_CODES[inp.dtype],
                                           REDOPS[op], float(factor), self.timeout_s, 512, nbatch, strides, tl_ptr,
                                           lean, bulk)
