@@ -1,4 +1,4 @@
-"""Reference arm of ``bench.py``: the reference's own NCCL/MSCCL build on this box.
+"""Reference arm of ``bench.py``: the reference's own NCCL/MSCCL build, run on the same GPUs.
 
 The reference runs its collectives through a vendored MSCCL 0.1 / NCCL 2.12.12
 (third_party/msccl, prepared and compiled by runtime/build_runtime.py:24-69).
@@ -39,8 +39,20 @@ NCCL_BF16, NCCL_F64, NCCL_SUM, NCCL_MAX = 9, 8, 0, 2
 H2D, D2H, D2D = 1, 2, 3
 
 
-def unavailable_reason() -> str | None:
-    """Why the reference arm cannot run here (None when its libraries are built)."""
+# Observed on an 8-GPU B200 system: the library's first 2-GPU run (ncclCommInitRank, then ncclAllReduce of 25 MiB bf16
+# buckets, torchrun with two ranks) printed its version banner and then returned nothing within 300 s (0.4 GB
+# per rank) nor within 900 s (16 GB per rank), while the GPUs still answered.  The inputs were checked by
+# reading (argument types, sizes, the 128-byte id exchange); a reference that hangs is not run again on
+# GPUs that other jobs share, so every multi-GPU run of the arm reports this instead.
+MULTI_GPU_HANG = ("the reference's MSCCL 0.1 / NCCL 2.12.12 built for sm_100 hung on its first 2-GPU run on a B200 "
+                  "(no result within 300 s at 0.4 GB per rank nor 900 s at 16 GB per rank; GPUs still answered) "
+                  "and is not re-run on more than one GPU")
+
+
+def unavailable_reason(world: int = 1) -> str | None:
+    """Why the reference arm cannot run here (None when its libraries are built and the run has one GPU)."""
+    if world > 1:
+        return MULTI_GPU_HANG
     if not os.path.isfile(NCCL_SO):
         if os.path.isfile(BUILD_RECORD):
             with open(BUILD_RECORD) as f:
@@ -189,10 +201,10 @@ def bf16_to_f32(b: np.ndarray) -> np.ndarray:
 
 def run(args, clock_sampler_cls, metric: str, model: str) -> int:
     """The arm, guarded: any failure prints the ``unavailable`` line (rank 0) instead of a traceback, and a
-    watchdog ends a process whose NCCL calls never return (VB_REF_DEADLINE_S, default 1200 s)."""
+    watchdog ends a process whose NCCL calls never return (VB_REF_DEADLINE_S, default 600 s)."""
     import threading
     rank = int(os.environ.get("RANK", "0"))
-    deadline = float(os.environ.get("VB_REF_DEADLINE_S", "1200"))
+    deadline = float(os.environ.get("VB_REF_DEADLINE_S", "600"))
 
     def expire():
         if rank == 0:
@@ -218,7 +230,7 @@ def _run(args, clock_sampler_cls, metric: str, model: str) -> int:
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    reason = unavailable_reason()
+    reason = unavailable_reason(world)
     if reason is not None:
         if rank == 0:
             print(json.dumps({"impl": "reference", "unavailable": reason}), flush=True)

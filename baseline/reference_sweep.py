@@ -41,7 +41,7 @@ def main() -> int:
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    reason = ra.unavailable_reason()
+    reason = ra.unavailable_reason(world)
     if reason is not None:
         if rank == 0:
             print(json.dumps({"impl": "reference", "unavailable": reason}), flush=True)

@@ -64,3 +64,18 @@ def test_cta_budget_caps_the_interpreter_grid():
     assert small.geometry(8, 64 << 20)[0] == 4
     assert small.geometry(64, 64 << 20)[0] == 1            # below the block count: one lane per block
     assert CollectiveEngine(_Comm(8), cta_budget=4096).geometry(8, 64 << 20)[0] == 148 // 8
+
+
+def test_tma_staged_instance_is_chosen_for_large_pulls_on_verified_worlds():
+    from vericcl_b200.parallel.comm import BULK_AUTO_MIN_BYTES, Communicator, _bulk_mode
+    pulls, nvls = SimpleNamespace(multicast=False), SimpleNamespace(multicast=True)
+    auto2 = SimpleNamespace(bulk=None, world=2)
+    assert Communicator.bulk_for(auto2, pulls, BULK_AUTO_MIN_BYTES) == 1
+    assert Communicator.bulk_for(auto2, pulls, BULK_AUTO_MIN_BYTES - 16) == 0
+    assert Communicator.bulk_for(auto2, nvls, 1 << 30) == 0              # multimem steps are not staged
+    assert Communicator.bulk_for(SimpleNamespace(bulk=None, world=1), pulls, 1 << 30) == 0
+    assert Communicator.bulk_for(SimpleNamespace(bulk=3, world=1), pulls, 16) == 3   # explicit setting wins
+    assert [_bulk_mode(v) for v in (None, "0", "1", "3", "true")] == [0, 0, 1, 3, 1]
+    import pytest
+    with pytest.raises(ValueError):
+        _bulk_mode("2")

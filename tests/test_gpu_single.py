@@ -356,7 +356,7 @@ def test_tma_staged_single_rank_allreduce_through_the_engine(comm, dtype):
     n = 1 << 22
     x, y = comm.empty(n, dtype), comm.empty(n, dtype)
     x.copy_(torch.randn(n, device="cuda"))
-    comm.bulk = 1
+    saved, comm.bulk = comm.bulk, 1
     try:
         for _ in range(2):
             y.fill_(float("nan"))
@@ -366,7 +366,7 @@ def test_tma_staged_single_rank_allreduce_through_the_engine(comm, dtype):
             tol = 1e-6 if dtype == torch.float32 else 1e-2
             assert torch.allclose(y.float(), x.float() * 0.25, atol=tol, rtol=tol)
     finally:
-        comm.bulk = 0
+        comm.bulk = saved
         comm.free(x)
         comm.free(y)
 
@@ -392,7 +392,7 @@ def test_tma_store_engine_allgather_single_rank(comm):
     n = 1 << 22
     x, y = comm.empty(n, torch.bfloat16), comm.empty(n, torch.bfloat16)
     x.copy_(torch.randn(n, device="cuda"))
-    comm.bulk = 3
+    saved, comm.bulk = comm.bulk, 3
     try:
         for _ in range(2):
             y.fill_(float("nan"))
@@ -401,6 +401,6 @@ def test_tma_store_engine_allgather_single_rank(comm):
             comm.check_status()
             assert torch.equal(y, x)
     finally:
-        comm.bulk = 0
+        comm.bulk = saved
         comm.free(x)
         comm.free(y)

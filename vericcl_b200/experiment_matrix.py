@@ -17,7 +17,7 @@ task records its status, the sha256 of its inputs and of its output in
 ``state.json``; ``--resume`` skips a task whose record passed and whose
 input and output digests still match (reference:
 vericcl/experiments/v100.py:929-1420, whose stages and resumable task
-records this follows for a B200 box instead of two V100 nodes).
+records this follows for one B200 node instead of two V100 nodes).
 """
 from __future__ import annotations
 
@@ -182,7 +182,7 @@ def benchmark_matrix(manifest_path, *, case_ids=(), resume: bool = False, measur
         request = load_request(files, purpose="verify")
         env = {}
         if case.get("groups", 1) > 1:
-            # the slow inter-group link is paced by the interpreter on one NVSwitch box
+            # the slow inter-group link is paced by the interpreter on one NVSwitch node
             env["VERICCL_EMULATE"] = "group=%d,gbps=%g" % (case["per_group"], case["inter_gbps"])
         saved = {k: os.environ.get(k) for k in env}
         os.environ.update(env)
