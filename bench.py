@@ -307,6 +307,13 @@ def main():
             out_host = torch.empty(32768, dtype=dtype, pin_memory=True)
 
             def e2e_step():
+                # host->device copies of bucket groups overlapped with the AllReduce of the groups already in
+                ar.sync_from_host(host, stream)
+                out_host.copy_(ar.grads[:32768], non_blocking=True)
+                stream.synchronize()
+                _ = float(out_host[0])
+
+            def e2e_serial():
                 flat.copy_(host, non_blocking=True)
                 ar.sync(stream, batched=batched)
                 out_host.copy_(ar.grads[:32768], non_blocking=True)
@@ -315,11 +322,16 @@ def main():
 
             e2e_step()
             ems = max_over_ranks(timed(e2e_step, args.e2e_steps, stream, barrier))
+            e2e_serial()
+            sms = max_over_ranks(timed(e2e_serial, args.e2e_steps, stream, barrier))
             e2e = {"value": round(bus / (ems * 1e-3) / 1e9 * world, 2),
                    "unit": "GB/s (sum over GPUs of per-GPU bus bandwidth)",
                    "ms_per_step": round(ems, 3), "h2d_bytes_per_step": int(total_bytes),
                    "d2h_bytes_per_step": int(out_host.numel() * esize),
-                   "api": "GradBucketAllReduce.sync after a pinned host->heap copy of all gradients"}
+                   "api": "GradBucketAllReduce.sync_from_host: pinned host->device copies of 8 bucket groups "
+                          "overlapped with the AllReduce of the groups already copied, then a device->host read",
+                   "serial": {"ms_per_step": round(sms, 3), "value": round(bus / (sms * 1e-3) / 1e9 * world, 2),
+                              "api": "one host->device copy of all gradients, then GradBucketAllReduce.sync"}}
             del host
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s (sum over GPUs of per-GPU bus bandwidth)",

@@ -404,3 +404,21 @@ def test_tma_store_engine_allgather_single_rank(comm):
         comm.bulk = saved
         comm.free(x)
         comm.free(y)
+
+
+def test_gradient_sync_from_host_matches_scaled_input(comm):
+    """sync_from_host: bucket groups copied in from pinned memory, each AllReduced (one rank: scaled) after its copy."""
+    from vericcl_b200.models import GradBucketAllReduce
+    numel = 5 * 65536 + 1000                    # a partial last bucket
+    ar = GradBucketAllReduce(comm, numel, dtype=torch.bfloat16, bucket_bytes=131072, scale=0.25)
+    host = torch.randn(numel).to(torch.bfloat16).pin_memory()
+    for step in range(2):
+        ar.grads.fill_(float("nan"))
+        ar.grads[numel:].zero_()
+        launches = ar.sync_from_host(host, groups=3)
+        torch.cuda.synchronize()
+        comm.check_status()
+        assert launches == 3
+        ref = host.float() * 0.25
+        assert torch.allclose(ar.flat.float().cpu(), ref, atol=1e-2, rtol=1e-2)
+    comm.free(ar.grads)

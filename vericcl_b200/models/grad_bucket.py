@@ -78,6 +78,49 @@ class GradBucketAllReduce:
             b = self.bucket(i)
             self.comm.run(plan, b, b, op="sum", scale=self.scale, stream=stream)
 
+    def sync_from_host(self, host: torch.Tensor, stream=None, *, groups: int = 8, copy_stream=None) -> int:
+        """Copy the gradients in from pinned host memory and AllReduce them, the two overlapped.
+
+        The buckets are cut into ``groups`` consecutive groups.  Group g is copied
+        host→device on ``copy_stream`` (a side stream by default) while the
+        AllReduce of group g-1 runs on ``stream``; each group's AllReduce waits
+        for its own copy only (an event).  The copy stream first waits for the
+        work already queued on ``stream``, so a previous step's readers of the
+        buffer finish before it is overwritten.  Returns the number of
+        AllReduce launches issued.  ``host`` holds ``numel`` elements of the
+        buffer's dtype; pinned memory makes the copies asynchronous.
+        """
+        if host.numel() != self.numel or host.dtype != self.dtype or host.is_cuda:
+            raise ValueError("host gradients must be a CPU tensor of %d %s elements" % (self.numel, self.dtype))
+        stream = torch.cuda.current_stream() if stream is None else stream
+        if copy_stream is None:
+            copy_stream = getattr(self, "_copy_stream", None)
+            if copy_stream is None:
+                copy_stream = self._copy_stream = torch.cuda.Stream()
+        groups = max(1, min(groups, self.buckets))
+        per = -(-self.buckets // groups)
+        copy_stream.wait_stream(stream)
+        launches = 0
+        for b0 in range(0, self.buckets, per):
+            b1 = min(self.buckets, b0 + per)
+            lo, hi = b0 * self.bucket_elems, min(self.numel, b1 * self.bucket_elems)
+            with torch.cuda.stream(copy_stream):
+                self.grads[lo:hi].copy_(host[lo:hi], non_blocking=True)
+                landed = torch.cuda.Event()
+                landed.record(copy_stream)
+            stream.wait_event(landed)
+            first = self.bucket(b0)
+            if self.plan.kind != "oneshot":
+                self.comm.run(self.plan, first, first, op="sum", scale=self.scale, stream=stream, nbatch=b1 - b0,
+                              in_stride=self.bucket_elems, out_stride=self.bucket_elems)
+                launches += 1
+            else:
+                for i in range(b0, b1):
+                    b = self.bucket(i)
+                    self.comm.run(self.plan, b, b, op="sum", scale=self.scale, stream=stream)
+                    launches += 1
+        return launches
+
     @property
     def launches_per_sync(self) -> int:
         return self.buckets if self.plan.kind == "oneshot" else 1
