@@ -126,7 +126,9 @@ def main():
     # one-shot flag-in-data path: every case three times in a row (both LL region halves are reused), AllReduce and
     # AllGather interleaved so they share the launch counter
     from vericcl_b200.models import CollectiveEngine
-    eng = CollectiveEngine(comm)
+    from vericcl_b200.models.collectives import ONESHOT_MAX_BYTES
+    # an explicit threshold routes to the one-shot kernel at any world size, so it is checked wherever this runs
+    eng = CollectiveEngine(comm, oneshot_max_bytes=ONESHOT_MAX_BYTES)
     oneshot = []
     for dtype in (torch.float32, torch.bfloat16, torch.float16):
         esize = torch.tensor([], dtype=dtype).element_size()

@@ -21,7 +21,7 @@ from vericcl_b200.synthesis import schedule_xml
 ONESHOT_MAX_BYTES = 1 << 20          # per-rank payloads up to this size take the one-shot flag-in-data path
 # world sizes whose one-shot / two-shot runs have passed the multi-GPU fp64 checks on B200s; other sizes take the
 # interpreter unless VERICCL_ONESHOT_ANY_WORLD=1 (or an explicit threshold) says otherwise
-ONESHOT_VERIFIED_WORLDS = frozenset({2, 4})
+ONESHOT_VERIFIED_WORLDS = frozenset({2, 4, 8})
 AG_NVLS_MAX_BYTES = 8 << 20          # larger AllGathers pull from peers (measured faster than multicast stores)
 PIECE_MIN_BYTES = 8 * 1024          # smallest useful piece per CTA per iteration
 PIECE_TARGET_BYTES = 512 * 1024     # pipeline a lane's work in pieces of about this size
