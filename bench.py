@@ -19,10 +19,10 @@ scale pass (an HBM read and write), labelled as such.  ``nvlink`` gives the
 bytes each GPU really sends per direction on the path the plan takes and
 their fraction of 900 GB/s (nominal) and 770 GB/s (measured peer copy).
 
-``cta_budget`` times the same sync restricted to 16, 32 and 64 CTAs per GPU
-(``--cta-budgets``): the interpreter otherwise takes one CTA on every SM, and
-in data-parallel training the SMs it leaves free are what the overlapping
-backward pass gets.
+``cta_budget`` times the same sync on 16, 32, 64 and 148 CTAs per GPU
+(``--cta-budgets``) beside the default (32 CTAs on an NVLS plan, every SM
+otherwise): in data-parallel training the SMs the sync leaves free are what
+the overlapping backward pass gets.
 
 ``--impl reference`` runs the reference's own MSCCL/NCCL 2.12.12 build instead
 (``baseline/reference_arm.py``), without PyTorch or this package.
@@ -58,7 +58,7 @@ def parse():
     ap.add_argument("--no-nccl", action="store_true")
     ap.add_argument("--per-bucket", action="store_true", help="one launch per bucket instead of one batched launch")
     ap.add_argument("--slices", type=int, default=None, help="slices per rank of the synthesized schedule")
-    ap.add_argument("--cta-budgets", default="16,32,64",
+    ap.add_argument("--cta-budgets", default="16,32,64,148",
                     help="also time the sync restricted to these CTAs per GPU (comma list; empty: skip)")
     return ap.parse_args()
 
@@ -252,7 +252,7 @@ def main():
     # the same sync on a CTA budget: the SMs left over are what overlapping backward compute gets
     budgets = None
     if args.cta_budgets:
-        budgets = {"full": {"ctas": ar.ctas_of(ar.plan), "ms_per_step": round(ms, 4),
+        budgets = {"default": {"ctas": ar.ctas_of(ar.plan), "ms_per_step": round(ms, 4),
                             "busbw_per_gpu_gbs": round(busbw, 2)}}
         for want in [int(v) for v in args.cta_budgets.split(",") if v.strip()]:
             bplan = ar.plan_with_budget(want)

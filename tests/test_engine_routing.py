@@ -67,12 +67,14 @@ def test_cta_budget_caps_the_interpreter_grid():
 
 
 def test_tma_staged_instance_is_chosen_for_large_pulls_on_verified_worlds():
-    from vericcl_b200.parallel.comm import BULK_AUTO_MIN_BYTES, Communicator, _bulk_mode
+    from vericcl_b200.parallel.comm import BULK_AUTO_MAX_BYTES, BULK_AUTO_MIN_BYTES, Communicator, _bulk_mode
     pulls, nvls = SimpleNamespace(multicast=False), SimpleNamespace(multicast=True)
     auto2 = SimpleNamespace(bulk=None, world=2)
     assert Communicator.bulk_for(auto2, pulls, BULK_AUTO_MIN_BYTES) == 1
     assert Communicator.bulk_for(auto2, pulls, BULK_AUTO_MIN_BYTES - 16) == 0
-    assert Communicator.bulk_for(auto2, nvls, 1 << 30) == 0              # multimem steps are not staged
+    assert Communicator.bulk_for(auto2, nvls, 1 << 28) == 0              # multimem steps are not staged
+    assert Communicator.bulk_for(auto2, pulls, BULK_AUTO_MAX_BYTES + 16) == 0
+    assert Communicator.bulk_for(SimpleNamespace(bulk=None, world=8), pulls, 1 << 26) == 0
     assert Communicator.bulk_for(SimpleNamespace(bulk=None, world=1), pulls, 1 << 30) == 0
     assert Communicator.bulk_for(SimpleNamespace(bulk=3, world=1), pulls, 16) == 3   # explicit setting wins
     assert [_bulk_mode(v) for v in (None, "0", "1", "3", "true")] == [0, 0, 1, 3, 1]

@@ -44,11 +44,13 @@ def _bulk_mode(value) -> int:
     return mode
 
 
-# Rank counts whose multi-GPU runs of the TMA-staged instance passed the fp64 collective checks, and the
-# payload from which it is chosen by default there: on two B200s it moved 64-256 MiB AllGathers 6-27 % and
-# AllReduces 2-5 % faster than the vector path, and was level at 16 MiB and slower at 1-4 MiB.
-BULK_VERIFIED_WORLDS = frozenset({2})
+# Rank counts on which the TMA-staged instance passed the fp64 collective checks and measured faster than the
+# vector path, and the payload window where it is chosen by default there.  Two B200s: 64-256 MiB AllGathers
+# 6-27 % and AllReduces 2-5 % faster, level at 16 MiB, slower at 1-4 MiB.  Four: AllGathers 16-256 MiB 3-5 %
+# faster, 1 GiB 14 % slower.  Eight: correct, but slower from 256 MiB, so not listed.
+BULK_VERIFIED_WORLDS = frozenset({2, 4})
 BULK_AUTO_MIN_BYTES = 16 << 20
+BULK_AUTO_MAX_BYTES = 256 << 20
 
 
 def _env_flag(name: str, default: bool) -> bool:
@@ -396,11 +398,13 @@ class Communicator:
 
     def bulk_for(self, plan, nbytes: int) -> int:
         """Interpreter instance mode for one launch: the explicit ``bulk`` setting, else TMA-staged loads (1) for
-        payloads of at least ``BULK_AUTO_MIN_BYTES`` per rank on verified rank counts when the plan has no
-        multicast steps (the staged path covers copy and reduce steps only), else the vector path (0)."""
+        payloads of ``BULK_AUTO_MIN_BYTES`` to ``BULK_AUTO_MAX_BYTES`` per rank on the rank counts in
+        ``BULK_VERIFIED_WORLDS`` when the plan has no multicast steps (the staged path covers copy and reduce
+        steps only), else the vector path (0)."""
         if self.bulk is not None:
             return int(self.bulk)
-        if self.world in BULK_VERIFIED_WORLDS and not plan.multicast and nbytes >= BULK_AUTO_MIN_BYTES:
+        if (self.world in BULK_VERIFIED_WORLDS and not plan.multicast
+                and BULK_AUTO_MIN_BYTES <= nbytes <= BULK_AUTO_MAX_BYTES):
             return 1
         return 0
 
