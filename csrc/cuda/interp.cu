@@ -52,6 +52,15 @@ __device__ __forceinline__ uint4 ld_vec(const void* p) {
   return v;
 }
 
+// the same load with an L2 prefetch hint: the L2 fetches the whole 256-byte block around the address
+__device__ __forceinline__ uint4 ld_vec_pf(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
 __device__ __forceinline__ void st_vec(void* p, const uint4& v) {
   asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                : "memory");
@@ -207,7 +216,7 @@ __device__ __forceinline__ float combine(float a, float b) {
 
 // Move one piece: dst[v] = scale? * op(src0[v], ..., src_{K-1}[v]) for vectors v in [0, nvec).
 // K is a compile-time source count so that all K*U loads of a thread are in flight together.
-template <int DT, int RED, int K, int U>
+template <int DT, int RED, int K, int U, bool PF = false>
 __device__ __forceinline__ void move_fixed(char* dst, const char* const* src, long long nvec, bool do_scale,
                                            float scale) {
   using V = VecT<DT>;
@@ -219,7 +228,7 @@ __device__ __forceinline__ void move_fixed(char* dst, const char* const* src, lo
       long long v = v0 + (long long)u * blockDim.x;
       if (v < nvec) {
 #pragma unroll
-        for (int k = 0; k < K; ++k) raw[k][u] = ld_vec(src[k] + v * 16);
+        for (int k = 0; k < K; ++k) raw[k][u] = PF ? ld_vec_pf(src[k] + v * 16) : ld_vec(src[k] + v * 16);
       }
     }
 #pragma unroll
@@ -438,18 +447,18 @@ __device__ bool move_bulk(char* dst, const char* const* src, int nsrc, long long
 }
 
 // LEAN selects the register-lean unrolls (2 and 3 sources one vector deep, copies eight deep) that build
-// without spills.
-template <int DT, int RED, bool LEAN>
+// without spills; PF adds the 256-byte L2 prefetch hint to the loads.
+template <int DT, int RED, bool LEAN, bool PF = false>
 __device__ void move_piece(char* dst, const char* const* src, int nsrc, long long nvec, bool do_scale, float scale) {
   switch (nsrc) {
-    case 1: move_fixed<DT, RED, 1, LEAN ? 8 : 4>(dst, src, nvec, do_scale, scale); break;
-    case 2: move_fixed<DT, RED, 2, LEAN ? 1 : 2>(dst, src, nvec, do_scale, scale); break;
-    case 3: move_fixed<DT, RED, 3, LEAN ? 1 : 2>(dst, src, nvec, do_scale, scale); break;
-    case 4: move_fixed<DT, RED, 4, 1>(dst, src, nvec, do_scale, scale); break;
-    case 5: move_fixed<DT, RED, 5, 1>(dst, src, nvec, do_scale, scale); break;
-    case 6: move_fixed<DT, RED, 6, 1>(dst, src, nvec, do_scale, scale); break;
-    case 7: move_fixed<DT, RED, 7, 1>(dst, src, nvec, do_scale, scale); break;
-    case 8: move_fixed<DT, RED, 8, 1>(dst, src, nvec, do_scale, scale); break;
+    case 1: move_fixed<DT, RED, 1, LEAN ? 8 : 4, PF>(dst, src, nvec, do_scale, scale); break;
+    case 2: move_fixed<DT, RED, 2, LEAN ? 1 : 2, PF>(dst, src, nvec, do_scale, scale); break;
+    case 3: move_fixed<DT, RED, 3, LEAN ? 1 : 2, PF>(dst, src, nvec, do_scale, scale); break;
+    case 4: move_fixed<DT, RED, 4, 1, PF>(dst, src, nvec, do_scale, scale); break;
+    case 5: move_fixed<DT, RED, 5, 1, PF>(dst, src, nvec, do_scale, scale); break;
+    case 6: move_fixed<DT, RED, 6, 1, PF>(dst, src, nvec, do_scale, scale); break;
+    case 7: move_fixed<DT, RED, 7, 1, PF>(dst, src, nvec, do_scale, scale); break;
+    case 8: move_fixed<DT, RED, 8, 1, PF>(dst, src, nvec, do_scale, scale); break;
     default: move_generic<DT, RED>(dst, src, nsrc, nvec, do_scale, scale); break;
   }
 }
@@ -601,7 +610,8 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
               return;
             }
           } else {
-            move_piece<DT, RED, LEAN>(dst, s_src, st.nsrc, nvec, (st.flags & F_SCALE) != 0, a.scale);
+            // the register-lean instance (one rank by default) adds the L2 prefetch hint to its loads
+            move_piece<DT, RED, LEAN, LEAN && !BULK>(dst, s_src, st.nsrc, nvec, (st.flags & F_SCALE) != 0, a.scale);
           }
           if (dr != a.rank) mc_pending = true;   // remote stores: fenced at system scope before the done flag
           __syncthreads();

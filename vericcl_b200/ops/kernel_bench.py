@@ -42,6 +42,7 @@ def main(argv=None) -> int:
     ap.add_argument("--bulk", type=int, default=0, choices=(0, 1, 3),
                     help="local reduce: 1 the TMA-staged kernel instance, 3 also TMA stores for plain copies")
     ap.add_argument("--no-scale", action="store_true", help="local reduce: no scale (K=1 is then a plain copy)")
+    ap.add_argument("--lean", action="store_true", help="local reduce: the register-lean instance (one-rank default)")
     ap.add_argument("--fanout", action="store_true", help="push AllGather: the fan-out mode")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
@@ -62,9 +63,9 @@ def main(argv=None) -> int:
         keep = []
         scaled = not args.no_scale
         fn = lambda: keep.append(mod.local_reduce(dst, srcs, 0, 0.5 if scaled else 1.0, scaled, lanes, 1,  # noqa: E731
-                                                  False, args.bulk))
+                                                  args.lean, args.bulk))
         nbytes = (args.k + 1) * n * esize
-        label = "interp_kernel local reduce K=%d%s%s" % (args.k, "" if scaled else " no scale",
+        label = "interp_kernel local reduce K=%d%s%s%s" % (args.k, "" if scaled else " no scale", " lean" if args.lean else "",
                                                          {0: "", 1: " (TMA-staged)", 3: " (TMA loads + stores)"}[args.bulk])
     elif args.kernel == "fp8_allgather":
         eng = CollectiveEngine(comm)
