@@ -532,7 +532,6 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
     for (int s = 0; s < blk.nsteps; ++s) {
       const DevStep st = a.steps[blk.step_begin + s];
       unsigned long long t_reach = 0, t_ready = 0, t_step0 = 0;
-      if (a.pace_group > 0 && threadIdx.x == 0) t_step0 = globaltimer();
       if (a.trace_buf && threadIdx.x == 0) t_reach = globaltimer();
       if (st.wait_count) {
         if (threadIdx.x < 32) {
@@ -543,6 +542,8 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
         if (*s_stop) return;
       }
       if (a.trace_buf && threadIdx.x == 0) t_ready = globaltimer();
+      // link emulation times the transfer from here: waiting for the inputs does not use the emulated link
+      if (a.pace_group > 0 && threadIdx.x == 0) t_step0 = globaltimer();
       const unsigned long long ev = base + (unsigned long long)it * stride + 2ull * s;
       if (st.flags & F_PUB_ARRIVE) {
         if (mc_pending) {
