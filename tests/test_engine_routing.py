@@ -67,8 +67,13 @@ def test_cta_budget_caps_the_interpreter_grid():
 
 
 def test_tma_staged_instance_is_chosen_for_large_pulls_on_verified_worlds():
-    from vericcl_b200.parallel.comm import BULK_AUTO_MAX_BYTES, BULK_AUTO_MIN_BYTES, Communicator, _bulk_mode
-    pulls, nvls = SimpleNamespace(multicast=False), SimpleNamespace(multicast=True)
+    from vericcl_b200.parallel.comm import (BULK_AUTO_MAX_BYTES, BULK_AUTO_MIN_BYTES, BULK_AUTO_MIN_REDUCE_BYTES,
+                                            Communicator, _bulk_mode)
+    pulls = SimpleNamespace(multicast=False, collective="allgather")
+    nvls = SimpleNamespace(multicast=True, collective="allreduce")
+    reduce_pulls = SimpleNamespace(multicast=False, collective="allreduce")
+    assert Communicator.bulk_for(SimpleNamespace(bulk=None, world=2), reduce_pulls, 25 << 20) == 0
+    assert Communicator.bulk_for(SimpleNamespace(bulk=None, world=2), reduce_pulls, BULK_AUTO_MIN_REDUCE_BYTES) == 1
     auto2 = SimpleNamespace(bulk=None, world=2)
     assert Communicator.bulk_for(auto2, pulls, BULK_AUTO_MIN_BYTES) == 1
     assert Communicator.bulk_for(auto2, pulls, BULK_AUTO_MIN_BYTES - 16) == 0

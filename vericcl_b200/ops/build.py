@@ -14,8 +14,11 @@ runtime/build_native.py:46, which build the patched MSCCL, the probe binary and 
 """
 from __future__ import annotations
 
+import fcntl
+import functools
 import hashlib
 import os
+import threading
 import shutil
 import subprocess
 import sys
@@ -31,6 +34,41 @@ EXT = sysconfig.get_config_var("EXT_SUFFIX") or ".so"
 
 PLAN_SOURCES = ["plan/xml_parse.cc", "plan/compile.cc", "plan/cpu_interp.cc"]
 RUNTIME_SOURCES = ["runtime/contract.cc", "runtime/control_transport.cc", "runtime/trace_io.cc"]
+
+
+_build_guard = threading.RLock()
+_build_depth = 0
+
+
+def _serialized(fn):
+    """Run a build function under an exclusive lock on a file in the output folder.
+
+    Every rank of a multi-GPU job imports the extension at the same moment; when
+    the in-tree module is stale, the first process to take the lock rebuilds it
+    and the others, once they get the lock, find it fresh instead of compiling
+    and renaming over the same files at once.  Nested builds (``build_all``)
+    take the lock once.
+    """
+    @functools.wraps(fn)
+    def wrapper(*args, **kwargs):
+        global _build_depth
+        with _build_guard:
+            if _build_depth:
+                _build_depth += 1
+                try:
+                    return fn(*args, **kwargs)
+                finally:
+                    _build_depth -= 1
+            OUT.mkdir(parents=True, exist_ok=True)
+            with open(OUT / ".build.lock", "a") as lock:
+                fcntl.flock(lock, fcntl.LOCK_EX)
+                _build_depth = 1
+                try:
+                    return fn(*args, **kwargs)
+                finally:
+                    _build_depth = 0
+                    fcntl.flock(lock, fcntl.LOCK_UN)
+    return wrapper
 
 
 def _digest(paths, flags) -> str:
@@ -67,6 +105,7 @@ def pybind_includes():
     return [pybind11.get_include(), sysconfig.get_paths()["include"]]
 
 
+@_serialized
 def build_plan_module(force: bool = False) -> Path:
     OUT.mkdir(parents=True, exist_ok=True)
     target = OUT / ("_vbplan" + EXT)
@@ -98,6 +137,7 @@ CUDA_SOURCES = ["cuda/interp.cu", "cuda/oneshot.cu", "cuda/helpers.cu", "cuda/pr
                 "cuda/fp8.cu", "runtime/symheap.cc", "runtime/cuda_ext.cc"]
 
 
+@_serialized
 def build_cuda_module(force: bool = False, jobs: int | None = None) -> Path:
     """nvcc/g++ build of the PyTorch CUDA extension ``_vbcuda`` for sm_100a."""
     OUT.mkdir(parents=True, exist_ok=True)
@@ -150,6 +190,7 @@ def build_cuda_module(force: bool = False, jobs: int | None = None) -> Path:
 CAPI_SOURCES = ["runtime/capi.cc"]
 
 
+@_serialized
 def build_capi(force: bool = False) -> Path:
     """Standalone C API library ``libvericcl_b200.so`` (C ABI, no Python)."""
     OUT.mkdir(parents=True, exist_ok=True)
@@ -176,6 +217,7 @@ def build_capi(force: bool = False) -> Path:
     return target
 
 
+@_serialized
 def build_driver(force: bool = False) -> Path:
     """``vericcl-native``: one rank of a schedule through the C API, with a JSON receipt."""
     lib = build_capi(force)
@@ -194,6 +236,7 @@ def build_driver(force: bool = False) -> Path:
     return target
 
 
+@_serialized
 def build_native_tests(force: bool = False) -> Path:
     """CPU-only tests of the contract utilities and the control plane (g++, no CUDA)."""
     OUT.mkdir(parents=True, exist_ok=True)
@@ -209,6 +252,7 @@ def build_native_tests(force: bool = False) -> Path:
     return target
 
 
+@_serialized
 def build_capi_cpu_tests(force: bool = False) -> Path:
     """The C API's execute path built with g++ against host stand-ins of the CUDA runtime and the heap."""
     OUT.mkdir(parents=True, exist_ok=True)
@@ -228,6 +272,7 @@ def build_capi_cpu_tests(force: bool = False) -> Path:
     return target
 
 
+@_serialized
 def build_all(force: bool = False) -> dict:
     out = {"plan": str(build_plan_module(force))}
     out["cuda"] = str(build_cuda_module(force))

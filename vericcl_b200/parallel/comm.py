@@ -49,7 +49,8 @@ def _bulk_mode(value) -> int:
 # 6-27 % and AllReduces 2-5 % faster, level at 16 MiB, slower at 1-4 MiB.  Four: AllGathers 16-256 MiB 3-5 %
 # faster, 1 GiB 14 % slower.  Eight: correct, but slower from 256 MiB, so not listed.
 BULK_VERIFIED_WORLDS = frozenset({2, 4})
-BULK_AUTO_MIN_BYTES = 16 << 20
+BULK_AUTO_MIN_BYTES = 16 << 20          # AllGather (copies only)
+BULK_AUTO_MIN_REDUCE_BYTES = 64 << 20   # plans with reduce steps: level at 16 MiB, 0.5 % slower on 25 MiB buckets
 BULK_AUTO_MAX_BYTES = 256 << 20
 
 
@@ -398,13 +399,14 @@ class Communicator:
 
     def bulk_for(self, plan, nbytes: int) -> int:
         """Interpreter instance mode for one launch: the explicit ``bulk`` setting, else TMA-staged loads (1) for
-        payloads of ``BULK_AUTO_MIN_BYTES`` to ``BULK_AUTO_MAX_BYTES`` per rank on the rank counts in
+        payloads of ``BULK_AUTO_MIN_BYTES`` (AllGather) or ``BULK_AUTO_MIN_REDUCE_BYTES`` (other collectives) to
+        ``BULK_AUTO_MAX_BYTES`` per rank on the rank counts in
         ``BULK_VERIFIED_WORLDS`` when the plan has no multicast steps (the staged path covers copy and reduce
         steps only), else the vector path (0)."""
         if self.bulk is not None:
             return int(self.bulk)
-        if (self.world in BULK_VERIFIED_WORLDS and not plan.multicast
-                and BULK_AUTO_MIN_BYTES <= nbytes <= BULK_AUTO_MAX_BYTES):
+        low = BULK_AUTO_MIN_BYTES if getattr(plan, "collective", "") == "allgather" else BULK_AUTO_MIN_REDUCE_BYTES
+        if self.world in BULK_VERIFIED_WORLDS and not plan.multicast and low <= nbytes <= BULK_AUTO_MAX_BYTES:
             return 1
         return 0
 
