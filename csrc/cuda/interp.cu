@@ -326,6 +326,20 @@ __device__ void mc_store_piece(char* mc_dst, const char* src, long long nvec) {
 
 __device__ void record_failure(const InterpArgs& a, int code, int block, int lane, int wait);
 
+// Books `need` ns on the link clock at *clock, starting no earlier than `ready`; returns the booking's end.  A
+// compare-and-swap loop (bounded: after 4096 lost races the step is booked without the clock).
+__device__ __forceinline__ unsigned long long pace_book(unsigned long long* clock, unsigned long long ready,
+                                                        unsigned long long need) {
+  unsigned long long cur = *reinterpret_cast<volatile unsigned long long*>(clock);
+  for (int tries = 0; tries < 4096; ++tries) {
+    const unsigned long long start = cur > ready ? cur : ready;
+    const unsigned long long prev = atomicCAS(clock, cur, start + need);
+    if (prev == cur) return start + need;
+    cur = prev;
+  }
+  return ready + need;
+}
+
 // Staging state of one CTA: the mbarriers, the shared buffers and the running count of staged tiles (the same
 // in every thread; a tile's buffer is count % kBulkStages and its mbarrier phase parity (count / kBulkStages) & 1).
 struct BulkState {
@@ -619,14 +633,19 @@ __device__ void run_cta(const InterpArgs& a, int block, int lane, unsigned long 
         }
       }
       if (a.pace_group > 0 && (st.op == OP_COPY || st.op == OP_REDUCE) && threadIdx.x == 0 && pr.hi > pr.lo) {
-        // link emulation: a step that pulled from another rank group lasts at least bytes / emulated rate
+        // link emulation: a step that pulled from another rank group books its bytes on this rank's emulated
+        // link (one clock shared by all CTAs of the rank: a token bucket at the rank's share of the link) and
+        // ends no earlier than its booking
         bool crosses = false;
         for (int i = 0; i < st.nsrc; ++i)
           crosses |= (a.srcs[st.src_begin + i].rank / a.pace_group) != (a.rank / a.pace_group);
         if (crosses) {
           const unsigned long long need =
               (unsigned long long)((double)(pr.hi - pr.lo) * esize * st.cnt * a.pace_ns_per_byte);
-          while (globaltimer() - t_step0 < need) {
+          const unsigned long long end = pace_book(&a.control->pace_clock, t_step0, need);
+          // the wait is bounded by the booking itself, and by the launch timeout as a last resort
+          const unsigned long long t0 = globaltimer();
+          while (globaltimer() < end && globaltimer() - t0 < a.timeout_ns) {
           }
         }
       }
@@ -763,7 +782,7 @@ cudaError_t launch_interp(const InterpArgs& a, cudaStream_t stream, int threads)
 void apply_emulation_env(InterpArgs* a) {
   // VERICCL_EMULATE="group=4,gbps=25": pace data steps that read another group of 4 ranks as if each
   // group's inter-group traffic shared one 25 GB/s link: every rank of the group gets an even share
-  // (25/4 GB/s), split across the launch's CTAs.
+  // (25/4 GB/s), which its CTAs share through the rank's link clock (Control::pace_clock).
   const char* env = getenv("VERICCL_EMULATE");
   a->pace_group = 0;
   a->pace_ns_per_byte = 0.f;
@@ -772,7 +791,7 @@ void apply_emulation_env(InterpArgs* a) {
   double gbps = 0;
   if (sscanf(env, "group=%d,gbps=%lf", &group, &gbps) == 2 && group > 0 && gbps > 0) {
     a->pace_group = group;
-    a->pace_ns_per_byte = (float)((double)(a->nblocks * a->nlanes) * group / gbps);
+    a->pace_ns_per_byte = (float)((double)group / gbps);
   }
 }
 

@@ -27,7 +27,9 @@ struct Control {
   unsigned int fp8_arrive;        // CTAs finished in the current fused fp8 AllGather launch
   unsigned int push_arrive;       // CTAs finished in the current push AllGather launch
   unsigned long long push_seq;    // push AllGather launch counter (its start and done flag values)
+  unsigned long long pace_clock;  // link emulation: %globaltimer until which this rank's emulated link is busy
 };
+static_assert(sizeof(Control) <= 256, "workspaces reserve 256 bytes for the control block");
 
 struct InterpArgs {
   const DevBlock* blocks;
@@ -48,7 +50,7 @@ struct InterpArgs {
   Control* control;                  // local control block
   unsigned long long timeout_ns;
   int pace_group;                    // >0: emulate slow links between rank groups of this size
-  float pace_ns_per_byte;            // per-CTA pacing of a data step that reads another group's memory
+  float pace_ns_per_byte;            // emulated link time per byte this rank reads from another group
   int trace;                         // record per-step timestamps into trace buffer
   unsigned long long* trace_buf;     // [nblocks*nlanes][max_steps*niters][2] (start, end) globaltimer
   int trace_stride;
