@@ -198,3 +198,20 @@ def test_link_class_probing_measures_representatives_and_covers_every_link():
         if key.split(":")[0] in ("link", "rrc", "copy", "reduce"):
             assert new_model.services[key][0].source == "measured", key
     assert report["represented"]
+
+
+def test_rank_shares_describe_the_emulated_link():
+    """With rank shares every rank reads from the other groups through its own inter_gbps / group-size resource."""
+    from vericcl_b200.topology.nvswitch import grouped_topology, multinode_topology
+    doc = multinode_topology(2, 4, inter_gbps=25.0, rank_shares=True)
+    shares = {r["id"]: r for r in doc["shared_resources"] if r["id"].startswith("nic-share-rx-")}
+    assert sorted(shares) == ["nic-share-rx-%d" % r for r in sorted(range(8), key=lambda r: "nic-share-rx-%d" % r)]
+    for rid, res in shares.items():
+        rank = int(rid.rsplit("-", 1)[1])
+        assert res["capacity_bytes_per_us"] == 25.0 * 1000.0 / 4
+        assert all(dst == rank and src // 4 != rank // 4 for src, dst in res["links"])
+    plain = grouped_topology([3, 1], rank_shares=False)
+    assert not any(r["id"].startswith("nic-share") for r in plain["shared_resources"])
+    uneven = grouped_topology([3, 1], inter_gbps=30.0, rank_shares=True)
+    caps = {r["id"]: r["capacity_bytes_per_us"] for r in uneven["shared_resources"] if "share" in r["id"]}
+    assert caps["nic-share-rx-0"] == 10000.0 and caps["nic-share-rx-3"] == 30000.0

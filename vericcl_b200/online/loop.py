@@ -5,7 +5,8 @@
 
 Builds the request for an AllReduce over ``groups`` NVSwitch groups joined by
 a slow shared inter-group link (each group's traffic to the other groups
-shares one ``inter_gbps`` resource), emulates that link on one box by pacing
+shares one ``inter_gbps`` resource, split evenly over the group's ranks as the
+emulator enforces it), emulates that link on one box by pacing
 the interpreter's inter-group steps (``VERICCL_EMULATE``), and runs the
 primary workflow with calibration and measured acceptance enabled:
 probe campaign → cost-model refit → verification against the refitted model
@@ -34,7 +35,8 @@ def loop_documents(*, groups: int, per_group: int, inter_gbps: float, size_bytes
     ranks = groups * per_group
     docs = example_documents("allreduce", "hierarchy", ranks, total_size_bytes=size_bytes,
                              slice_size_bytes=slice_bytes or size_bytes // ranks, datatype=datatype,
-                             topology=multinode_topology(groups, per_group, inter_gbps=inter_gbps),
+                             topology=multinode_topology(groups, per_group, inter_gbps=inter_gbps,
+                                                         rank_shares=True),
                              tuning_rounds=rounds, calibration=True, scratch_bytes=4 * size_bytes)
     docs["sketch"]["trace_and_measure"].update({"enabled": True, "pairs": pairs, "max_rounds": 2,
                                                 "max_cv": 0.05, "warmup_iterations": 2, "timed_iterations": 5})

@@ -65,25 +65,31 @@ def hbm_local_costs(ranks: int, hbm_gbps: float = B200_HBM_GBPS) -> list:
 
 def multinode_topology(groups: int, per_group: int, *, intra_gbps: float = B200_NVLINK_GBPS,
                        inter_gbps: float = 25.0, intra_alpha_us: float = B200_ALPHA_US,
-                       inter_alpha_us: float = 5.0) -> dict:
+                       inter_alpha_us: float = 5.0, rank_shares: bool = False) -> dict:
     """Emulated multi-node topology: NVSwitch groups joined by a slow shared link.
 
     Used for the online repair configuration (2 groups × 4 ranks with a
     25 GB/s inter-group link, emulated on one box by throttling channels).
     Each group's outbound and inbound inter-group traffic shares one NIC-like
-    resource of ``inter_gbps``.
+    resource of ``inter_gbps``; ``rank_shares`` adds the emulator's even split
+    of it (see :func:`grouped_topology`).
     """
     return grouped_topology([per_group] * groups, inter_gbps=inter_gbps, inter_alpha_us=inter_alpha_us,
-                            name="emulated-%dx%d" % (groups, per_group))
+                            name="emulated-%dx%d" % (groups, per_group), rank_shares=rank_shares)
 
 
 def grouped_topology(sizes, *, inter_gbps: float = 25.0, inter_alpha_us: float = 5.0, gateways=None,
-                     name: str | None = None) -> dict:
+                     name: str | None = None, rank_shares: bool = False) -> dict:
     """NVSwitch groups of the given sizes (they may differ) joined by slow shared inter-group links.
 
     ``gateways``: per group, the ranks that own the group's inter-group
     links (default: every member); links between non-gateway members of
     different groups are left out, as on nodes whose NICs hang off some GPUs.
+    ``rank_shares``: also give every rank one resource of ``inter_gbps`` / (its
+    group's size) on the inter-group links into it.  That is how the link
+    emulator (``VERICCL_EMULATE``) enforces the shared link: each rank reads
+    from other groups through its own even share, a token bucket, rather than
+    drawing on the group's link while the other members are idle.
     """
     ranks = sum(sizes)
     starts = [sum(sizes[:i]) for i in range(len(sizes))]
@@ -117,6 +123,18 @@ def grouped_topology(sizes, *, inter_gbps: float = 25.0, inter_alpha_us: float =
     for rid, members in sorted(nic.items()):
         doc["shared_resources"].append({"id": rid, "kind": "nic", "capacity_bytes_per_us": inter_gbps * 1000.0,
                                         "links": members})
+    if rank_shares:
+        shares = {}
+        for edge in doc["directed_links"]:
+            if group[edge["src"]] != group[edge["dst"]]:
+                rid = "nic-share-rx-%d" % edge["dst"]
+                shares.setdefault(rid, []).append([edge["src"], edge["dst"]])
+                edge["resources"].append(rid)
+        for rid, members in sorted(shares.items()):
+            dst = members[0][1]
+            doc["shared_resources"].append({"id": rid, "kind": "nic",
+                                            "capacity_bytes_per_us": inter_gbps * 1000.0 / sizes[group[dst]],
+                                            "links": members})
     doc["groups"] = [node["ranks"] for node in doc["nodes"]]
     doc["multicast_groups"] = [node["ranks"] for node in doc["nodes"] if len(node["ranks"]) > 1]
     return doc
