@@ -2,6 +2,7 @@
 
     python -m vericcl_b200.online.loop --project-root runs [--groups 2] [--per-group 4]
         [--inter-gbps 25] [--size-bytes 134217728] [--rounds 3] [--pairs 6] [--datatype float32]
+        [--no-final-measure] [--no-rank-shares]
 
 Builds the request for an AllReduce over ``groups`` NVSwitch groups joined by
 a slow shared inter-group link (each group's traffic to the other groups
@@ -31,12 +32,12 @@ from vericcl_b200.topology.nvswitch import multinode_topology
 
 
 def loop_documents(*, groups: int, per_group: int, inter_gbps: float, size_bytes: int, rounds: int,
-                   datatype: str, pairs: int, slice_bytes: int | None = None) -> dict:
+                   datatype: str, pairs: int, slice_bytes: int | None = None, rank_shares: bool = True) -> dict:
     ranks = groups * per_group
     docs = example_documents("allreduce", "hierarchy", ranks, total_size_bytes=size_bytes,
                              slice_size_bytes=slice_bytes or size_bytes // ranks, datatype=datatype,
                              topology=multinode_topology(groups, per_group, inter_gbps=inter_gbps,
-                                                         rank_shares=True),
+                                                         rank_shares=rank_shares),
                              tuning_rounds=rounds, calibration=True, scratch_bytes=4 * size_bytes)
     docs["sketch"]["trace_and_measure"].update({"enabled": True, "pairs": pairs, "max_rounds": 2,
                                                 "max_cv": 0.05, "warmup_iterations": 2, "timed_iterations": 5})
@@ -48,14 +49,14 @@ def loop_documents(*, groups: int, per_group: int, inter_gbps: float, size_bytes
 
 def run_loop(project_root, *, groups: int = 2, per_group: int = 4, inter_gbps: float = 25.0,
              size_bytes: int = 128 << 20, rounds: int = 3, datatype: str = "float32", pairs: int = 6,
-             case: str = "online-loop", measure_final: bool = True) -> dict:
+             case: str = "online-loop", measure_final: bool = True, rank_shares: bool = True) -> dict:
     emulate = "group=%d,gbps=%g" % (per_group, inter_gbps)
     previous = os.environ.get("VERICCL_EMULATE")
     os.environ["VERICCL_EMULATE"] = emulate
     try:
         return _run_loop(Path(project_root), emulate, groups=groups, per_group=per_group, inter_gbps=inter_gbps,
                          size_bytes=size_bytes, rounds=rounds, datatype=datatype, pairs=pairs, case=case,
-                         measure_final=measure_final)
+                         measure_final=measure_final, rank_shares=rank_shares)
     finally:
         if previous is None:
             os.environ.pop("VERICCL_EMULATE", None)
@@ -64,11 +65,11 @@ def run_loop(project_root, *, groups: int = 2, per_group: int = 4, inter_gbps: f
 
 
 def _run_loop(root: Path, emulate: str, *, groups, per_group, inter_gbps, size_bytes, rounds, datatype, pairs, case,
-              measure_final) -> dict:
+              measure_final, rank_shares=True) -> dict:
     from vericcl_b200.cli.main import main as cli_main
     from vericcl_b200.utils.jsonio import strict_load
     docs = loop_documents(groups=groups, per_group=per_group, inter_gbps=inter_gbps, size_bytes=size_bytes,
-                          rounds=rounds, datatype=datatype, pairs=pairs)
+                          rounds=rounds, datatype=datatype, pairs=pairs, rank_shares=rank_shares)
     files = write_documents(root / "inputs" / case, docs)
     run_id = "loop-%s" % time.strftime("%Y%m%d-%H%M%S")
     argv = ["solve", "--project-root", str(root), "--case", case, "--run-id", run_id]
@@ -137,10 +138,13 @@ def main(argv=None) -> int:
     ap.add_argument("--pairs", type=int, default=6)
     ap.add_argument("--datatype", default="float32")
     ap.add_argument("--no-final-measure", action="store_true")
+    ap.add_argument("--no-rank-shares", action="store_true",
+                    help="describe only the group-shared link, not the emulator's per-rank shares of it")
     args = ap.parse_args(argv)
     summary = run_loop(args.project_root, groups=args.groups, per_group=args.per_group, inter_gbps=args.inter_gbps,
                        size_bytes=args.size_bytes, rounds=args.rounds, datatype=args.datatype, pairs=args.pairs,
-                       case=args.case, measure_final=not args.no_final_measure)
+                       case=args.case, measure_final=not args.no_final_measure,
+                       rank_shares=not args.no_rank_shares)
     print(json.dumps(summary, default=str))
     return 0 if summary.get("exit_code") == 0 else 1
 

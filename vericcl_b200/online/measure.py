@@ -1,5 +1,14 @@
 """Device-timed schedule measurement and the workflow's measured-acceptance hook.
 
+    python -m vericcl_b200.online.measure --inputs DIR --xml schedule.xml [--sidecar schedule.json]
+        [--emulate group=2,gbps=25] [--no-measure] [--iters 10] [--warmup 3]
+
+prints, for one solved schedule and the request documents in ``DIR``
+(topology/sketch/atom/runtime.json), its predicted time under that topology
+(with ``--sidecar``: the initial cost model of the request, exact event
+simulation) and its device time on the local GPUs (C-API driver, slowest rank
+per invocation, mean over ``--iters``), optionally on an emulated slow link.
+
 ``native_measure`` runs one XML schedule on the local GPUs through the C-API
 driver and returns the mean per-invocation device time (slowest rank per
 invocation).  ``measured_acceptance`` builds the workflow hook: for an
@@ -49,3 +58,44 @@ def measured_acceptance(request, ledger_path, *, measure=None):
                                 alpha=alpha, max_cv=cfg["max_cv"], max_rounds=cfg["max_rounds"],
                                 min_relative_gain=cfg["min_relative_gain"])
     return hook
+
+
+def main(argv=None) -> int:
+    import argparse
+    import json
+    import os
+    from pathlib import Path
+
+    ap = argparse.ArgumentParser(prog="vericcl_b200.online.measure")
+    ap.add_argument("--inputs", required=True, help="folder with topology/sketch/atom/runtime.json")
+    ap.add_argument("--xml", required=True)
+    ap.add_argument("--sidecar", default=None, help="the schedule's sidecar (schedule.json): also predict")
+    ap.add_argument("--emulate", default=None, help="VERICCL_EMULATE for the measurement, e.g. group=2,gbps=25")
+    ap.add_argument("--no-measure", action="store_true")
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    args = ap.parse_args(argv)
+    from vericcl_b200.input.loader import load_request
+    inputs = Path(args.inputs)
+    files = {k: inputs / (k + ".json") for k in ("topology", "sketch", "atom", "runtime")}
+    xml = Path(args.xml).read_text()
+    out = {"xml": args.xml, "inputs": args.inputs}
+    if args.sidecar:
+        from vericcl_b200.program.sidecar import bundle_from_sidecar
+        from vericcl_b200.topology import load_topology
+        from vericcl_b200.utils.jsonio import strict_load
+        request = load_request(files, purpose="verify")
+        bundle = bundle_from_sidecar(request, load_topology(request), xml, strict_load(args.sidecar))
+        out["t_pred_us"] = bundle.t_pred_us
+    if not args.no_measure:
+        if args.emulate:
+            os.environ["VERICCL_EMULATE"] = args.emulate
+        out["emulate"] = os.environ.get("VERICCL_EMULATE")
+        out["device_us"] = native_measure(xml, load_request(files, [], purpose="solve"), iters=args.iters,
+                                          warmup=args.warmup)
+    print(json.dumps(out))
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
