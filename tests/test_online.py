@@ -96,8 +96,11 @@ def test_clock_alignment_and_trace(tmp_path):
     assert report["global_span_us"] > 0 and report["tails"]
 
 
-def test_online_loop_two_groups_without_gpu(tmp_path):
+def test_online_loop_two_groups_without_gpu(tmp_path, capsys):
     """The emulated 2×4 online loop runs end to end; without GPUs calibration and measurement are skipped."""
+    import json
+    from pathlib import Path
+    from vericcl_b200.online import measure
     from vericcl_b200.online.loop import loop_documents, run_loop
     docs = loop_documents(groups=2, per_group=4, inter_gbps=25.0, size_bytes=1 << 23, rounds=1,
                           datatype="float32", pairs=4)
@@ -108,6 +111,13 @@ def test_online_loop_two_groups_without_gpu(tmp_path):
     assert summary["best"]["checks"]["semantic"]["status"] == "valid"
     assert len(summary["rounds"]) == 1
     assert summary["rounds"][0]["cut_lower_bound_us"] <= summary["rounds"][0]["start_t_pred_us"]
+    # the measure CLI re-predicts the solved schedule from its sidecar (no GPU: prediction only)
+    run = Path(summary["run"])
+    capsys.readouterr()
+    assert measure.main(["--inputs", str(tmp_path / "inputs" / "online-loop"), "--xml", str(run / "schedule.xml"),
+                         "--sidecar", str(run / "schedule.json"), "--no-measure"]) == 0
+    out = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert abs(out["t_pred_us"] - summary["best"]["t_pred_us"]) < 1e-6 * out["t_pred_us"]
 
 
 def test_trace_buffer_decoding_with_uneven_blocks():
