@@ -1,0 +1,109 @@
+"""Unit tests of helpers otherwise exercised only through the workflow: strict JSON, the isomorphism signature,
+bandwidth packing of broadcast trees and the fixed-route timing MILP."""
+import json
+
+import pytest
+
+from vericcl_b200.composer import compose_routes
+from vericcl_b200.errors import InputValidationError
+from vericcl_b200.examples import example_documents
+from vericcl_b200.input.loader import resolve_documents
+from vericcl_b200.solver.demands import build_demands
+from vericcl_b200.solver.routing import choose_trees
+from vericcl_b200.synthesis import plan_for
+from vericcl_b200.topology import load_topology
+from vericcl_b200.topology.nvswitch import grouped_topology, nvswitch_topology
+from vericcl_b200.utils.jsonio import atomic_write_json, canonical_dumps, strict_load, strict_loads
+
+
+def _topology(doc, ranks, coll="allgather", slices=1, size=1 << 20):
+    d = example_documents(coll, "hierarchy", ranks, total_size_bytes=size * slices, slice_size_bytes=size,
+                          topology=doc, scratch_bytes=size * slices * ranks)
+    req = resolve_documents(d)
+    return req, load_topology(req)
+
+
+# -- strict JSON ---------------------------------------------------------------------------------------------------
+def test_strict_json_rejects_duplicates_non_finite_and_deep_nesting():
+    assert strict_loads('{"a": 1, "b": [1, 2.5]}') == {"a": 1, "b": [1, 2.5]}
+    for bad in ('{"a": 1, "a": 2}', '{"a": NaN}', '[Infinity]', '{"a": -Infinity}', '{"a": '):
+        with pytest.raises(InputValidationError):
+            strict_loads(bad)
+    with pytest.raises(InputValidationError):
+        strict_loads("[" * 70 + "]" * 70)
+
+
+def test_canonical_dumps_is_order_independent_and_atomic_write_round_trips(tmp_path):
+    a, b = {"z": 1, "a": [1, {"y": 2, "b": 3}]}, {"a": [1, {"b": 3, "y": 2}], "z": 1}
+    assert canonical_dumps(a) == canonical_dumps(b)
+    with pytest.raises(InputValidationError):
+        canonical_dumps({"x": float("nan")})
+    path = atomic_write_json(tmp_path / "sub" / "doc.json", a)
+    assert strict_load(path) == a and json.loads(path.read_text()) == a
+    assert not [p for p in path.parent.iterdir() if p.name != "doc.json"]      # no temporary file left behind
+
+
+# -- isomorphism signature -----------------------------------------------------------------------------------------
+def _slow(pairs, ranks=4):
+    doc = nvswitch_topology(ranks, nvls=False)
+    for e in doc["directed_links"]:
+        if (e["src"], e["dst"]) in pairs:
+            e["beta_us_per_byte"] *= 4
+    return doc
+
+
+def test_signature_is_invariant_under_relabelling_and_sees_cost_changes():
+    from vericcl_b200.topology.isomorphism import canonical_labelling, exact_domain_signature
+    _, base = _topology(_slow({(0, 1), (1, 0)}), 4)             # one slow pair breaks the full symmetry
+    _, moved = _topology(_slow({(2, 3), (3, 2)}), 4)            # the same domain with ranks relabelled
+    assert exact_domain_signature(base) == exact_domain_signature(moved)
+    sig, mapping = canonical_labelling(base)
+    assert sorted(mapping) == [0, 1, 2, 3] and sorted(mapping.values()) == [0, 1, 2, 3]
+    _, changed = _topology(_slow({(0, 1), (1, 0), (2, 3)}), 4)  # a third slow link: not isomorphic any more
+    assert exact_domain_signature(changed) != sig
+    _, full = _topology(_slow(set()), 4)
+    assert exact_domain_signature(full) not in (sig, exact_domain_signature(changed))
+
+
+# -- bandwidth packing ---------------------------------------------------------------------------------------------
+def test_packing_spans_every_destination_and_respects_the_budget():
+    from fractions import Fraction
+    from vericcl_b200.solver.trees.packing import min_time_budget, pack_bandwidth
+    _, topo = _topology(grouped_topology([2, 2], inter_gbps=25.0), 4)
+    budget, trees = pack_bandwidth(topo, 0, [1, 2, 3], 4, 1 << 20)
+    assert sum(count for _, count in trees) == 4
+    for edges, _ in trees:
+        reached = {0} | {b for _, b in edges}
+        assert {1, 2, 3} <= reached
+        assert all(b != 0 for _, b in edges)                   # nothing flows back into the root
+    assert budget >= min_time_budget(topo, 0, [1, 2, 3], 4, 1 << 20)
+    assert isinstance(budget, Fraction) and budget > 0
+
+
+# -- fixed-route timing MILP ---------------------------------------------------------------------------------------
+def test_timing_milp_respects_dependencies_and_connections():
+    from vericcl_b200.solver.timing import makespan, optimize_fixed_routes
+    s = 4096
+    d = example_documents("allreduce", "hierarchy", 4, total_size_bytes=s * 8, slice_size_bytes=s,
+                          max_channels=2, scratch_bytes=s * 8 * 4)
+    req = resolve_documents(d)
+    topo = load_topology(req)
+    plan = plan_for(req, topo)
+    dem = build_demands(plan, topo, s)
+    net = compose_routes(plan, dem, choose_trees(dem, topo, s), topo, s, channels=2, origin="direct")
+    timed = optimize_fixed_routes(net, topo, time_limit=2.0)
+    assert "+timing" in timed.origin
+    ops = {op.operation_id: op for op in timed.operations}
+    from vericcl_b200.topology.model import LinkKey
+    dur = {k: topo.link(LinkKey(op.src_rank, op.dst_rank)).time_us(s) for k, op in ops.items()}
+    for op in ops.values():
+        for dep in op.dependencies:
+            assert op.priority_time >= ops[dep].priority_time + dur[dep] - 1e-6
+    by_conn = {}
+    for op in ops.values():
+        by_conn.setdefault((op.src_rank, op.dst_rank, op.channel), []).append(op)
+    for members in by_conn.values():
+        members.sort(key=lambda o: o.priority_time)
+        for a, b in zip(members, members[1:]):
+            assert b.priority_time >= a.priority_time + dur[a.operation_id] - 1e-6
+    assert makespan(timed, topo) > 0

@@ -68,7 +68,6 @@ def extract_arborescences(topology, root, dests, k: int, slice_bytes: int, budge
     g = _capacity_graph(topology, allowed, budget, slice_bytes)
     trees = []
     remaining = k
-    targets = set(dests) | {root}
     while remaining > 0:
         h = nx.DiGraph()
         for a, b, data in g.edges(data=True):
@@ -95,8 +94,6 @@ def extract_arborescences(topology, root, dests, k: int, slice_bytes: int, budge
             g[a][b]["capacity"] -= count
         trees.append((edges, count))
         remaining -= count
-        del targets
-        targets = set()
     return trees
 
 
