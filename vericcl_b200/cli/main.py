@@ -1,10 +1,11 @@
-"""Command line: ``python -m vericcl_b200 {solve,verify,calibrate,inspect,resume}``.
+"""Command line: ``python -m vericcl_b200 {solve,verify,calibrate,inspect,resume,manual-generate}``.
 
 Arguments mirror the reference CLI (vericcl/cli/main.py:22-80): the four
 input files, ``--project-root``, ``--case``, ``--run-id``, repeated
 ``--set FIELD=JSON`` overrides and ``--override-input``; ``verify`` adds
 ``--xml --sidecar --model [--tune]``; ``inspect`` and ``resume`` take
-``--run``.  Exit codes: 0 ok, 2 invalid input, 5 semantic failure, 7 budget,
+``--run``; ``manual-generate`` writes an editable manual-stage input folder
+(``--out``) from the four inputs.  Exit codes: 0 ok, 2 invalid input, 5 semantic failure, 7 budget,
 8 runtime failure, 130 interrupted.
 """
 from __future__ import annotations
@@ -44,6 +45,12 @@ def build_parser():
     i.add_argument("--run", required=True)
     r = sub.add_parser("resume", help="continue a run from its checkpoint")
     r.add_argument("--run", required=True)
+    m = sub.add_parser("manual-generate", help="write an editable manual-stage plan as a new input folder")
+    for name in ("topology", "sketch", "atom", "runtime"):
+        m.add_argument("--" + name, required=True)
+    m.add_argument("--out", required=True, help="folder for the four documents with atom.manual enabled")
+    m.add_argument("--from", dest="source", choices=("direct", "hierarchy"), default="direct",
+                   help="the plan whose stages become manual nodes")
     return parser
 
 
@@ -145,6 +152,38 @@ def resume_run(args) -> int:
     return 0 if result.status == "ok" else 5
 
 
+def manual_generate(args) -> int:
+    """Manual nodes (stages, groups, roots, dependencies, input/output states) from the direct or hierarchy plan
+    of the given inputs, written with the other three documents into ``--out``; the result is re-planned once
+    to check it (reference: README.md "manual-generate")."""
+    from vericcl_b200.examples import write_documents
+    from vericcl_b200.input.loader import load_request
+    from vericcl_b200.planner.direct import build_direct_plan
+    from vericcl_b200.planner.manual import manual_nodes_from_plan, plan_manual
+    from vericcl_b200.topology import load_topology
+    from vericcl_b200.utils.jsonio import strict_load
+    files = _files(args)
+    docs = {name: strict_load(path) for name, path in files.items()}
+    request = load_request(files)
+    topology = load_topology(request)
+    if args.source == "hierarchy":
+        from vericcl_b200.planner.hierarchy import plan_hierarchy
+        plan = plan_hierarchy(request, topology)
+    else:
+        plan = build_direct_plan(request, topology)
+    nodes = manual_nodes_from_plan(plan)
+    atom = dict(docs["atom"])
+    manual = dict(atom.get("manual") or {})
+    manual.update(enabled=True, nodes=nodes)
+    atom["manual"] = manual
+    docs["atom"] = atom
+    paths = write_documents(Path(args.out), docs)
+    checked = plan_manual(load_request(paths), topology)
+    print(json.dumps({"out": str(Path(args.out)), "nodes": len(nodes),
+                      "stages": len({n["stage_id"] for n in nodes}), "planned_nodes": len(checked.nodes)}))
+    return 0
+
+
 def main(argv=None) -> int:
     parser = build_parser()
     args = parser.parse_args(argv)
@@ -153,6 +192,8 @@ def main(argv=None) -> int:
             return new_run(args)
         if args.command == "inspect":
             return inspect_run(args)
+        if args.command == "manual-generate":
+            return manual_generate(args)
         return resume_run(args)
     except KeyboardInterrupt:
         return 130
