@@ -9,7 +9,6 @@ mismatch.  Used by tests/test_gpu_multi.py.
 import json
 import os
 import sys
-import time
 import zlib
 
 import torch

@@ -1,6 +1,5 @@
 """Inventory coverage report (vericcl_b200/coverage.py) and the example catalog runner."""
 import json
-import re
 from pathlib import Path
 
 from vericcl_b200.coverage import DEFAULT_REQUIREMENTS, coverage, main, render

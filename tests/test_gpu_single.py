@@ -121,7 +121,6 @@ def test_engine_collectives_on_strided_views(comm):
 
 
 def test_trace_capture(comm):
-    from vericcl_b200.online.clock_sync import align_bracketed_globaltimers
     from vericcl_b200.online.trace import analyze_trace_causality, capture_once
     from vericcl_b200.synthesis import schedule_xml
     plan = comm.compile(schedule_xml("allreduce", 1, 1), nlanes=8, niters=2)

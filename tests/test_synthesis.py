@@ -1,4 +1,3 @@
-import numpy as np
 import pytest
 
 from vericcl_b200.examples import example_documents

@@ -1,6 +1,5 @@
 """Job transport on the CPU: ranks on "remote" hosts through fake ssh/scp, ownership, inventory, manifests."""
 import json
-import os
 import stat
 import sys
 from pathlib import Path

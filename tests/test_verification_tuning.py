@@ -5,11 +5,10 @@ from vericcl_b200.input.loader import resolve_documents
 from vericcl_b200.performance.initial import initial_cost_model
 from vericcl_b200.synthesis import Lowerer, synthesize
 from vericcl_b200.topology import load_topology
-from vericcl_b200.topology.nvswitch import multinode_topology
 from vericcl_b200.tuning.strategies import solve_repair, variant_path, variant_reshape
 from vericcl_b200.verification.bdd import BDD, select_compatible
 from vericcl_b200.verification.bottlenecks import analyze
-from vericcl_b200.verification.global_bound import certify_global_cut, check_global_cut
+from vericcl_b200.verification.global_bound import certify_global_cut
 
 
 def test_bdd_counts_and_selects():

@@ -14,7 +14,6 @@ from __future__ import annotations
 import hashlib
 import time
 from datetime import datetime, timezone
-from pathlib import Path
 
 from vericcl_b200.errors import RuntimeFailure
 from vericcl_b200.execution.events import verify_sequence

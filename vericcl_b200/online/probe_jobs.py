@@ -17,7 +17,7 @@ probe_jobs.py:16-216, probe_xml.py:13).
 """
 from __future__ import annotations
 
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 from itertools import combinations
 
 PRIORITY = {"link_intra": 0, "local": 1, "link_inter": 2, "shared": 3}

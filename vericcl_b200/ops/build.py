@@ -19,7 +19,6 @@ import functools
 import hashlib
 import os
 import threading
-import shutil
 import subprocess
 import sys
 import sysconfig

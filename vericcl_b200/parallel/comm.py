@@ -24,7 +24,7 @@ import torch
 
 from vericcl_b200.errors import RuntimeFailure
 from vericcl_b200.ops import native
-from vericcl_b200.program.device import DTYPES, REDOPS, REDUCING
+from vericcl_b200.program.device import REDOPS, REDUCING
 
 DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 TORCH_DTYPES = {"float32": torch.float32, "bfloat16": torch.bfloat16, "float16": torch.float16}

@@ -6,7 +6,7 @@ Logical values (contributor sets) and physical addresses are kept apart:
 """
 from __future__ import annotations
 
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 from typing import Mapping
 
 

@@ -22,7 +22,6 @@ which derives the first, fourth and fifth kinds from its MSCCL limits).
 from __future__ import annotations
 
 import math
-from dataclasses import replace
 
 from vericcl_b200.errors import InputValidationError
 from vericcl_b200.semantics.collective import PARTITIONED

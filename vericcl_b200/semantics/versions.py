@@ -13,7 +13,6 @@ from __future__ import annotations
 from dataclasses import dataclass
 from typing import Mapping
 
-from vericcl_b200.errors import SemanticError
 from vericcl_b200.semantics.collective import CollectiveKind, CollectiveSpec, input_ranks, required_outputs
 
 

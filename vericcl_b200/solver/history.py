@@ -11,7 +11,6 @@ vericcl/solver/history_index.py:62-146).
 from __future__ import annotations
 
 import json
-import re
 import time
 from pathlib import Path
 

@@ -13,7 +13,6 @@ which uses a SCIP integer master with lazily generated tree columns).
 from __future__ import annotations
 
 import networkx as nx
-import numpy as np
 
 from vericcl_b200.errors import SolverError
 from vericcl_b200.solver.milp import Model

@@ -10,7 +10,7 @@ from __future__ import annotations
 
 import itertools
 
-from vericcl_b200.topology.model import LinkKey, Topology
+from vericcl_b200.topology.model import Topology
 from vericcl_b200.utils.hashing import digest
 
 

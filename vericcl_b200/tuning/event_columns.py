@@ -16,7 +16,6 @@ active-mode rates inside a SCIP disjunction model).
 """
 from __future__ import annotations
 
-from dataclasses import replace
 
 from vericcl_b200.composer.compose import NetworkCandidate
 from vericcl_b200.errors import SemanticError
