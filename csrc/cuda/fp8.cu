@@ -221,29 +221,40 @@ __global__ void __launch_bounds__(kFp8Threads) fp8_allgather_kernel(const Fp8AgA
   const long long esize = DT == DT_F32 ? 4 : 2;
   char* my_stage = a.base[a.rank] + par_off;
   char* out = static_cast<char*>(a.out);
-  // ---- phase A: quantize this rank's groups, write their dequantized values into our own part
-  for (long long base = g0 + (threadIdx.x & ~31); base < g1; base += kFp8Threads) {
-    const long long g = base + lane;
-    const bool live = g < g1;
-    float f[16];
-    float amax = 0.f;
-    if (live) {
-      load16<DT>(a.in, g, f);
+  // ---- phase A: quantize this rank's groups, write their dequantized values into our own part.  Each thread
+  // loads two groups (kFp8Threads apart) before it works on either, so twice the input is in flight.
+  constexpr int UA = 2;
+  for (long long base = g0 + (threadIdx.x & ~31); base < g1; base += (long long)UA * kFp8Threads) {
+    float f[UA][16];
+    bool live[UA];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(f[i]));
+    for (int u = 0; u < UA; ++u) {
+      const long long g = base + (long long)u * kFp8Threads + lane;
+      live[u] = g < g1;
+      if (live[u]) load16<DT>(a.in, g, f[u]);
     }
-    // the 8 lanes of one 128-element block (aligned: base is a multiple of 32 groups) share its amax
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
-    const float scale = amax > 0.f ? amax / 448.f : 1.f;
-    if (live) {
-      const uint4 q = encode16(f, 1.f / scale);
-      *reinterpret_cast<uint4*>(my_stage + g * 16) = q;
-      if ((g % kGroupsPerBlock) == 0)
-        reinterpret_cast<float*>(my_stage + pad16(a.n))[g / kGroupsPerBlock] = scale;
-      decode16(q, scale, f);
-      store16<DT>(out + (long long)a.rank * a.n * esize, g, f);
+#pragma unroll
+    for (int u = 0; u < UA; ++u) {
+      const long long g = base + (long long)u * kFp8Threads + lane;
+      float amax = 0.f;
+      if (live[u]) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(f[u][i]));
+      }
+      // the 8 lanes of one 128-element block (aligned: base is a multiple of 32 groups, and so is
+      // u * kFp8Threads) share its amax; every lane of the warp takes part in the shuffles
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+      const float scale = amax > 0.f ? amax / 448.f : 1.f;
+      if (live[u]) {
+        const uint4 q = encode16(f[u], 1.f / scale);
+        *reinterpret_cast<uint4*>(my_stage + g * 16) = q;
+        if ((g % kGroupsPerBlock) == 0)
+          reinterpret_cast<float*>(my_stage + pad16(a.n))[g / kGroupsPerBlock] = scale;
+        decode16(q, scale, f[u]);
+        store16<DT>(out + (long long)a.rank * a.n * esize, g, f[u]);
+      }
     }
   }
   __syncthreads();
