@@ -107,3 +107,44 @@ def test_timing_milp_respects_dependencies_and_connections():
         for a, b in zip(members, members[1:]):
             assert b.priority_time >= a.priority_time + dur[a.operation_id] - 1e-6
     assert makespan(timed, topo) > 0
+
+
+# -- paths ---------------------------------------------------------------------------------------------------------
+def test_shortest_path_sets_respect_allowed_ranks_and_hop_count():
+    from vericcl_b200.topology.paths import path_links, path_time_us, shortest_path_set
+    doc = nvswitch_topology(4, nvls=False)
+    doc["directed_links"] = [e for e in doc["directed_links"] if (e["src"], e["dst"]) != (0, 3)]
+    for res in doc["shared_resources"]:
+        res["links"] = [pair for pair in res["links"] if tuple(pair) != (0, 3)]
+    _, topo = _topology(doc, 4)
+    paths = shortest_path_set(topo, 0, 3)
+    assert sorted(paths) == [(0, 1, 3), (0, 2, 3)]                  # two hops, both relays
+    assert shortest_path_set(topo, 0, 3, allowed={0, 2, 3}) == [(0, 2, 3)]
+    assert shortest_path_set(topo, 0, 3, allowed={0, 3}) == []
+    assert shortest_path_set(topo, 0, 3, limit=1) in ([(0, 1, 3)], [(0, 2, 3)])
+    assert [(k.src, k.dst) for k in path_links((0, 2, 3))] == [(0, 2), (2, 3)]
+    one = path_time_us(topo, (0, 2), 1 << 20)
+    assert path_time_us(topo, (0, 2, 3), 1 << 20) == pytest.approx(2 * one)
+
+
+# -- publication ---------------------------------------------------------------------------------------------------
+def test_publication_writes_every_artifact_and_a_report(tmp_path):
+    import zipfile
+    from vericcl_b200.execution.context import RunContext
+    from vericcl_b200.execution.publication import publish_results
+    ctx = RunContext.create(tmp_path, "case", "solve", run_id="r1", input_files={})
+    (ctx.process / "events.jsonl").write_text('{"event": "x"}\n')
+    best = {"t_pred_us": 12.5, "model_version": "m1", "origin": "direct",
+            "checks": {"semantic": {"status": "valid", "detail": None},
+                       "storage": {"status": "valid", "detail": "a|b"}}}
+    result = {"status": "ok", "stop_reason": "round limit",
+              "recommendations": [{"kind": "slice", "parameters": {"slice_size_bytes": 4096},
+                                   "reason_codes": ["step_limit"], "requires_resolve": True}]}
+    publish_results(ctx, xml="<algo/>", sidecar={"a": 1}, model={"version": "m1"}, result=result, best=best)
+    for name in ("schedule.xml", "schedule.json", "model.json", "report.md", "details.zip"):
+        assert (ctx.directory / name).exists(), name
+    report = (ctx.directory / "report.md").read_text()
+    assert "T_pred: 12.500 us" in report and "| storage | valid | a/b |" in report
+    assert "| slice | slice_size_bytes=4096 | step_limit | yes |" in report
+    with zipfile.ZipFile(ctx.directory / "details.zip") as z:
+        assert any(n.endswith("events.jsonl") for n in z.namelist())
