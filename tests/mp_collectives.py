@@ -74,7 +74,8 @@ def main():
         dname = str(dtype).split(".")[-1]
         xml = schedule_xml(coll, world, slices, inplace=inplace, datatype=dname)
         op = "avg" if coll == "allreduce" and lanes == 4 else "sum"
-        plan = comm.compile(xml, nlanes=lanes, niters=iters, push=push,
+        # VERICCL_MERGE=0: every XML thread block on CTAs of its own (the unmerged device program)
+        plan = comm.compile(xml, nlanes=lanes, niters=iters, push=push, merge=os.environ.get("VERICCL_MERGE") != "0",
                             multicast=comm.multicast and not push and coll in ("allreduce", "allgather"))
         seed = zlib.crc32(repr((coll, dname, inplace, slices, lanes, iters, count)).encode()) % 100000
         x = inputs_for(rank, count, dtype, seed).cuda()
