@@ -153,23 +153,25 @@ def test_publication_writes_every_artifact_and_a_report(tmp_path):
 # -- work graph records --------------------------------------------------------------------------------------------
 def test_work_operations_validate_their_kind_rules():
     from vericcl_b200.errors import SemanticError
-    from vericcl_b200.performance.events import COMM_KINDS, Executable, WorkOperation
+    from vericcl_b200.performance.events import COMM_KINDS, Executable, Movement, WorkOperation
     assert COMM_KINDS == {"send", "rrc", "mc_reduce", "mc_store"}
-    send = WorkOperation("s", "send", "link:0:1", 4096, flow_id="f", resources=("nvlink-tx-0",))
-    copy = WorkOperation("c", "copy", "copy:0", 4096, dependencies=("s",))
-    nop = WorkOperation("n", "nop", None, 0, dependencies=("c",))
+    send = WorkOperation("s", "send", Movement("link:0:1", 4096), flow_id="f", crosses=("nvlink-tx-0",))
+    copy = WorkOperation("c", "copy", Movement("copy:0", 4096), after=("s",))
+    nop = WorkOperation("n", "nop", after=("c",), release_us=2.5)
     exe = Executable((send, copy, nop), output_operations=("n",))
-    assert exe.by_id()["c"].dependencies == ("s",) and exe.output_operations == ("n",)
-    bad = [lambda: WorkOperation("x", "teleport", "k", 1),
-           lambda: WorkOperation("x", "send", "k", 16),                        # network work without a flow
-           lambda: WorkOperation("x", "copy", None, 16),                       # data without a cost component
-           lambda: WorkOperation("x", "nop", "k", 0),                          # a nop with a cost component
-           lambda: WorkOperation("x", "copy", "k", 16, resources=("r",)),      # local work on a shared resource
-           lambda: WorkOperation("x", "copy", "k", -1),
-           lambda: WorkOperation("x", "copy", "k", True),
-           lambda: WorkOperation("x", "copy", "k", 16, dependencies=("a", "a")),
-           lambda: WorkOperation("x", "copy", "k", 16, source_override="measured"),
-           lambda: Executable((copy,)),                                        # waits for an unknown operation
+    assert exe.by_id()["c"].after == ("s",) and exe.output_operations == ("n",)
+    assert (copy.component, copy.nbytes, nop.component, nop.nbytes) == ("copy:0", 4096, None, 0)
+    bad = [lambda: WorkOperation("x", "teleport", Movement("k", 1)),
+           lambda: WorkOperation("x", "send", Movement("k", 16)),              # network work without a flow
+           lambda: WorkOperation("x", "copy"),                                # data work without a movement
+           lambda: WorkOperation("x", "nop", Movement("k", 16)),              # a nop that moves data
+           lambda: WorkOperation("x", "copy", Movement("k", 16), crosses=("r",)),   # local work on a shared resource
+           lambda: Movement("k", 0),
+           lambda: Movement("k", True),
+           lambda: Movement("", 16),
+           lambda: WorkOperation("x", "copy", Movement("k", 16), after=("a", "a")),
+           lambda: WorkOperation("x", "copy", Movement("k", 16), estimated="yes"),
+           lambda: Executable((copy,)),                                       # waits for an unknown operation
            lambda: Executable((send, send)),
            lambda: Executable((send,), output_operations=("zz",))]
     for make in bad:

@@ -4,7 +4,7 @@ The rules (the behaviour the reference specifies for its predictor,
 vericcl/performance/simulation.py:136; the algorithm below is this project's):
 
 * An operation is *released* once all its dependencies have completed and its
-  ``not_before_us`` has passed.  A dependency-only operation completes there.
+  ``release_us`` has passed.  A dependency-only operation completes there.
 * A released data operation first spends its segment's α moving nothing,
   then drains its payload as a fluid whose rate is constant between two
   consecutive events (a release, the end of an α, a completion).
@@ -39,6 +39,7 @@ from vericcl_b200.performance.model import CostModel
 
 _MEASURED = frozenset({"measured", "history"})
 SHARED_ESTIMATE = "initial_sharing_estimate"
+ESTIMATED = "estimated"             # the source label of work marked estimated (priced, not measured)
 
 
 @dataclass(frozen=True)
@@ -64,8 +65,8 @@ class Prediction:
         ops = executable.by_id()
         node = max(self.end_times, key=lambda k: (self.end_times[k], k))
         chain = [node]
-        while ops[node].dependencies:
-            node = max(ops[node].dependencies, key=lambda k: (self.end_times.get(k, 0.0), k))
+        while ops[node].after:
+            node = max(ops[node].after, key=lambda k: (self.end_times.get(k, 0.0), k))
             chain.append(node)
         chain.reverse()
         return chain
@@ -95,9 +96,9 @@ class _Numbers:
 def _successors_in_order(executable: Executable):
     """Successor lists, and a check that the dependency graph has no cycle (iterative depth-first search)."""
     succ = {op.operation_id: [] for op in executable.operations}
-    deps = {op.operation_id: op.dependencies for op in executable.operations}
+    deps = {op.operation_id: op.after for op in executable.operations}
     for op in executable.operations:
-        for d in op.dependencies:
+        for d in op.after:
             succ[d].append(op.operation_id)
     state = dict.fromkeys(deps, 0)          # 0 unseen, 1 on the stack, 2 finished
     for root in deps:
@@ -123,7 +124,7 @@ def _sharing_groups(active_ops):
     """Partition network operations into groups connected through common resources (breadth-first search)."""
     users: dict = {}
     for op in active_ops:
-        for r in op.resources:
+        for r in op.crosses:
             users.setdefault(r, []).append(op)
     seen, groups = set(), []
     for op in active_ops:
@@ -134,7 +135,7 @@ def _sharing_groups(active_ops):
         while frontier:
             cur = frontier.pop()
             group.append(cur)
-            for r in cur.resources:
+            for r in cur.crosses:
                 for other in users[r]:
                     if other.operation_id not in seen:
                         seen.add(other.operation_id)
@@ -193,26 +194,26 @@ class _Replay:
         for key, op in self.ops.items():
             if op.kind == "nop":
                 continue
-            seg = self.model.service_for(op.cost_key, op.payload_bytes)
+            seg = self.model.service_for(op.component, op.nbytes)
             if seg is None:
-                self.missing.add("service:" + op.cost_key)
+                self.missing.add("service:" + op.component)
                 blocked.add(key)
             else:
                 self.seg[key] = seg
-            for r in op.resources:
+            for r in op.crosses:
                 if self.model.capacity(r) is None:
                     self.missing.add("resource:" + r)
                     blocked.add(key)
         # whatever waits for, or shares a resource with, untimeable work cannot be timed either
         by_res: dict = {}
         for op in self.ops.values():
-            for r in op.resources:
+            for r in op.crosses:
                 by_res.setdefault(r, []).append(op.operation_id)
         todo = list(blocked)
         while todo:
             key = todo.pop()
             spread = list(self.succ[key])
-            for r in self.ops[key].resources:
+            for r in self.ops[key].crosses:
                 spread.extend(by_res[r])
             for other in spread:
                 if other not in blocked:
@@ -230,12 +231,12 @@ class _Replay:
             else:
                 seg = self.seg[op.operation_id]
                 rates[op.operation_id] = 1 / num(seg.beta_us_per_byte)
-                src[op.operation_id] = op.source_override or seg.source
+                src[op.operation_id] = ESTIMATED if op.estimated else seg.source
         for group in _sharing_groups(network):
             flows = [op.flow_id for op in group]
             if len(set(flows)) < len(flows):
                 raise SemanticError("two concurrent operations claim one flow id in %s" % sorted(flows))
-            self.used.update("resource:" + r for op in group for r in op.resources)
+            self.used.update("resource:" + r for op in group for r in op.crosses)
             mode = self.model.measured_mode(group)
             if mode is not None:
                 self.used.add("profile:" + mode.profile_id)
@@ -246,24 +247,24 @@ class _Replay:
             if len(group) > 1:
                 modes.add(tuple(sorted(flows)))
             caps = {op.operation_id: 1 / num(self.seg[op.operation_id].beta_us_per_byte) for op in group}
-            cross = {op.operation_id: op.resources for op in group}
-            capacity = {r: num(self.model.capacity(r)) for op in group for r in op.resources}
+            cross = {op.operation_id: op.crosses for op in group}
+            capacity = {r: num(self.model.capacity(r)) for op in group for r in op.crosses}
             fair = max_min_rates(caps, cross, capacity, num(0))
             for op in group:
                 k = op.operation_id
                 rates[k] = fair[k]
                 shared = len(group) > 1 or fair[k] < caps[k]
-                src[k] = SHARED_ESTIMATE if shared else (op.source_override or self.seg[k].source)
+                src[k] = SHARED_ESTIMATE if shared else (ESTIMATED if op.estimated else self.seg[k].source)
         return rates, src, modes
 
     def run(self) -> Prediction:
         num, ops = self.num, self.ops
         zero = num(0)
-        waiting = {k: len(op.dependencies) for k, op in ops.items() if k not in self.blocked}
+        waiting = {k: len(op.after) for k, op in ops.items() if k not in self.blocked}
         calendar: list = []      # (time, phase, operation): phase 0 release, 1 end of alpha
         for k, n in waiting.items():
             if n == 0:
-                heapq.heappush(calendar, (num(ops[k].not_before_us), 0, k))
+                heapq.heappush(calendar, (num(ops[k].release_us), 0, k))
         start, end, segments = {}, {}, []
         left, drain = {}, {}     # bytes still to move; operations draining now
         source_time: dict = {}
@@ -276,7 +277,7 @@ class _Replay:
                 if s in waiting:
                     waiting[s] -= 1
                     if waiting[s] == 0:
-                        heapq.heappush(calendar, (max(t, num(ops[s].not_before_us)), 0, s))
+                        heapq.heappush(calendar, (max(t, num(ops[s].release_us)), 0, s))
 
         while calendar or drain:
             # everything that happens at `now`: releases, ends of α (in that order, each by id)
@@ -289,9 +290,9 @@ class _Replay:
                         finish(key, now)
                         continue
                     seg = self.seg[key]
-                    self.used.add("service:" + op.cost_key)
-                    sources.add(op.source_override or seg.source)
-                    left[key] = num(op.payload_bytes)
+                    self.used.add("service:" + op.component)
+                    sources.add(ESTIMATED if op.estimated else seg.source)
+                    left[key] = num(op.nbytes)
                     heapq.heappush(calendar, (now + num(seg.alpha_us), 1, key))
                 else:
                     drain[key] = op
@@ -317,7 +318,7 @@ class _Replay:
             now = horizon
             for k in sorted(drain):
                 if done_at[k] <= horizon or left[k] <= zero or \
-                        (not num.exact and left[k] <= 1e-9 * ops[k].payload_bytes):
+                        (not num.exact and left[k] <= 1e-9 * ops[k].nbytes):
                     del drain[k]
                     finish(k, now)
         if any(n > 0 for n in waiting.values()):

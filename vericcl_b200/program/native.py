@@ -114,7 +114,7 @@ def lower_program(storage, request, *, tb_layout: str | None = None, name: str =
 
 def build_executable(program: NativeProgram, storage, request, topology, model_context: dict):
     """Physical work graph for T_pred: instruction deps + TB order + NOP waits."""
-    from vericcl_b200.performance.events import Executable, WorkOperation
+    from vericcl_b200.performance.events import Executable, Movement, WorkOperation
     from vericcl_b200.topology.model import LinkKey
     deps, _ = execution_dependencies(program)
     instructions = {i.operation_id: i for i in storage.instructions}
@@ -133,7 +133,8 @@ def build_executable(program: NativeProgram, storage, request, topology, model_c
             flow = "%s:%d:%d:c%d" % (ins.kind, src.rank, dst.rank, ins.channel)
         else:
             cost, resources, flow = "copy:%d" % ins.rank, (), None
-        ops.append(WorkOperation(key, ins.kind, cost, size, tuple(sorted(deps[key])), resources, flow))
+        ops.append(WorkOperation(key, ins.kind, Movement(cost, size), after=tuple(sorted(deps[key])),
+                                 crosses=resources, flow_id=flow))
     outputs = sorted({storage.values[s].producer for s in storage.outputs.values()
                       if storage.values[s].producer is not None})
     return Executable(tuple(ops), tuple(outputs), dict(model_context))

@@ -66,7 +66,7 @@ def _utilisation(executable, prediction):
     busy = defaultdict(float)
     ops = {op.operation_id: op for op in executable.operations}
     for key, t0, t1, rate, _src in prediction.segments:
-        for res in ops[key].resources:
+        for res in ops[key].crosses:
             busy[res] += t1 - t0
     span = max(prediction.t_pred_us or 0.0, 1e-12)
     return {res: round(t / span, 6) for res, t in sorted(busy.items())}
@@ -82,14 +82,14 @@ def causes_on_path(executable, prediction, model, path):
         op = ops[key]
         if op.kind == "nop":
             continue
-        ready = max((prediction.end_times.get(d, 0.0) for d in op.dependencies), default=0.0)
+        ready = max((prediction.end_times.get(d, 0.0) for d in op.after), default=0.0)
         start = prediction.start_times.get(key, 0.0)
-        cost = model.service_for(op.cost_key, op.payload_bytes)
+        cost = model.service_for(op.component, op.nbytes)
         own_rate = 1.0 / cost.beta_us_per_byte if cost else None
         slowed = [s for s in seg_by_op[key] if own_rate and s[2] < own_rate * (1 - 1e-9)]
         if slowed:
             out.append(Cause("resource_overlap", key, {"min_rate": min(s[2] for s in slowed), "own_rate": own_rate,
-                                                        "resources": list(op.resources)}))
+                                                        "resources": list(op.crosses)}))
         elif start > ready + 1e-9:
             out.append(Cause("tb_wait", key, {"waited_us": start - ready}))
         else:
@@ -103,24 +103,24 @@ def causes_on_path(executable, prediction, model, path):
 
 def _faster_relay(model, op):
     """A rank c whose two hops a→c→b each move this payload faster than the direct link a→b, or None."""
-    if not (op.cost_key or "").startswith("link:"):
+    if not (op.component or "").startswith("link:"):
         return None
-    _, a, b = op.cost_key.split(":")
-    direct = model.service_for(op.cost_key, op.payload_bytes)
+    _, a, b = op.component.split(":")
+    direct = model.service_for(op.component, op.nbytes)
     if direct is None:
         return None
-    limit = direct.time_us(op.payload_bytes)
+    limit = direct.time_us(op.nbytes)
     best = None
     for key in model.services:
         parts = key.split(":")
         if parts[0] != "link" or parts[1] != a or parts[2] == b:
             continue
         c = parts[2]
-        first = model.service_for(key, op.payload_bytes)
-        second = model.service_for("link:%s:%s" % (c, b), op.payload_bytes)
+        first = model.service_for(key, op.nbytes)
+        second = model.service_for("link:%s:%s" % (c, b), op.nbytes)
         if first is None or second is None:
             continue
-        slower = max(first.time_us(op.payload_bytes), second.time_us(op.payload_bytes))
+        slower = max(first.time_us(op.nbytes), second.time_us(op.nbytes))
         if slower < limit and (best is None or slower < best[0]):
             best = (slower, int(c))
     return None if best is None else best[1]

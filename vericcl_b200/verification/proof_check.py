@@ -106,20 +106,20 @@ def optimistic_relaxation(executable, model):
     ops = {op.operation_id: op for op in executable.operations}
     finish, pending = {}, dict(ops)
     while pending:
-        ready = sorted(k for k, op in pending.items() if set(op.dependencies) <= finish.keys())
+        ready = sorted(k for k, op in pending.items() if set(op.after) <= finish.keys())
         if not ready:
             raise SemanticError("relaxation dependencies contain a cycle")
         for key in ready:
             op = pending.pop(key)
-            start = max([rational(op.not_before_us)] + [finish[d] for d in op.dependencies])
+            start = max([rational(op.release_us)] + [finish[d] for d in op.after])
             if op.kind == "nop":
                 finish[key] = start
                 continue
-            cost = model.service_for(op.cost_key, op.payload_bytes)
+            cost = model.service_for(op.component, op.nbytes)
             if cost is None:
-                raise SemanticError("the relaxation needs a service cost for " + op.cost_key)
+                raise SemanticError("the relaxation needs a service cost for " + op.component)
             rate = max(1 / rational(cost.beta_us_per_byte), fastest)
-            finish[key] = start + rational(cost.alpha_us) + Fraction(op.payload_bytes) / rate
+            finish[key] = start + rational(cost.alpha_us) + Fraction(op.nbytes) / rate
     bounds = [finish[k] for k in sorted(finish)] or [Fraction(0)]
     return [[1] for _ in bounds], [str(v) for v in bounds], [1]
 
