@@ -66,23 +66,26 @@ def test_cta_budget_caps_the_interpreter_grid():
     assert CollectiveEngine(_Comm(8), cta_budget=4096).geometry(8, 64 << 20)[0] == 148 // 8
 
 
-def test_tma_staged_instance_is_chosen_for_large_pulls_on_verified_worlds():
-    from vericcl_b200.parallel.comm import (BULK_AUTO_MAX_BYTES, BULK_AUTO_MIN_BYTES, BULK_AUTO_MIN_REDUCE_BYTES,
-                                            Communicator, _bulk_mode)
-    pulls = SimpleNamespace(multicast=False, collective="allgather")
-    nvls = SimpleNamespace(multicast=True, collective="allreduce")
-    reduce_pulls = SimpleNamespace(multicast=False, collective="allreduce")
-    assert Communicator.bulk_for(SimpleNamespace(bulk=None, world=2), reduce_pulls, 25 << 20) == 0
-    assert Communicator.bulk_for(SimpleNamespace(bulk=None, world=2), reduce_pulls, BULK_AUTO_MIN_REDUCE_BYTES) == 1
-    auto2 = SimpleNamespace(bulk=None, world=2)
-    assert Communicator.bulk_for(auto2, pulls, BULK_AUTO_MIN_BYTES) == 1
-    assert Communicator.bulk_for(auto2, pulls, BULK_AUTO_MIN_BYTES - 16) == 0
-    assert Communicator.bulk_for(auto2, nvls, 1 << 28) == 0              # multimem steps are not staged
-    assert Communicator.bulk_for(auto2, pulls, BULK_AUTO_MAX_BYTES + 16) == 0
-    assert Communicator.bulk_for(SimpleNamespace(bulk=None, world=8), pulls, 1 << 26) == 0
-    assert Communicator.bulk_for(SimpleNamespace(bulk=None, world=1), pulls, 1 << 30) == 0
-    assert Communicator.bulk_for(SimpleNamespace(bulk=3, world=1), pulls, 16) == 3   # explicit setting wins
-    assert [_bulk_mode(v) for v in (None, "0", "1", "3", "true")] == [0, 0, 1, 3, 1]
+def test_tma_staged_instance_is_chosen_inside_the_measured_windows():
     import pytest
+    from vericcl_b200.parallel.comm import BULK_WINDOWS, Communicator, _bulk_mode
+    ag = SimpleNamespace(multicast=False, collective="allgather")
+    ar = SimpleNamespace(multicast=False, collective="allreduce")
+    nvls = SimpleNamespace(multicast=True, collective="allreduce")
+    mib = 1 << 20
+
+    def pick(world, plan, nbytes, bulk=None):
+        return Communicator.bulk_for(SimpleNamespace(bulk=bulk, world=world), plan, nbytes)
+
+    assert [pick(2, ag, n * mib) for n in (4, 16, 256, 1024)] == [0, 1, 1, 0]
+    assert [pick(2, ar, n * mib) for n in (16, 25, 64, 256, 512)] == [0, 0, 1, 1, 0]
+    assert [pick(4, ag, n * mib) for n in (16, 256, 1024)] == [1, 1, 0]
+    assert pick(4, ar, 128 * mib) == 0                          # pull reductions on four ranks: not measured
+    assert [pick(8, ag, n * mib) for n in (8, 16, 32, 64)] == [0, 1, 1, 0]
+    assert pick(2, nvls, 128 * mib) == 0                        # multimem steps are not staged
+    assert pick(1, ag, 64 * mib) == 0 and pick(16, ag, 64 * mib) == 0
+    assert pick(1, ag, 16, bulk=3) == 3                         # an explicit setting wins
+    assert set(BULK_WINDOWS) == {2, 4, 8}
+    assert [_bulk_mode(v) for v in (None, "0", "1", "3", "true")] == [0, 0, 1, 3, 1]
     with pytest.raises(ValueError):
         _bulk_mode("2")

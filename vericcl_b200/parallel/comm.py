@@ -44,14 +44,17 @@ def _bulk_mode(value) -> int:
     return mode
 
 
-# Rank counts on which the TMA-staged instance passed the fp64 collective checks and measured faster than the
-# vector path, and the payload window where it is chosen by default there.  Two B200s: 64-256 MiB AllGathers
-# 6-27 % and AllReduces 2-5 % faster, level at 16 MiB, slower at 1-4 MiB.  Four: AllGathers 16-256 MiB 3-5 %
-# faster, 1 GiB 14 % slower.  Eight: correct, but slower from 256 MiB, so not listed.
-BULK_VERIFIED_WORLDS = frozenset({2, 4})
-BULK_AUTO_MIN_BYTES = 16 << 20          # AllGather (copies only)
-BULK_AUTO_MIN_REDUCE_BYTES = 64 << 20   # plans with reduce steps: level at 16 MiB, 0.5 % slower on 25 MiB buckets
-BULK_AUTO_MAX_BYTES = 256 << 20
+# Per rank count, the per-rank payload windows (bytes, inclusive) in which the TMA-staged instance measured
+# faster than the vector path on B200s, after passing the fp64 collective checks on that many GPUs:
+#   2 ranks: AllGather 16-256 MiB +3-27 %; pull AllReduce 64-256 MiB +2-5 %, 16-25 MiB level or 0.5 % slower.
+#   4 ranks: AllGather 16-256 MiB +3-5 %, 1 GiB 14 % slower (pull reductions not measured).
+#   8 ranks: AllGather 16 MiB +6.6 %, 64 MiB 1.8 % slower, 256 MiB-1 GiB 6-28 % slower; the window stops at 32 MiB
+#            because the crossover between 16 and 64 MiB is not measured.
+BULK_WINDOWS = {
+    2: {"allgather": (16 << 20, 256 << 20), "other": (64 << 20, 256 << 20)},
+    4: {"allgather": (16 << 20, 256 << 20)},
+    8: {"allgather": (16 << 20, 32 << 20)},
+}
 
 
 def _env_flag(name: str, default: bool) -> bool:
@@ -398,15 +401,14 @@ class Communicator:
                              trace_stride)
 
     def bulk_for(self, plan, nbytes: int) -> int:
-        """Interpreter instance mode for one launch: the explicit ``bulk`` setting, else TMA-staged loads (1) for
-        payloads of ``BULK_AUTO_MIN_BYTES`` (AllGather) or ``BULK_AUTO_MIN_REDUCE_BYTES`` (other collectives) to
-        ``BULK_AUTO_MAX_BYTES`` per rank on the rank counts in
-        ``BULK_VERIFIED_WORLDS`` when the plan has no multicast steps (the staged path covers copy and reduce
-        steps only), else the vector path (0)."""
+        """Interpreter instance mode for one launch: the explicit ``bulk`` setting, else TMA-staged loads (1) when
+        the plan has no multicast steps (the staged path covers copy and reduce steps only) and the per-rank
+        payload lies in this rank count's measured window (``BULK_WINDOWS``), else the vector path (0)."""
         if self.bulk is not None:
             return int(self.bulk)
-        low = BULK_AUTO_MIN_BYTES if getattr(plan, "collective", "") == "allgather" else BULK_AUTO_MIN_REDUCE_BYTES
-        if self.world in BULK_VERIFIED_WORLDS and not plan.multicast and low <= nbytes <= BULK_AUTO_MAX_BYTES:
+        windows = BULK_WINDOWS.get(self.world, {})
+        window = windows.get("allgather" if getattr(plan, "collective", "") == "allgather" else "other")
+        if window is not None and not plan.multicast and window[0] <= nbytes <= window[1]:
             return 1
         return 0
 
