@@ -90,3 +90,16 @@ def test_invalid_manual_nodes_are_refused(tmp_path, edit, message):
     with pytest.raises(InputValidationError, match=message):
         request = load_request(files)
         plan_manual(request, load_topology(request))
+
+
+def test_vericcl_module_alias_runs_the_same_cli(tmp_path):
+    """``python -m vericcl`` (the reference's module name) answers with the same commands."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    proc = subprocess.run([sys.executable, "-m", "vericcl", "--help"], cwd=root, capture_output=True, text=True,
+                          timeout=120)
+    assert proc.returncode == 0
+    for verb in ("solve", "verify", "calibrate", "inspect", "resume", "manual-generate"):
+        assert verb in proc.stdout
