@@ -187,8 +187,8 @@ def test_bracket_fit_recovers_offset_and_drift_and_drops_a_contradicting_sample(
 
 
 def test_link_class_probing_measures_representatives_and_covers_every_link():
-    """On 2 x 4 groups, 16 probe jobs (two links per class, one rank per node, one shared mode per resource kind)
-    stand in for the 168 of per-link probing; every link and local component ends up measured."""
+    """On 2 x 4 groups, a few probe jobs (two links per class, one rank per node, one shared mode per resource
+    class) stand in for the 168 of per-link probing; every link and local component ends up measured."""
     from vericcl_b200.online.loop import loop_documents
     from vericcl_b200.online.probe_jobs import link_classes, plan_probes
     docs = loop_documents(groups=2, per_group=4, inter_gbps=25.0, size_bytes=8 << 20, rounds=1,
@@ -201,6 +201,10 @@ def test_link_class_probing_measures_representatives_and_covers_every_link():
     every["sketch"] = dict(docs["sketch"], calibration=dict(docs["sketch"]["calibration"], probe_scope="every_link"))
     assert len(jobs) < len(plan_probes(resolve_documents(every), topo)) // 5
     assert len(link_classes(topo)) == 2                 # intra-group and inter-group links
+    shared = {j.resources[0] for j in jobs if j.mode == "shared"}
+    # one NVLink port, one group NIC and one rank's share of it: three classes, each probed once
+    assert any(r.startswith("nvlink-") for r in shared) and any(r.startswith("nic-share-rx-") for r in shared)
+    assert any(r.startswith("nic-") and "share" not in r for r in shared)
     model = initial_cost_model(req)
     executor = campaign.simulated_executor(topo, source="native_interpreter", noise=0.001)
     new_model, _, report = campaign.run_calibration(req, topo, model, executor)

@@ -136,9 +136,12 @@ def plan_probes(request, topology, *, max_channels: int = 1, include_shared: boo
             if len(members) < 2:
                 continue
             if cfg.get("probe_scope", "every_link") == "link_classes":
-                if res.kind in kinds_done:
-                    continue               # one resource of each kind stands for the others
-                kinds_done.add(res.kind)
+                # one resource of each class (kind, capacity, number of member links) stands for the others:
+                # a group's NIC and a rank's share of it are both NICs, but not interchangeable
+                cls = (res.kind, round(float(res.capacity_bytes_per_us), 6), len(members))
+                if cls in kinds_done:
+                    continue
+                kinds_done.add(cls)
             pairs = list(combinations(members, 2))[:2]
             for i, (a, b) in enumerate(pairs):
                 jobs.append(ProbeJob("shared-%s-%d" % (rid, i), "shared",
