@@ -346,9 +346,11 @@ def main():
                            "launch": "per-bucket" if args.per_bucket else "all buckets in one persistent launch",
                            "plan": {"lanes": ar.plan.nlanes, "iters": ar.plan.niters,
                                     "nvls": bool(ar.plan.multicast), "heap_multicast": comm.multicast,
-                                    "instance": {0: "vector loads", 1: "TMA-staged loads", 3: "TMA loads + stores"}[
-                                        comm.bulk_for(ar.plan, ar.bucket_elems * esize)] if ar.plan.kind != "oneshot"
-                                    else "one-shot",
+                                    "instance": ("one-shot" if ar.plan.kind == "oneshot" else
+                                                 {0: "register-lean vector loads (L2 prefetch hint)" if comm.lean
+                                                  else "vector loads", 1: "TMA-staged loads",
+                                                  3: "TMA loads + stores"}[
+                                                     comm.bulk_for(ar.plan, ar.bucket_elems * esize)]),
                                     "stats": ar.plan.device_plan.stats() if ar.plan.device_plan is not None
                                     else {"path": ar.plan.kind}},
                            "l2": "inputs (16 GB) larger than the 126 MB L2; no flush needed"},
