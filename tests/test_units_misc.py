@@ -177,3 +177,18 @@ def test_work_operations_validate_their_kind_rules():
     for make in bad:
         with pytest.raises(SemanticError):
             make()
+
+
+# -- gradient bucket groups ----------------------------------------------------------------------------------------
+def test_bucket_groups_cover_every_bucket_once_in_order():
+    from vericcl_b200.models.grad_bucket import bucket_groups
+    assert bucket_groups(611, 8) == [(i * 77, min(611, (i + 1) * 77)) for i in range(8)]
+    assert bucket_groups(6, 3) == [(0, 2), (2, 4), (4, 6)]
+    assert bucket_groups(5, 3) == [(0, 2), (2, 4), (4, 5)]
+    assert bucket_groups(2, 8) == [(0, 1), (1, 2)]
+    assert bucket_groups(3, 0) == [(0, 3)] and bucket_groups(0, 4) == []
+    for n in range(1, 40):
+        for g in range(1, 12):
+            runs = bucket_groups(n, g)
+            assert runs[0][0] == 0 and runs[-1][1] == n and len(runs) <= g
+            assert all(a[1] == b[0] for a, b in zip(runs, runs[1:]))

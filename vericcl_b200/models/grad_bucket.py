@@ -21,6 +21,16 @@ DEFAULT_BUCKET_BYTES = 25 * 1024 * 1024
 NVLS_BUCKET_CTAS = 32
 
 
+def bucket_groups(buckets: int, groups: int) -> list:
+    """``[(first, end), ...]``: ``buckets`` consecutive buckets cut into at most ``groups`` runs of equal length
+    (the last may be shorter), in order."""
+    if buckets < 1:
+        return []
+    groups = max(1, min(groups, buckets))
+    per = -(-buckets // groups)
+    return [(b0, min(buckets, b0 + per)) for b0 in range(0, buckets, per)]
+
+
 class GradBucketAllReduce:
     def __init__(self, comm, numel: int, *, dtype=torch.bfloat16, bucket_bytes: int = DEFAULT_BUCKET_BYTES,
                  scale: float | None = None, slices_per_rank: int | None = None, cta_budget: int | None = None):
@@ -104,12 +114,9 @@ class GradBucketAllReduce:
             copy_stream = getattr(self, "_copy_stream", None)
             if copy_stream is None:
                 copy_stream = self._copy_stream = torch.cuda.Stream()
-        groups = max(1, min(groups, self.buckets))
-        per = -(-self.buckets // groups)
         copy_stream.wait_stream(stream)
         launches = 0
-        for b0 in range(0, self.buckets, per):
-            b1 = min(self.buckets, b0 + per)
+        for b0, b1 in bucket_groups(self.buckets, groups):
             lo, hi = b0 * self.bucket_elems, min(self.numel, b1 * self.bucket_elems)
             with torch.cuda.stream(copy_stream):
                 self.grads[lo:hi].copy_(host[lo:hi], non_blocking=True)
