@@ -192,3 +192,28 @@ def test_bucket_groups_cover_every_bucket_once_in_order():
             runs = bucket_groups(n, g)
             assert runs[0][0] == 0 and runs[-1][1] == n and len(runs) <= g
             assert all(a[1] == b[0] for a, b in zip(runs, runs[1:]))
+
+
+# -- the largest communicator: 16 ranks ----------------------------------------------------------------------------
+@pytest.mark.parametrize("coll,slices", [("allreduce", 16), ("allgather", 1), ("reduce_scatter", 16)])
+def test_sixteen_rank_programs_on_the_cpu_oracle(coll, slices):
+    """The symmetric heap's limit is 16 ranks: schedules of that size compile and run correctly (CPU interpreter,
+    seeded CTA order, two launches so flag epochs advance)."""
+    import numpy as np
+    from vericcl_b200.program.device import compile_xml, run_cpu
+    from vericcl_b200.synthesis import schedule_xml
+    p = 16
+    compiled = compile_xml(schedule_xml(coll, p, slices), nlanes=2, niters=2)
+    count = p * slices * 16
+    rng = np.random.default_rng(16)
+    inputs = [rng.uniform(-1, 1, count).astype(np.float32) for _ in range(p)]
+    outs = run_cpu(compiled, inputs, seed=3, launches=2)
+    total = np.sum(inputs, axis=0, dtype=np.float64)
+    for r in range(p):
+        if coll == "allreduce":
+            np.testing.assert_allclose(outs[r][:count], total, rtol=1e-5, atol=1e-5)
+        elif coll == "allgather":
+            np.testing.assert_array_equal(outs[r][:count * p], np.concatenate(inputs))
+        else:
+            part = count // p
+            np.testing.assert_allclose(outs[r][:part], total[r * part:(r + 1) * part], rtol=1e-5, atol=1e-5)
