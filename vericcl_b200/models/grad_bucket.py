@@ -7,6 +7,13 @@ scale (for example 1/world for averaging, or a loss-scale correction) is fused
 into the final store of each reduced slice, so no separate elementwise pass
 runs.  A partial last bucket is padded inside the buffer so every bucket uses
 the same compiled plan geometry (the padding holds zeros).
+
+All buckets run in one persistent launch by default.  On an NVLS plan the
+launch keeps to ``NVLS_BUCKET_CTAS`` CTAs per GPU, which measured as fast as
+every SM, so a backward pass can overlap it; ``cta_budget`` sets another
+budget.  ``sync_from_host`` takes the gradients from pinned host memory and
+overlaps their host-to-device copy, group of buckets by group, with the
+AllReduce of the groups already copied.
 """
 from __future__ import annotations
 
