@@ -75,5 +75,12 @@ def main(spec_path: str) -> int:
     return 0
 
 
+USAGE = ("usage: torchrun --nproc-per-node P -m vericcl_b200.online.probe_worker SPEC.json\n"
+         "runs the probe jobs listed in SPEC.json (written by the calibration campaign) on P GPUs and writes "
+         "their device times to the file named by its \"output\" field")
+
 if __name__ == "__main__":
+    if len(sys.argv) != 2 or sys.argv[1] in ("-h", "--help"):
+        print(USAGE)
+        sys.exit(0 if len(sys.argv) == 2 else 2)
     sys.exit(main(sys.argv[1]))

@@ -283,4 +283,9 @@ def build_all(force: bool = False) -> dict:
 
 
 if __name__ == "__main__":
+    if "-h" in sys.argv or "--help" in sys.argv:
+        print("usage: python -m vericcl_b200.ops.build [--force]\n"
+              "builds the in-tree native modules (sm_100a CUDA extension, schedule compiler, C API, driver, "
+              "CPU test binaries) that are out of date, or all of them with --force")
+        sys.exit(0)
     print(build_all(force="--force" in sys.argv))
