@@ -57,6 +57,11 @@ def stale(root: Path = ROOT) -> list:
 
 def main(argv=None) -> int:
     argv = sys.argv[1:] if argv is None else argv
+    if "-h" in argv or "--help" in argv:
+        print("usage: python -m vericcl_b200.input.docs [--check]\n"
+              "regenerates docs/input-schema.md and schemas/*.schema.json from the input schema; --check only "
+              "lists the files that are out of date (exit 1 when any is)")
+        return 0
     if "--check" in argv:
         bad = stale()
         for path in bad:
