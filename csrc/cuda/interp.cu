@@ -2,9 +2,10 @@
 //
 // One CTA per (device block, lane).  A CTA walks its block's steps for every
 // pipeline iteration; each data step moves the CTA's piece of one or more
-// chunks with 16-byte vector loads from local or peer-mapped memory (NVLink
-// through NVSwitch), combines sources in fp32, applies the fused scale and
-// stores once.  Ordering uses 64-bit monotone flags in the symmetric heap:
+// chunks from local or peer-mapped memory (NVLink through NVSwitch) — with
+// 16-byte vector loads, or, in the staged instances, with TMA bulk copies into
+// shared memory — combines sources in fp32, applies the fused scale and
+// stores once (NVLS steps use multimem.ld_reduce / multimem.st instead).  Ordering uses 64-bit monotone flags in the symmetric heap:
 // waits poll with ld.acquire.sys (warp 0, one wait per lane), publications
 // use st.release.sys after a CTA barrier.  Every wait is bounded by a
 // %globaltimer deadline; on expiry the CTA records the failure in the
