@@ -4,6 +4,10 @@
     python -m vericcl_b200.ops.kernel_bench --kernel fp8_allgather --elems 268435456 --dtype bfloat16
     python -m vericcl_b200.ops.kernel_bench --kernel push_allgather --elems 268435456 --dtype bfloat16
 
+Options: ``--k`` sources of the local reduce, ``--no-scale`` (K = 1 is then a plain
+copy), ``--lean`` (the register-lean instance), ``--bulk 1|3`` (TMA-staged loads,
+and TMA stores for plain copies), ``--fanout`` (push AllGather fan-out order).
+
 Each run: ``--warmup`` untimed launches, then ``--iters`` launches between two
 CUDA events on the current stream; the inputs are larger than the 126 MB L2
 at the default sizes, so no flush is needed.  Bytes are the algorithmic HBM
