@@ -217,3 +217,31 @@ def test_sixteen_rank_programs_on_the_cpu_oracle(coll, slices):
         else:
             part = count // p
             np.testing.assert_allclose(outs[r][:part], total[r * part:(r + 1) * part], rtol=1e-5, atol=1e-5)
+
+
+# -- experiments report pivot --------------------------------------------------------------------------------------
+def test_report_pivot_tabulates_x_nccl_by_size(tmp_path, capsys):
+    from vericcl_b200.experiments import load_points, main, pivot, report_rows
+
+    def point(coll, gpus, size, x, variant=None, graph=False):
+        d = {"coll": coll, "n_gpus": gpus, "bytes_per_rank": size, "time_us": 10.0, "busbw_gbs": 1.0,
+             "path": "interp", "graph": graph, "nccl_time_us": 10.0 * x, "speedup_vs_nccl": x}
+        if variant:
+            d["variant"] = variant
+        return json.dumps(d)
+
+    log = tmp_path / "sweep.log"
+    log.write_text("\n".join([point("allreduce", 8, 1 << 20, 1.5), point("allreduce", 8, 1 << 24, 0.9),
+                              point("allgather", 8, 1 << 24, 1.1), point("allreduce", 8, 1 << 20, 2.0, "BULK=1"),
+                              point("allreduce", 8, 1 << 10, 3.0, graph=True)]) + "\n")
+    rows = report_rows(load_points([log]))
+    table = pivot(rows)
+    lines = table.splitlines()
+    assert lines[0] == "| coll | GPUs | mode | 1 KiB | 1 MiB | 16 MiB |"
+    assert "| allreduce | 8 | eager |  | 1.50 | 0.90* |" in lines
+    assert "| allreduce | 8 | graph | 3.00 |  |  |" in lines
+    assert "| allgather | 8 | eager |  |  | 1.10 |" in lines
+    assert lines[-1] == "1 of 4 cells below 1.0 (marked *)"
+    assert "2.00" in pivot(rows, variant="BULK=1") and "1.50" not in pivot(rows, variant="BULK=1")
+    assert main(["report", str(log), "--pivot"]) == 0
+    assert "0.90*" in capsys.readouterr().out

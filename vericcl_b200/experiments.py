@@ -124,6 +124,36 @@ def markdown(rows) -> str:
     return "\n".join(lines) + "\n"
 
 
+def pivot(rows, *, variant: str = "") -> str:
+    """× NCCL per (collective, GPUs, mode) row and message-size column, for one variant (default: the engine's
+    default path, i.e. rows without a variant); cells below 1.0 are marked with an asterisk."""
+    picked = [r for r in rows if r["variant"] == variant and r["x_nccl"] is not None]
+    sizes = sorted({r["size"] for r in picked}, key=_size_bytes)
+    keys = sorted({(r["coll"], r["gpus"], r["mode"]) for r in picked})
+    cell = {(r["coll"], r["gpus"], r["mode"], r["size"]): r for r in picked}
+    lines = ["| coll | GPUs | mode | " + " | ".join(sizes) + " |", "|" + "---|" * (3 + len(sizes))]
+    behind = 0
+    for key in keys:
+        vals = []
+        for size in sizes:
+            r = cell.get(key + (size,))
+            if r is None:
+                vals.append("")
+                continue
+            x = r["x_nccl"]
+            behind += x < 1.0
+            vals.append(("%.2f" % x) + ("*" if x < 1.0 else ""))
+        lines.append("| %s | %d | %s | " % key + " | ".join(vals) + " |")
+    lines.append("")
+    lines.append("%d of %d cells below 1.0 (marked *)" % (behind, len(cell)))
+    return "\n".join(lines) + "\n"
+
+
+def _size_bytes(text: str) -> int:
+    number, unit = text.split()
+    return int(number) * {"B": 1, "KiB": 1 << 10, "MiB": 1 << 20, "GiB": 1 << 30}[unit]
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(prog="vericcl_b200.experiments")
     sub = ap.add_subparsers(dest="command", required=True)
@@ -135,6 +165,8 @@ def main(argv=None) -> int:
     r = sub.add_parser("report")
     r.add_argument("files", nargs="+")
     r.add_argument("--markdown", action="store_true")
+    r.add_argument("--pivot", action="store_true", help="× NCCL as a size × (collective, GPUs, mode) table")
+    r.add_argument("--variant", default="", help="with --pivot: the variant to tabulate (default: none)")
     from vericcl_b200 import overhead
     overhead.add_arguments(sub.add_parser("overhead", help="pipeline wall-clock attribution or schedule replay"))
     args = ap.parse_args(argv)
@@ -146,7 +178,9 @@ def main(argv=None) -> int:
             print(" ".join(cmd))
         return 0
     rows = report_rows(load_points(args.files))
-    if args.markdown:
+    if args.pivot:
+        sys.stdout.write(pivot(rows, variant=args.variant))
+    elif args.markdown:
         sys.stdout.write(markdown(rows))
     else:
         for row in rows:
