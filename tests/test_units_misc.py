@@ -245,3 +245,28 @@ def test_report_pivot_tabulates_x_nccl_by_size(tmp_path, capsys):
     assert "2.00" in pivot(rows, variant="BULK=1") and "1.50" not in pivot(rows, variant="BULK=1")
     assert main(["report", str(log), "--pivot"]) == 0
     assert "0.90*" in capsys.readouterr().out
+
+
+# -- slack and near-critical operations ----------------------------------------------------------------------------
+def test_slack_index_finds_every_chain_that_ends_at_t_pred():
+    from vericcl_b200.performance import CostModel, Executable, ServiceCost, WorkOperation, predict
+    from vericcl_b200.performance.events import Movement
+    from vericcl_b200.verification.bottlenecks import near_critical, slack_index
+    services = {"copy:0": (ServiceCost(0.0, 0.01),), "copy:1": (ServiceCost(0.0, 0.01),),
+                "copy:2": (ServiceCost(0.0, 0.01),)}
+    model = CostModel("slack", services, {})
+    ops = (WorkOperation("a1", "copy", Movement("copy:0", 1000)),                  # 10 µs
+           WorkOperation("a2", "copy", Movement("copy:0", 1000), after=("a1",)),   # ends at 20
+           WorkOperation("b1", "copy", Movement("copy:1", 2000)),                  # ends at 20: a second chain
+           WorkOperation("c1", "copy", Movement("copy:2", 500)),                   # ends at 5: 15 µs of slack
+           WorkOperation("end", "nop", after=("a2", "b1", "c1")))
+    ex = Executable(ops)
+    pred = predict(ex, model, exact=True)
+    assert pred.t_pred_us == pytest.approx(20.0)
+    slack = slack_index(ex, pred)
+    assert slack["a1"] == pytest.approx(0.0) and slack["a2"] == pytest.approx(0.0)
+    assert slack["b1"] == pytest.approx(0.0) and slack["c1"] == pytest.approx(15.0)
+    crit = near_critical(ex, pred)
+    assert set(crit) == {"a1", "a2", "b1"}                  # both chains, never the nop or the slack operation
+    path = pred.critical_path(ex)
+    assert not ({"a1", "a2"} <= set(path) and "b1" in path)  # the single critical path covers one chain only

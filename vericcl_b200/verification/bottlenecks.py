@@ -1,8 +1,9 @@
 """Bottleneck analysis of an exact prediction and lazy repair-strategy streams.
 
 The exact prediction gives every operation's start/end and the rate segments
-it ran at.  ``analyze`` walks the critical chain that ends at T_pred and
-classifies each link of it:
+it ran at.  ``analyze`` walks the critical chain that ends at T_pred, then the
+other operations with zero slack (``slack_index``: chains that end at T_pred
+too), and classifies each operation:
 
 * ``resource_overlap`` — the operation ran below its own link rate because a
   shared resource (NVLink port, NIC) was split with concurrent flows;
@@ -249,12 +250,56 @@ def storage_causes(bundle, path) -> list:
     return out
 
 
+def slack_index(executable, prediction) -> dict:
+    """Per operation, how much later (µs) it could end without moving T_pred, the predicted durations fixed.
+
+    An operation nothing waits for may end as late as T_pred; any other as late as the earliest latest start
+    of the operations that wait for it (latest end minus predicted duration), computed over the dependency
+    graph in reverse topological order.  Zero slack marks every operation on some critical chain, not only the
+    one chain :meth:`Prediction.critical_path` follows.  Shared-resource effects are taken as predicted.
+    """
+    if prediction.t_pred_us is None or not prediction.end_times:
+        return {}
+    ops = executable.by_id()
+    succ = defaultdict(list)
+    for op in executable.operations:
+        for d in op.after:
+            succ[d].append(op.operation_id)
+    pending = {k: len(succ[k]) for k in ops}
+    todo = [k for k, n in pending.items() if n == 0]
+    latest_end = {}
+    end, start, horizon = prediction.end_times, prediction.start_times, prediction.t_pred_us
+    while todo:
+        key = todo.pop()
+        after = succ[key]
+        latest_end[key] = horizon if not after else min(
+            latest_end[s] - (end.get(s, 0.0) - start.get(s, end.get(s, 0.0))) for s in after)
+        for d in ops[key].after:
+            pending[d] -= 1
+            if pending[d] == 0:
+                todo.append(d)
+    return {k: max(0.0, latest_end[k] - end.get(k, 0.0)) for k in latest_end}
+
+
+def near_critical(executable, prediction, *, tolerance: float = 1e-3) -> list:
+    """Operations whose slack is within ``tolerance`` × T_pred, latest-ending first."""
+    slack = slack_index(executable, prediction)
+    limit = tolerance * (prediction.t_pred_us or 0.0)
+    ops = executable.by_id()
+    keys = [k for k, v in slack.items() if v <= limit and ops[k].kind != "nop"]
+    return sorted(keys, key=lambda k: (-prediction.end_times.get(k, 0.0), k))
+
+
 def analyze(bundle, model, *, batch_size: int = 16, trace=None) -> Analysis:
-    """Causes on the predicted critical path (and, with a measured ``trace`` report, its slowest steps)."""
+    """Causes on the predicted critical path, then on the other near-critical operations (zero slack: other
+    chains that end at T_pred), and, with a measured ``trace`` report, its slowest steps."""
     pred = bundle.prediction
     path = pred.critical_path(bundle.executable)
+    on_path = set(path)
+    others = [k for k in near_critical(bundle.executable, pred) if k not in on_path][:max(len(path), 1)]
     causes = trace_causes(trace, bundle) + storage_causes(bundle, path) + \
-        causes_on_path(bundle.executable, pred, model, path)
+        causes_on_path(bundle.executable, pred, model, path) + \
+        causes_on_path(bundle.executable, pred, model, others)
     stream = list(strategy_stream(causes, bundle.network))
     return Analysis(pred.t_pred_us, path, causes, _utilisation(bundle.executable, pred),
                     choose_batch(stream, batch_size))
