@@ -44,3 +44,15 @@ def test_bf16_round_trip_matches_torch():
     ref = torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().astype(np.uint16)
     assert np.array_equal(bits, ref)
     assert np.array_equal(reference_arm.bf16_to_f32(bits), torch.from_numpy(x).to(torch.bfloat16).float().numpy())
+
+
+def test_bench_and_sweep_command_lines():
+    """The driver's contract flags exist (bench: --gpus --steps --warmup --impl; sweep: sizes and variants)."""
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--help"], cwd=ROOT, capture_output=True,
+                         text=True, timeout=120)
+    assert out.returncode == 0
+    for flag in ("--gpus", "--steps", "--warmup", "--impl", "--cta-budgets", "--e2e-steps", "--per-bucket"):
+        assert flag in out.stdout, flag
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "sweep.py"), "--help"], cwd=ROOT, capture_output=True,
+                         text=True, timeout=120)
+    assert out.returncode == 0 and "--variants" in out.stdout and "--graph" in out.stdout
