@@ -50,3 +50,33 @@ def test_engine_applies_a_tuning_table():
     assert (eng.oneshot_max_bytes, eng.twoshot_max_bytes, eng.ag_nvls_max_bytes) == (2 * MiB, 8 * MiB, 32 * MiB)
     explicit = CollectiveEngine(_Comm(), oneshot_max_bytes=0, tuning={"oneshot_max_bytes": 2 * MiB})
     assert explicit.oneshot_max_bytes == 0
+
+
+def test_staged_windows_come_from_the_measured_crossovers():
+    from vericcl_b200.models.tuner import staged_window
+    vector = _series(lambda s: 10 + s / 400e3)
+    staged = {s: (vector[s] * 0.9 if 1 * MiB <= s <= 16 * MiB else vector[s] * 1.05) for s in SIZES}
+    assert staged_window(vector, staged) == [1 * MiB, 16 * MiB]
+    assert staged_window(vector, {s: vector[s] * 0.995 for s in SIZES}) is None      # within the 1 % margin
+    times = {("allreduce", "interp"): _series(lambda s: 1.0), ("allgather", "interp"): _series(lambda s: 1.0),
+             ("allgather", "pull_vector"): vector, ("allgather", "pull_staged"): staged}
+    table = derive_thresholds(times, default_ag_nvls=8 * MiB)
+    assert table["bulk_windows"] == {"allgather": [1 * MiB, 16 * MiB]}
+
+
+def test_engine_installs_measured_staged_windows():
+    from vericcl_b200.models.collectives import CollectiveEngine
+    from vericcl_b200.parallel.comm import Communicator
+    comm = _Comm()
+    comm.bulk, comm.bulk_windows = None, None
+    CollectiveEngine(comm, tuning={"bulk_windows": {"allgather": [1 * MiB, 16 * MiB]}})
+    assert comm.bulk_windows == {"allgather": (1 * MiB, 16 * MiB)}
+    ag = SimpleNamespace(multicast=False, collective="allgather")
+    assert Communicator.bulk_for(comm, ag, 4 * MiB) == 1
+    assert Communicator.bulk_for(comm, ag, 64 * MiB) == 0                # outside the measured window
+    ar = SimpleNamespace(multicast=False, collective="allreduce")
+    assert Communicator.bulk_for(comm, ar, 4 * MiB) == 0                 # no window measured for reductions
+    forced = _Comm()
+    forced.bulk, forced.bulk_windows = 0, None                            # an explicit setting keeps priority
+    CollectiveEngine(forced, tuning={"bulk_windows": {"allgather": [1, 2]}})
+    assert forced.bulk_windows is None

@@ -66,6 +66,9 @@ class CollectiveEngine:
                 if given is None and name in tuning:
                     setattr(self, name, int(tuning[name]))
             self._explicit_oneshot |= "oneshot_max_bytes" in tuning or "twoshot_max_bytes" in tuning
+            if "bulk_windows" in tuning and getattr(comm, "bulk", None) is None:
+                # the staged instance's measured windows on this machine replace the built-in ones
+                comm.bulk_windows = {k: tuple(v) for k, v in tuning["bulk_windows"].items()}
         self._max_ctas = comm._mod.max_ctas(512)
         self.max_lanes = max_lanes or self._max_ctas
         self._staging: dict = {}

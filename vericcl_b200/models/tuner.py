@@ -14,7 +14,11 @@ over ranks) over sizes 64 KiB … 64 MiB per rank in powers of 2 and derives:
 * ``twoshot_max_bytes`` — the largest size above that up to which the
   two-shot AllReduce beats the interpreter at every size (0: never);
 * ``ag_nvls_max_bytes`` — the smallest size from which peer pulls beat NVLS
-  multicast for AllGather (kept at the default without NVLS).
+  multicast for AllGather (kept at the default without NVLS);
+* ``bulk_windows`` — per collective kind (``allgather``, ``other``), the
+  longest run of consecutive sizes at which the TMA-staged instance beat the
+  vector path by at least 1 % on pull plans (``[first, last]`` bytes per
+  rank, or absent), which then replaces the built-in windows.
 
 The result is a small JSON table keyed by rank count, GPU name and driver;
 ``CollectiveEngine(tuning=load_tuning(path, comm))`` applies it.
@@ -71,7 +75,31 @@ def derive_thresholds(times: dict, *, default_ag_nvls: int) -> dict:
             if pull is not None and mc is not None and pull < mc:
                 ag_nvls = size
                 break
-    return {"oneshot_max_bytes": oneshot, "twoshot_max_bytes": twoshot, "ag_nvls_max_bytes": ag_nvls}
+    table = {"oneshot_max_bytes": oneshot, "twoshot_max_bytes": twoshot, "ag_nvls_max_bytes": ag_nvls}
+    windows = {}
+    for kind, coll in (("allgather", "allgather"), ("other", "allreduce")):
+        if times.get((coll, "pull_vector")) and times.get((coll, "pull_staged")):
+            window = staged_window(times[(coll, "pull_vector")], times[(coll, "pull_staged")])
+            if window is not None:
+                windows[kind] = window
+    if any((c, "pull_staged") in times for c in ("allgather", "allreduce")):
+        table["bulk_windows"] = windows
+    return table
+
+
+def staged_window(vector: dict, staged: dict, *, margin: float = 0.01):
+    """``[first, last]``: the longest run of consecutive measured sizes at which the staged time is at least
+    ``margin`` below the vector time (None when there is none)."""
+    sizes = sorted(set(vector) & set(staged))
+    best, run = None, []
+    for size in sizes:
+        if staged[size] < vector[size] * (1.0 - margin):
+            run.append(size)
+            if best is None or len(run) > len(best):
+                best = list(run)
+        else:
+            run = []
+    return None if not best else [best[0], best[-1]]
 
 
 def machine_key(world: int) -> str:
@@ -144,6 +172,7 @@ def measure_paths(comm, sizes=DEFAULT_SIZES, *, iters: int = 20, warmup: int = 5
             dist.all_reduce(t, op=dist.ReduceOp.MAX, group=comm.control_group)
         return float(t.item())
 
+    vector_or_staged = {"pull_vector": 0, "pull_staged": 1}
     for size in sizes:
         count = size // esize
         buf = comm.empty(count, dtype)
@@ -166,6 +195,23 @@ def measure_paths(comm, sizes=DEFAULT_SIZES, *, iters: int = 20, warmup: int = 5
                     fn = (lambda p=plan: comm.run(p, inp, gout))
                 out.setdefault((coll, name), {})[size] = timed(fn)
                 comm.check_status()
+        # the staged instance against the vector path on pull plans (AllGather pulls; AllReduce without NVLS)
+        for coll, eng in (("allgather", engines["interp_p2p"]), ("allreduce", engines["interp"])):
+            plan = eng.plan(coll, count, dtype, inplace=coll == "allreduce")
+            if world < 2 or plan.kind == "oneshot" or plan.multicast:
+                continue
+            saved = comm.bulk
+            try:
+                for label, mode in vector_or_staged.items():
+                    comm.bulk = mode
+                    if coll == "allreduce":
+                        fn = (lambda p=plan: comm.run(p, buf, buf))
+                    else:
+                        fn = (lambda p=plan: comm.run(p, inp, gout))
+                    out.setdefault((coll, label), {})[size] = timed(fn)
+                    comm.check_status()
+            finally:
+                comm.bulk = saved
         for t in (buf, inp, gout):
             comm.free(t)
     return out

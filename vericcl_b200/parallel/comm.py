@@ -142,6 +142,9 @@ class Communicator:
         # Unset (None): chosen per launch by bulk_for()
         env = os.environ.get("VERICCL_BULK")
         self.bulk = None if env is None else _bulk_mode(env)
+        # per-machine staged windows from a tuning table ({"allgather": [lo, hi], "other": [lo, hi]}); None: the
+        # built-in BULK_WINDOWS of this rank count
+        self.bulk_windows = None
         self._lock = threading.Lock()
         self._closed = False
 
@@ -403,10 +406,12 @@ class Communicator:
     def bulk_for(self, plan, nbytes: int) -> int:
         """Interpreter instance mode for one launch: the explicit ``bulk`` setting, else TMA-staged loads (1) when
         the plan has no multicast steps (the staged path covers copy and reduce steps only) and the per-rank
-        payload lies in this rank count's measured window (``BULK_WINDOWS``), else the vector path (0)."""
+        payload lies in this rank count's measured window (``bulk_windows`` from a tuning table, else
+        ``BULK_WINDOWS``), else the vector path (0)."""
         if self.bulk is not None:
             return int(self.bulk)
-        windows = BULK_WINDOWS.get(self.world, {})
+        windows = BULK_WINDOWS.get(self.world, {}) if getattr(self, "bulk_windows", None) is None \
+            else self.bulk_windows
         window = windows.get("allgather" if getattr(plan, "collective", "") == "allgather" else "other")
         if window is not None and not plan.multicast and window[0] <= nbytes <= window[1]:
             return 1
