@@ -195,15 +195,18 @@ def test_bucket_groups_cover_every_bucket_once_in_order():
 
 
 # -- the largest communicator: 16 ranks ----------------------------------------------------------------------------
-@pytest.mark.parametrize("coll,slices", [("allreduce", 16), ("allgather", 1), ("reduce_scatter", 16)])
-def test_sixteen_rank_programs_on_the_cpu_oracle(coll, slices):
+@pytest.mark.parametrize("coll,slices,variant", [("allreduce", 16, {}), ("allgather", 1, {}),
+                                                  ("reduce_scatter", 16, {}), ("allgather", 1, {"push": True}),
+                                                  ("allreduce", 16, {"multicast": True}),
+                                                  ("allgather", 1, {"merge": False})])
+def test_sixteen_rank_programs_on_the_cpu_oracle(coll, slices, variant):
     """The symmetric heap's limit is 16 ranks: schedules of that size compile and run correctly (CPU interpreter,
     seeded CTA order, two launches so flag epochs advance)."""
     import numpy as np
     from vericcl_b200.program.device import compile_xml, run_cpu
     from vericcl_b200.synthesis import schedule_xml
     p = 16
-    compiled = compile_xml(schedule_xml(coll, p, slices), nlanes=2, niters=2)
+    compiled = compile_xml(schedule_xml(coll, p, slices), nlanes=2, niters=2, **variant)
     count = p * slices * 16
     rng = np.random.default_rng(16)
     inputs = [rng.uniform(-1, 1, count).astype(np.float32) for _ in range(p)]
