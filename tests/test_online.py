@@ -229,3 +229,45 @@ def test_rank_shares_describe_the_emulated_link():
     uneven = grouped_topology([3, 1], inter_gbps=30.0, rank_shares=True)
     caps = {r["id"]: r["capacity_bytes_per_us"] for r in uneven["shared_resources"] if "share" in r["id"]}
     assert caps["nic-share-rx-0"] == 10000.0 and caps["nic-share-rx-3"] == 30000.0
+
+
+def test_online_loop_dry_run_adopts_a_measured_improvement(tmp_path):
+    """The 2 x 4 loop end to end on the host: the probe campaign runs on an analytic executor, and the paired
+    acceptance measures a stand-in device whose times follow the exact prediction (with 0.2 % noise), so a
+    candidate the model predicts faster is adopted through the statistics, with its ledger entries written."""
+    import random
+    from types import SimpleNamespace
+    from vericcl_b200.execution.context import RunContext
+    from vericcl_b200.input.loader import load_request
+    from vericcl_b200.examples import write_documents
+    from vericcl_b200.online.acceptance import compare_measured
+    from vericcl_b200.online.loop import loop_documents
+    from vericcl_b200.workflow import PrimaryWorkflow
+    docs = loop_documents(groups=2, per_group=4, inter_gbps=25.0, size_bytes=128 << 20, rounds=2,
+                          datatype="float32", pairs=6)
+    files = write_documents(tmp_path / "in", docs)
+    req = load_request(files)
+    topo = load_topology(req)
+    ctx = RunContext.create(tmp_path, "c", "solve", run_id="r", input_files=files)
+    ctx.update_run_json(effective_request=dict(req.request_config))
+    rng = random.Random(5)
+    verdicts = []
+
+    def measure(incumbent, candidate):
+        times = {"A": incumbent.t_pred_us, "B": candidate.t_pred_us}
+        verdict = compare_measured(lambda label: times[label] * (1 + rng.uniform(-0.002, 0.002)), pairs=6,
+                                   seed=1, alpha=0.05, max_cv=0.05, max_rounds=2, min_relative_gain=0.0)
+        verdicts.append(verdict)
+        return verdict
+    executor = campaign.simulated_executor(topo, source="native_interpreter", noise=0.001)
+    wf = PrimaryWorkflow(req, ctx, probe_executor=executor, measure=measure)
+    result = wf.run()
+    assert result.status == "ok"
+    assert verdicts and all(v.accepted for v in verdicts), verdicts
+    adopted = [r for r in result.rounds if r.get("result") == "improved"]
+    assert len(adopted) == len(verdicts)
+    for r in adopted:
+        assert r["t_pred_us"] < r["start_t_pred_us"]
+        # the cut bound under the calibrated model stays the link bound: 128 MiB into a group over 25 GB/s
+        assert r["cut_lower_bound_us"] == pytest.approx((128 << 20) / 25e3, rel=1e-3)
+    assert (ctx.process / "reports" / "calibration.json").exists()

@@ -273,3 +273,25 @@ def test_slack_index_finds_every_chain_that_ends_at_t_pred():
     assert set(crit) == {"a1", "a2", "b1"}                  # both chains, never the nop or the slack operation
     path = pred.critical_path(ex)
     assert not ({"a1", "a2"} <= set(path) and "b1" in path)  # the single critical path covers one chain only
+
+
+# -- cut bound under measured sharing modes ------------------------------------------------------------------------
+def test_cut_rate_uses_measured_modes_only_on_their_own_links_and_resources():
+    from fractions import Fraction
+    from vericcl_b200.performance import RateProfile
+    from vericcl_b200.performance.initial import initial_cost_model
+    from vericcl_b200.verification.global_bound import _rate
+    req, topo = _topology(grouped_topology([2, 2], inter_gbps=25.0), 4, coll="allreduce", slices=4)
+    model = initial_cost_model(req)
+    base = _rate(topo, {0, 1}, model)
+    assert base == Fraction(25000)                     # the group's NIC: 25 GB/s out of group {0, 1}
+    # a measured mode of two NVLink flows inside group 0 must not lift the inter-group cut
+    fast = RateProfile("nvlink-pair", frozenset({"send:0:1:c1", "send:1:0:c1"}),
+                       {"send:0:1:c1": 700000.0, "send:1:0:c1": 700000.0})
+    with_mode = model.with_updates("m2", profiles=(fast,))[0]
+    assert _rate(topo, {0, 1}, with_mode) == base
+    # a measured mode through the NIC that beats its nominal capacity raises the cut to what was measured
+    nic = RateProfile("nic-pair", frozenset({"send:0:2:c1", "send:1:3:c1"}),
+                      {"send:0:2:c1": 20000.0, "send:1:3:c1": 20000.0})
+    with_nic = model.with_updates("m3", profiles=(nic,))[0]
+    assert _rate(topo, {0, 1}, with_nic) == Fraction(40000)

@@ -30,17 +30,44 @@ class CutBound:
     exact: tuple
 
 
+def _flow_link(flow_id: str):
+    """(src, dst) of a transfer flow id ``kind:src:dst:c<channel>``; None for local work."""
+    parts = str(flow_id).split(":")
+    if len(parts) >= 3 and parts[0] in ("send", "rrc") and parts[1].isdigit() and parts[2].isdigit():
+        return int(parts[1]), int(parts[2])
+    return None
+
+
 def _link_cap(topology, model, key) -> Fraction:
-    """Fastest rate (bytes/µs) any operation can reach on link ``key`` under the model."""
+    """Fastest rate (bytes/µs) any operation can reach on link ``key`` under the model: its own service
+    curves, and the measured rates of sharing modes for flows on this very link."""
     rates = []
     if model is not None:
         for name in ("link:%d:%d" % (key.src, key.dst), "rrc:%d:%d" % (key.src, key.dst)):
             rates += [1 / Fraction(str(c.beta_us_per_byte)) for c in model.services.get(name, ())]
         for profile in model.profiles:
-            rates += [Fraction(str(r)) for r in profile.rates.values()]
+            rates += [Fraction(str(r)) for flow, r in profile.rates.items() if _flow_link(flow) == (key.src, key.dst)]
     if not rates:
         rates = [Fraction(1) / Fraction(str(topology.links[key].beta_us_per_byte))]
     return max(rates)
+
+
+def _resource_cap(model, rid, links, nominal) -> Fraction | None:
+    """Capacity of a shared resource under the model: its modelled capacity, raised to the largest combined
+    rate any measured sharing mode reached through it (a measured mode may beat the nominal share)."""
+    # with a model, only the resources it constrains bound the cut (an unmodelled resource never slows a
+    # predicted schedule, so using it here could put the bound above T_pred)
+    capacity = nominal if model is None else model.resources.get(rid)
+    if capacity is None:
+        return None
+    best = Fraction(str(capacity))
+    if model is not None:
+        members = {(l.src, l.dst) for l in links}
+        for profile in model.profiles:
+            through = sum((Fraction(str(r)) for flow, r in profile.rates.items() if _flow_link(flow) in members),
+                          Fraction(0))
+            best = max(best, through)
+    return best
 
 
 def _rate(topology, inside, model=None):
@@ -51,8 +78,9 @@ def _rate(topology, inside, model=None):
     tried (all links, any single covering resource, the senders' ports, the
     receivers' ports, a greedy cheapest cover) is returned.  With a cost
     model, link rates are the model's fastest for the link and resource
-    capacities the model's; a model with measured concurrency profiles (whose
-    rates may exceed a resource's nominal share) bounds links only.
+    capacities the model's, each raised to the largest combined rate a
+    measured sharing mode reached through it, so the bound stays valid when
+    a measured mode beats a nominal share.
     """
     outside = set(range(topology.rank_count)) - set(inside)
     crossing = {k for k in topology.links if k.src in inside and k.dst in outside}
@@ -61,13 +89,11 @@ def _rate(topology, inside, model=None):
     caps = {k: _link_cap(topology, model, k) for k in crossing}
     bound = sum(caps.values())
     families = {}
-    if model is not None and model.profiles:
-        return bound
     for rid, res in topology.resources.items():
         members = frozenset(l for l in res.links if l in crossing)
-        capacity = res.capacity_bytes_per_us if model is None else model.resources.get(rid)
+        capacity = _resource_cap(model, rid, res.links, res.capacity_bytes_per_us)
         if members and capacity is not None:
-            families[rid] = (members, Fraction(str(capacity)))
+            families[rid] = (members, capacity)
     for rid, (members, cap) in families.items():
         if members == crossing:
             bound = min(bound, cap)
