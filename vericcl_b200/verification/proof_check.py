@@ -98,11 +98,15 @@ def fixed_work(strategies) -> bool:
 
 
 def optimistic_relaxation(executable, model):
-    """(A, b, c) of the fixed-work relaxation: T ≥ optimistic finish of every operation."""
-    fastest = Fraction(0)
+    """(A, b, c) of the fixed-work relaxation: T ≥ optimistic finish of every operation.
+
+    Each operation runs at the faster of its own service rate and the largest rate any measured sharing mode
+    gives its flow (the only rates the simulator can give it), with no contention at all.
+    """
+    measured = {}
     for profile in model.profiles:
-        for rate in profile.rates.values():
-            fastest = max(fastest, rational(rate))
+        for flow, rate in profile.rates.items():
+            measured[flow] = max(measured.get(flow, Fraction(0)), rational(rate))
     ops = {op.operation_id: op for op in executable.operations}
     finish, pending = {}, dict(ops)
     while pending:
@@ -118,7 +122,7 @@ def optimistic_relaxation(executable, model):
             cost = model.service_for(op.component, op.nbytes)
             if cost is None:
                 raise SemanticError("the relaxation needs a service cost for " + op.component)
-            rate = max(1 / rational(cost.beta_us_per_byte), fastest)
+            rate = max(1 / rational(cost.beta_us_per_byte), measured.get(op.flow_id, Fraction(0)))
             finish[key] = start + rational(cost.alpha_us) + Fraction(op.nbytes) / rate
     bounds = [finish[k] for k in sorted(finish)] or [Fraction(0)]
     return [[1] for _ in bounds], [str(v) for v in bounds], [1]
