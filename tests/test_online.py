@@ -271,3 +271,20 @@ def test_online_loop_dry_run_adopts_a_measured_improvement(tmp_path):
         # the cut bound under the calibrated model stays the link bound: 128 MiB into a group over 25 GB/s
         assert r["cut_lower_bound_us"] == pytest.approx((128 << 20) / 25e3, rel=1e-3)
     assert (ctx.process / "reports" / "calibration.json").exists()
+
+
+def test_recalibration_replaces_measured_sharing_modes():
+    """Publishing a second calibration of the same modes keeps one mode per flow set (no duplicate ids)."""
+    from vericcl_b200.performance import RateProfile
+    base = initial_cost_model(resolve_documents(example_documents("allgather", "hierarchy", 4,
+                                                                  total_size_bytes=1 << 20,
+                                                                  slice_size_bytes=1 << 18)))
+    mode = RateProfile("shared-x-0", frozenset({"send:0:1:c1", "send:2:1:c1"}),
+                       {"send:0:1:c1": 300.0, "send:2:1:c1": 300.0})
+    first, _ = campaign.publish_model(base, {}, (mode,), stamp="2026-01-01T00:00:00+00:00")
+    again = RateProfile("shared-x-0", mode.flows, {"send:0:1:c1": 320.0, "send:2:1:c1": 310.0})
+    second, _ = campaign.publish_model(first, {}, (again,), stamp="2026-01-02T00:00:00+00:00")
+    assert [p.rates["send:0:1:c1"] for p in second.profiles] == [320.0]
+    renamed = RateProfile("shared-y-0", mode.flows, {"send:0:1:c1": 330.0, "send:2:1:c1": 330.0})
+    third, _ = campaign.publish_model(second, {}, (renamed,), stamp="2026-01-03T00:00:00+00:00")
+    assert [p.profile_id for p in third.profiles] == ["shared-y-0"]

@@ -35,7 +35,14 @@ def publish_model(model, fitted: dict, profiles=(), *, stamp: str | None = None)
     version = "measured-" + digest({"base": model.version, "services": {k: [asdict(c) for c in v]
                                                                          for k, v in services.items()},
                                     "profiles": [p.as_json() for p in profiles]})[:24]
-    merged_profiles = tuple(model.profiles) + tuple(profiles) if profiles else None
+    merged_profiles = None
+    if profiles:
+        # a new measurement of a sharing mode replaces the old one: same id, or the same set of flows (two modes
+        # of one flow set would make the prediction ambiguous)
+        fresh_ids = {p.profile_id for p in profiles}
+        fresh_flows = {p.flows for p in profiles}
+        kept = [p for p in model.profiles if p.profile_id not in fresh_ids and p.flows not in fresh_flows]
+        merged_profiles = tuple(kept) + tuple(profiles)
     return model.with_updates(version, services=services, profiles=merged_profiles)
 
 
