@@ -288,3 +288,38 @@ def test_recalibration_replaces_measured_sharing_modes():
     renamed = RateProfile("shared-y-0", mode.flows, {"send:0:1:c1": 330.0, "send:2:1:c1": 330.0})
     third, _ = campaign.publish_model(second, {}, (renamed,), stamp="2026-01-03T00:00:00+00:00")
     assert [p.profile_id for p in third.profiles] == ["shared-y-0"]
+
+
+def test_calibrated_model_round_trips_into_verify_and_tune(tmp_path):
+    """A solve calibrated on the analytic executor publishes a model with measured sharing modes; verifying and
+    tuning the published schedule under that model keeps the cut bound at the link bound and never gets worse."""
+    from vericcl_b200.execution.context import RunContext
+    from vericcl_b200.examples import write_documents
+    from vericcl_b200.input.loader import load_request
+    from vericcl_b200.online.loop import loop_documents
+    from vericcl_b200.performance.model import CostModel
+    from vericcl_b200.utils.jsonio import strict_load
+    from vericcl_b200.workflow import PrimaryWorkflow
+    docs = loop_documents(groups=2, per_group=2, inter_gbps=25.0, size_bytes=8 << 20, rounds=1,
+                          datatype="float32", pairs=4)
+    docs["sketch"]["trace_and_measure"]["enabled"] = False
+    files = write_documents(tmp_path / "in", docs)
+    req = load_request(files)
+    topo = load_topology(req)
+    ctx = RunContext.create(tmp_path, "c", "solve", run_id="r", input_files=files)
+    ctx.update_run_json(effective_request=dict(req.request_config))
+    executor = campaign.simulated_executor(topo, source="native_interpreter", noise=0.001)
+    solved = PrimaryWorkflow(req, ctx, probe_executor=executor).run()
+    assert solved.status == "ok"
+    model = CostModel.from_json(strict_load(ctx.directory / "model.json"))
+    assert model.profiles and model.version.startswith("measured-")
+    req2 = load_request(files, purpose="verify")
+    ctx2 = RunContext.create(tmp_path, "c", "verify", run_id="v", input_files=files)
+    ctx2.update_run_json(effective_request=dict(req2.request_config))
+    verified = PrimaryWorkflow(req2, ctx2, purpose="verify", tune=True, model=model,
+                               verify_inputs={"xml": (ctx.directory / "schedule.xml").read_text(),
+                                              "sidecar": strict_load(ctx.directory / "schedule.json")}).run()
+    assert verified.status == "ok"
+    assert verified.best["t_pred_us"] <= solved.best["t_pred_us"] + 1e-9
+    bound = verified.rounds[0]["cut_lower_bound_us"]
+    assert (8 << 20) / 25e3 <= bound <= verified.best["t_pred_us"]
