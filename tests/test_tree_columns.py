@@ -1,0 +1,47 @@
+"""Tree column generation against the shared-resource master, with the LP's own duals."""
+from vericcl_b200.examples import example_documents
+from vericcl_b200.input.loader import resolve_documents
+from vericcl_b200.solver.milp import Model
+from vericcl_b200.solver.trees.columns import generate_trees
+from vericcl_b200.topology.nvswitch import multinode_topology
+
+
+def test_lp_duals_match_the_textbook_signs():
+    # min x + 2y  s.t.  x + y >= 3 (dual 1: raising 3 costs 1 per unit),  y <= 5,  x <= 2 (binds: dual -1)
+    m = Model("duals")
+    x, y = m.continuous("x"), m.continuous("y")
+    m.add_ge([(1, x), (1, y)], 3.0, name="cover")
+    m.add_le([(1, y)], 5.0, name="ycap")
+    m.add_le([(1, x)], 2.0, name="xcap")
+    m.minimize([(1, x), (2, y)])
+    sol, duals = m.solve_lp_duals()
+    assert abs(sol.objective - 4.0) < 1e-9
+    assert abs(duals[0] - 2.0) < 1e-9 and abs(duals[1]) < 1e-9 and abs(duals[2] + 1.0) < 1e-9
+
+
+def _shared_nic_topology():
+    from vericcl_b200.topology import load_topology
+    d = example_documents("allgather", "constructive_trees", 4, total_size_bytes=4 << 20, slice_size_bytes=1 << 20,
+                          topology=multinode_topology(2, 2, inter_gbps=25.0, rank_shares=True))
+    return load_topology(resolve_documents(d))
+
+
+def test_shared_nics_get_relay_trees():
+    """2 groups × 2 ranks, one 25 GB/s NIC per group, each rank's receive share half of it.
+
+    A star from every root crosses the NIC twice per slice; a tree that crosses
+    once and relays inside the other group halves the NIC time, and the LP's
+    duals find it.  Each group's NIC carries its two roots' slices: 2 roots × 4
+    slices × 2 crossings × 42 µs with stars, half that with relay trees.
+    """
+    topo = _shared_nic_topology()
+    slice_bytes = 1 << 20
+    groups = [{"id": "g%d" % r, "root": r, "dests": [d for d in range(4) if d != r], "slices": 4,
+               "reverse": False} for r in range(4)]
+    picks, z = generate_trees(topo, groups, slice_bytes)
+    star_z = 2 * 4 * 2 * slice_bytes / 25e3
+    assert z <= star_z / 2 + 1e-6
+    for gid, chosen in picks.items():
+        assert sum(count for _, count in chosen) == 4
+        for edges, _ in chosen:
+            assert len([(a, b) for a, b in edges if a // 2 != b // 2]) == 1     # one NIC crossing per slice

@@ -164,6 +164,54 @@ class Model:
             return _solve_arrays(self.arrays(), [v.name for v in self.vars], self.objective_constant,
                                  time_limit, mip_gap)
 
+    def solve_lp_duals(self, *, time_limit: float = 60.0):
+        """Solve the LP relaxation and return ``(solution, duals)``: ``duals[r]`` = ∂objective/∂(bound of row r).
+
+        For a ``≤`` row the dual is ≤ 0 (raising the bound can only lower the
+        minimum), for a ``≥`` row ≥ 0, and an equality row's dual is free.  A
+        row bounded on both sides reports the side that binds.  Integrality is
+        ignored.
+        """
+        from scipy.optimize import linprog
+        c, lb, ub, _, a, lo, hi = self.arrays()
+        start = time.monotonic()
+        ub_rows, ub_rhs, ub_sign, ub_of, eq_rows, eq_rhs, eq_of = [], [], [], [], [], [], []
+        dense = a.toarray() if a is not None else np.zeros((0, len(c)))
+        for r in range(dense.shape[0]):
+            if lo[r] == hi[r]:
+                eq_of.append(r)
+                eq_rows.append(dense[r])
+                eq_rhs.append(hi[r])
+                continue
+            if hi[r] != INF:
+                ub_of.append(r)
+                ub_rows.append(dense[r])
+                ub_rhs.append(hi[r])
+                ub_sign.append(1.0)
+            if lo[r] != -INF:
+                ub_of.append(r)
+                ub_rows.append(-dense[r])
+                ub_rhs.append(-lo[r])
+                ub_sign.append(-1.0)
+        with _solver_output_to_stderr():
+            res = linprog(c, A_ub=np.array(ub_rows) if ub_rows else None, b_ub=ub_rhs or None,
+                          A_eq=np.array(eq_rows) if eq_rows else None, b_eq=eq_rhs or None,
+                          bounds=list(zip(lb, [None if u == INF else u for u in ub])), method="highs",
+                          options={"time_limit": max(0.05, float(time_limit))})
+        runtime = time.monotonic() - start
+        if res.x is None or res.status != 0:
+            return Solution("error" if res.x is None else "feasible", None, {}, None, runtime, str(res.message)), {}
+        duals = [0.0] * dense.shape[0]
+        for k, r in enumerate(ub_of):
+            value = float(res.ineqlin.marginals[k]) * ub_sign[k]
+            if abs(value) > abs(duals[r]):
+                duals[r] = value
+        for k, r in enumerate(eq_of):
+            duals[r] = float(res.eqlin.marginals[k])
+        values = {v.name: float(x) for v, x in zip(self.vars, res.x)}
+        return Solution("optimal", float(res.fun) + self.objective_constant, values, None, runtime,
+                        str(res.message)), duals
+
 
 _QUIET_LOCK = threading.Lock()
 _QUIET = {"depth": 0, "saved": None}

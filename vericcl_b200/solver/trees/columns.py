@@ -7,8 +7,10 @@ NVLink port or a NIC) is busy for at most ``z`` µs; minimise ``z``.  Pricing:
 for each demand group, a minimum-cost arborescence under the master's dual
 prices (edge cost = Σ over the edge's resources of dual × per-slice busy
 time), found with Edmonds' algorithm; columns with negative reduced cost are
-added until none remains (reference: vericcl/solver/trees/operators.py:204-533,
-which uses a SCIP integer master with lazily generated tree columns).
+added until none remains.  The prices are the LP's own duals (HiGHS
+marginals), so the loop stops at the LP optimum over all trees the pricing
+can find (reference: vericcl/solver/trees/operators.py:204-533, which uses a
+SCIP integer master with lazily generated tree columns).
 """
 from __future__ import annotations
 
@@ -81,10 +83,10 @@ def generate_trees(topology, groups, slice_bytes, *, max_rounds: int = 30, time_
     duals = {}
     for _ in range(max_rounds):
         lp, cons, z = _master(topology, groups, columns, slice_bytes, integer=False)
-        sol = lp.solve(time_limit=time_limit)
+        sol, row_duals = lp.solve_lp_duals(time_limit=time_limit)
         if not sol.usable:
             raise SolverError("tree master LP failed: " + sol.message)
-        duals = _duals(lp, topology, groups, columns, slice_bytes, sol)
+        duals = _duals(lp, groups, cons, row_duals)
         added = 0
         for g in groups:
             allowed = set(g.get("allowed") or range(topology.rank_count))
@@ -129,29 +131,18 @@ def _master(topology, groups, columns, slice_bytes, integer):
     return m, cons, z
 
 
-def _duals(model, topology, groups, columns, slice_bytes, sol):
-    """Recover LP duals by solving the dual-feasibility conditions on active columns.
+def _duals(model, groups, cons, row_duals):
+    """Dual prices of the master LP.
 
-    HiGHS through ``scipy.optimize.milp`` does not expose duals, so we price
-    with resource weights proportional to their load share at the optimum
-    (``load_r / z``) and demand prices equal to the cheapest column's cost under
-    those weights — a standard heuristic pricing that keeps generating columns
-    on the bottleneck resources.
+    With resource rows ``Σ busy·y − z ≤ 0`` (dual π_r ≥ 0) and demand rows
+    ``Σ_t y = slices`` (dual μ_d), a tree column of group d has reduced cost
+    ``Σ_r π_r · busy_r(tree) − μ_d``; pricing adds the cheapest tree when that
+    is negative.  HiGHS reports ∂objective/∂bound, which is −π_r for a
+    resource row and μ_d for a demand row.
     """
-    z = max(sol.values["z"], 1e-12)
-    loads = {}
-    for g in groups:
-        for t, edges in enumerate(columns[g["id"]]):
-            y = sol.values["y:%s:%d" % (g["id"], t)]
-            for rid, busy in _tree_usage(topology, edges, slice_bytes).items():
-                loads[rid] = loads.get(rid, 0.0) + busy * y
-    res = {rid: (load / z) ** 4 for rid, load in loads.items()}
+    res = {rid: max(0.0, -row_duals[row]) for rid, row in cons.items()}
     demand = {}
     for g in groups:
-        best = None
-        for edges in columns[g["id"]]:
-            cost = sum(res.get(rid, 0.0) * busy / slice_bytes * slice_bytes
-                       for rid, busy in _tree_usage(topology, edges, slice_bytes).items()) / slice_bytes
-            best = cost if best is None else min(best, cost)
-        demand[g["id"]] = best or 0.0
+        row = next(i for i, r in enumerate(model.rows) if r[3] == "demand:%s" % g["id"])
+        demand[g["id"]] = row_duals[row]
     return {"res": res, "demand": demand}
