@@ -45,3 +45,30 @@ def test_shared_nics_get_relay_trees():
         assert sum(count for _, count in chosen) == 4
         for edges, _ in chosen:
             assert len([(a, b) for a, b in edges if a // 2 != b // 2]) == 1     # one NIC crossing per slice
+
+
+def test_lp_duals_of_equality_and_ranged_rows():
+    # min 3a + b  s.t.  a + b = 4 (free dual),  1 <= a <= 10 (ranged; the lower side binds: dual 2)
+    m = Model("ranged")
+    a, b = m.continuous("a"), m.continuous("b")
+    m.add_eq([(1, a), (1, b)], 4.0, name="sum")
+    m.add([(1, a)], 1.0, 10.0, name="range")
+    m.minimize([(3, a), (1, b)])
+    sol, duals = m.solve_lp_duals()
+    assert abs(sol.values["a"] - 1.0) < 1e-9 and abs(sol.values["b"] - 3.0) < 1e-9
+    assert abs(duals[0] - 1.0) < 1e-9 and abs(duals[1] - 2.0) < 1e-9
+
+
+def test_reduction_trees_cross_the_nic_once():
+    """Reduce groups are in-trees: every rank's slice reaches the owner with one NIC crossing per slice."""
+    topo = _shared_nic_topology()
+    slice_bytes = 1 << 20
+    groups = [{"id": "r%d" % r, "root": r, "dests": [d for d in range(4) if d != r], "slices": 2,
+               "reverse": True} for r in range(4)]
+    picks, z = generate_trees(topo, groups, slice_bytes)
+    assert z <= 2 * 2 * slice_bytes / 25e3 + 1e-6          # two owners per group × 2 slices × one crossing
+    for gid, chosen in picks.items():
+        owner = int(gid[1:])
+        for edges, _ in chosen:
+            assert all(b == owner or any(a2 == b for a2, _ in edges) for _, b in edges)   # edges point to the owner
+            assert len([(a, b) for a, b in edges if a // 2 != b // 2]) == 1
