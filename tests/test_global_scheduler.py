@@ -49,3 +49,31 @@ def test_one_channel_is_left_alone_and_synthesis_keeps_the_better_assignment():
                           max_channels=4, scratch_bytes=4096 * 16 * 4)
     bundle = synthesize(resolve_documents(d), channels=4, timing=False)
     assert bundle.can_execute
+
+
+def _blocks(candidate):
+    blocks = {}
+    for op in candidate.operations:
+        blocks.setdefault(op.src_rank, set()).add((op.dst_rank, "send", op.channel))
+        blocks.setdefault(op.dst_rank, set()).add((op.src_rank, "recv", op.channel))
+    return blocks
+
+
+def test_the_thread_block_budget_per_rank_holds():
+    req, topo, net = _network("allreduce", 4, 16, 4)
+    roomy = _blocks(assign_channels(net, topo, 4))
+    assert max(len(b) for b in roomy.values()) > 8                 # without a budget the links use several channels
+    capped = assign_channels(net, topo, 4, max_blocks_per_rank=8)
+    assert max(len(b) for b in _blocks(capped).values()) <= 8
+    b = lower_candidate(req, topo, capped)
+    assert b.can_execute, b.checks
+    ok, err = check_program_numerics(parse_xml(b.xml), count_per_rank=16 * 16, seed=5)
+    assert ok, err
+
+
+def test_a_budget_below_one_block_per_connection_gives_each_connection_one():
+    _, topo, net = _network("allreduce", 4, 16, 4)
+    capped = assign_channels(net, topo, 4, max_blocks_per_rank=2)
+    blocks = _blocks(capped)
+    # each rank talks to 3 peers both ways: 6 blocks is the least any assignment can use
+    assert all(len(b) == 6 for b in blocks.values())

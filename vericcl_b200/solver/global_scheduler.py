@@ -9,7 +9,10 @@ can start earliest, and among equally early ones the channel carrying the
 least work so far, so channels of a link stay balanced.  Channel budgets per
 rank are respected: a rank may open at most ``max_blocks_per_rank`` distinct
 (peer, direction, channel) thread blocks, the runtime limit the admission
-checks enforce (reference: vericcl/solver/global_scheduler.py:113-229, which
+checks enforce.  Every (peer, direction) a rank needs keeps one block in
+reserve, so extra channels early in the schedule never crowd out a
+connection that opens later; below one block per connection each
+connection gets exactly one (reference: vericcl/solver/global_scheduler.py:113-229, which
 assigns channels and resource slots for the whole candidate at once).
 """
 from __future__ import annotations
@@ -37,6 +40,21 @@ def assign_channels(candidate: NetworkCandidate, topology, channels: int, *,
     heapq.heapify(heap)
     free, work = {}, {}           # (src, dst, channel) -> time it frees up / work assigned so far
     blocks = {}                   # rank -> set of (peer, direction, channel) thread blocks in use
+    # rank -> (peer, direction) pairs it must open at least one block for, and those it has opened
+    needed, opened = {}, {}
+    for op in ops.values():
+        needed.setdefault(op.src_rank, set()).add((op.dst_rank, "send"))
+        needed.setdefault(op.dst_rank, set()).add((op.src_rank, "recv"))
+
+    def admits(rank, pair, channel):
+        if (pair + (channel,)) in blocks.get(rank, ()):
+            return True
+        if pair not in opened.get(rank, ()):
+            return True           # a connection's first block: reserved for it from the start
+        # an extra channel: it must leave one block for every pair the rank has not opened yet
+        unopened = len(needed[rank] - opened.get(rank, set()))
+        return len(blocks.get(rank, ())) + unopened + 1 <= max_blocks_per_rank
+
     chosen = {}
     while heap:
         _, key = heapq.heappop(heap)
@@ -47,22 +65,21 @@ def assign_channels(candidate: NetworkCandidate, topology, channels: int, *,
         best = None
         for c in range(limit):
             conn = (op.src_rank, op.dst_rank, c)
-            new_blocks = (((op.dst_rank, "send", c) not in blocks.get(op.src_rank, set())) +
-                          ((op.src_rank, "recv", c) not in blocks.get(op.dst_rank, set())))
-            if new_blocks and (len(blocks.get(op.src_rank, ())) >= max_blocks_per_rank or
-                               len(blocks.get(op.dst_rank, ())) >= max_blocks_per_rank):
+            if not (admits(op.src_rank, (op.dst_rank, "send"), c) and admits(op.dst_rank, (op.src_rank, "recv"), c)):
                 continue
             start = max(ready_at[key], free.get(conn, 0.0))
             rank_key = (start, work.get(conn, 0.0), c)
             if best is None or rank_key < best[0]:
                 best = (rank_key, c)
-        c = best[1] if best is not None else op.channel
+        c = best[1] if best is not None else 0      # unreachable: a connection's open channel is always admitted
         conn = (op.src_rank, op.dst_rank, c)
         start = max(ready_at[key], free.get(conn, 0.0))
         free[conn] = start + dur
         work[conn] = work.get(conn, 0.0) + dur
         blocks.setdefault(op.src_rank, set()).add((op.dst_rank, "send", c))
         blocks.setdefault(op.dst_rank, set()).add((op.src_rank, "recv", c))
+        opened.setdefault(op.src_rank, set()).add((op.dst_rank, "send"))
+        opened.setdefault(op.dst_rank, set()).add((op.src_rank, "recv"))
         chosen[key] = c
         for nxt in succ[key]:
             indeg[nxt] -= 1

@@ -95,7 +95,8 @@ def synthesize(request, model=None, *, channels: int = 1, timing: bool = True, p
     if channels > 1:
         # channels chosen for the whole schedule at once instead of round-robin per link
         from vericcl_b200.solver.global_scheduler import assign_channels
-        global_net = assign_channels(network, topology, channels)
+        global_net = assign_channels(network, topology, channels,
+                                     max_blocks_per_rank=request.request_config["runtime"]["limits"]["tbs_per_rank"])
         try:
             alt = lower_candidate(request, topology, global_net, model, plan=plan, origin=global_net.origin)
         except SemanticError:
