@@ -72,3 +72,12 @@ def test_reduction_trees_cross_the_nic_once():
         for edges, _ in chosen:
             assert all(b == owner or any(a2 == b for a2, _ in edges) for _, b in edges)   # edges point to the owner
             assert len([(a, b) for a, b in edges if a // 2 != b // 2]) == 1
+
+
+def test_an_unreachable_destination_is_a_solver_error():
+    import pytest
+    from vericcl_b200.errors import SolverError
+    topo = _shared_nic_topology()
+    groups = [{"id": "g0", "root": 0, "dests": [1, 2, 3], "slices": 1, "reverse": False, "allowed": [0, 1, 2]}]
+    with pytest.raises(SolverError, match="reaches ranks \\[3\\]"):
+        generate_trees(topo, groups, 1 << 20)

@@ -53,7 +53,10 @@ def _price(topology, root, dests, allowed, duals, slice_bytes, reverse):
             continue
         cost = sum(duals.get(rid, 0.0) * per * slice_bytes for rid, per in _resources(topology, key.src, key.dst))
         g.add_edge(a, b, weight=cost + 1e-9)
-    reach = nx.descendants(g, root) | {root}
+    reach = (nx.descendants(g, root) if root in g else set()) | {root}
+    cut_off = sorted(set(dests) - reach)
+    if cut_off:
+        raise SolverError("no tree from rank %d reaches ranks %s over the allowed links" % (root, cut_off))
     arb = nx.minimum_spanning_arborescence(g.subgraph(reach), attr="weight")
     keep = set()
     for d in dests:
