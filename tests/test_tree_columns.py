@@ -81,3 +81,47 @@ def test_an_unreachable_destination_is_a_solver_error():
     groups = [{"id": "g0", "root": 0, "dests": [1, 2, 3], "slices": 1, "reverse": False, "allowed": [0, 1, 2]}]
     with pytest.raises(SolverError, match="reaches ranks \\[3\\]"):
         generate_trees(topo, groups, 1 << 20)
+
+
+def _spans(edges, root, dests, reverse):
+    parent = {}
+    for a, b in edges:
+        child, up = (a, b) if reverse else (b, a)
+        assert child not in parent, "two parents for rank %d" % child
+        parent[child] = up
+    for d in dests:
+        node, hops = d, 0
+        while node != root:
+            node = parent[node]
+            hops += 1
+            assert hops <= len(parent), "cycle above rank %d" % d
+    return True
+
+
+def test_random_shared_nic_topologies_give_spanning_trees_no_worse_than_stars():
+    from hypothesis import given, settings, strategies as st
+    from vericcl_b200.solver.trees.columns import _master, _star
+    from vericcl_b200.topology import load_topology
+
+    @settings(max_examples=12, deadline=None)
+    @given(groups_n=st.integers(2, 3), per=st.integers(1, 3), shares=st.booleans(), reverse=st.booleans(),
+           slices=st.integers(1, 3), gbps=st.sampled_from([12.5, 25.0, 50.0]))
+    def check(groups_n, per, shares, reverse, slices, gbps):
+        ranks = groups_n * per
+        d = example_documents("allgather", "constructive_trees", ranks, total_size_bytes=ranks * 4096,
+                              slice_size_bytes=4096,
+                              topology=multinode_topology(groups_n, per, inter_gbps=gbps, rank_shares=shares))
+        topo = load_topology(resolve_documents(d))
+        spec = [{"id": "g%d" % r, "root": r, "dests": [x for x in range(ranks) if x != r], "slices": slices,
+                 "reverse": reverse} for r in range(ranks)]
+        picks, z = generate_trees(topo, spec, 1 << 20)
+        stars = {g["id"]: [_star(g["root"], g["dests"], reverse)] for g in spec}
+        star_sol = _master(topo, spec, stars, 1 << 20, integer=True)[0].solve()
+        assert z <= star_sol.values["z"] + 1e-6
+        for g in spec:
+            assert sum(count for _, count in picks[g["id"]]) == slices
+            for edges, _ in picks[g["id"]]:
+                assert all(topo.has_link(a, b) for a, b in edges)
+                assert _spans(edges, g["root"], g["dests"], reverse)
+
+    check()
