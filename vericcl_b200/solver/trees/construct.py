@@ -48,7 +48,14 @@ def construct_trees(request, topology, demands, slice_bytes, *, time_limit: floa
     for index, ((kind, root, members), ds) in enumerate(groups.items()):
         spec.append({"id": "g%d" % index, "root": root, "dests": list(members), "slices": len(ds),
                      "reverse": kind == "reduce"})
-    picks, _ = generate_trees(topology, spec, slice_bytes, time_limit=time_limit)
+    # an owner broadcasts a slice only after its reduction tree has delivered it, so the reduction trees and the
+    # broadcast trees are two phases: each phase gets its own master and balances its own load (one joint master
+    # may load a rank's receive share with two reductions and leave it idle in the broadcasts, doubling the time)
+    picks = {}
+    for phase in (True, False):
+        part = [g for g in spec if g["reverse"] is phase]
+        if part:
+            picks.update(generate_trees(topology, part, slice_bytes, time_limit=time_limit)[0])
     for index, ((kind, root, members), ds) in enumerate(groups.items()):
         _assign(ds, picks["g%d" % index], chosen)
     return chosen
