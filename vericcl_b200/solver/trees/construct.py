@@ -4,7 +4,8 @@ Demands are grouped by root (AllGather: one group per source rank; AllReduce:
 a reduction group into each slice owner plus the owner's broadcast group).
 Without shared resources on a symmetric topology the fast path packs
 edge-disjoint arborescences by max-flow (:mod:`packing`); otherwise tree
-columns are generated against the shared-resource master (:mod:`columns`).
+columns are generated against the shared-resource master (:mod:`columns`),
+one master for the reduction trees and one for the broadcast trees.
 Each slice is then bound to one chosen tree, and the fixed routes are
 composed and timed like any other plan (reference:
 vericcl/solver/constructive.py:27-36, vericcl/solver/trees/operators.py:537).
