@@ -145,3 +145,13 @@ def test_allreduce_trees_balance_each_phase_on_eight_ranks_behind_two_nics():
         assert bundle.can_execute, bundle.checks
         times[method] = bundle.t_pred_us
     assert times["constructive_trees"] <= 1.15 * times["hierarchy"]
+
+
+def test_lp_duals_of_an_infeasible_model_are_unusable():
+    m = Model("infeasible")
+    x = m.continuous("x")
+    m.add_ge([(1, x)], 2.0, name="low")
+    m.add_le([(1, x)], 1.0, name="high")
+    m.minimize([(1, x)])
+    sol, duals = m.solve_lp_duals()
+    assert sol.status == "infeasible" and not sol.usable and duals == []

@@ -200,7 +200,9 @@ class Model:
                           options={"time_limit": max(0.05, float(time_limit))})
         runtime = time.monotonic() - start
         if res.x is None or res.status != 0:
-            return Solution("error" if res.x is None else "feasible", None, {}, None, runtime, str(res.message)), {}
+            # duals are only meaningful at a proven optimum: anything else (limit, infeasible, unbounded) is unusable
+            status = {1: "timeout", 2: "infeasible"}.get(res.status, "error")
+            return Solution(status, None, {}, None, runtime, str(res.message)), []
         duals = [0.0] * dense.shape[0]
         for k, r in enumerate(ub_of):
             value = float(res.ineqlin.marginals[k]) * ub_sign[k]
